@@ -1,0 +1,327 @@
+// Block-diffusion draft attention and causal verify attention over the paged bf16 K/V cache, sm_100a.
+//
+// Rows of one request and one KV head: the GQA group's G query heads x K window rows (row r = g*K + j), packed into
+// m16 tiles, one compute warp per tile.  Window row j sits at position base + j, base = seq_len (+1 for verify, whose
+// window starts after the committed x0).  Row j sees cache positions [0, lim(j)):
+//   draft  (reference selfspec_diffusion_worker.py:702-704, fast_sampling.py:508-510): lim(0) = base + 1 (x0 is
+//          causal), lim(j >= 1) = base + K (the B mask rows see the whole block, bidirectionally);
+//   causal (verify, fast_sampling.py:512-514; also chunked prefill): lim(j) = base + j + 1.
+// Cache layout [page][kv_head][page_size = 16][128] per layer (bf16), K and V separate.  A producer warp streams
+// 64-token tiles (4 pages, both 64-dim halves of K and V) with 2-D TMA loads in the 128-byte swizzle; compute warps
+// run S = Q K^T and O += P V on mma.sync m16n8k16 with an fp32 online softmax (quad shuffles).
+// Split-KV: CTA (split, kv_head, request) covers cache positions [split*chunk, (split+1)*chunk); when a request needs
+// more than one split, each writes (m, l, O) partials and the last split to arrive merges them in split order.
+#include "params.cuh"
+
+namespace gr {
+
+constexpr int kTile = 64;                       // tokens per pipeline stage
+constexpr int kHalfBytes = kTile * 128;         // 64 rows x 64 dims bf16
+constexpr int kStageBytes = 4 * kHalfBytes;     // K lo, K hi, V lo, V hi
+constexpr int kStages = 3;
+
+__device__ __forceinline__ int row_limit(const AttnParams& p, int j, int base) {
+  if (p.draft) return j == 0 ? base + 1 : base + p.K;
+  return base + j + 1;
+}
+
+__global__ void __launch_bounds__(288, 1) attention_kernel(const __grid_constant__ CUtensorMap tmk,
+                                                           const __grid_constant__ CUtensorMap tmv,
+                                                           const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int G = p.n_q_heads / p.n_kv_heads;
+  const int R = G * p.K;
+  const int n_mt = (R + 15) / 16;
+  const int R_pad = n_mt * 16;
+  uint8_t* kv_smem = smem;                                    // kStages x kStageBytes
+  uint8_t* q_smem = smem + kStages * kStageBytes;             // 2 halves x R_pad x 128 B
+  uint64_t* full = reinterpret_cast<uint64_t*>(q_smem + 2 * R_pad * 128);
+  uint64_t* empty = full + kStages;
+  int* flag = reinterpret_cast<int*>(empty + kStages);
+
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t seq = p.seq_lens[b];
+  const int base = static_cast<int>(seq) + p.base_add;
+  const int L = base + p.K;                          // the last row's limit
+  const int n_active = (L + p.chunk - 1) / p.chunk;
+  if (split >= n_active) return;
+  const int kv_beg = split * p.chunk;
+  const int kv_end = min(L, kv_beg + p.chunk);
+  const int n_tiles = (kv_end - kv_beg + kTile - 1) / kTile;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, n_mt);
+    }
+    *flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmk);
+    tma_prefetch_desc(&tmv);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) pdl_trigger();
+  pdl_wait();
+
+  const int* pt = p.page_table + (size_t)b * p.pt_stride;
+  if (warp == n_mt) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const int last_page = (L - 1) / p.page_size;
+      int issued = 0;
+      for (int i = 0; i < n_tiles; ++i) {
+        const int s = i % kStages;
+        if (i >= kStages && !mbar_wait(empty + s, ((i / kStages) - 1) & 1, p.status, GR_ERR_TIMEOUT)) break;
+        mbar_arrive_expect_tx(full + s, kStageBytes);
+        uint8_t* st = kv_smem + s * kStageBytes;
+        const int page0 = (kv_beg + i * kTile) / p.page_size;
+#pragma unroll
+        for (int pg = 0; pg < 4; ++pg) {
+          const int lp = page0 + pg;
+          const int phys = pt[min(lp, last_page)];  // pages past the request's last hold no visible token
+          const int y = (phys * p.n_kv_heads + kvh) * p.page_size;
+          tma_load_2d(st + 0 * kHalfBytes + pg * 2048, &tmk, full + s, 0, y);
+          tma_load_2d(st + 1 * kHalfBytes + pg * 2048, &tmk, full + s, 64, y);
+          tma_load_2d(st + 2 * kHalfBytes + pg * 2048, &tmv, full + s, 0, y);
+          tma_load_2d(st + 3 * kHalfBytes + pg * 2048, &tmv, full + s, 64, y);
+        }
+        issued = i + 1;
+      }
+      for (int i = max(0, issued - kStages); i < issued; ++i)
+        mbar_wait(full + (i % kStages), (i / kStages) & 1, p.status, GR_ERR_TIMEOUT);
+    }
+  } else {
+    // ------------------------------------------------------------ compute warps
+    // stage this warp's 16 query rows into shared memory (128-byte swizzle, two 64-dim halves)
+    const size_t q_row_stride = (size_t)p.n_q_heads * 128;
+    for (int e = lane; e < 16 * 16; e += 32) {
+      const int rr = e >> 4, chunk = e & 15;
+      const int r = warp * 16 + rr;
+      uint4 val = make_uint4(0, 0, 0, 0);
+      if (r < R) {
+        const int g = r / p.K, j = r % p.K;
+        const __nv_bfloat16* src = p.q + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128 + chunk * 8;
+        val = *reinterpret_cast<const uint4*>(src);
+      }
+      *reinterpret_cast<uint4*>(q_smem + (chunk >> 3) * (R_pad * 128) + sw128(r, chunk & 7)) = val;
+    }
+    __syncwarp();
+    uint32_t qf[8][4];
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const uint32_t a = smem_u32(q_smem + (ks >> 2) * (R_pad * 128) +
+                                  sw128(warp * 16 + (lane & 15), 2 * (ks & 3) + (lane >> 4)));
+      ldsm_x4(a, qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+    }
+    const int g4 = lane >> 2, t4 = lane & 3;
+    int lim[2];
+    bool live[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = warp * 16 + g4 + 8 * h;
+      live[h] = r < R;
+      lim[h] = live[h] ? min(row_limit(p, r % p.K, base), kv_end) : 0;
+    }
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+    float o[16][4];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+
+    for (int i = 0; i < n_tiles; ++i) {
+      const int s = i % kStages;
+      if (!mbar_wait(full + s, (i / kStages) & 1, p.status, GR_ERR_TIMEOUT)) {
+        *flag = 1;
+        break;
+      }
+      const uint8_t* st = kv_smem + s * kStageBytes;
+      const int tok0 = kv_beg + i * kTile;
+      // S = Q K^T for 16 rows x 64 tokens
+      float sc[8][4];
+#pragma unroll
+      for (int n = 0; n < 8; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint8_t* kh = st + (ks >> 2) * kHalfBytes;
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {
+          const int trow = np * 16 + (lane & 7) + ((lane >> 4) << 3);
+          const int ch = 2 * (ks & 3) + ((lane >> 3) & 1);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(smem_u32(kh + sw128(trow, ch)), b0, b1, b2, b3);
+          mma_16816(sc[2 * np], qf[ks], b0, b1);
+          mma_16816(sc[2 * np + 1], qf[ks], b2, b3);
+        }
+      }
+      // mask + online softmax (rows g4 and g4+8 of this warp's tile)
+      float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int h = e >> 1;
+          const int tok = tok0 + n * 8 + 2 * t4 + (e & 1);
+          const float x = (tok < lim[h]) ? sc[n][e] * p.scale_log2 : -INFINITY;
+          sc[n][e] = x;
+          mx[h] = fmaxf(mx[h], x);
+        }
+      }
+      float alpha[2], msafe[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+        const float mn = fmaxf(m_run[h], mx[h]);
+        msafe[h] = (mn == -INFINITY) ? 0.f : mn;
+        alpha[h] = (m_run[h] == -INFINITY) ? 0.f : exp2f(m_run[h] - msafe[h]);
+        m_run[h] = mn;
+      }
+      float rs[2] = {0.f, 0.f};
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int h = e >> 1;
+          const float pe = exp2f(sc[n][e] - msafe[h]);
+          sc[n][e] = pe;
+          rs[h] += pe;
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 1);
+        rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 2);
+        l_run[h] = l_run[h] * alpha[h] + rs[h];
+      }
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        o[n][0] *= alpha[0];
+        o[n][1] *= alpha[0];
+        o[n][2] *= alpha[1];
+        o[n][3] *= alpha[1];
+      }
+      // O += P V
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t pa[4];
+        pa[0] = pack_bf16(sc[2 * kk][0], sc[2 * kk][1]);
+        pa[1] = pack_bf16(sc[2 * kk][2], sc[2 * kk][3]);
+        pa[2] = pack_bf16(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
+        pa[3] = pack_bf16(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
+        const int trow = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+#pragma unroll
+        for (int dp = 0; dp < 8; ++dp) {
+          const uint8_t* vh = st + (2 + (dp >> 2)) * kHalfBytes;
+          const int ch = 2 * (dp & 3) + (lane >> 4);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(smem_u32(vh + sw128(trow, ch)), b0, b1, b2, b3);
+          mma_16816(o[2 * dp], pa, b0, b1);
+          mma_16816(o[2 * dp + 1], pa, b2, b3);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty + s);
+    }
+
+    // ------------------------------------------------------------ write / merge
+    if (n_active == 1) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (!live[h]) continue;
+        const int r = warp * 16 + g4 + 8 * h;
+        const int g = r / p.K, j = r % p.K;
+        const float inv = l_run[h] > 0.f ? 1.f / l_run[h] : 0.f;
+        __nv_bfloat16* dst = p.out + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128;
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+          const int d = n * 8 + 2 * t4;
+          *reinterpret_cast<uint32_t*>(dst + d) = pack_bf16(o[n][2 * h] * inv, o[n][2 * h + 1] * inv);
+        }
+      }
+    } else {
+      const size_t slot = ((size_t)b * p.n_kv_heads + kvh) * p.max_splits + split;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int r = warp * 16 + g4 + 8 * h;
+        float* dst = p.ws_o + (slot * R_pad + r) * 128;
+#pragma unroll
+        for (int n = 0; n < 16; ++n) {
+          const int d = n * 8 + 2 * t4;
+          *reinterpret_cast<float2*>(dst + d) = make_float2(o[n][2 * h], o[n][2 * h + 1]);
+        }
+        if (t4 == 0) {
+          float* ml = p.ws_ml + (slot * R_pad + r) * 2;
+          ml[0] = m_run[h];
+          ml[1] = l_run[h];
+        }
+      }
+    }
+  }
+  if (n_active == 1) return;
+
+  // last split to arrive merges every split's partial in split order
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* tk = p.ws_ticket + (size_t)b * p.n_kv_heads + kvh;
+    const int prev = atomicAdd(tk, 1);
+    *flag = (prev == n_active - 1) ? 2 : 0;
+    if (*flag) *tk = 0;
+  }
+  __syncthreads();
+  if (*flag != 2) return;
+  __threadfence();
+  const size_t slot0 = ((size_t)b * p.n_kv_heads + kvh) * p.max_splits;
+  const size_t q_row_stride = (size_t)p.n_q_heads * 128;
+  for (int e = threadIdx.x; e < R * 64; e += blockDim.x) {
+    const int r = e >> 6, d = (e & 63) * 2;
+    float M = -INFINITY;
+    for (int s = 0; s < n_active; ++s) M = fmaxf(M, __ldcg(p.ws_ml + ((slot0 + s) * R_pad + r) * 2));
+    const float Ms = (M == -INFINITY) ? 0.f : M;
+    float Lsum = 0.f, a0 = 0.f, a1 = 0.f;
+    for (int s = 0; s < n_active; ++s) {
+      const float* ml = p.ws_ml + ((slot0 + s) * R_pad + r) * 2;
+      const float ms = __ldcg(ml), ls = __ldcg(ml + 1);
+      const float w = (ms == -INFINITY) ? 0.f : exp2f(ms - Ms);
+      Lsum += ls * w;
+      const float* os = p.ws_o + ((slot0 + s) * R_pad + r) * 128 + d;
+      a0 += __ldcg(os) * w;
+      a1 += __ldcg(os + 1) * w;
+    }
+    const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+    const int g = r / p.K, j = r % p.K;
+    __nv_bfloat16* dst = p.out + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128 + d;
+    *reinterpret_cast<uint32_t*>(dst) = pack_bf16(a0 * inv, a1 * inv);
+  }
+}
+
+size_t attention_smem_bytes(int K, int G) {
+  const int R_pad = ((G * K + 15) / 16) * 16;
+  return 1024 + kStages * kStageBytes + 2 * R_pad * 128 + 2 * kStages * 8 + 16;
+}
+
+cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p,
+                             cudaStream_t stream, bool pdl) {
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const int G = p.n_q_heads / p.n_kv_heads;
+  const int n_mt = (G * p.K + 15) / 16;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.max_splits, p.n_kv_heads, p.bs);
+  cfg.blockDim = dim3(32 * (n_mt + 1));
+  cfg.dynamicSmemBytes = attention_smem_bytes(p.K, G);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attention_kernel, tmk, tmv, p);
+}
+
+}  // namespace gr

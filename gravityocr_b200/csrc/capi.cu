@@ -1,0 +1,420 @@
+// extern "C" entry points of libgravity_b200.so (declared in include/gravity_b200.h): argument checks, tile and
+// split heuristics, TMA tensor-map encoding (cached per buffer) and the launches.
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "params.cuh"
+
+namespace gr {
+
+// ------------------------------------------------------------------ tensor maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+using MapKey = std::tuple<uintptr_t, uint64_t, uint64_t, uint32_t, uint32_t>;
+static std::mutex g_map_mu;
+static std::map<MapKey, CUtensorMap> g_maps;
+
+// 2-D bf16 tensor [rows, cols] (cols contiguous, row stride = cols), box [box_rows, box_cols], 128-byte swizzle.
+static int tensor_map_2d(const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows, uint32_t box_cols,
+                         CUtensorMap* out) {
+  const MapKey key{reinterpret_cast<uintptr_t>(base), rows, cols, box_rows, box_cols};
+  {
+    std::lock_guard<std::mutex> g(g_map_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+      *out = it->second;
+      return GR_OK;
+    }
+  }
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return GR_ERR_TMA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((cols * 2) & 15)) return GR_ERR_ARG;
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return GR_ERR_TMA;
+  std::lock_guard<std::mutex> g(g_map_mu);
+  if (g_maps.size() > 4096) g_maps.clear();
+  g_maps[key] = m;
+  *out = m;
+  return GR_OK;
+}
+
+static bool g_pdl = true;
+static int g_sms = 0;
+
+static int num_sms() {
+  if (!g_sms) {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    g_sms = n;
+  }
+  return g_sms;
+}
+
+struct LinearShape {
+  int nt, m_tiles, n_tiles, kc;
+};
+static LinearShape linear_shape(int n_out, int k_in, int m) {
+  LinearShape s;
+  s.m_tiles = (m + 255) / 256;
+  const int per = (m + s.m_tiles - 1) / s.m_tiles;
+  s.nt = ((per + 15) / 16) * 16;
+  if (s.nt < 16) s.nt = 16;
+  s.n_tiles = n_out / 128;
+  s.kc = k_in / 64;
+  return s;
+}
+
+static int default_splits(const LinearShape& s, int epi) {
+  const int units = s.n_tiles * s.m_tiles;
+  const int target = (num_sms() * 9) / 10;
+  if (units >= target || epi == GR_EPI_ARGMAX) return 1;
+  for (int sp = 2; sp <= s.kc; ++sp) {
+    if (s.kc % sp) continue;
+    if (s.kc / sp < 2) break;
+    if (units * sp >= target) return sp;
+  }
+  // largest divisor keeping >= 2 chunks per split
+  int best = 1;
+  for (int sp = 2; sp <= s.kc / 2; ++sp)
+    if (s.kc % sp == 0) best = sp;
+  return best;
+}
+
+struct LinearWs {
+  int* ticket;
+  int* arg_ticket;
+  float* partial;
+  float* arg;
+  size_t bytes;
+};
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+// Every call shares one scratch buffer, whatever its shape: the tickets live in a fixed region at its head (so a
+// later call of another shape never finds another call's partial sums where its tickets are), then the fp32
+// split-K partials, then the per-tile argmax records.
+constexpr size_t kMaxTiles = 4096;     // feature tiles x token tiles of one call
+constexpr size_t kMaxArgTiles = 1024;  // token tiles of one lm_head call
+constexpr size_t kTicketBytes = kMaxTiles * sizeof(int) + kMaxArgTiles * sizeof(int);
+static LinearWs linear_ws_layout(void* base, const LinearShape& s, int m, int splits) {
+  LinearWs w;
+  uint8_t* p = static_cast<uint8_t*>(base);
+  const size_t tiles = static_cast<size_t>(s.n_tiles) * s.m_tiles;
+  w.ticket = reinterpret_cast<int*>(p);
+  w.arg_ticket = reinterpret_cast<int*>(p + kMaxTiles * sizeof(int));
+  size_t off = kTicketBytes;
+  w.partial = reinterpret_cast<float*>(p + off);
+  off += splits > 1 ? align256(tiles * splits * s.nt * 128 * sizeof(float)) : 0;
+  w.arg = reinterpret_cast<float*>(p + off);
+  off += align256(static_cast<size_t>(s.n_tiles) * m * 3 * sizeof(float));
+  w.bytes = off;
+  return w;
+}
+
+// attention scratch: tickets of (request, kv head) at the head, then the split partials
+constexpr size_t kAttnTicketBytes = 65536;  // 16384 (request, kv head) pairs
+
+}  // namespace gr
+
+using namespace gr;
+
+extern "C" {
+
+int gr_version(void) { return 100; }
+
+const char* gr_status_string(int code) {
+  switch (code) {
+    case GR_OK: return "ok";
+    case GR_ERR_ARG: return "invalid argument";
+    case GR_ERR_CUDA: return "CUDA runtime error";
+    case GR_ERR_TMA: return "tensor map encoding failed";
+    case GR_ERR_TIMEOUT: return "device wait timed out";
+    case GR_ERR_BAD_ID: return "token id out of range";
+    case GR_ERR_BAD_PAGE: return "position beyond page-table capacity";
+    case GR_ERR_UNSUPPORTED: return "unsupported configuration";
+    default: return "unknown status";
+  }
+}
+
+void gr_set_pdl(int enable) { g_pdl = enable != 0; }
+int gr_num_sms(void) { return num_sms(); }
+
+int gr_linear_default_splits(int n_out, int k_in, int m) {
+  if (n_out <= 0 || k_in <= 0 || m <= 0) return 1;
+  return default_splits(linear_shape(n_out, k_in, m), GR_EPI_STORE_F32);
+}
+
+size_t gr_linear_workspace_bytes(int n_out, int m, int splits) {
+  if (n_out <= 0 || m <= 0) return 0;
+  LinearShape s = linear_shape(n_out, 64, m);
+  if (splits < 1) splits = 1;
+  return linear_ws_layout(nullptr, s, m, splits).bytes;
+}
+
+int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr_epilogue* epi, int splits,
+              void* workspace, size_t workspace_bytes, const void* prefetch, size_t prefetch_bytes, int32_t* status,
+              void* stream) {
+  if (!w || !x || !epi || m <= 0 || n_out <= 0 || (n_out % 128) || k_in <= 0 || (k_in % 64)) return GR_ERR_ARG;
+  if (epi->mode < GR_EPI_STORE_F32 || epi->mode > GR_EPI_ARGMAX) return GR_ERR_ARG;
+  LinearShape s = linear_shape(n_out, k_in, m);
+  if (splits <= 0) splits = default_splits(s, epi->mode);
+  if (s.kc % splits) return GR_ERR_ARG;
+  const int kc = s.kc / splits;
+  LinearWs ws = linear_ws_layout(workspace, s, m, splits);
+  if (!workspace || workspace_bytes < ws.bytes) return GR_ERR_ARG;
+  if (static_cast<size_t>(s.n_tiles) * s.m_tiles > kMaxTiles || static_cast<size_t>(s.m_tiles) > kMaxArgTiles)
+    return GR_ERR_UNSUPPORTED;
+  if (epi->mode == GR_EPI_QKV_ROPE) {
+    if (!epi->q_out || !epi->k_cache || !epi->v_cache || !epi->row_pos || !epi->row_slot || !epi->inv_freq ||
+        epi->rotary_dim % 32 || epi->rotary_dim > 128 || n_out != (epi->n_q_heads + 2 * epi->n_kv_heads) * 128 ||
+        epi->page_size <= 0)
+      return GR_ERR_ARG;
+  } else if (epi->mode == GR_EPI_ARGMAX) {
+    if (!epi->out_idx) return GR_ERR_ARG;
+  } else if (!epi->out || epi->ld_out <= 0) {
+    return GR_ERR_ARG;
+  }
+  // stages: deep enough to cover latency; keep two CTAs per SM when the grid has more units than SMs
+  const int units = s.n_tiles * s.m_tiles * splits;
+  int stages = kc < 6 ? kc : 6;
+  while (stages > 1 && linear_smem_bytes(s.nt, stages) > 220 * 1024) --stages;
+  if (units > num_sms())
+    while (stages > 2 && linear_smem_bytes(s.nt, stages) > 112 * 1024) --stages;
+  CUtensorMap tmw, tmx;
+  int rc = tensor_map_2d(w, static_cast<uint64_t>(n_out), static_cast<uint64_t>(k_in), 128, 64, &tmw);
+  if (rc) return rc;
+  rc = tensor_map_2d(x, static_cast<uint64_t>(m), static_cast<uint64_t>(k_in), static_cast<uint32_t>(s.nt), 64, &tmx);
+  if (rc) return rc;
+  LinearParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.n_out = n_out;
+  p.k_in = k_in;
+  p.m = m;
+  p.nt = s.nt;
+  p.m_tiles = s.m_tiles;
+  p.n_tiles = s.n_tiles;
+  p.splits = splits;
+  p.kc_per_split = kc;
+  p.stages = stages;
+  p.out = epi->out;
+  p.ld_out = epi->ld_out;
+  p.q_out = static_cast<__nv_bfloat16*>(epi->q_out);
+  p.k_cache = static_cast<__nv_bfloat16*>(epi->k_cache);
+  p.v_cache = static_cast<__nv_bfloat16*>(epi->v_cache);
+  p.row_pos = epi->row_pos;
+  p.row_slot = epi->row_slot;
+  p.inv_freq = epi->inv_freq;
+  p.rotary_dim = epi->rotary_dim;
+  p.n_q_heads = epi->n_q_heads;
+  p.n_kv_heads = epi->n_kv_heads;
+  p.page_size = epi->page_size;
+  p.out_idx = epi->out_idx;
+  p.out_top1 = epi->out_top1;
+  p.out_gap = epi->out_gap;
+  p.ws_partial = ws.partial;
+  p.ws_ticket = ws.ticket;
+  p.ws_arg = ws.arg;
+  p.ws_arg_ticket = ws.arg_ticket;
+  p.prefetch = static_cast<const uint8_t*>(prefetch);
+  p.prefetch_bytes = prefetch ? prefetch_bytes : 0;
+  p.status = status;
+  cudaError_t e = launch_linear(epi->mode, tmw, tmx, p, units, linear_smem_bytes(s.nt, stages),
+                                static_cast<cudaStream_t>(stream), g_pdl);
+  return e == cudaSuccess ? GR_OK : GR_ERR_CUDA;
+}
+
+size_t gr_attention_workspace_bytes(int bs, int K, int n_q_heads, int n_kv_heads, int max_splits) {
+  if (bs <= 0 || K <= 0 || n_kv_heads <= 0 || max_splits <= 0) return 0;
+  const int G = n_q_heads / n_kv_heads;
+  const size_t R_pad = ((G * K + 15) / 16) * 16;
+  const size_t slots = static_cast<size_t>(bs) * n_kv_heads * max_splits;
+  return kAttnTicketBytes + align256(slots * R_pad * 128 * sizeof(float)) + align256(slots * R_pad * 2 * sizeof(float));
+}
+
+int gr_bd_attention(const void* q, const void* k_cache, const void* v_cache, int64_t n_pages, const int32_t* page_table,
+                    int pt_stride, const int64_t* seq_lens, int bs, int K, int draft, int base_add, int n_q_heads,
+                    int n_kv_heads, int page_size, int chunk, int max_splits, void* out, void* workspace,
+                    size_t workspace_bytes, int32_t* status, void* stream) {
+  if (!q || !k_cache || !v_cache || !page_table || !seq_lens || !out || bs <= 0 || K <= 0 || n_pages <= 0)
+    return GR_ERR_ARG;
+  if (n_kv_heads <= 0 || n_q_heads % n_kv_heads || page_size != 16 || chunk <= 0 || chunk % 64 || max_splits <= 0)
+    return GR_ERR_ARG;
+  const int G = n_q_heads / n_kv_heads;
+  if (G * K > 128 || static_cast<size_t>(bs) * n_kv_heads * sizeof(int) > kAttnTicketBytes) return GR_ERR_UNSUPPORTED;
+  const size_t need = gr_attention_workspace_bytes(bs, K, n_q_heads, n_kv_heads, max_splits);
+  if (max_splits > 1 && (!workspace || workspace_bytes < need)) return GR_ERR_ARG;
+  const uint64_t rows = static_cast<uint64_t>(n_pages) * n_kv_heads * page_size;
+  CUtensorMap tmk, tmv;
+  int rc = tensor_map_2d(k_cache, rows, 128, static_cast<uint32_t>(page_size), 64, &tmk);
+  if (rc) return rc;
+  rc = tensor_map_2d(v_cache, rows, 128, static_cast<uint32_t>(page_size), 64, &tmv);
+  if (rc) return rc;
+  AttnParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.page_table = page_table;
+  p.pt_stride = pt_stride;
+  p.seq_lens = seq_lens;
+  p.bs = bs;
+  p.K = K;
+  p.draft = draft ? 1 : 0;
+  p.base_add = base_add;
+  p.n_q_heads = n_q_heads;
+  p.n_kv_heads = n_kv_heads;
+  p.page_size = page_size;
+  p.chunk = chunk;
+  p.max_splits = max_splits;
+  p.scale_log2 = (1.0f / sqrtf(128.0f)) * 1.4426950408889634f;
+  if (workspace) {
+    uint8_t* b = static_cast<uint8_t*>(workspace);
+    const size_t R_pad = ((G * K + 15) / 16) * 16;
+    const size_t slots = static_cast<size_t>(bs) * n_kv_heads * max_splits;
+    p.ws_ticket = reinterpret_cast<int*>(b);
+    b += kAttnTicketBytes;
+    p.ws_o = reinterpret_cast<float*>(b);
+    b += align256(slots * R_pad * 128 * sizeof(float));
+    p.ws_ml = reinterpret_cast<float*>(b);
+  }
+  p.status = status;
+  cudaError_t e = launch_attention(tmk, tmv, p, static_cast<cudaStream_t>(stream), g_pdl);
+  return e == cudaSuccess ? GR_OK : GR_ERR_CUDA;
+}
+
+int gr_embed_rows(int mode, int bs, int K, const int64_t* seeds, const int64_t* req_pool_idx, const int32_t* ids32,
+                  const int64_t* ids64, const float* row_embeds, const int64_t* seq_lens, const int32_t* page_table,
+                  int pt_stride, int page_size, int pages_per_req, const void* embed, int vocab, int mask_id,
+                  const void* norm_w, float eps, int hidden, float* h_out, void* x_out, int32_t* row_pos,
+                  int64_t* row_slot, int32_t* row_ids, int32_t* status, void* stream) {
+  if (bs <= 0 || K <= 0 || !seq_lens || !page_table || !embed || !norm_w || !h_out || !x_out || !row_pos || !row_slot)
+    return GR_ERR_ARG;
+  if (hidden <= 0 || hidden % 8 || page_size <= 0 || pages_per_req <= 0) return GR_ERR_ARG;
+  if (mode == GR_ROWS_DRAFT && (!seeds || !req_pool_idx)) return GR_ERR_ARG;
+  if (mode == GR_ROWS_VERIFY && !ids32) return GR_ERR_ARG;
+  if (mode == GR_ROWS_EXPLICIT && !ids64) return GR_ERR_ARG;
+  if (mode < GR_ROWS_DRAFT || mode > GR_ROWS_EXPLICIT) return GR_ERR_ARG;
+  EmbedParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.mode = mode;
+  p.bs = bs;
+  p.K = K;
+  p.hidden = hidden;
+  p.vocab = vocab;
+  p.mask_id = mask_id;
+  p.page_size = page_size;
+  p.pt_stride = pt_stride;
+  p.pages_per_req = pages_per_req;
+  p.seeds = seeds;
+  p.rpi = req_pool_idx;
+  p.ids32 = ids32;
+  p.ids64 = ids64;
+  p.row_embeds = row_embeds;
+  p.seq_lens = seq_lens;
+  p.page_table = page_table;
+  p.embed = static_cast<const __nv_bfloat16*>(embed);
+  p.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
+  p.eps = eps;
+  p.h_out = h_out;
+  p.x_out = static_cast<__nv_bfloat16*>(x_out);
+  p.row_pos = row_pos;
+  p.row_slot = row_slot;
+  p.row_ids = row_ids;
+  p.status = status;
+  return launch_embed_rows(p, static_cast<cudaStream_t>(stream), g_pdl) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
+}
+
+int gr_residual_norm(int m, int hidden, const float* h_in, const float* y, const void* w_a, const void* w_b, float eps,
+                     float* h_out, void* x_out, void* stream) {
+  if (m <= 0 || hidden <= 0 || hidden % 8 || !h_in || !y || !w_a || !w_b || !h_out || !x_out) return GR_ERR_ARG;
+  if (h_in == h_out) return GR_ERR_ARG;
+  ResNormParams p;
+  p.m = m;
+  p.hidden = hidden;
+  p.h_in = h_in;
+  p.y = y;
+  p.w_a = static_cast<const __nv_bfloat16*>(w_a);
+  p.w_b = static_cast<const __nv_bfloat16*>(w_b);
+  p.eps = eps;
+  p.h_out = h_out;
+  p.x_out = static_cast<__nv_bfloat16*>(x_out);
+  return launch_residual_norm(p, static_cast<cudaStream_t>(stream), g_pdl) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
+}
+
+int gr_accept_commit(int bs, int K, const int32_t* am, const int32_t* v, int64_t* seeds, const int64_t* req_pool_idx,
+                     int64_t* seq_lens, int x0_committed, const int64_t* loc, int32_t* packed, int64_t* released,
+                     int32_t* n_released, int64_t* out_next, int32_t* n_committed, int32_t* rounds,
+                     int32_t* accept_len, void* stream) {
+  if (bs <= 0 || K < 2 || !am || !v || !seeds || !req_pool_idx || !seq_lens || !packed || !released || !out_next)
+    return GR_ERR_ARG;
+  CommitParams p;
+  p.bs = bs;
+  p.K = K;
+  p.x0_committed = x0_committed ? 1 : 0;
+  p.am = am;
+  p.v = v;
+  p.seeds = seeds;
+  p.rpi = req_pool_idx;
+  p.seq_lens = seq_lens;
+  p.loc = loc;
+  p.packed = packed;
+  p.released = released;
+  p.n_released = n_released;
+  p.out_next = out_next;
+  p.n_committed = n_committed;
+  p.rounds = rounds;
+  p.accept_len = accept_len;
+  return launch_accept_commit(p, static_cast<cudaStream_t>(stream), g_pdl) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
+}
+
+int gr_draft_override(int bs, int K, int32_t* am, const int32_t* g, int g_stride, const int32_t* n_committed,
+                      const int32_t* accept_plan, int plan_stride, const int32_t* rounds, int vocab, int mask_id,
+                      void* stream) {
+  if (bs <= 0 || K < 2 || !am || !g || !n_committed || !accept_plan || !rounds || vocab <= 0) return GR_ERR_ARG;
+  OverrideParams p;
+  p.bs = bs;
+  p.K = K;
+  p.g_stride = g_stride;
+  p.plan_stride = plan_stride;
+  p.vocab = vocab;
+  p.mask_id = mask_id;
+  p.am = am;
+  p.g = g;
+  p.n_committed = n_committed;
+  p.plan = accept_plan;
+  p.rounds = rounds;
+  return launch_draft_override(p, static_cast<cudaStream_t>(stream), g_pdl) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
+}
+
+int gr_pack_gate_up(const void* src, void* dst, int intermediate, int hidden, void* stream) {
+  if (!src || !dst || intermediate % 64 || hidden % 8) return GR_ERR_ARG;
+  return launch_pack_gate_up(static_cast<const __nv_bfloat16*>(src), static_cast<__nv_bfloat16*>(dst), intermediate,
+                             hidden, static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? GR_OK
+             : GR_ERR_CUDA;
+}
+
+}  // extern "C"

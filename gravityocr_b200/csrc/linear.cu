@@ -1,0 +1,401 @@
+// Weight-streaming GEMM for the decoder's projections and lm_head, sm_100a (tcgen05 + TMA + TMEM).
+//
+//   out[t, f] = sum_k X[t, k] * W[f, k]        X: [M, K] bf16 activations, W: [N, K] bf16 weights (nn.Linear layout)
+//
+// Swap-AB mapping: a CTA owns a 128-feature slab of W (the MMA's M = 128 rows) and NT tokens (the MMA's N, 16..256),
+// so M = bs*(B+1) tokens as small as 5 still drive a full-height tensor-core tile and every weight byte is read once
+// per token tile.  One unit of work = (feature tile, token tile, K split).  Per CTA:
+//   warp 0      TMA producer: W tile 128x64 and X tile NTx64 per stage (128-byte swizzle), S-stage mbarrier ring.
+//               Weight tiles do not depend on the previous kernel, so the first S stages are issued before
+//               griddepcontrol.wait (programmatic dependent launch): the weight stream starts while the previous
+//               kernel drains.
+//   warp 1      allocates TMEM (NT fp32 columns), one thread issues tcgen05.mma (M=128, N=NT, K=16) x 4 per stage,
+//               tcgen05.commit frees the stage and finally signals the accumulator.
+//   warps 2-5   epilogue: tcgen05.ld of their TMEM lane quadrant (lane = output feature, column = token).
+// Split-K: each split writes an fp32 partial tile to the workspace; the last CTA of a tile to arrive (atomic ticket)
+// sums the partials in split order (deterministic) and runs the epilogue, then re-arms the ticket for the next launch.
+// Epilogues: fp32 / bf16 store, SwiGLU (gate and up rows interleaved per 64 features by the host), Q/K/V with
+// interleaved-pair partial RoPE and the paged K/V cache write, and lm_head's vocab-wide argmax (top-1 index, top-1
+// value and top-2 gap; logits are never written).
+#include "params.cuh"
+
+namespace gr {
+
+constexpr int kThreads = 192;
+constexpr uint32_t kWStageBytes = 128 * 128;  // 128 rows x 64 bf16
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+struct Top2 {
+  float v1;
+  int i1;
+  float v2;
+};
+__device__ __forceinline__ Top2 top2_merge(Top2 a, Top2 b) {
+  const bool bw = (b.v1 > a.v1) || (b.v1 == a.v1 && b.i1 < a.i1);
+  Top2 r;
+  if (bw) {
+    r.v1 = b.v1;
+    r.i1 = b.i1;
+    r.v2 = fmaxf(a.v1, b.v2);
+  } else {
+    r.v1 = a.v1;
+    r.i1 = a.i1;
+    r.v2 = fmaxf(a.v2, b.v1);
+  }
+  return r;
+}
+__device__ __forceinline__ Top2 top2_warp(Top2 x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    Top2 y;
+    y.v1 = __shfl_xor_sync(0xffffffffu, x.v1, o);
+    y.i1 = __shfl_xor_sync(0xffffffffu, x.i1, o);
+    y.v2 = __shfl_xor_sync(0xffffffffu, x.v2, o);
+    x = top2_merge(x, y);
+  }
+  return x;
+}
+
+// Apply the epilogue to 16 consecutive tokens [t0, t0+16) of feature row f_local of this tile.  Called by all 128
+// epilogue threads together (it may use warp shuffles, the epilogue barrier and `scratch` shared memory).
+template <int EPI>
+__device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, int m_tile, int f_local, int t0,
+                                           const float* v, float* scratch) {
+  const int lane = threadIdx.x & 31;
+  const int t_end = min(p.m, (m_tile + 1) * p.nt);
+  if constexpr (EPI == GR_EPI_STORE_F32 || EPI == GR_EPI_STORE_BF16) {
+    const int f = n_tile * 128 + f_local;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int t = t0 + i;
+      if (t < t_end) {
+        if constexpr (EPI == GR_EPI_STORE_F32)
+          static_cast<float*>(p.out)[(size_t)t * p.ld_out + f] = v[i];
+        else
+          static_cast<__nv_bfloat16*>(p.out)[(size_t)t * p.ld_out + f] = __float2bfloat16_rn(v[i]);
+      }
+    }
+  } else if constexpr (EPI == GR_EPI_SWIGLU) {
+    // rows 0..63 of the tile are gate features 64*n_tile + j, rows 64..127 the matching up features
+    if (f_local >= 64) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) scratch[i * 64 + (f_local - 64)] = v[i];
+    }
+    epi_bar();
+    if (f_local < 64) {
+      const int f = n_tile * 64 + f_local;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int t = t0 + i;
+        const float g = v[i];
+        const float u = scratch[i * 64 + f_local];
+        const float a = u * (g / (1.0f + expf(-g)));
+        if (t < t_end) static_cast<__nv_bfloat16*>(p.out)[(size_t)t * p.ld_out + f] = __float2bfloat16_rn(a);
+      }
+    }
+    epi_bar();
+  } else if constexpr (EPI == GR_EPI_QKV_ROPE) {
+    // tile = one head: [0, nq) query heads, [nq, nq+nkv) key heads, then value heads; f_local = head dim
+    const int head = n_tile;
+    const int d = f_local;
+    const bool is_q = head < p.n_q_heads;
+    const bool is_v = head >= p.n_q_heads + p.n_kv_heads;
+    const bool rot = !is_v && (d & ~31) < p.rotary_dim;  // warp-uniform: rotary_dim is a multiple of 32
+    float o[16];
+    if (rot) {
+      const float fr = p.inv_freq[d >> 1];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float partner = __shfl_xor_sync(0xffffffffu, v[i], 1);
+        const int t = min(t0 + i, t_end - 1);
+        const float ang = static_cast<float>(p.row_pos[t]) * fr;
+        float s, c;
+        sincosf(ang, &s, &c);
+        o[i] = (d & 1) ? (v[i] * c + partner * s) : (v[i] * c - partner * s);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) o[i] = v[i];
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int t = t0 + i;
+      if (t >= t_end) continue;
+      const __nv_bfloat16 b = __float2bfloat16_rn(o[i]);
+      if (is_q) {
+        p.q_out[(size_t)t * (p.n_q_heads * 128) + head * 128 + d] = b;
+      } else {
+        const int kvh = is_v ? head - p.n_q_heads - p.n_kv_heads : head - p.n_q_heads;
+        const int64_t slot = p.row_slot[t];
+        const int64_t page = slot / p.page_size, off = slot % p.page_size;
+        const size_t idx = (((size_t)page * p.n_kv_heads + kvh) * p.page_size + off) * 128 + d;
+        (is_v ? p.v_cache : p.k_cache)[idx] = b;
+      }
+    }
+  } else if constexpr (EPI == GR_EPI_ARGMAX) {
+    const int warp = (threadIdx.x >> 5) - 2;
+    const int f = n_tile * 128 + f_local;
+    Top2* sm = reinterpret_cast<Top2*>(scratch);  // [4 warps][16 tokens]
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      Top2 x{v[i], f, -INFINITY};
+      x = top2_warp(x);
+      if (lane == 0) sm[warp * 16 + i] = x;
+    }
+    epi_bar();
+    if (threadIdx.x < 64 + 16) {
+      const int i = threadIdx.x - 64;
+      Top2 x = sm[i];
+#pragma unroll
+      for (int w = 1; w < 4; ++w) x = top2_merge(x, sm[w * 16 + i]);
+      const int t = t0 + i;
+      if (t < t_end) {
+        float* dst = p.ws_arg + ((size_t)n_tile * p.m + t) * 3;
+        dst[0] = x.v1;
+        dst[1] = __int_as_float(x.i1);
+        dst[2] = x.v2;
+      }
+    }
+    epi_bar();
+  }
+}
+
+// lm_head: after every feature tile of a token tile has written its per-token top-2, the last one reduces them.
+__device__ void argmax_finish(const LinearParams& p, int m_tile, int* flag) {
+  __threadfence();
+  epi_bar();
+  if (threadIdx.x == 64) {
+    const int prev = atomicAdd(&p.ws_arg_ticket[m_tile], 1);
+    *flag = (prev == p.n_tiles - 1);
+  }
+  epi_bar();
+  if (!*flag) return;
+  __threadfence();
+  const int warp = (threadIdx.x >> 5) - 2, lane = threadIdx.x & 31;
+  const int t_beg = m_tile * p.nt, t_end = min(p.m, t_beg + p.nt);
+  for (int t = t_beg + warp; t < t_end; t += 4) {
+    Top2 x{-INFINITY, 0x7fffffff, -INFINITY};
+    for (int n = lane; n < p.n_tiles; n += 32) {
+      const float* s = p.ws_arg + ((size_t)n * p.m + t) * 3;
+      Top2 y{__ldcg(s), __float_as_int(__ldcg(s + 1)), __ldcg(s + 2)};
+      x = top2_merge(x, y);
+    }
+    x = top2_warp(x);
+    if (lane == 0) {
+      p.out_idx[t] = x.i1;
+      if (p.out_top1) p.out_top1[t] = x.v1;
+      if (p.out_gap) p.out_gap[t] = x.v1 - x.v2;
+    }
+  }
+  if (threadIdx.x == 64) p.ws_arg_ticket[m_tile] = 0;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    linear_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
+                  const LinearParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = p.stages;
+  const uint32_t x_stage_bytes = static_cast<uint32_t>(p.nt) * 128u;
+  uint8_t* w_smem = smem;
+  uint8_t* x_smem = smem + S * kWStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(x_smem + S * x_stage_bytes);
+  uint64_t* empty = full + S;
+  uint64_t* accum = empty + S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] abort, [1] last-split, [2] last-argmax
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int u = blockIdx.x;
+  const int m_tile = u % p.m_tiles;
+  u /= p.m_tiles;
+  const int split = u % p.splits;
+  const int n_tile = u / p.splits;
+  const int kc = p.kc_per_split, kc0 = split * kc;
+  const uint32_t tmem_cols = p.nt <= 32 ? 32u : (p.nt <= 64 ? 64u : (p.nt <= 128 ? 128u : 256u));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    mbar_init(accum, 1);
+    flags[0] = flags[1] = flags[2] = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmw);
+    tma_prefetch_desc(&tmx);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, tmem_cols);
+  if (p.prefetch_bytes && warp == 2 && lane == 0) {
+    // warm L2 with this CTA's share of the next kernel's weights
+    const unsigned long long per = ((p.prefetch_bytes / gridDim.x) + 4095ull) & ~4095ull;
+    const unsigned long long b0 = per * blockIdx.x;
+    const unsigned long long b1 = min(b0 + per, p.prefetch_bytes & ~15ull);
+    for (unsigned long long b = b0; b < b1; b += 32768ull)
+      l2_prefetch(p.prefetch + b, static_cast<uint32_t>(min(32768ull, b1 - b)));
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) pdl_trigger();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      const int pre = min(S, kc);
+      for (int c = 0; c < pre; ++c) {
+        mbar_arrive_expect_tx(full + c, kWStageBytes + x_stage_bytes);
+        tma_load_2d_hint(w_smem + c * kWStageBytes, &tmw, full + c, (kc0 + c) * 64, n_tile * 128, pol);
+      }
+      pdl_wait();
+      for (int c = 0; c < pre; ++c)
+        tma_load_2d(x_smem + c * x_stage_bytes, &tmx, full + c, (kc0 + c) * 64, m_tile * p.nt);
+      int issued = pre;
+      for (int c = pre; c < kc; ++c) {
+        const int s = c % S;
+        if (!mbar_wait(empty + s, ((c / S) - 1) & 1, p.status, GR_ERR_TIMEOUT)) {
+          flags[0] = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(full + s, kWStageBytes + x_stage_bytes);
+        tma_load_2d_hint(w_smem + s * kWStageBytes, &tmw, full + s, (kc0 + c) * 64, n_tile * 128, pol);
+        tma_load_2d(x_smem + s * x_stage_bytes, &tmx, full + s, (kc0 + c) * 64, m_tile * p.nt);
+        issued = c + 1;
+      }
+      // no copy may still be landing in shared memory when the CTA exits
+      for (int c = max(0, issued - S); c < issued; ++c) mbar_wait(full + (c % S), (c / S) & 1, p.status, GR_ERR_TIMEOUT);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(128, p.nt);
+      for (int c = 0; c < kc; ++c) {
+        const int s = c % S;
+        if (!mbar_wait(full + s, (c / S) & 1, p.status, GR_ERR_TIMEOUT)) {
+          flags[0] = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t wa = smem_u32(w_smem + s * kWStageBytes);
+        const uint32_t xa = smem_u32(x_smem + s * x_stage_bytes);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc_mma_bf16(tmem, smem_desc_sw128(wa + kk * 32), smem_desc_sw128(xa + kk * 32), idesc, (c | kk) != 0);
+        tc_commit(empty + s);
+      }
+      tc_commit(accum);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue warps 2..5
+    pdl_wait();
+    const int quad = warp & 3;
+    const int f_local = quad * 32 + lane;
+    const bool ok = mbar_wait(accum, 0, p.status, GR_ERR_TIMEOUT);
+    tc_fence_after();
+    float* scratch = reinterpret_cast<float*>(w_smem);  // the stage ring is idle once the accumulator is final
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const int t_beg = m_tile * p.nt;
+    const int rows = min(p.nt, p.m - t_beg);
+    bool run = ok && !flags[0];
+    epi_bar();
+    run = run && !flags[0];
+    if (p.splits == 1) {
+      if (run) {
+        for (int c0 = 0; c0 < p.nt; c0 += 16) {
+          float v[16];
+          tmem_ld16(t_lane + c0, v);
+          epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, scratch);
+        }
+      }
+    } else {
+      const int tile = n_tile * p.m_tiles + m_tile;
+      float* part = p.ws_partial + ((size_t)tile * p.splits + split) * p.nt * 128;
+      if (run) {
+        for (int c0 = 0; c0 < p.nt; c0 += 16) {
+          float v[16];
+          tmem_ld16(t_lane + c0, v);
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (c0 + i < rows) part[(c0 + i) * 128 + f_local] = v[i];
+        }
+      }
+      __threadfence();
+      epi_bar();
+      if (threadIdx.x == 64) {
+        const int prev = atomicAdd(&p.ws_ticket[tile], 1);
+        flags[1] = (prev == p.splits - 1);
+      }
+      epi_bar();
+      if (flags[1]) {
+        __threadfence();
+        const float* base = p.ws_partial + (size_t)tile * p.splits * p.nt * 128;
+        for (int c0 = 0; c0 < p.nt; c0 += 16) {
+          float v[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float a = 0.f;
+            if (c0 + i < rows)
+              for (int s = 0; s < p.splits; ++s) a += __ldcg(base + ((size_t)s * p.nt + c0 + i) * 128 + f_local);
+            v[i] = a;
+          }
+          epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, scratch);
+        }
+        if (threadIdx.x == 64) p.ws_ticket[tile] = 0;
+      }
+    }
+    if constexpr (EPI == GR_EPI_ARGMAX) {
+      if (p.splits == 1 || flags[1]) argmax_finish(p, m_tile, &flags[2]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, tmem_cols);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+size_t linear_smem_bytes(int nt, int stages) {
+  return 1024 + static_cast<size_t>(stages) * (kWStageBytes + static_cast<size_t>(nt) * 128) +
+         (2 * stages + 1) * 8 + 16;
+}
+
+template <int EPI>
+cudaError_t launch_linear_t(const CUtensorMap& tmw, const CUtensorMap& tmx, const LinearParams& p, int grid,
+                            size_t smem, cudaStream_t stream, bool pdl) {
+  auto kern = linear_kernel<EPI>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, tmw, tmx, p);
+}
+
+cudaError_t launch_linear(int epi, const CUtensorMap& tmw, const CUtensorMap& tmx, const LinearParams& p, int grid,
+                          size_t smem, cudaStream_t stream, bool pdl) {
+  switch (epi) {
+    case GR_EPI_STORE_F32: return launch_linear_t<GR_EPI_STORE_F32>(tmw, tmx, p, grid, smem, stream, pdl);
+    case GR_EPI_STORE_BF16: return launch_linear_t<GR_EPI_STORE_BF16>(tmw, tmx, p, grid, smem, stream, pdl);
+    case GR_EPI_SWIGLU: return launch_linear_t<GR_EPI_SWIGLU>(tmw, tmx, p, grid, smem, stream, pdl);
+    case GR_EPI_QKV_ROPE: return launch_linear_t<GR_EPI_QKV_ROPE>(tmw, tmx, p, grid, smem, stream, pdl);
+    case GR_EPI_ARGMAX: return launch_linear_t<GR_EPI_ARGMAX>(tmw, tmx, p, grid, smem, stream, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace gr

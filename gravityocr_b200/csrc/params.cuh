@@ -1,0 +1,111 @@
+// Parameter blocks of the kernels and their launchers, shared by the kernel files and the C-ABI layer.
+#pragma once
+
+#include "common.cuh"
+
+namespace gr {
+struct LinearParams {
+  int n_out, k_in, m;
+  int nt, m_tiles, n_tiles, splits, kc_per_split, stages;
+  void* out;
+  int ld_out;
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  const int* row_pos;
+  const int64_t* row_slot;
+  const float* inv_freq;
+  int rotary_dim, n_q_heads, n_kv_heads, page_size;
+  int* out_idx;
+  float* out_top1;
+  float* out_gap;
+  float* ws_partial;
+  int* ws_ticket;
+  float* ws_arg;
+  int* ws_arg_ticket;
+  const uint8_t* prefetch;
+  unsigned long long prefetch_bytes;
+  int* status;
+};
+struct AttnParams {
+  const __nv_bfloat16* q;
+  __nv_bfloat16* out;
+  const int* page_table;
+  int pt_stride;
+  const int64_t* seq_lens;
+  int bs, K, draft, base_add;
+  int n_q_heads, n_kv_heads, page_size;
+  int chunk, max_splits;
+  float scale_log2;
+  float* ws_o;
+  float* ws_ml;
+  int* ws_ticket;
+  int* status;
+};
+struct EmbedParams {
+  int mode, bs, K, hidden, vocab, mask_id, page_size, pt_stride, pages_per_req;
+  const int64_t* seeds;
+  const int64_t* rpi;
+  const int32_t* ids32;
+  const int64_t* ids64;
+  const float* row_embeds;
+  const int64_t* seq_lens;
+  const int32_t* page_table;
+  const __nv_bfloat16* embed;
+  const __nv_bfloat16* norm_w;
+  float eps;
+  float* h_out;
+  __nv_bfloat16* x_out;
+  int32_t* row_pos;
+  int64_t* row_slot;
+  int32_t* row_ids;
+  int32_t* status;
+};
+struct ResNormParams {
+  int m, hidden;
+  const float* h_in;
+  const float* y;
+  const __nv_bfloat16* w_a;
+  const __nv_bfloat16* w_b;
+  float eps;
+  float* h_out;
+  __nv_bfloat16* x_out;
+};
+struct CommitParams {
+  int bs, K, x0_committed;
+  const int32_t* am;
+  const int32_t* v;
+  int64_t* seeds;
+  const int64_t* rpi;
+  int64_t* seq_lens;
+  const int64_t* loc;
+  int32_t* packed;
+  int64_t* released;
+  int32_t* n_released;
+  int64_t* out_next;
+  int32_t* n_committed;
+  int32_t* rounds;
+  int32_t* accept_len;
+};
+struct OverrideParams {
+  int bs, K, g_stride, plan_stride, vocab, mask_id;
+  int32_t* am;
+  const int32_t* g;
+  const int32_t* n_committed;
+  const int32_t* plan;
+  const int32_t* rounds;
+};
+
+size_t linear_smem_bytes(int nt, int stages);
+cudaError_t launch_linear(int epi, const CUtensorMap& tmw, const CUtensorMap& tmx, const LinearParams& p, int grid,
+                          size_t smem, cudaStream_t stream, bool pdl);
+size_t attention_smem_bytes(int K, int G);
+cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p, cudaStream_t stream,
+                             bool pdl);
+cudaError_t launch_embed_rows(const EmbedParams& p, cudaStream_t s, bool pdl);
+cudaError_t launch_residual_norm(const ResNormParams& p, cudaStream_t s, bool pdl);
+cudaError_t launch_accept_commit(const CommitParams& p, cudaStream_t s, bool pdl);
+cudaError_t launch_draft_override(const OverrideParams& p, cudaStream_t s, bool pdl);
+cudaError_t launch_pack_gate_up(const __nv_bfloat16* src, __nv_bfloat16* dst, int I, int H, cudaStream_t s);
+
+}  // namespace gr

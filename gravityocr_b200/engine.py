@@ -1,0 +1,371 @@
+"""The self-speculative round on one B200: device weights, the paged K/V pool, the forward composed from the C-ABI
+kernels, the draft / verify / accept-commit round and its CUDA-graph capture per (B, batch).
+
+Data layout in HBM (bf16 unless noted):
+  * weights per layer: ``qkv`` [q_dim + 2 kv_dim, H] (q, k, v rows stacked), ``o`` [H, q_dim], ``gate_up`` [2I, H]
+    re-tiled so every 128-row tile holds 64 gate rows and the matching 64 up rows, ``down`` [H, I], 4 norm vectors;
+    ``embed`` [V, H], ``norm`` [H], ``lm_head`` [V, H].
+  * K/V cache: two tensors [layers, pages, kv_heads, page_size=16, head_dim] -- one (page, head) block of a layer is
+    4 KiB contiguous, the TMA box of the attention kernel; requests own fixed page tables [bs, pages_per_req] int32.
+  * per-forward activations for M = bs*K rows: residual ``h`` fp32 x2 (ping-pong), ``x`` bf16 (normed GEMM input),
+    ``q`` / ``attn`` bf16 [M, q_dim], ``y`` fp32 [M, H] (o_proj / down_proj output), ``act`` bf16 [M, I].
+  * round state (device, int64 like the reference's ``seq_lens`` / seed pool): ``seq_lens`` (K/V length; x0 not yet
+    in K/V), ``seeds`` pool by req_pool_idx, ``n_committed`` / ``rounds`` int32; ``packed`` [bs, K+2] int32 + status
+    word -- the round's only device->host copy.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib as L
+from .config import ModelConfig
+
+
+def rope_inv_freq(cfg: ModelConfig) -> torch.Tensor:
+    """transformers modeling_glm_ocr.py:708-710, computed on the CPU in fp32 exactly as there."""
+    rd = cfg.rotary_dim
+    return 1.0 / (cfg.rope_theta ** (torch.arange(0, rd, 2, dtype=torch.int64).to(dtype=torch.float32) / rd))
+
+
+class DeviceWeights:
+    """bf16 weights on one GPU in the kernels' layout."""
+
+    def __init__(self, cfg: ModelConfig, weights: Dict[str, torch.Tensor], device: torch.device):
+        self.cfg = cfg
+        dev = device
+        bf = torch.bfloat16
+        up = lambda t: t.to(device=dev, dtype=bf).contiguous()
+        self.embed = up(weights["embed_tokens"])
+        self.norm = up(weights["norm"])
+        self.lm_head = up(weights["lm_head"])
+        self.layers = []
+        for l in range(cfg.n_layers):
+            p = f"layers.{l}."
+            qkv = up(torch.cat([weights[p + "q_proj"], weights[p + "k_proj"], weights[p + "v_proj"]], 0))
+            gu_raw = up(weights[p + "gate_up_proj"])
+            gu = torch.empty_like(gu_raw)
+            L.pack_gate_up(gu_raw, gu, cfg.intermediate)
+            del gu_raw
+            self.layers.append({
+                "qkv": qkv, "o": up(weights[p + "o_proj"]), "gate_up": gu, "down": up(weights[p + "down_proj"]),
+                "in": up(weights[p + "input_layernorm"]), "psa": up(weights[p + "post_self_attn_layernorm"]),
+                "pa": up(weights[p + "post_attention_layernorm"]), "pm": up(weights[p + "post_mlp_layernorm"]),
+            })
+        self.inv_freq = rope_inv_freq(cfg).to(dev)
+        torch.cuda.synchronize(dev)
+
+    def streamed_bytes(self) -> int:
+        n = self.norm.numel() + self.lm_head.numel()
+        for d in self.layers:
+            n += sum(d[k].numel() for k in ("qkv", "o", "gate_up", "down", "in", "psa", "pa", "pm"))
+        return 2 * n
+
+
+class PagePool:
+    """Fixed-size page pool of the paged K/V cache; pages are handed out per request and returned on release."""
+
+    def __init__(self, cfg: ModelConfig, n_pages: int, page_size: int, device: torch.device):
+        self.cfg = cfg
+        self.page_size = page_size
+        self.n_pages = n_pages
+        shape = (cfg.n_layers, n_pages, cfg.n_kv_heads, page_size, cfg.head_dim)
+        self.k = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+        self.v = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+        self.free: List[int] = list(range(n_pages - 1, -1, -1))
+
+    def alloc(self, n: int) -> List[int]:
+        if n > len(self.free):
+            raise RuntimeError(f"K/V pool exhausted: need {n} pages, {len(self.free)} free")
+        return [self.free.pop() for _ in range(n)]
+
+    def release(self, pages: Sequence[int]) -> None:
+        self.free.extend(int(p) for p in pages)
+
+    @staticmethod
+    def bytes_needed(cfg: ModelConfig, n_pages: int, page_size: int) -> int:
+        return 2 * cfg.n_layers * n_pages * cfg.n_kv_heads * page_size * cfg.head_dim * 2
+
+
+def attention_split(bs: int, K: int, max_len: int, avg_len: int, n_kv: int, sms: int) -> Tuple[int, int]:
+    """Cache tokens per split and the split-grid extent: enough (request, head, split) units to fill the SMs a few
+    times over, never less than one 64-token tile per split."""
+    work = max(1, avg_len) * bs * n_kv
+    chunk = int(math.ceil(work / (4 * sms) / 64.0)) * 64
+    chunk = max(64, min(chunk, 4096))
+    max_splits = max(1, int(math.ceil((max_len + K + 1) / chunk)))
+    return chunk, max_splits
+
+
+@dataclass
+class RoundBuffers:
+    bs: int
+    K: int
+    seq_lens: torch.Tensor      # int64 [bs]
+    page_table: torch.Tensor    # int32 [bs, pages_per_req]
+    rpi: torch.Tensor           # int64 [bs]
+    seeds: torch.Tensor         # int64 [pool]
+    n_committed: torch.Tensor   # int32 [bs]
+    rounds: torch.Tensor        # int32 [bs]
+    am: torch.Tensor            # int32 [bs*K]  draft argmax = verify input [a0, d1..]
+    v: torch.Tensor             # int32 [bs*K]  verify argmax
+    gap_d: torch.Tensor         # fp32 [bs*K]
+    gap_v: torch.Tensor
+    top_d: torch.Tensor
+    top_v: torch.Tensor
+    readback: torch.Tensor      # int32 [bs*(K+2) + 4]: packed rows, then n_released, status
+    released: torch.Tensor      # int64 [bs*K]
+    out_next: torch.Tensor      # int64 [bs]
+    accept_len: torch.Tensor    # int32 [bs]
+    attn_chunk: int
+    attn_splits: int
+    override_g: Optional[torch.Tensor] = None      # int32 [bs, g_len] forced-accept replay stream
+    override_plan: Optional[torch.Tensor] = None   # int32 [bs, max_rounds]
+
+    @property
+    def packed(self) -> torch.Tensor:
+        return self.readback[: self.bs * (self.K + 2)].view(self.bs, self.K + 2)
+
+    @property
+    def n_released(self) -> torch.Tensor:
+        return self.readback[self.bs * (self.K + 2): self.bs * (self.K + 2) + 1]
+
+    @property
+    def status(self) -> torch.Tensor:
+        return self.readback[self.bs * (self.K + 2) + 1: self.bs * (self.K + 2) + 2]
+
+
+class Engine:
+    """One model replica on one GPU: the forward, the round and graph capture."""
+
+    def __init__(self, cfg: ModelConfig, weights: Dict[str, torch.Tensor], *, max_rows: int, n_pages: int,
+                 page_size: int = 16, device: Optional[torch.device] = None, pdl: bool = True):
+        L.load()
+        if page_size != 16:
+            raise ValueError("the attention kernel's TMA box is one 16-token page")
+        self.cfg = cfg
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.page_size = page_size
+        L.set_pdl(pdl)
+        self.w = DeviceWeights(cfg, weights, self.device)
+        self.pool = PagePool(cfg, n_pages, page_size, self.device)
+        self.max_rows = max_rows
+        dev, H = self.device, cfg.hidden
+        self.h = [torch.zeros((max_rows, H), dtype=torch.float32, device=dev) for _ in range(2)]
+        self.x = torch.zeros((max_rows, H), dtype=torch.bfloat16, device=dev)
+        self.q = torch.zeros((max_rows, cfg.q_dim), dtype=torch.bfloat16, device=dev)
+        self.attn = torch.zeros((max_rows, cfg.q_dim), dtype=torch.bfloat16, device=dev)
+        self.y = torch.zeros((max_rows, H), dtype=torch.float32, device=dev)
+        self.act = torch.zeros((max_rows, cfg.intermediate), dtype=torch.bfloat16, device=dev)
+        self.row_pos = torch.zeros((max_rows,), dtype=torch.int32, device=dev)
+        self.row_slot = torch.zeros((max_rows,), dtype=torch.int64, device=dev)
+        self.row_ids = torch.zeros((max_rows,), dtype=torch.int32, device=dev)
+        self.status = torch.zeros((4,), dtype=torch.int32, device=dev)
+        self.lin_ws = torch.zeros((self.linear_ws_bytes(max_rows),), dtype=torch.uint8, device=dev)
+        self.attn_ws: Optional[torch.Tensor] = None
+        self.sms = L.num_sms()
+        self.graphs: Dict[Tuple[int, int], torch.cuda.CUDAGraph] = {}
+
+    # ------------------------------------------------------------------ workspace
+    def gemm_shapes(self) -> List[Tuple[int, int]]:
+        c = self.cfg
+        return [(c.qkv_dim, c.hidden), (c.hidden, c.q_dim), (2 * c.intermediate, c.hidden), (c.hidden, c.intermediate),
+                (c.vocab, c.hidden)]
+
+    def linear_ws_bytes(self, m: int) -> int:
+        """Scratch of every projection at M = m rows with its default split-K (tickets, partials, argmax tiles)."""
+        return max(L.linear_workspace_bytes(n, m, L.linear_default_splits(n, k, m)) for n, k in self.gemm_shapes())
+
+    def reserve(self, m: int) -> None:
+        """Grow the projection scratch for M = m rows (never during graph capture)."""
+        need = self.linear_ws_bytes(m)
+        if self.lin_ws.numel() < need:
+            self.lin_ws = torch.zeros((need,), dtype=torch.uint8, device=self.device)
+
+    def _attn_workspace(self, bs: int, K: int, splits: int) -> torch.Tensor:
+        need = L.attention_workspace_bytes(bs, K, self.cfg.n_q_heads, self.cfg.n_kv_heads, splits)
+        if self.attn_ws is None or self.attn_ws.numel() < need:
+            self.attn_ws = torch.zeros((max(need, 256),), dtype=torch.uint8, device=self.device)
+        return self.attn_ws
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, rows_mode: int, bs: int, K: int, seq_lens: torch.Tensor, page_table: torch.Tensor, *,
+                out_idx: torch.Tensor, out_top1: Optional[torch.Tensor] = None, out_gap: Optional[torch.Tensor] = None,
+                seeds=None, rpi=None, ids32=None, ids64=None, row_embeds=None, attn_chunk: int = 64,
+                attn_splits: int = 1, status: Optional[torch.Tensor] = None) -> None:
+        """One pass of the decoder over M = bs*K rows; writes each row's argmax (and top-1 / gap) to out_idx."""
+        cfg, w, M = self.cfg, self.w, bs * K
+        if M > self.max_rows:
+            raise ValueError(f"{M} rows > max_rows {self.max_rows}")
+        st = status if status is not None else self.status
+        if self.lin_ws.numel() < self.linear_ws_bytes(M):
+            raise RuntimeError(f"projection scratch too small for M={M}; call reserve() before capture")
+        draft = rows_mode == L.ROWS_DRAFT
+        base_add = 1 if rows_mode == L.ROWS_VERIFY else 0
+        L.embed_rows(rows_mode, bs, K, seeds=seeds, rpi=rpi, ids32=ids32, ids64=ids64, row_embeds=row_embeds,
+                     seq_lens=seq_lens, page_table=page_table, page_size=self.page_size, embed=w.embed, vocab=cfg.vocab,
+                     mask_id=cfg.mask_id, norm_w=w.layers[0]["in"], eps=cfg.rms_eps, h_out=self.h[0], x_out=self.x,
+                     row_pos=self.row_pos, row_slot=self.row_slot, row_ids=self.row_ids, status=st)
+        ws_attn = self._attn_workspace(bs, K, attn_splits) if attn_splits > 1 else None
+        cur = 0
+        for l, d in enumerate(w.layers):
+            nxt = w.layers[l + 1] if l + 1 < len(w.layers) else None
+            e = L.Epilogue()
+            e.mode = L.EPI_QKV_ROPE
+            e.q_out = self.q.data_ptr()
+            e.k_cache = self.pool.k[l].data_ptr()
+            e.v_cache = self.pool.v[l].data_ptr()
+            e.row_pos = self.row_pos.data_ptr()
+            e.row_slot = self.row_slot.data_ptr()
+            e.inv_freq = w.inv_freq.data_ptr()
+            e.rotary_dim = cfg.rotary_dim
+            e.n_q_heads = cfg.n_q_heads
+            e.n_kv_heads = cfg.n_kv_heads
+            e.page_size = self.page_size
+            L.linear(d["qkv"], self.x, M, e, self.lin_ws, prefetch=d["o"], status=st)
+            L.bd_attention(self.q, self.pool.k[l], self.pool.v[l], page_table, seq_lens, bs, K, draft, base_add,
+                           cfg.n_q_heads, cfg.n_kv_heads, self.page_size, attn_chunk, attn_splits, self.attn, ws_attn,
+                           status=st)
+            e = L.Epilogue()
+            e.mode = L.EPI_STORE_F32
+            e.out = self.y.data_ptr()
+            e.ld_out = cfg.hidden
+            L.linear(d["o"], self.attn, M, e, self.lin_ws, prefetch=d["gate_up"], status=st)
+            L.residual_norm(M, self.h[cur], self.y, d["psa"], d["pa"], cfg.rms_eps, self.h[1 - cur], self.x)
+            cur ^= 1
+            e = L.Epilogue()
+            e.mode = L.EPI_SWIGLU
+            e.out = self.act.data_ptr()
+            e.ld_out = cfg.intermediate
+            L.linear(d["gate_up"], self.x, M, e, self.lin_ws, prefetch=d["down"], status=st)
+            e = L.Epilogue()
+            e.mode = L.EPI_STORE_F32
+            e.out = self.y.data_ptr()
+            e.ld_out = cfg.hidden
+            pf = nxt["qkv"] if nxt is not None else w.lm_head[: min(w.lm_head.shape[0], 16384)]
+            L.linear(d["down"], self.act, M, e, self.lin_ws, prefetch=pf, status=st)
+            L.residual_norm(M, self.h[cur], self.y, d["pm"], nxt["in"] if nxt is not None else w.norm, cfg.rms_eps,
+                            self.h[1 - cur], self.x)
+            cur ^= 1
+        e = L.Epilogue()
+        e.mode = L.EPI_ARGMAX
+        e.out_idx = out_idx.data_ptr()
+        e.out_top1 = 0 if out_top1 is None else out_top1.data_ptr()
+        e.out_gap = 0 if out_gap is None else out_gap.data_ptr()
+        L.linear(w.lm_head, self.x, M, e, self.lin_ws, status=st)
+
+    def final_hidden(self) -> torch.Tensor:
+        """Normed input of lm_head of the last forward (bf16 [max_rows, H]); for logits checks in tests."""
+        return self.x
+
+    # ------------------------------------------------------------------ requests
+    def pages_for(self, max_len: int) -> int:
+        return (max_len + self.page_size - 1) // self.page_size
+
+    def new_round_buffers(self, bs: int, K: int, pages_per_req: int, pool_size: Optional[int] = None,
+                          max_len: Optional[int] = None, avg_len: Optional[int] = None) -> RoundBuffers:
+        dev = self.device
+        pool_size = pool_size or bs
+        ml = max_len or pages_per_req * self.page_size
+        chunk, splits = attention_split(bs, K, ml, avg_len or ml, self.cfg.n_kv_heads, self.sms)
+        i32 = dict(dtype=torch.int32, device=dev)
+        i64 = dict(dtype=torch.int64, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        return RoundBuffers(
+            bs=bs, K=K, seq_lens=torch.zeros((bs,), **i64), page_table=torch.zeros((bs, pages_per_req), **i32),
+            rpi=torch.arange(bs, **i64), seeds=torch.zeros((pool_size,), **i64), n_committed=torch.zeros((bs,), **i32),
+            rounds=torch.zeros((bs,), **i32), am=torch.zeros((bs * K,), **i32), v=torch.zeros((bs * K,), **i32),
+            gap_d=torch.zeros((bs * K,), **f32), gap_v=torch.zeros((bs * K,), **f32),
+            top_d=torch.zeros((bs * K,), **f32), top_v=torch.zeros((bs * K,), **f32),
+            readback=torch.zeros((bs * (K + 2) + 4,), **i32), released=torch.zeros((bs * K,), **i64),
+            out_next=torch.zeros((bs,), **i64), accept_len=torch.zeros((bs,), **i32),
+            attn_chunk=chunk, attn_splits=splits)
+
+    def prefill(self, rb: RoundBuffers, prefixes: List[torch.Tensor], prefix_ids: List[torch.Tensor],
+                chunk: int = 64, attn_chunk: Optional[int] = None) -> List[int]:
+        """Causal prefill of each request's prefix through the same kernels (chunks of ``chunk`` rows, causal
+        attention).  prefixes[b]: fp32 [P_b, H] layer-0 input rows (image embeddings + prompt embeddings);
+        prefix_ids[b]: int64 [P_b] ids (< 0 where the row comes from ``prefixes``).  Sets seq_lens = P_b, the seed
+        pool (seeds[rpi[b]] = first generated token), n_committed = 1.  Returns the first tokens."""
+        bs = rb.bs
+        dev = self.device
+        lens = [int(p.shape[0]) for p in prefixes]
+        cap = rb.page_table.shape[1] * self.page_size
+        for n in lens:
+            if ((n + chunk - 1) // chunk) * chunk > cap:
+                raise ValueError(f"prefix of {n} rows needs {((n + chunk - 1) // chunk) * chunk} slots, capacity {cap}")
+        n_chunks = max((n + chunk - 1) // chunk for n in lens)
+        H = self.cfg.hidden
+        first = [0] * bs
+        self.reserve(bs * chunk)
+        out_idx = torch.zeros((bs * chunk,), dtype=torch.int32, device=dev)
+        for c in range(n_chunks):
+            active = [b for b in range(bs) if lens[b] > c * chunk]
+            nb = len(active)
+            rows_e = torch.zeros((nb * chunk, H), dtype=torch.float32)
+            ids = torch.zeros((nb * chunk,), dtype=torch.int64)
+            for i, b in enumerate(active):
+                s0, s1 = c * chunk, min(lens[b], (c + 1) * chunk)
+                rows_e[i * chunk: i * chunk + s1 - s0] = prefixes[b][s0:s1].float()
+                ids[i * chunk: i * chunk + s1 - s0] = prefix_ids[b][s0:s1]
+            seq = torch.full((nb,), c * chunk, dtype=torch.int64).to(dev)
+            pt = rb.page_table[torch.tensor(active, device=dev)].contiguous()
+            rows_e, ids = rows_e.to(dev), ids.to(dev)
+            ml = (c + 1) * chunk
+            ach, asp = attention_split(nb, chunk, ml, ml, self.cfg.n_kv_heads, self.sms)
+            if attn_chunk:
+                ach, asp = attn_chunk, int(math.ceil(ml / attn_chunk))
+            self.forward(L.ROWS_EXPLICIT, nb, chunk, seq, pt, out_idx=out_idx, ids64=ids, row_embeds=rows_e,
+                         attn_chunk=ach, attn_splits=asp, status=rb.status)
+            res = out_idx.cpu()
+            for i, b in enumerate(active):
+                if c * chunk <= lens[b] - 1 < (c + 1) * chunk:
+                    first[b] = int(res[i * chunk + (lens[b] - 1 - c * chunk)])
+        rb.seq_lens.copy_(torch.tensor(lens, dtype=torch.int64))
+        rb.seeds[rb.rpi] = torch.tensor(first, dtype=torch.int64, device=dev)
+        rb.n_committed.fill_(1)
+        rb.rounds.zero_()
+        self.check_status(rb)
+        return first
+
+    def check_status(self, rb: RoundBuffers) -> None:
+        s = int(rb.status.item())
+        if s != 0:
+            raise RuntimeError(f"device status {s}: {L.load().gr_status_string(s).decode()}")
+
+    # ------------------------------------------------------------------ the round
+    def round_launch(self, rb: RoundBuffers, override: bool = False) -> None:
+        """Enqueue one round: draft forward, optional forced-accept override, verify forward, accept-and-commit."""
+        bs, K = rb.bs, rb.K
+        self.forward(L.ROWS_DRAFT, bs, K, rb.seq_lens, rb.page_table, out_idx=rb.am, out_top1=rb.top_d,
+                     out_gap=rb.gap_d, seeds=rb.seeds, rpi=rb.rpi, attn_chunk=rb.attn_chunk,
+                     attn_splits=rb.attn_splits, status=rb.status)
+        if override:
+            L.draft_override(bs, K, rb.am, rb.override_g, rb.n_committed, rb.override_plan, rb.rounds,
+                             self.cfg.vocab, self.cfg.mask_id)
+        self.forward(L.ROWS_VERIFY, bs, K, rb.seq_lens, rb.page_table, out_idx=rb.v, out_top1=rb.top_v,
+                     out_gap=rb.gap_v, ids32=rb.am, attn_chunk=rb.attn_chunk, attn_splits=rb.attn_splits,
+                     status=rb.status)
+        L.accept_commit(bs, K, rb.am, rb.v, rb.seeds, rb.rpi, rb.seq_lens, rb.packed, rb.released, rb.out_next,
+                        x0_committed=False, n_released=rb.n_released, n_committed=rb.n_committed, rounds=rb.rounds,
+                        accept_len=rb.accept_len)
+
+    def capture(self, rb: RoundBuffers, override: bool = False, warmup: int = 0) -> torch.cuda.CUDAGraph:
+        """Capture one round (both forwards and the commit) into a CUDA graph; replays read the device-resident
+        lengths, seeds and page tables, so one graph serves every round of this (B, batch) bucket."""
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                self.round_launch(rb, override)
+        torch.cuda.current_stream().wait_stream(s)
+        self.graphs[(rb.K, rb.bs)] = g
+        return g
+
+
+def host_rows(readback_host: torch.Tensor, bs: int, K: int) -> List[List[int]]:
+    return readback_host[: bs * (K + 2)].view(bs, K + 2).tolist()

@@ -1,0 +1,81 @@
+"""Seeded random-init weights and synthetic request inputs (no checkpoint or dataset is available).
+
+Weights follow the baseline: every parameter (norm weights included) is drawn N(0, 0.02).  The draw order is fixed
+here so the CUDA path, the CPU oracle and the reference's own transformers model (loaded with the same tensors by
+``tests/golden/make_golden.py``) all hold identical values.  Names are transformers' GLM-OCR parameter names with
+the ``model.language_model.`` prefix dropped.
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Tuple
+
+import torch
+
+from .config import ModelConfig
+
+INIT_STD = 0.02
+
+
+def weight_shapes(cfg: ModelConfig) -> List[Tuple[str, Tuple[int, ...]]]:
+    h, i = cfg.hidden, cfg.intermediate
+    out: List[Tuple[str, Tuple[int, ...]]] = [("embed_tokens", (cfg.vocab, h))]
+    for l in range(cfg.n_layers):
+        p = f"layers.{l}."
+        out += [
+            (p + "q_proj", (cfg.q_dim, h)),
+            (p + "k_proj", (cfg.kv_dim, h)),
+            (p + "v_proj", (cfg.kv_dim, h)),
+            (p + "o_proj", (h, cfg.q_dim)),
+            (p + "gate_up_proj", (2 * i, h)),
+            (p + "down_proj", (h, i)),
+            (p + "input_layernorm", (h,)),
+            (p + "post_self_attn_layernorm", (h,)),
+            (p + "post_attention_layernorm", (h,)),
+            (p + "post_mlp_layernorm", (h,)),
+        ]
+    out += [("norm", (h,)), ("lm_head", (cfg.vocab, h))]
+    return out
+
+
+def random_weights(cfg: ModelConfig, seed: int, dtype: torch.dtype = torch.bfloat16) -> Dict[str, torch.Tensor]:
+    """N(0, 0.02) for every tensor, drawn in ``weight_shapes`` order from one CPU generator.
+
+    The values are drawn in fp32 and rounded once to ``dtype``; with dtype=float32 nothing is rounded."""
+    g = torch.Generator().manual_seed(int(seed))
+    w: Dict[str, torch.Tensor] = {}
+    for name, shape in weight_shapes(cfg):
+        t = torch.empty(shape, dtype=torch.float32)
+        t.normal_(0.0, INIT_STD, generator=g)
+        w[name] = t if dtype == torch.float32 else t.to(dtype)
+    return w
+
+
+def request_inputs(cfg: ModelConfig, seed: int, n_image: int, n_prompt: int, index: int = 0,
+                   dtype: torch.dtype = torch.bfloat16) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Synthetic prefix of one request: ``n_image`` image-embedding vectors N(0,1)*0.02 (injected as inputs_embeds at
+    image-token positions) followed by ``n_prompt`` prompt ids uniform in [0, vocab-1) excluding mask_id.
+
+    Returns (image_embeds [n_image, hidden] fp32 holding ``dtype``-rounded values, prompt_ids [n_prompt] int64)."""
+    g = torch.Generator().manual_seed(int(seed) * 1_000_003 + 7919 * int(index) + 1)
+    img = torch.randn((n_image, cfg.hidden), generator=g, dtype=torch.float32) * 0.02
+    if dtype != torch.float32:
+        img = img.to(dtype).float()
+    ids = torch.randint(0, cfg.vocab - 1, (n_prompt,), generator=g, dtype=torch.int64)
+    bad = ids == cfg.mask_id
+    while bool(bad.any()):
+        ids[bad] = torch.randint(0, cfg.vocab - 1, (int(bad.sum()),), generator=g, dtype=torch.int64)
+        bad = ids == cfg.mask_id
+    return img, ids
+
+
+def prefix_token_ids(cfg: ModelConfig, n_image: int, prompt_ids: torch.Tensor) -> torch.Tensor:
+    """Prefix ids as the processor lays them out: image placeholder ids, then the prompt ids."""
+    return torch.cat([torch.full((n_image,), cfg.image_token_id, dtype=torch.int64), prompt_ids.to(torch.int64)])
+
+
+def prefix_embeddings(weights: Dict[str, torch.Tensor], cfg: ModelConfig, image_embeds: torch.Tensor,
+                      prompt_ids: torch.Tensor) -> torch.Tensor:
+    """Layer-0 input of the prefix in fp32: image vectors at image positions, embedding rows elsewhere
+    (reference ``src/fast_sampling.py:483-488`` masked_scatter)."""
+    e = weights["embed_tokens"][prompt_ids.to(torch.int64)].float()
+    return torch.cat([image_embeds.float(), e], dim=0)

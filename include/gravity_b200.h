@@ -1,0 +1,152 @@
+/* C ABI of the B200-native self-speculative decode round (libgravity_b200.so).
+ *
+ * Plain pointers and sizes only: every tensor argument is a device pointer owned by the caller, every call takes the
+ * CUDA stream to launch on (as a void*, NULL = legacy default stream), returns GR_OK or an error code, allocates
+ * nothing and never synchronises.  Kernels record run-time faults (a bounded wait that ran out, an out-of-range id
+ * or page) in the caller's device `status` word (first error wins); the host reads it with the round's readback.
+ *
+ * Each entry cites the reference interface it replaces (trillion-labs/GravityOCR; paths inside that project).
+ * Shapes use B = bd_size, K = B + 1 rows per request, M = bs * K rows per forward, H = hidden.
+ */
+#ifndef GRAVITY_B200_H
+#define GRAVITY_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum gr_status_code {
+  GR_OK = 0,
+  GR_ERR_ARG = 1,         /* invalid argument (shape, alignment, unsupported size) */
+  GR_ERR_CUDA = 2,        /* a CUDA runtime call failed (launch, attribute) */
+  GR_ERR_TMA = 3,         /* cuTensorMapEncodeTiled rejected a tensor map */
+  GR_ERR_TIMEOUT = 4,     /* device: a bounded wait ran out (written to the status word) */
+  GR_ERR_BAD_ID = 5,      /* device: a token id outside [0, vocab) */
+  GR_ERR_BAD_PAGE = 6,    /* device: a position beyond the request's page-table capacity */
+  GR_ERR_UNSUPPORTED = 7  /* the build does not support this configuration */
+};
+
+/* Epilogues of gr_linear. */
+enum gr_epilogue_mode {
+  GR_EPI_STORE_F32 = 0,  /* out[t, f] fp32 */
+  GR_EPI_STORE_BF16 = 1, /* out[t, f] bf16 */
+  GR_EPI_SWIGLU = 2,     /* out[t, j] = up * silu(gate), bf16; weight rows interleaved per 64 (gr_pack_gate_up) */
+  GR_EPI_QKV_ROPE = 3,   /* q -> q_out, k/v -> paged cache with partial interleaved RoPE */
+  GR_EPI_ARGMAX = 4      /* vocab-wide argmax per row: out_idx, out_top1, out_gap; no logits written */
+};
+
+/* Row sources of gr_embed_rows. */
+enum gr_rows_mode {
+  GR_ROWS_DRAFT = 0,    /* row (b, j): id = j == 0 ? seeds[rpi[b]] : mask_id, position seq_lens[b] + j */
+  GR_ROWS_VERIFY = 1,   /* row (b, j): id = ids32[b*K + j] (the draft argmax), position seq_lens[b] + 1 + j */
+  GR_ROWS_EXPLICIT = 2  /* row t: id = ids64[t] (id < 0: take row_embeds[t]), position seq_lens[b] + j */
+};
+
+typedef struct gr_epilogue {
+  int mode;               /* gr_epilogue_mode */
+  void* out;              /* STORE_*, SWIGLU: [M, ld_out] */
+  int ld_out;
+  /* QKV_ROPE: weight rows are [q heads | k heads | v heads] x head_dim 128 */
+  void* q_out;            /* bf16 [M, n_q_heads*128] */
+  void* k_cache;          /* bf16 [pages, n_kv_heads, page_size, 128] of this layer */
+  void* v_cache;
+  const int32_t* row_pos;  /* [M] RoPE position of each row */
+  const int64_t* row_slot; /* [M] cache slot (page * page_size + offset) of each row */
+  const float* inv_freq;   /* [rotary_dim / 2] */
+  int rotary_dim, n_q_heads, n_kv_heads, page_size;
+  /* ARGMAX */
+  int32_t* out_idx;       /* [M] */
+  float* out_top1;        /* [M] or NULL */
+  float* out_gap;         /* [M] top-1 minus top-2 logit, or NULL */
+} gr_epilogue;
+
+/* Library identity / diagnostics. */
+int gr_version(void);
+const char* gr_status_string(int code);
+/* Programmatic dependent launch on (1, default) / off (0) for every later launch. */
+void gr_set_pdl(int enable);
+/* Number of SMs the split heuristics assume (queried from device 0 on first use). */
+int gr_num_sms(void);
+
+/* Workspace (scratch) sizes in bytes for the calls below; the caller allocates them once, zero-filled, and passes
+ * them on every call (the kernels leave their tickets re-armed at zero). */
+size_t gr_linear_workspace_bytes(int n_out, int m, int splits);
+size_t gr_attention_workspace_bytes(int bs, int K, int n_q_heads, int n_kv_heads, int max_splits);
+
+/* Split-K count gr_linear would use by default for this shape (0 in `splits` below). */
+int gr_linear_default_splits(int n_out, int k_in, int m);
+
+/* Weight-streaming projection with a fused epilogue:  y[t, f] = sum_k x[t, k] * w[f, k].
+ * w: bf16 [n_out, k_in] row-major (nn.Linear); x: bf16 [m, k_in] row-major; n_out % 128 == 0, k_in % 64 == 0,
+ * k_in * 2 and the row strides 16-byte aligned.  splits = 0 picks gr_linear_default_splits.  prefetch /
+ * prefetch_bytes: optional global range (the next kernel's weights) warmed into L2 while this one streams.
+ * Replaces the cuBLAS GEMMs behind transformers' GlmOcrTextAttention q/k/v/o_proj and GlmOcrTextMLP
+ * gate_up/down_proj (models/glm_ocr/modeling_glm_ocr.py:188-191, 242-243) plus, for GR_EPI_QKV_ROPE, RoPE (:121-165)
+ * and the SGLang KV-cache write; for GR_EPI_ARGMAX the lm_head + logits.argmax of
+ * patches/sglang/python/sglang/srt/speculative/selfspec_diffusion_worker.py:739-742 and src/fast_sampling.py:571-575. */
+int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr_epilogue* epi, int splits,
+              void* workspace, size_t workspace_bytes, const void* prefetch, size_t prefetch_bytes, int32_t* status,
+              void* stream);
+
+/* Layer-0 input rows of a forward and the window plan: for each row its token id, RoPE position and cache slot;
+ * h_out[t] = embedding row (fp32), x_out[t] = RMSNorm(h_out[t]) * norm_w (bf16).
+ * Replaces the draft window build of selfspec_diffusion_worker.py:689-706 (_draft_block: [seed | mask x (K-1)],
+ * positions seq_lens + j), the verify ids/positions of :849-884 (_fulldraft_verify: am[:, :K], seq_lens + 1 + j),
+ * the embedding lookup with image-embedding injection of src/fast_sampling.py:483-488, and the first
+ * input_layernorm (modeling_glm_ocr.py:50-64). */
+int gr_embed_rows(int mode, int bs, int K, const int64_t* seeds, const int64_t* req_pool_idx, const int32_t* ids32,
+                  const int64_t* ids64, const float* row_embeds, const int64_t* seq_lens, const int32_t* page_table,
+                  int pt_stride, int page_size, int pages_per_req, const void* embed, int vocab, int mask_id,
+                  const void* norm_w, float eps, int hidden, float* h_out, void* x_out, int32_t* row_pos,
+                  int64_t* row_slot, int32_t* row_ids, int32_t* status, void* stream);
+
+/* Sandwich-norm step: h_out = h_in + w_a * RMSNorm(y); x_out = w_b * RMSNorm(h_out) (bf16).  The decoder layer's
+ * post_self_attn / post_attention and post_mlp / next input_layernorm pairs (modeling_glm_ocr.py:281-302), and the
+ * final model norm before lm_head. */
+int gr_residual_norm(int m, int hidden, const float* h_in, const float* y, const void* w_a, const void* w_b, float eps,
+                     float* h_out, void* x_out, void* stream);
+
+/* Block-diffusion draft attention (draft = 1: row 0 causal, mask rows see the whole window) or causal verify /
+ * prefill attention (draft = 0) over the paged cache.  q/out: bf16 [bs*K, n_q_heads, 128]; k_cache/v_cache: bf16
+ * [n_pages, n_kv_heads, page_size = 16, 128] of one layer; page_table int32 [bs, pt_stride]; window row j of request b
+ * sits at position seq_lens[b] + base_add + j.  chunk: cache tokens per split (multiple of 64); max_splits: grid
+ * extent (splits past a request's length exit at once).
+ * Replaces flashinfer BatchPrefillWithPagedKVCacheWrapper in the draft (NON_CAUSAL + CAUSAL re-run of row 0) and
+ * verify (CAUSAL) roles planned by patches/sglang/python/sglang/srt/speculative/selfspec_fast_attn.py:168-440 and
+ * the flex_attention masks of src/fast_sampling.py:508-514. */
+int gr_bd_attention(const void* q, const void* k_cache, const void* v_cache, int64_t n_pages, const int32_t* page_table,
+                    int pt_stride, const int64_t* seq_lens, int bs, int K, int draft, int base_add, int n_q_heads,
+                    int n_kv_heads, int page_size, int chunk, int max_splits, void* out, void* workspace,
+                    size_t workspace_bytes, int32_t* status, void* stream);
+
+/* Accept and commit (one CTA): acc = leading d_j == v[j-1] matches (linear-chain greedy verify); packed[b] =
+ * (a0, acc, v[0..acc], zeros); seeds[rpi[b]] = out_next[b] = v[acc]; seq_lens[b] += acc + 1 (+1 more when
+ * x0_committed == 0, i.e. x0 is committed here); released = the verify rows acc+1..K-1 compacted in row order, as
+ * loc[b*K + j] when loc != NULL (physical slots, the reference free list) else as logical positions;
+ * n_committed[b] += acc + 2 and rounds[b] += 1 when given.
+ * Replaces sgl_kernel verify_tree_greedy on the linear chain (selfspec_diffusion_worker.py:530-548) and the Triton
+ * _ss_commit_kernel (patches/sglang/python/sglang/srt/speculative/selfspec_fast_commit.py:108-147). */
+int gr_accept_commit(int bs, int K, const int32_t* am, const int32_t* v, int64_t* seeds, const int64_t* req_pool_idx,
+                     int64_t* seq_lens, int x0_committed, const int64_t* loc, int32_t* packed, int64_t* released,
+                     int32_t* n_released, int64_t* out_next, int32_t* n_committed, int32_t* rounds,
+                     int32_t* accept_len, void* stream);
+
+/* Forced-accept replay (no reference counterpart; the baseline's config-2 replay mode): overwrite the draft so that
+ * exactly A = accept_plan[b, rounds[b]] drafts match the known stream g: am[b, j] = g[b, c + j] for 1 <= j <= A and
+ * am[b, A+1] = (g[b, c + A + 1] + 1) mod vocab (skipping mask_id), c = n_committed[b]. */
+int gr_draft_override(int bs, int K, int32_t* am, const int32_t* g, int g_stride, const int32_t* n_committed,
+                      const int32_t* accept_plan, int plan_stride, const int32_t* rounds, int vocab, int mask_id,
+                      void* stream);
+
+/* Host helper: reorder gate_up rows [gate(I) | up(I)] into 128-row tiles of 64 gate + 64 matching up rows (the
+ * layout GR_EPI_SWIGLU expects).  src/dst: bf16 [2*I, H] device buffers. */
+int gr_pack_gate_up(const void* src, void* dst, int intermediate, int hidden, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GRAVITY_B200_H */

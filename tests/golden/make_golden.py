@@ -1,0 +1,259 @@
+"""Generate the golden vectors that pin the CPU oracle to the reference implementation.
+
+Run in the build container, where the reference tree is readable (it is never read on the GPU box):
+
+    python tests/golden/make_golden.py [--ref /path/to/GravityOCR] [--only natcache_small,commit_kernel,...]
+
+Outputs (small JSON files next to this script):
+  * ``natcache_<case>.json``: the reference's own ``generate_speculative_natcache`` (``src/fast_sampling.py:425``) and
+    ``teacher_force_argmax`` (``:631``) run unmodified on CPU on a random-init transformers ``GlmOcrForConditionalGeneration``
+    holding ``gravityocr_b200.weights.random_weights`` -- per-round trace, committed stream, teacher-forced argmax.
+    Settings follow the reference's own ``--no_dynamo`` (``src/infer_omnidocbench.py:614-616``); the processor and the
+    vision tower are stubbed so the seeded image embeddings are injected as inputs_embeds at image-token positions and
+    positions are 1-D (``get_rope_index`` -> arange).
+  * ``commit_kernel.json``: the reference Triton ``_ss_commit_kernel`` (``selfspec_fast_commit.py:108-147``) executed
+    by the Triton CPU interpreter on seeded inputs (its source is parsed out of the reference file at generation time).
+  * ``commit_rules.json``: ``cut_index`` and ``host_commit`` of ``selfspec_commit_rules.py`` on seeded rows.
+"""
+from __future__ import annotations
+
+import argparse
+import ast
+import json
+import os
+import random
+import sys
+import time
+import types
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+
+NATCACHE_CASES = {
+    # name: (n_layers, n_image, n_prompt, max_new_tokens, bd, weight_seed, input_seed)
+    "small": (2, 64, 16, 48, 16, 0, 0),
+    "config0": (16, 256, 32, 128, 16, 0, 0),
+}
+
+
+def _dump(name, obj):
+    path = os.path.join(HERE, name)
+    with open(path, "w") as f:
+        json.dump(obj, f, separators=(",", ":"))
+    print(f"wrote {path} ({os.path.getsize(path)} B)")
+
+
+def gen_natcache(ref: str, case: str):
+    import torch
+    torch._dynamo.config.disable = True
+    sys.path.insert(0, os.path.join(ref, "src"))
+    import fast_sampling as fs
+    from models.glm_ocr_dllm import GlmOcrBlockDiffusion
+    from transformers import GlmOcrConfig, GlmOcrForConditionalGeneration
+    from gravityocr_b200.config import small_model
+    from gravityocr_b200.weights import random_weights, request_inputs, prefix_token_ids
+
+    L, n_img, n_txt, new, bd, wseed, iseed = NATCACHE_CASES[case]
+    cfg = small_model(L)
+    hf = GlmOcrConfig()
+    tc = hf.text_config
+    tc.num_hidden_layers = L
+    tc.hidden_size = cfg.hidden
+    tc.num_attention_heads = cfg.n_q_heads
+    tc.num_key_value_heads = cfg.n_kv_heads
+    tc.head_dim = cfg.head_dim
+    tc.intermediate_size = cfg.intermediate
+    tc.vocab_size = cfg.vocab
+    tc.rms_norm_eps = cfg.rms_eps
+    tc.rope_parameters = {"rope_theta": cfg.rope_theta, "rope_type": "default",
+                          "partial_rotary_factor": cfg.rotary_dim / cfg.head_dim, "mrope_section": [8, 12, 12]}
+    hf.vision_config.depth = 1
+    torch.manual_seed(0)
+    glm = GlmOcrForConditionalGeneration(hf).float().eval()
+    w = random_weights(cfg, wseed, torch.float32)
+    sd = {}
+    for k, t in w.items():
+        if k == "lm_head":
+            sd["lm_head.weight"] = t
+        elif k.startswith("layers."):
+            _, l, n = k.split(".", 2)
+            mod = "self_attn." if n.endswith("_proj") and n[0] in "qkvo" else ("mlp." if n.endswith("_proj") else "")
+            sd[f"model.language_model.layers.{l}.{mod}{n}.weight"] = t
+        else:
+            sd[f"model.language_model.{k}.weight"] = t
+    missing, unexpected = glm.load_state_dict(sd, strict=False)
+    assert not unexpected and all("visual" in m for m in missing), (missing, unexpected)
+
+    m = object.__new__(GlmOcrBlockDiffusion)
+    torch.nn.Module.__init__(m)
+    m.glm = glm
+    m.bd_size = bd
+    m.mask_id = cfg.mask_id
+    m.image_token_id = hf.image_token_id
+    m.loop_enabled = False
+    glm.model.language_model.config._attn_implementation = "flex_attention"
+    img, txt = request_inputs(cfg, iseed, n_img, n_txt, 0, torch.float32)
+    ids = prefix_token_ids(cfg, n_img, txt)[None]
+
+    class _Enc(dict):
+        def to(self, dev):
+            return self
+
+    class _Proc:
+        def apply_chat_template(self, *a, **k):
+            return ""
+
+        def __call__(self, *a, **k):
+            return _Enc({"input_ids": ids, "mm_token_type_ids": torch.zeros_like(ids),
+                         "pixel_values": torch.zeros(1), "image_grid_thw": None})
+
+    m.processor = _Proc()
+    m.tokenizer = types.SimpleNamespace(eos_token_id=None, decode=lambda *a, **k: "")
+    mm = glm.model
+    mm.get_image_features = lambda pv, thw, return_dict=True: types.SimpleNamespace(pooler_output=[img])
+    mm.get_rope_index = lambda ids_, mmtt, image_grid_thw=None, video_grid_thw=None, attention_mask=None: (
+        torch.arange(ids_.shape[1])[None, None, :].expand(3, 1, -1), None)
+    from PIL import Image
+    im = Image.new("RGB", (8, 8))
+    t0 = time.time()
+    tr = []
+    _, st = fs.generate_speculative_natcache(m, im, max_new_tokens=new, return_stats=True, trace=tr)
+    t1 = time.time()
+    stream = [t for d in tr for t in d["new_tokens"]]
+    tf = fs.teacher_force_argmax(m, im, "x", stream[:new])
+    t2 = time.time()
+    print(f"natcache {case}: {t1 - t0:.1f}s, teacher force {t2 - t1:.1f}s, stats {st}")
+    _dump(f"natcache_{case}.json", {
+        "source": "reference src/fast_sampling.py generate_speculative_natcache + teacher_force_argmax (CPU, fp32)",
+        "n_layers": L, "n_image": n_img, "n_prompt": n_txt, "max_new_tokens": new, "bd": bd,
+        "weight_seed": wseed, "input_seed": iseed, "mask_id": cfg.mask_id, "prompt_ids": txt.tolist(),
+        "stream": stream, "teacher_force_argmax": tf, "stats": st,
+        "trace": [{"k": d["k"], "draft": d["draft"], "ar_pred": d["ar_pred"], "new_tokens": d["new_tokens"]} for d in tr],
+        "seconds": round(t1 - t0, 2), "threads": torch.get_num_threads(),
+    })
+
+
+def gen_commit_kernel(ref: str):
+    os.environ["TRITON_INTERPRET"] = "1"
+    import torch
+    import triton
+    import triton.language as tl
+    src = os.path.join(ref, "patches/sglang/python/sglang/srt/speculative/selfspec_fast_commit.py")
+    tree = ast.parse(open(src).read())
+    fn = [n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name == "_ss_commit_kernel"][0]
+    ns = {"triton": triton, "tl": tl}
+    exec(compile(ast.Module(body=[fn], type_ignores=[]), src, "exec"), ns)
+    kern = ns["_ss_commit_kernel"]
+    rng = random.Random(1234)
+    cases = []
+    for K in (5, 9, 17, 33):
+        for bs in (1, 2, 3, 8, 33):
+            pool = 2 * bs + 3
+            predict = torch.tensor([rng.randrange(0, 59392) for _ in range(bs * K + 1)], dtype=torch.int32)
+            accs = [rng.choice([0, K - 1, rng.randrange(0, K)]) for _ in range(bs)]
+            acc = torch.tensor(accs, dtype=torch.int32)
+            a0m = torch.tensor([[rng.randrange(0, 59392) for _ in range(K)] for _ in range(bs)], dtype=torch.int64)
+            a0 = a0m[:, 0]
+            rpi = torch.tensor(rng.sample(range(pool), bs), dtype=torch.int64)
+            seeds = torch.tensor([rng.randrange(0, 59392) for _ in range(pool)], dtype=torch.int64)
+            sl = torch.tensor([rng.randrange(1, 9000) for _ in range(bs)], dtype=torch.int64)
+            loc = torch.tensor(rng.sample(range(10 * bs * K + 100), bs * K), dtype=torch.int64)
+            packed = torch.zeros((bs, K + 2), dtype=torch.int32)
+            free = torch.full((bs * K,), -1, dtype=torch.int64)
+            out = torch.zeros((bs,), dtype=torch.int64)
+            inp = {"predict": predict.tolist(), "acc": accs, "a0": a0.tolist(), "rpi": rpi.tolist(),
+                   "seeds": seeds.tolist(), "seq_lens": sl.tolist(), "loc": loc.tolist()}
+            kern[(bs,)](predict, acc, a0, a0.stride(0), rpi, seeds, sl, loc, packed, free, out,
+                        K=K, KP2=triton.next_power_of_2(K), BS_POW2=triton.next_power_of_2(max(bs, 2)))
+            n_free = sum(K - 1 - a for a in accs)
+            cases.append({"K": K, "bs": bs, "pool": pool, "in": inp,
+                          "out": {"packed": packed.tolist(), "seeds": seeds.tolist(), "seq_lens": sl.tolist(),
+                                  "free": free[:n_free].tolist(), "free_tail": free[n_free:].tolist(), "out": out.tolist()}})
+    _dump("commit_kernel.json", {"source": "reference selfspec_fast_commit.py _ss_commit_kernel under TRITON_INTERPRET=1",
+                                 "cases": cases})
+
+
+def gen_commit_rules(ref: str):
+    sys.path.insert(0, os.path.join(ref, "patches/sglang/python/sglang/srt/speculative"))
+    import selfspec_commit_rules as R
+    rng = random.Random(99)
+    V = 59392
+    cut = []
+    for _ in range(400):
+        n = rng.randrange(1, 35)
+        T = [rng.choice([rng.randrange(0, V), rng.randrange(0, V), rng.choice([-1, V + 1, V, 7, 11])]) for _ in range(n)]
+        budget = rng.choice([0, 1, 2, n - 1, n, n + 1, rng.randrange(0, 2 * n + 2)])
+        stop = frozenset(rng.sample([7, 11, 13, 151329, 59246], rng.randrange(0, 3)))
+        cut.append({"T": T, "budget": budget, "stop": sorted(stop), "vocab": V, "j": R.cut_index(T, budget, stop, V)})
+
+    class _SP:
+        def __init__(self, mx):
+            self.max_new_tokens = mx
+            self.ignore_eos = False
+            self.stop_token_ids = [7]
+            self.stop_strs = None
+            self.stop_regex_strs = None
+
+    class _Req:
+        """Minimal stand-in: the fast path only reads these attributes; finish state is not recorded."""
+
+        def __init__(self, mx, out):
+            self.sampling_params = _SP(mx)
+            self.eos_token_ids = {11}
+            self.tokenizer = None
+            self.grammar = None
+            self.to_finish = None
+            self.vocab_size = V
+            self.output_ids = list(out)
+            self.spec_verify_ct = 0
+            self.spec_accepted_tokens = 0
+            self.hist = []
+
+        def finished(self):
+            return False
+
+        def check_finished(self, n=1):
+            pass
+
+        def update_spec_acceptance_histogram(self, a):
+            self.hist.append(a)
+
+    hc = []
+    for _ in range(60):
+        bs = rng.randrange(1, 6)
+        K = rng.choice([5, 17, 33])
+        reqs, rows, budgets = [], [], []
+        for _ in range(bs):
+            prev = rng.randrange(0, 40)
+            mx = prev + rng.randrange(1, K + 4)
+            r = _Req(mx, [1] * prev)
+            a = rng.randrange(0, K)
+            row = [rng.randrange(0, V), a] + [rng.choice([rng.randrange(0, V), 7, 11, 12]) for _ in range(a + 1)] + [0] * (K - 1 - a)
+            reqs.append(r)
+            rows.append(row)
+            budgets.append(mx - prev)
+        toks, js, accs = R.host_commit(reqs, rows)
+        hc.append({"K": K, "rows": rows, "budgets": budgets, "stop": [7, 11], "vocab": V,
+                   "toks": toks, "js": js, "accs": accs, "accepted_counters": [q.spec_accepted_tokens for q in reqs]})
+    _dump("commit_rules.json", {"source": "reference selfspec_commit_rules.py cut_index / host_commit",
+                                "cut_index": cut, "host_commit": hc})
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default=os.environ.get("GRAVITYOCR_REF", "/root/reference"))
+    ap.add_argument("--only", default="commit_kernel,commit_rules,natcache_small,natcache_config0")
+    a = ap.parse_args()
+    only = a.only.split(",")
+    if "commit_rules" in only:
+        gen_commit_rules(a.ref)
+    if "commit_kernel" in only:
+        gen_commit_kernel(a.ref)
+    for case in NATCACHE_CASES:
+        if f"natcache_{case}" in only:
+            gen_natcache(a.ref, case)
+
+
+if __name__ == "__main__":
+    main()
