@@ -1,0 +1,483 @@
+#!/usr/bin/env python
+"""Benchmark of the self-speculative decode round on B200s (driver contract: one JSON line from rank 0).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one replica per GPU, requests sharded, no collective)
+
+Workload (weak scaling): 64 concurrent requests per GPU, prefixes U[256, 4096] image-embedding
+tokens + 32 prompt tokens, B = 16 (K = 17 rows per forward), paged K/V with 16-token pages, bf16, seed 3; random-init
+weights N(0, 0.02) (no checkpoint), synthetic inputs (no dataset).  Prefill runs first (not timed).  A step is one
+self-spec round over the whole batch: draft forward + causal verify forward + accept-and-commit, replayed from CUDA
+graphs with every length, seed and page table resident on the device.  value = committed tokens of all ranks / the
+slowest rank's device time.  The workload is far larger than L2 (1.16 GB of weights and ~11 GB of K/V per forward).
+
+Also reported on rank 0 at N = 1: the bs-1 crop workload (config 2: prefix 256 + 32, 1024 tokens) in natural and
+forced-accept replay modes, per-forward % of the measured HBM roofline, the dominant kernel's roofline, the
+end-to-end number through the served worker API (per-round H2D of the batch's request slots and D2H of the packed
+commit rows), and the CPU port of the reference round on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "self-spec decode tokens/s & tokens/forward @bs1/bs64, %HBM roofline, 1/2/4/8 B200"
+K_BD = 16
+SEED = 3
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--bd", type=int, default=K_BD)
+    ap.add_argument("--no-bs1", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--profile-small", action="store_true", help="short run for ncu captures (no extras)")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------- workload
+def workload(cfg, n_req: int, seed: int):
+    g = torch.Generator().manual_seed(seed)
+    n_img = torch.randint(256, 4097, (n_req,), generator=g).tolist()
+    out_len = torch.randint(256, 2049, (n_req,), generator=g).tolist()
+    return n_img, out_len
+
+
+def request_rows(cfg, weights, seed, idx, n_img, n_prompt=32):
+    from gravityocr_b200.weights import request_inputs
+    img, txt = request_inputs(cfg, seed, n_img, n_prompt, idx, torch.bfloat16)
+    emb = weights["embed_tokens"][txt].float()
+    x = torch.cat([img, emb], 0)
+    ids = torch.cat([torch.full((n_img,), -1, dtype=torch.int64), txt])
+    return x, ids
+
+
+class ClockSampler:
+    """nvidia-smi samples (200 ms) during the timed region."""
+
+    FIELDS = ["index", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
+              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={','.join(self.FIELDS)}", "--format=csv,noheader,nounits",
+                                       "-i", str(self.gpu), "-lms", "200"], stdout=subprocess.PIPE,
+                                      stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.p is not None:
+            time.sleep(0.25)
+            self.p.terminate()
+            try:
+                self.out, _ = self.p.communicate(timeout=5)
+            except Exception:
+                self.p.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (self.out or "").strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------- CPU port of the reference round
+def cpu_round_port(cfg, weights, seq_lens, K, rounds, threads=None):
+    """The oracle's restatement of the reference round (fp32, torch CPU, all host threads) on a synthetic K/V prefix
+    of the given lengths; returns (tokens/s, committed tokens, seconds, threads)."""
+    from oracle.decoder_ref import OracleDecoder, SpecState, spec_round
+    n = threads or os.cpu_count() or 1
+    torch.set_num_threads(n)
+    m = OracleDecoder(cfg, weights)
+    g = torch.Generator().manual_seed(11)
+    toks, secs = 0, 0.0
+    for S in seq_lens:
+        cache = m.new_cache(S + rounds * (K + 1) + K + 2)
+        cache.k[:, :S].normal_(0, 1, generator=g)
+        cache.v[:, :S].normal_(0, 1, generator=g)
+        st = SpecState(cache, S, 1, [1], S)
+        t0 = time.perf_counter()
+        for _ in range(rounds):
+            spec_round(m, st, K)
+        secs += time.perf_counter() - t0
+        toks += len(st.out) - 1
+    return toks / secs, toks, secs, n
+
+
+def run_reference(a):
+    from gravityocr_b200 import dp
+    from gravityocr_b200.config import ModelConfig
+    from gravityocr_b200.weights import random_weights
+    rank, world, _ = dp.dist_env()
+    if rank != 0:
+        return 0
+    cfg = ModelConfig()
+    K = a.bd + 1
+    w = random_weights(cfg, SEED, torch.bfloat16)
+    w32 = {k: v.float() for k, v in w.items()}
+    n_img, _ = workload(cfg, a.batch, SEED)
+    S = [n_img[0] + 32]
+    rounds = max(1, min(4, a.steps))
+    tps, toks, secs, n = cpu_round_port(cfg, w32, S, K, rounds)
+    steps_done = a.warmup + a.steps
+    line = {"impl": "reference", "metric": METRIC, "value": round(tps, 4), "unit": "tokens/s", "n_gpus": a.gpus,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(1000 * secs / rounds, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": "config3-bs64-serving (CPU sample: request 0)", "batch_per_gpu": a.batch, "K": K,
+                       "prefix": S, "page_size": 16},
+            "cpu_baseline": {"value": round(tps, 4), "unit": "tokens/s", "cores": n, "kind": "port",
+                             "sample": f"{rounds} full-draft rounds of request 0 (prefix {S[0]} tokens, synthetic K/V), "
+                                       f"fp32 torch on {n} host threads"},
+            "e2e": {"value": round(tps, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "reference is Python (SGLang / transformers) and cannot run on the GPU box; its round is timed as "
+                    "the oracle's CPU port", "steps_run": steps_done}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------- native
+def time_graphs(gd, gv, steps):
+    """Replay draft and verify graphs `steps` times; returns (total ms, draft ms, verify ms)."""
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for e in ev:
+        e[0].record()
+        gd.replay()
+        e[1].record()
+        gv.replay()
+        e[2].record()
+    t1.record()
+    torch.cuda.synchronize()
+    d = sum(e[0].elapsed_time(e[1]) for e in ev)
+    v = sum(e[1].elapsed_time(e[2]) for e in ev)
+    return t0.elapsed_time(t1), d, v
+
+
+def main():
+    a = _args()
+    if a.impl == "reference":
+        return run_reference(a)
+    from gravityocr_b200 import _lib as L
+    from gravityocr_b200 import dp
+    from gravityocr_b200.config import ModelConfig
+    from gravityocr_b200.engine import Engine
+    from gravityocr_b200.metrics import attention_bytes, forward_bytes
+    from gravityocr_b200.weights import random_weights
+
+    rank, world, local = dp.dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dp.init("nccl" if world > 1 else "gloo", timeout_s=600)
+    hbm_peak, tc_peak, peak_src = peaks()
+    cfg = ModelConfig()
+    K = a.bd + 1
+    bs = a.batch
+    w = random_weights(cfg, SEED, torch.bfloat16)
+
+    # ---- this rank's requests: equal-count, work-balanced shard of the global request list
+    n_img, out_len = workload(cfg, bs * world, SEED)
+    work = [n_img[i] + 32 + out_len[i] for i in range(bs * world)]
+    mine = dp.balanced_shards(work, world)[rank]
+    prefix = [n_img[i] + 32 for i in mine]
+    rounds_max = a.warmup + a.steps + (0 if a.no_e2e else min(a.steps, 50)) + 8
+    cap = max(prefix) + rounds_max * (K + 1) + 2 * K + 64
+    ppr = (cap + 15) // 16
+    chunk = 64
+    eng = Engine(cfg, w, max_rows=max(bs * K, bs * chunk), n_pages=bs * ppr + 8 + 256, device=dev)  # +256: bs-1 run
+    eng.reserve(bs * K)
+    rb = eng.new_round_buffers(bs, K, ppr, max_len=cap, avg_len=int(sum(prefix) / len(prefix)))
+    for b in range(bs):
+        rb.page_table[b] = torch.tensor(eng.pool.alloc(ppr), dtype=torch.int32, device=dev)
+    xs, ids = zip(*[request_rows(cfg, w, SEED, i, n_img[i]) for i in mine])
+    t_pf = time.perf_counter()
+    eng.prefill(rb, list(xs), list(ids), chunk=chunk)
+    torch.cuda.synchronize()
+    t_pf = time.perf_counter() - t_pf
+    del xs, ids
+
+    # ---- graphs (one eager round first: sizes every scratch buffer before capture)
+    eng.round_launch(rb)
+    torch.cuda.synchronize()
+    eng.check_status(rb)
+    gd, gv = eng.capture_split(rb)
+    for _ in range(a.warmup):
+        gd.replay()
+        gv.replay()
+    torch.cuda.synchronize()
+    eng.check_status(rb)
+
+    ncom0 = rb.n_committed.clone()
+    seq0 = rb.seq_lens.cpu().tolist()
+    dp.barrier(dev)
+    torch.cuda.synchronize()
+    prof = os.environ.get("GR_PROFILE_RANGE") == "1"  # ncu --profile-from-start off: capture the timed rounds only
+    with ClockSampler(local) as clk:
+        if prof:
+            torch.cuda.cudart().cudaProfilerStart()
+        total_ms, draft_ms, verify_ms = time_graphs(gd, gv, a.steps)
+        if prof:
+            torch.cuda.cudart().cudaProfilerStop()
+    dp.barrier(dev)
+    eng.check_status(rb)
+    seq1 = rb.seq_lens.cpu().tolist()
+    tokens = int((rb.n_committed - ncom0).sum().item())
+    elapsed = dp.max_over_ranks(total_ms, dev)
+    tokens_all = dp.sum_over_ranks(float(tokens), dev)
+    value = tokens_all / (elapsed / 1000.0)
+    fwd = 2 * a.steps
+    tok_per_fwd = tokens / (fwd * bs)
+    # per-forward HBM roofline (average over the timed rounds: the lengths grow linearly)
+    seq_mid = [(x + y) / 2 for x, y in zip(seq0, seq1)]
+    bd = forward_bytes(cfg, seq_mid, K, verify=False)
+    bv = forward_bytes(cfg, seq_mid, K, verify=True)
+    frac_d = bd / (draft_ms / a.steps / 1000.0) / (hbm_peak * 1e9)
+    frac_v = bv / (verify_ms / a.steps / 1000.0) / (hbm_peak * 1e9)
+
+    # ---- dominant kernel at this batch: the verify attention (K/V streaming); timed alone on this stream
+    seq_now = rb.seq_lens.cpu().tolist()
+    ws = eng._attn_workspace(bs, K, rb.attn_splits)
+    st = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_rep = 20
+    for i in range(n_rep + 3):
+        if i == 3:
+            ev0.record(st)
+        l = i % cfg.n_layers  # rotate layers: each launch reads K/V that is not in L2
+        L.bd_attention(eng.q, eng.pool.k[l], eng.pool.v[l], rb.page_table, rb.seq_lens, bs, K, False, 1,
+                       cfg.n_q_heads, cfg.n_kv_heads, 16, rb.attn_chunk, rb.attn_splits, eng.attn, ws, status=rb.status)
+    ev1.record(st)
+    torch.cuda.synchronize()
+    attn_ms = ev0.elapsed_time(ev1) / n_rep
+    attn_b = attention_bytes(cfg, seq_now, K, 1)
+    attn_gbs = attn_b / (attn_ms / 1000.0) / 1e9
+    launches = a.steps * (2 * eng.kernels_per_forward() + 1)
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": round(elapsed / a.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights N(0,0.02) and inputs; no checkpoint or dataset)",
+        "config": {"workload": "config3-bs64-serving", "batch_per_gpu": bs, "bd_size": a.bd, "K": K, "page_size": 16,
+                   "prefix": "U[256,4096] image + 32 prompt", "seed": SEED, "parallelism": f"dp{world} (replicas)",
+                   "l2": "inputs larger than L2 (1.16 GB weights + K/V per forward)",
+                   "no_finish": "output budgets U[256,2048] exceed the timed rounds"},
+        "tokens_per_forward": round(tok_per_fwd, 4),
+        "hbm_roofline_per_forward": {"draft": round(frac_d, 4), "verify": round(frac_v, 4), "peak_gbs": hbm_peak,
+                                     "peak": peak_src, "draft_ms": round(draft_ms / a.steps, 4),
+                                     "verify_ms": round(verify_ms / a.steps, 4),
+                                     "bytes_draft": bd, "bytes_verify": bv},
+        "roofline": {"kernel": "attention_kernel (verify, one layer)", "bound": "hbm",
+                     "achieved": round(attn_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(attn_gbs / hbm_peak, 4), "traffic": None,
+                     "algorithmic_bytes": attn_b, "avg_launch_ms": round(attn_ms, 5), "peak_source": peak_src},
+        "gpu_launches": launches,
+        "prefill_s": round(t_pf, 2),
+    }
+    if rank == 0:
+        line["clocks"] = clk.summary()
+
+    # ---- end to end through the served worker API (rank 0's replica, same batch, from its current state)
+    if not a.no_e2e and not a.profile_small:
+        line["e2e"] = e2e_worker(eng, rb, cfg, K, min(a.steps, 50), dev)
+
+    if rank == 0 and world == 1 and not a.profile_small:
+        if not a.no_bs1:
+            line["bs1"] = bs1_crop(eng, cfg, w, K, dev, hbm_peak)
+        if not a.no_cpu:
+            w32 = {k: v.float() for k, v in w.items()}
+            tps, toks, secs, n = cpu_round_port(cfg, w32, [prefix[0]], K, 4)
+            line["cpu_baseline"] = {"value": round(tps, 4), "unit": "tokens/s", "cores": n, "kind": "port",
+                                    "sample": f"4 full-draft rounds of one config-3 request (prefix {prefix[0]}, "
+                                              f"synthetic K/V), fp32 torch on {n} host threads: {toks} tokens in "
+                                              f"{secs:.1f} s"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dp.finish()
+    return 0
+
+
+def e2e_worker(eng, rb, cfg, K, steps, dev):
+    """Rounds through SelfSpecDiffusionWorker.forward_batch_generation: per round the scheduler's request slots
+    are copied host->device from pinned memory, and the packed commit rows + status are read back (plus the host
+    finish rules)."""
+    from gravityocr_b200.compat.sglang_worker import ReqToPagePool, SelfSpecDiffusionWorker
+    from gravityocr_b200.compat.types import ForwardMode, Req, SamplingParams, ScheduleBatch
+    import types as _t
+    bs = rb.bs
+    pool = ReqToPagePool.__new__(ReqToPagePool)
+    pool.engine, pool.size, pool.pages_per_req = eng, bs, rb.page_table.shape[1]
+    pool.table, pool.owned = rb.page_table.clone(), {}
+    target = _t.SimpleNamespace(engine=eng, req_to_page=pool)
+    args = _t.SimpleNamespace(speculative_num_draft_tokens=K, page_size=16, model_path="")
+    os.environ["SELFSPEC_MASK_ID"] = str(cfg.mask_id)
+    wk = SelfSpecDiffusionWorker(args, 0, 0, None, 0, 0, 0, 0, target)
+    wk._seeds().copy_(rb.seeds)
+    reqs = []
+    for b in range(bs):
+        r = Req(b, torch.zeros((0, cfg.hidden)), [], SamplingParams(max_new_tokens=1 << 30), cfg.vocab)
+        r._spec_seed_ready = True
+        reqs.append(r)
+    rpi_host = torch.arange(bs, dtype=torch.int64).pin_memory()
+    rpi_dev = torch.empty((bs,), dtype=torch.int64, device=dev)
+    batch = ScheduleBatch(reqs, rpi_dev, rb.seq_lens.clone(), ForwardMode.DECODE, rb.seq_lens.cpu())
+    for _ in range(3):  # warm-up (captures the worker's graph)
+        rpi_dev.copy_(rpi_host, non_blocking=True)
+        wk.forward_batch_generation(batch)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    toks = 0
+    e0.record()
+    for _ in range(steps):
+        rpi_dev.copy_(rpi_host, non_blocking=True)
+        res = wk.forward_batch_generation(batch)
+        toks += sum(len(t) for t in res.next_token_ids_cpu)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    return {"value": round(toks / (ms / 1000.0), 2), "unit": "tokens/s", "h2d_bytes_per_step": bs * 8,
+            "d2h_bytes_per_step": int(rb.readback.numel() * 4), "steps": steps,
+            "api": "SelfSpecDiffusionWorker.forward_batch_generation"}
+
+
+def bs1_crop(eng, cfg, w, K, dev, hbm_peak):
+    """Config 2 shape at batch 1 (prefix 256 + 32, 1024 generated tokens): natural mode and forced-accept replay
+    (drafts overwritten from the natural stream so accept lengths are U{0..B}, seed 2)."""
+    from gravityocr_b200.metrics import forward_bytes
+    n_tok = 1024
+    P = 256 + 32
+    cap = P + 2 * n_tok + 4 * K + 64
+    ppr = (cap + 15) // 16
+    eng.reserve(K)
+    rb = eng.new_round_buffers(1, K, ppr, max_len=cap, avg_len=P + n_tok // 2)
+    pages = eng.pool.alloc(ppr)
+    rb.page_table[0] = torch.tensor(pages, dtype=torch.int32, device=dev)
+    x, ids = request_rows(cfg, w, 2, 0, 256)
+    eng.prefill(rb, [x], [ids])
+    snap = (rb.seq_lens.clone(), rb.seeds.clone(), rb.n_committed.clone(), rb.rounds.clone())
+
+    def restore():
+        rb.seq_lens.copy_(snap[0]); rb.seeds.copy_(snap[1]); rb.n_committed.copy_(snap[2]); rb.rounds.copy_(snap[3])
+
+    eng.round_launch(rb)
+    torch.cuda.synchronize()
+    restore()
+    gd, gv = eng.capture_split(rb)
+    out = {}
+    # natural mode: rounds until 1024 tokens are committed (device counters; one sync at the end)
+    rounds = 0
+    hist = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    d_ms = v_ms = 0.0
+    while True:
+        ta, tb, tc = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        ta.record(); gd.replay(); tb.record(); gv.replay(); tc.record()
+        hist.append((ta, tb, tc))
+        rounds += 1
+        if rounds % 32 == 0 and int(rb.n_committed[0]) >= n_tok:
+            break
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    d_ms = sum(a.elapsed_time(b) for a, b, c in hist) / rounds
+    v_ms = sum(b.elapsed_time(c) for a, b, c in hist) / rounds
+    n = int(rb.n_committed[0]) - 1
+    S_mid = P + n // 2
+    out["natural"] = {"tokens_per_s": round(n / (ms / 1000.0), 1), "tokens": n, "rounds": rounds,
+                      "tokens_per_forward": round(n / (2 * rounds), 4), "draft_ms": round(d_ms, 4),
+                      "verify_ms": round(v_ms, 4),
+                      "hbm_frac_draft": round(forward_bytes(cfg, [S_mid], K, False) / (d_ms / 1e3) / (hbm_peak * 1e9), 4),
+                      "hbm_frac_verify": round(forward_bytes(cfg, [S_mid], K, True) / (v_ms / 1e3) / (hbm_peak * 1e9), 4)}
+    # the natural stream g, read from the committed rows of a replay with per-round readback
+    restore()
+    g = [int(rb.seeds[0])]
+    while len(g) < n_tok + K + 2:
+        gd.replay(); gv.replay()
+        row = rb.packed[0].tolist()
+        g += [row[0]] + row[2: 3 + row[1]]
+    # forced-accept replay
+    restore()
+    gen = torch.Generator().manual_seed(2)
+    plan = torch.randint(0, K, (1, 2 * n_tok), generator=gen, dtype=torch.int32)
+    rb.override_g = torch.tensor([g + [0] * (2 * K)], dtype=torch.int32, device=dev)
+    rb.override_plan = plan.to(dev)
+    fd, fv = eng.capture_split(rb, override=True)
+    restore()
+    rounds = 0
+    e0.record()
+    while True:
+        fd.replay(); fv.replay()
+        rounds += 1
+        if rounds % 16 == 0 and int(rb.n_committed[0]) >= n_tok:
+            break
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    n = int(rb.n_committed[0]) - 1
+    # untimed check of the same replay: every round accepts exactly its planned A_r and the stream is g
+    restore()
+    f_out, accs = [int(rb.seeds[0])], []
+    while len(f_out) < n_tok:
+        fd.replay(); fv.replay()
+        row = rb.packed[0].tolist()
+        accs.append(row[1])
+        f_out += [row[0]] + row[2: 3 + row[1]]
+    same = f_out == g[: len(f_out)] and accs == plan[0, : len(accs)].tolist()
+    out["forced_accept"] = {"tokens_per_s": round(n / (ms / 1000.0), 1), "tokens": n, "rounds": rounds,
+                            "tokens_per_forward": round(n / (2 * rounds), 4),
+                            "plan": "A_r ~ U{0..16}, seed 2", "stream_equals_natural_and_accepts_plan": same}
+    eng.pool.release(pages)
+    out["workload"] = "config2-bs1-crop (prefix 256 + 32, 1024 tokens), weights of the config-3 replica"
+    return out
+
+
+if __name__ == "__main__":
+    sys.exit(main())

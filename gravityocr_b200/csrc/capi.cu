@@ -117,7 +117,7 @@ static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // Every call shares one scratch buffer, whatever its shape: the tickets live in a fixed region at its head (so a
 // later call of another shape never finds another call's partial sums where its tickets are), then the fp32
 // split-K partials, then the per-tile argmax records.
-constexpr size_t kMaxTiles = 4096;     // feature tiles x token tiles of one call
+constexpr size_t kMaxTiles = 16384;    // feature tiles x token tiles of one call (lm_head at 8192 rows)
 constexpr size_t kMaxArgTiles = 1024;  // token tiles of one lm_head call
 constexpr size_t kTicketBytes = kMaxTiles * sizeof(int) + kMaxArgTiles * sizeof(int);
 static LinearWs linear_ws_layout(void* base, const LinearShape& s, int m, int splits) {

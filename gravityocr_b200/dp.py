@@ -63,3 +63,14 @@ def sum_over_ranks(x: float, device=None) -> float:
 def finish() -> None:
     if dist.is_initialized():
         dist.destroy_process_group()
+
+
+def balanced_shards(work: Sequence[float], n: int) -> List[List[int]]:
+    """Equal-count shards (every replica runs the same batch size) with loads balanced by snake order over the
+    requests sorted by expected work."""
+    order = sorted(range(len(work)), key=lambda i: (-work[i], i))
+    shards: List[List[int]] = [[] for _ in range(n)]
+    for k, i in enumerate(order):
+        r = k % (2 * n)
+        shards[r if r < n else 2 * n - 1 - r].append(i)
+    return [sorted(s) for s in shards]

@@ -195,14 +195,17 @@ class Engine:
     def forward(self, rows_mode: int, bs: int, K: int, seq_lens: torch.Tensor, page_table: torch.Tensor, *,
                 out_idx: torch.Tensor, out_top1: Optional[torch.Tensor] = None, out_gap: Optional[torch.Tensor] = None,
                 seeds=None, rpi=None, ids32=None, ids64=None, row_embeds=None, attn_chunk: int = 64,
-                attn_splits: int = 1, status: Optional[torch.Tensor] = None) -> None:
-        """One pass of the decoder over M = bs*K rows; writes each row's argmax (and top-1 / gap) to out_idx."""
+                attn_splits: int = 1, status: Optional[torch.Tensor] = None, head: bool = True) -> None:
+        """One pass of the decoder over M = bs*K rows; writes each row's argmax (and top-1 / gap) to out_idx.
+        head=False stops before lm_head (the normed final hidden rows stay in ``self.x``)."""
         cfg, w, M = self.cfg, self.w, bs * K
         if M > self.max_rows:
             raise ValueError(f"{M} rows > max_rows {self.max_rows}")
         st = status if status is not None else self.status
         if self.lin_ws.numel() < self.linear_ws_bytes(M):
-            raise RuntimeError(f"projection scratch too small for M={M}; call reserve() before capture")
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError(f"projection scratch too small for M={M}; call reserve() before capture")
+            self.reserve(M)
         draft = rows_mode == L.ROWS_DRAFT
         base_add = 1 if rows_mode == L.ROWS_VERIFY else 0
         L.embed_rows(rows_mode, bs, K, seeds=seeds, rpi=rpi, ids32=ids32, ids64=ids64, row_embeds=row_embeds,
@@ -250,6 +253,8 @@ class Engine:
             L.residual_norm(M, self.h[cur], self.y, d["pm"], nxt["in"] if nxt is not None else w.norm, cfg.rms_eps,
                             self.h[1 - cur], self.x)
             cur ^= 1
+        if not head:
+            return
         e = L.Epilogue()
         e.mode = L.EPI_ARGMAX
         e.out_idx = out_idx.data_ptr()
@@ -319,11 +324,19 @@ class Engine:
             if attn_chunk:
                 ach, asp = attn_chunk, int(math.ceil(ml / attn_chunk))
             self.forward(L.ROWS_EXPLICIT, nb, chunk, seq, pt, out_idx=out_idx, ids64=ids, row_embeds=rows_e,
-                         attn_chunk=ach, attn_splits=asp, status=rb.status)
-            res = out_idx.cpu()
-            for i, b in enumerate(active):
-                if c * chunk <= lens[b] - 1 < (c + 1) * chunk:
-                    first[b] = int(res[i * chunk + (lens[b] - 1 - c * chunk)])
+                         attn_chunk=ach, attn_splits=asp, status=rb.status, head=False)
+            # lm_head only on the rows that end a prefix (the first generated token of those requests)
+            ends = [(b, i * chunk + (lens[b] - 1 - c * chunk)) for i, b in enumerate(active)
+                    if c * chunk <= lens[b] - 1 < (c + 1) * chunk]
+            if ends:
+                rows = self.x[torch.tensor([r for _, r in ends], device=dev)].contiguous()
+                e = L.Epilogue()
+                e.mode = L.EPI_ARGMAX
+                e.out_idx = out_idx.data_ptr()
+                L.linear(self.w.lm_head, rows, len(ends), e, self.lin_ws, status=rb.status)
+                res = out_idx[: len(ends)].cpu()
+                for k, (b, _) in enumerate(ends):
+                    first[b] = int(res[k])
         rb.seq_lens.copy_(torch.tensor(lens, dtype=torch.int64))
         rb.seeds[rb.rpi] = torch.tensor(first, dtype=torch.int64, device=dev)
         rb.n_committed.fill_(1)
@@ -337,8 +350,8 @@ class Engine:
             raise RuntimeError(f"device status {s}: {L.load().gr_status_string(s).decode()}")
 
     # ------------------------------------------------------------------ the round
-    def round_launch(self, rb: RoundBuffers, override: bool = False) -> None:
-        """Enqueue one round: draft forward, optional forced-accept override, verify forward, accept-and-commit."""
+    def draft_launch(self, rb: RoundBuffers, override: bool = False) -> None:
+        """Enqueue the draft forward over [x0 | mask x (K-1)] (+ the forced-accept override when asked)."""
         bs, K = rb.bs, rb.K
         self.forward(L.ROWS_DRAFT, bs, K, rb.seq_lens, rb.page_table, out_idx=rb.am, out_top1=rb.top_d,
                      out_gap=rb.gap_d, seeds=rb.seeds, rpi=rb.rpi, attn_chunk=rb.attn_chunk,
@@ -346,12 +359,25 @@ class Engine:
         if override:
             L.draft_override(bs, K, rb.am, rb.override_g, rb.n_committed, rb.override_plan, rb.rounds,
                              self.cfg.vocab, self.cfg.mask_id)
+
+    def verify_launch(self, rb: RoundBuffers) -> None:
+        """Enqueue the causal verify forward over [a0, d1..d_{K-1}] and the accept-and-commit kernel."""
+        bs, K = rb.bs, rb.K
         self.forward(L.ROWS_VERIFY, bs, K, rb.seq_lens, rb.page_table, out_idx=rb.v, out_top1=rb.top_v,
                      out_gap=rb.gap_v, ids32=rb.am, attn_chunk=rb.attn_chunk, attn_splits=rb.attn_splits,
                      status=rb.status)
         L.accept_commit(bs, K, rb.am, rb.v, rb.seeds, rb.rpi, rb.seq_lens, rb.packed, rb.released, rb.out_next,
                         x0_committed=False, n_released=rb.n_released, n_committed=rb.n_committed, rounds=rb.rounds,
                         accept_len=rb.accept_len)
+
+    def round_launch(self, rb: RoundBuffers, override: bool = False) -> None:
+        """Enqueue one round: draft forward, optional forced-accept override, verify forward, accept-and-commit."""
+        self.draft_launch(rb, override)
+        self.verify_launch(rb)
+
+    def kernels_per_forward(self) -> int:
+        """Kernel launches of one forward: embed + per layer (4 projections, attention, 2 residual norms) + lm_head."""
+        return 2 + 7 * self.cfg.n_layers
 
     def capture(self, rb: RoundBuffers, override: bool = False, warmup: int = 0) -> torch.cuda.CUDAGraph:
         """Capture one round (both forwards and the commit) into a CUDA graph; replays read the device-resident
@@ -365,6 +391,19 @@ class Engine:
         torch.cuda.current_stream().wait_stream(s)
         self.graphs[(rb.K, rb.bs)] = g
         return g
+
+    def capture_split(self, rb: RoundBuffers, override: bool = False) -> Tuple[torch.cuda.CUDAGraph, torch.cuda.CUDAGraph]:
+        """Two graphs per (B, batch): the draft forward, and the verify forward + commit (timed separately)."""
+        gd, gv = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(gd, stream=s):
+                self.draft_launch(rb, override)
+            with torch.cuda.graph(gv, stream=s):
+                self.verify_launch(rb)
+        torch.cuda.current_stream().wait_stream(s)
+        return gd, gv
 
 
 def host_rows(readback_host: torch.Tensor, bs: int, K: int) -> List[List[int]]:
