@@ -17,7 +17,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("GRAVITY_B200_LIB", os.path.join(_HERE, "libgravity_b200.so"))
 
 GR_OK = 0
-EPI_STORE_F32, EPI_STORE_BF16, EPI_SWIGLU, EPI_QKV_ROPE, EPI_ARGMAX = range(5)
+EPI_STORE_F32, EPI_STORE_BF16, EPI_SWIGLU, EPI_QKV_ROPE, EPI_ARGMAX, EPI_PARTIAL_F32 = range(6)
 ROWS_DRAFT, ROWS_VERIFY, ROWS_EXPLICIT = range(3)
 
 # every symbol include/gravity_b200.h declares
@@ -62,7 +62,7 @@ _SIGS = {
     "gr_linear": (_I, [_P, _I, _I, _P, _I, ctypes.POINTER(Epilogue), _I, _P, _Z, _P, _Z, _P, _P]),
     "gr_embed_rows": (_I, [_I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _I, _I, _P, _F, _I, _P, _P, _P,
                            _P, _P, _P, _P]),
-    "gr_residual_norm": (_I, [_I, _I, _P, _P, _P, _P, _F, _P, _P, _P]),
+    "gr_residual_norm": (_I, [_I, _I, _P, _P, _I, _P, _P, _F, _P, _P, _P]),
     "gr_bd_attention": (_I, [_P, _P, _P, _L, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _Z, _P, _P]),
     "gr_accept_commit": (_I, [_I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "gr_draft_override": (_I, [_I, _I, _P, _P, _I, _P, _P, _I, _P, _I, _I, _P]),
@@ -157,9 +157,9 @@ def embed_rows(mode: int, bs: int, K: int, *, seeds=None, rpi=None, ids32=None, 
     _check(rc, "gr_embed_rows")
 
 
-def residual_norm(m: int, h_in, y, w_a, w_b, eps: float, h_out, x_out, stream=None) -> None:
-    rc = load().gr_residual_norm(m, h_in.shape[-1], h_in.data_ptr(), y.data_ptr(), w_a.data_ptr(), w_b.data_ptr(), eps,
-                                 h_out.data_ptr(), x_out.data_ptr(), _stream(stream))
+def residual_norm(m: int, h_in, y, w_a, w_b, eps: float, h_out, x_out, y_parts: int = 1, stream=None) -> None:
+    rc = load().gr_residual_norm(m, h_in.shape[-1], h_in.data_ptr(), y.data_ptr(), y_parts, w_a.data_ptr(),
+                                 w_b.data_ptr(), eps, h_out.data_ptr(), x_out.data_ptr(), _stream(stream))
     _check(rc, "gr_residual_norm")
 
 

@@ -274,25 +274,34 @@ __global__ void __launch_bounds__(288, 1) attention_kernel(const __grid_constant
   __threadfence();
   const size_t slot0 = ((size_t)b * p.n_kv_heads + kvh) * p.max_splits;
   const size_t q_row_stride = (size_t)p.n_q_heads * 128;
-  for (int e = threadIdx.x; e < R * 64; e += blockDim.x) {
-    const int r = e >> 6, d = (e & 63) * 2;
+  // one warp per row; lane l owns dims 4l..4l+3; splits merged in split order
+  const int n_warps = blockDim.x >> 5;
+  for (int r = warp; r < R; r += n_warps) {
     float M = -INFINITY;
-    for (int s = 0; s < n_active; ++s) M = fmaxf(M, __ldcg(p.ws_ml + ((slot0 + s) * R_pad + r) * 2));
+    for (int s = lane; s < n_active; s += 32) M = fmaxf(M, __ldcg(p.ws_ml + ((slot0 + s) * R_pad + r) * 2));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     const float Ms = (M == -INFINITY) ? 0.f : M;
-    float Lsum = 0.f, a0 = 0.f, a1 = 0.f;
+    float Lsum = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
     for (int s = 0; s < n_active; ++s) {
-      const float* ml = p.ws_ml + ((slot0 + s) * R_pad + r) * 2;
-      const float ms = __ldcg(ml), ls = __ldcg(ml + 1);
-      const float w = (ms == -INFINITY) ? 0.f : exp2f(ms - Ms);
-      Lsum += ls * w;
-      const float* os = p.ws_o + ((slot0 + s) * R_pad + r) * 128 + d;
-      a0 += __ldcg(os) * w;
-      a1 += __ldcg(os + 1) * w;
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + ((slot0 + s) * R_pad + r) * 2));
+      const float4 os = __ldcg(reinterpret_cast<const float4*>(p.ws_o + ((slot0 + s) * R_pad + r) * 128) + lane);
+      const float w = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - Ms);
+      Lsum += ml.y * w;
+      acc.x += os.x * w;
+      acc.y += os.y * w;
+      acc.z += os.z * w;
+      acc.w += os.w * w;
     }
     const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
     const int g = r / p.K, j = r % p.K;
-    __nv_bfloat16* dst = p.out + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128 + d;
-    *reinterpret_cast<uint32_t*>(dst) = pack_bf16(a0 * inv, a1 * inv);
+    __nv_bfloat16* dst = p.out + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128 + lane * 4;
+    uint2 pk;
+    pk.x = pack_bf16(acc.x * inv, acc.y * inv);
+    pk.y = pack_bf16(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<uint2*>(dst) = pk;
   }
 }
 

@@ -179,12 +179,13 @@ int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr
               void* workspace, size_t workspace_bytes, const void* prefetch, size_t prefetch_bytes, int32_t* status,
               void* stream) {
   if (!w || !x || !epi || m <= 0 || n_out <= 0 || (n_out % 128) || k_in <= 0 || (k_in % 64)) return GR_ERR_ARG;
-  if (epi->mode < GR_EPI_STORE_F32 || epi->mode > GR_EPI_ARGMAX) return GR_ERR_ARG;
+  if (epi->mode < GR_EPI_STORE_F32 || epi->mode > GR_EPI_PARTIAL_F32) return GR_ERR_ARG;
   LinearShape s = linear_shape(n_out, k_in, m);
   if (splits <= 0) splits = default_splits(s, epi->mode);
   if (s.kc % splits) return GR_ERR_ARG;
+  const size_t ws_splits = epi->mode == GR_EPI_PARTIAL_F32 ? 1 : static_cast<size_t>(splits);
   const int kc = s.kc / splits;
-  LinearWs ws = linear_ws_layout(workspace, s, m, splits);
+  LinearWs ws = linear_ws_layout(workspace, s, m, static_cast<int>(ws_splits));
   if (!workspace || workspace_bytes < ws.bytes) return GR_ERR_ARG;
   if (static_cast<size_t>(s.n_tiles) * s.m_tiles > kMaxTiles || static_cast<size_t>(s.m_tiles) > kMaxArgTiles)
     return GR_ERR_UNSUPPORTED;
@@ -347,13 +348,14 @@ int gr_embed_rows(int mode, int bs, int K, const int64_t* seeds, const int64_t* 
   return launch_embed_rows(p, static_cast<cudaStream_t>(stream), g_pdl) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
 }
 
-int gr_residual_norm(int m, int hidden, const float* h_in, const float* y, const void* w_a, const void* w_b, float eps,
-                     float* h_out, void* x_out, void* stream) {
+int gr_residual_norm(int m, int hidden, const float* h_in, const float* y, int y_parts, const void* w_a,
+                     const void* w_b, float eps, float* h_out, void* x_out, void* stream) {
   if (m <= 0 || hidden <= 0 || hidden % 8 || !h_in || !y || !w_a || !w_b || !h_out || !x_out) return GR_ERR_ARG;
-  if (h_in == h_out) return GR_ERR_ARG;
+  if (h_in == h_out || y_parts < 1 || hidden > 8 * 192 * 4) return GR_ERR_ARG;
   ResNormParams p;
   p.m = m;
   p.hidden = hidden;
+  p.y_parts = y_parts;
   p.h_in = h_in;
   p.y = y;
   p.w_a = static_cast<const __nv_bfloat16*>(w_a);

@@ -61,19 +61,20 @@ __device__ __forceinline__ Top2 top2_warp(Top2 x) {
 // epilogue threads together (it may use warp shuffles, the epilogue barrier and `scratch` shared memory).
 template <int EPI>
 __device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, int m_tile, int f_local, int t0,
-                                           const float* v, float* scratch) {
+                                           const float* v, float* scratch, int split) {
   const int lane = threadIdx.x & 31;
   const int t_end = min(p.m, (m_tile + 1) * p.nt);
-  if constexpr (EPI == GR_EPI_STORE_F32 || EPI == GR_EPI_STORE_BF16) {
+  if constexpr (EPI == GR_EPI_STORE_F32 || EPI == GR_EPI_STORE_BF16 || EPI == GR_EPI_PARTIAL_F32) {
     const int f = n_tile * 128 + f_local;
+    const size_t base = EPI == GR_EPI_PARTIAL_F32 ? (size_t)split * p.m * p.ld_out : 0;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const int t = t0 + i;
       if (t < t_end) {
-        if constexpr (EPI == GR_EPI_STORE_F32)
-          static_cast<float*>(p.out)[(size_t)t * p.ld_out + f] = v[i];
-        else
+        if constexpr (EPI == GR_EPI_STORE_BF16)
           static_cast<__nv_bfloat16*>(p.out)[(size_t)t * p.ld_out + f] = __float2bfloat16_rn(v[i]);
+        else
+          static_cast<float*>(p.out)[base + (size_t)t * p.ld_out + f] = v[i];
       }
     }
   } else if constexpr (EPI == GR_EPI_SWIGLU) {
@@ -301,12 +302,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool run = ok && !flags[0];
     epi_bar();
     run = run && !flags[0];
-    if (p.splits == 1) {
+    if (p.splits == 1 || EPI == GR_EPI_PARTIAL_F32) {
       if (run) {
         for (int c0 = 0; c0 < p.nt; c0 += 16) {
           float v[16];
           tmem_ld16(t_lane + c0, v);
-          epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, scratch);
+          epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, scratch, split);
         }
       }
     } else {
@@ -332,15 +333,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         __threadfence();
         const float* base = p.ws_partial + (size_t)tile * p.splits * p.nt * 128;
         for (int c0 = 0; c0 < p.nt; c0 += 16) {
+          // split order is fixed (deterministic sums); the 16 rows' loads of one split are independent
           float v[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float a = 0.f;
-            if (c0 + i < rows)
-              for (int s = 0; s < p.splits; ++s) a += __ldcg(base + ((size_t)s * p.nt + c0 + i) * 128 + f_local);
-            v[i] = a;
+          for (int i = 0; i < 16; ++i) v[i] = 0.f;
+          for (int s = 0; s < p.splits; ++s) {
+            const float* src = base + ((size_t)s * p.nt + c0) * 128 + f_local;
+            float x[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) x[i] = (c0 + i < rows) ? __ldcg(src + i * 128) : 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] += x[i];
           }
-          epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, scratch);
+          epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, scratch, split);
         }
         if (threadIdx.x == 64) p.ws_ticket[tile] = 0;
       }
@@ -394,6 +399,7 @@ cudaError_t launch_linear(int epi, const CUtensorMap& tmw, const CUtensorMap& tm
     case GR_EPI_SWIGLU: return launch_linear_t<GR_EPI_SWIGLU>(tmw, tmx, p, grid, smem, stream, pdl);
     case GR_EPI_QKV_ROPE: return launch_linear_t<GR_EPI_QKV_ROPE>(tmw, tmx, p, grid, smem, stream, pdl);
     case GR_EPI_ARGMAX: return launch_linear_t<GR_EPI_ARGMAX>(tmw, tmx, p, grid, smem, stream, pdl);
+    case GR_EPI_PARTIAL_F32: return launch_linear_t<GR_EPI_PARTIAL_F32>(tmw, tmx, p, grid, smem, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -62,7 +62,7 @@ struct EmbedParams {
   int32_t* status;
 };
 struct ResNormParams {
-  int m, hidden;
+  int m, hidden, y_parts;
   const float* h_in;
   const float* y;
   const __nv_bfloat16* w_a;

@@ -94,8 +94,8 @@ def attention_split(bs: int, K: int, max_len: int, avg_len: int, n_kv: int, sms:
     """Cache tokens per split and the split-grid extent: enough (request, head, split) units to fill the SMs a few
     times over, never less than one 64-token tile per split."""
     work = max(1, avg_len) * bs * n_kv
-    chunk = int(math.ceil(work / (4 * sms) / 64.0)) * 64
-    chunk = max(64, min(chunk, 4096))
+    chunk = int(math.ceil(work / (2 * sms) / 64.0)) * 64
+    chunk = max(256, min(chunk, 4096))  # >= 4 pipeline tiles per split: the split merge is not free
     max_splits = max(1, int(math.ceil((max_len + K + 1) / chunk)))
     return chunk, max_splits
 
@@ -158,7 +158,8 @@ class Engine:
         self.x = torch.zeros((max_rows, H), dtype=torch.bfloat16, device=dev)
         self.q = torch.zeros((max_rows, cfg.q_dim), dtype=torch.bfloat16, device=dev)
         self.attn = torch.zeros((max_rows, cfg.q_dim), dtype=torch.bfloat16, device=dev)
-        self.y = torch.zeros((max_rows, H), dtype=torch.float32, device=dev)
+        self.y = torch.zeros((0,), dtype=torch.float32, device=dev)   # split-K partials of o_proj / down_proj
+        self._grow_y(max_rows)
         self.act = torch.zeros((max_rows, cfg.intermediate), dtype=torch.bfloat16, device=dev)
         self.row_pos = torch.zeros((max_rows,), dtype=torch.int32, device=dev)
         self.row_slot = torch.zeros((max_rows,), dtype=torch.int64, device=dev)
@@ -179,11 +180,22 @@ class Engine:
         """Scratch of every projection at M = m rows with its default split-K (tickets, partials, argmax tiles)."""
         return max(L.linear_workspace_bytes(n, m, L.linear_default_splits(n, k, m)) for n, k in self.gemm_shapes())
 
+    def splits(self, n_out: int, k_in: int, m: int) -> int:
+        return L.linear_default_splits(n_out, k_in, m)
+
+    def _grow_y(self, m: int) -> None:
+        c = self.cfg
+        parts = max(self.splits(c.hidden, c.q_dim, m), self.splits(c.hidden, c.intermediate, m))
+        need = parts * m * c.hidden
+        if self.y.numel() < need:
+            self.y = torch.zeros((need,), dtype=torch.float32, device=self.device)
+
     def reserve(self, m: int) -> None:
-        """Grow the projection scratch for M = m rows (never during graph capture)."""
+        """Grow the projection scratch and the partial-sum buffer for M = m rows (never during graph capture)."""
         need = self.linear_ws_bytes(m)
         if self.lin_ws.numel() < need:
             self.lin_ws = torch.zeros((need,), dtype=torch.uint8, device=self.device)
+        self._grow_y(m)
 
     def _attn_workspace(self, bs: int, K: int, splits: int) -> torch.Tensor:
         need = L.attention_workspace_bytes(bs, K, self.cfg.n_q_heads, self.cfg.n_kv_heads, splits)
@@ -202,9 +214,11 @@ class Engine:
         if M > self.max_rows:
             raise ValueError(f"{M} rows > max_rows {self.max_rows}")
         st = status if status is not None else self.status
-        if self.lin_ws.numel() < self.linear_ws_bytes(M):
+        c_ = self.cfg
+        y_need = max(self.splits(c_.hidden, c_.q_dim, M), self.splits(c_.hidden, c_.intermediate, M)) * M * c_.hidden
+        if self.lin_ws.numel() < self.linear_ws_bytes(M) or self.y.numel() < y_need:
             if torch.cuda.is_current_stream_capturing():
-                raise RuntimeError(f"projection scratch too small for M={M}; call reserve() before capture")
+                raise RuntimeError(f"scratch too small for M={M}; call reserve() before capture")
             self.reserve(M)
         draft = rows_mode == L.ROWS_DRAFT
         base_add = 1 if rows_mode == L.ROWS_VERIFY else 0
@@ -233,11 +247,13 @@ class Engine:
                            cfg.n_q_heads, cfg.n_kv_heads, self.page_size, attn_chunk, attn_splits, self.attn, ws_attn,
                            status=st)
             e = L.Epilogue()
-            e.mode = L.EPI_STORE_F32
+            e.mode = L.EPI_PARTIAL_F32
             e.out = self.y.data_ptr()
             e.ld_out = cfg.hidden
-            L.linear(d["o"], self.attn, M, e, self.lin_ws, prefetch=d["gate_up"], status=st)
-            L.residual_norm(M, self.h[cur], self.y, d["psa"], d["pa"], cfg.rms_eps, self.h[1 - cur], self.x)
+            sp_o = self.splits(cfg.hidden, cfg.q_dim, M)
+            L.linear(d["o"], self.attn, M, e, self.lin_ws, splits=sp_o, prefetch=d["gate_up"], status=st)
+            L.residual_norm(M, self.h[cur], self.y, d["psa"], d["pa"], cfg.rms_eps, self.h[1 - cur], self.x,
+                            y_parts=sp_o)
             cur ^= 1
             e = L.Epilogue()
             e.mode = L.EPI_SWIGLU
@@ -245,13 +261,14 @@ class Engine:
             e.ld_out = cfg.intermediate
             L.linear(d["gate_up"], self.x, M, e, self.lin_ws, prefetch=d["down"], status=st)
             e = L.Epilogue()
-            e.mode = L.EPI_STORE_F32
+            e.mode = L.EPI_PARTIAL_F32
             e.out = self.y.data_ptr()
             e.ld_out = cfg.hidden
+            sp_d = self.splits(cfg.hidden, cfg.intermediate, M)
             pf = nxt["qkv"] if nxt is not None else w.lm_head[: min(w.lm_head.shape[0], 16384)]
-            L.linear(d["down"], self.act, M, e, self.lin_ws, prefetch=pf, status=st)
+            L.linear(d["down"], self.act, M, e, self.lin_ws, splits=sp_d, prefetch=pf, status=st)
             L.residual_norm(M, self.h[cur], self.y, d["pm"], nxt["in"] if nxt is not None else w.norm, cfg.rms_eps,
-                            self.h[1 - cur], self.x)
+                            self.h[1 - cur], self.x, y_parts=sp_d)
             cur ^= 1
         if not head:
             return

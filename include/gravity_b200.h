@@ -35,7 +35,9 @@ enum gr_epilogue_mode {
   GR_EPI_STORE_BF16 = 1, /* out[t, f] bf16 */
   GR_EPI_SWIGLU = 2,     /* out[t, j] = up * silu(gate), bf16; weight rows interleaved per 64 (gr_pack_gate_up) */
   GR_EPI_QKV_ROPE = 3,   /* q -> q_out, k/v -> paged cache with partial interleaved RoPE */
-  GR_EPI_ARGMAX = 4      /* vocab-wide argmax per row: out_idx, out_top1, out_gap; no logits written */
+  GR_EPI_ARGMAX = 4,     /* vocab-wide argmax per row: out_idx, out_top1, out_gap; no logits written */
+  GR_EPI_PARTIAL_F32 = 5 /* split-K partials, out[split][t][f] fp32 (split stride m * ld_out); the consumer sums
+                            them (gr_residual_norm with y_parts = splits) */
 };
 
 /* Row sources of gr_embed_rows. */
@@ -103,11 +105,12 @@ int gr_embed_rows(int mode, int bs, int K, const int64_t* seeds, const int64_t* 
                   const void* norm_w, float eps, int hidden, float* h_out, void* x_out, int32_t* row_pos,
                   int64_t* row_slot, int32_t* row_ids, int32_t* status, void* stream);
 
-/* Sandwich-norm step: h_out = h_in + w_a * RMSNorm(y); x_out = w_b * RMSNorm(h_out) (bf16).  The decoder layer's
+/* Sandwich-norm step: h_out = h_in + w_a * RMSNorm(y); x_out = w_b * RMSNorm(h_out) (bf16).  y may arrive as
+ * y_parts split-K partials (y[p * m * hidden + t * hidden + f], summed in order p = 0, 1, ...).  The decoder layer's
  * post_self_attn / post_attention and post_mlp / next input_layernorm pairs (modeling_glm_ocr.py:281-302), and the
  * final model norm before lm_head. */
-int gr_residual_norm(int m, int hidden, const float* h_in, const float* y, const void* w_a, const void* w_b, float eps,
-                     float* h_out, void* x_out, void* stream);
+int gr_residual_norm(int m, int hidden, const float* h_in, const float* y, int y_parts, const void* w_a,
+                     const void* w_b, float eps, float* h_out, void* x_out, void* stream);
 
 /* Block-diffusion draft attention (draft = 1: row 0 causal, mask rows see the whole window) or causal verify /
  * prefill attention (draft = 0) over the paged cache.  q/out: bf16 [bs*K, n_q_heads, 128]; k_cache/v_cache: bf16

@@ -415,3 +415,27 @@ def test_attention_shared_workspace_across_batches():
         torch.cuda.synchronize()
         ref = _attn_ref(q, kc, vc, pt_d, seq_d, K, draft, base_add, nq, nkv)
         torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=1.5e-2)
+
+
+@pytest.mark.parametrize("n_out,k_in,m", [(1536, 2048, 17), (1536, 4608, 17), (1536, 4608, 1088), (1536, 2048, 300)])
+def test_linear_partials_summed_by_residual_norm(n_out, k_in, m):
+    """o_proj / down_proj write split-K partials; the residual norm sums them in split order."""
+    g = torch.Generator().manual_seed(m + k_in)
+    w, x = _rand((n_out, k_in), g, 0.02), _rand((m, k_in), g)
+    sp = L.linear_default_splits(n_out, k_in, m)
+    y = torch.full((sp, m, n_out), float("nan"), device=DEV)
+    e = L.Epilogue()
+    e.mode, e.out, e.ld_out = L.EPI_PARTIAL_F32, y.data_ptr(), n_out
+    L.linear(w, x, m, e, _ws(n_out, k_in, m, 1), splits=sp)
+    h = torch.randn((m, n_out), generator=g).to(DEV) * 0.1
+    wa, wb = _rand((n_out,), g, 0.02), _rand((n_out,), g, 0.02)
+    h2 = torch.zeros_like(h)
+    xo = torch.zeros((m, n_out), dtype=torch.bfloat16, device=DEV)
+    L.residual_norm(m, h, y, wa, wb, 1e-5, h2, xo, y_parts=sp)
+    torch.cuda.synchronize()
+    ref_y = x.float() @ w.float().T
+    torch.testing.assert_close(y.sum(0), ref_y, rtol=1e-3, atol=2e-4 * math.sqrt(k_in))
+    rms = lambda t, ww: ww.float() * (t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + 1e-5))
+    hr = h + rms(ref_y, wa)
+    torch.testing.assert_close(h2, hr, rtol=1e-3, atol=1e-5)
+    torch.testing.assert_close(xo.float(), rms(hr, wb), rtol=1e-2, atol=1e-4)
