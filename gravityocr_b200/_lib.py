@@ -23,7 +23,8 @@ ROWS_DRAFT, ROWS_VERIFY, ROWS_EXPLICIT = range(3)
 # every symbol include/gravity_b200.h declares
 EXPORTS = ("gr_version", "gr_status_string", "gr_set_pdl", "gr_num_sms", "gr_linear_workspace_bytes",
            "gr_attention_workspace_bytes", "gr_linear_default_splits", "gr_linear", "gr_embed_rows",
-           "gr_residual_norm", "gr_bd_attention", "gr_accept_commit", "gr_draft_override", "gr_pack_gate_up")
+           "gr_residual_norm", "gr_bd_attention", "gr_accept_commit", "gr_draft_override", "gr_pack_gate_up",
+           "gr_bd_attention_noalloc")
 
 
 class Epilogue(ctypes.Structure):
@@ -67,7 +68,10 @@ _SIGS = {
     "gr_accept_commit": (_I, [_I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "gr_draft_override": (_I, [_I, _I, _P, _P, _I, _P, _P, _I, _P, _I, _I, _P]),
     "gr_pack_gate_up": (_I, [_P, _P, _I, _I, _P]),
+    "gr_bd_attention_noalloc": (_I, [_P, _P, _P, _L, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
 }
+GR_ERR_SCRATCH_LIMIT = 8
+NOALLOC_SCRATCH_BYTES = 8 << 20
 
 
 def load(path: Optional[str] = None):
@@ -195,3 +199,15 @@ def pack_gate_up(src: torch.Tensor, dst: torch.Tensor, intermediate: int, stream
     _need(dst, torch.bfloat16, "dst")
     rc = load().gr_pack_gate_up(src.data_ptr(), dst.data_ptr(), intermediate, src.shape[1], _stream(stream))
     _check(rc, "gr_pack_gate_up")
+
+
+def bd_attention_noalloc(q, k_cache, v_cache, page_table, seq_lens, bs: int, K: int, draft: bool, base_add: int,
+                         n_q_heads: int, n_kv_heads: int, page_size: int, chunk: int, max_splits: int, out,
+                         status=None, stream=None) -> None:
+    """``bd_attention`` for callers that cannot allocate device memory: the split scratch is the library's own
+    fixed 8 MiB device array (see ``gr_bd_attention_noalloc`` in include/gravity_b200.h for the limits)."""
+    rc = load().gr_bd_attention_noalloc(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[0],
+                                        page_table.data_ptr(), page_table.shape[1], seq_lens.data_ptr(), bs, K,
+                                        1 if draft else 0, base_add, n_q_heads, n_kv_heads, page_size, chunk,
+                                        max_splits, out.data_ptr(), _ptr(status), _stream(stream))
+    _check(rc, "gr_bd_attention_noalloc")

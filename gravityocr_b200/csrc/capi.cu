@@ -156,6 +156,7 @@ const char* gr_status_string(int code) {
     case GR_ERR_BAD_ID: return "token id out of range";
     case GR_ERR_BAD_PAGE: return "position beyond page-table capacity";
     case GR_ERR_UNSUPPORTED: return "unsupported configuration";
+    case GR_ERR_SCRATCH_LIMIT: return "needs more scratch than the 8 MiB no-alloc array (use gr_bd_attention with a workspace)";
     default: return "unknown status";
   }
 }
@@ -420,3 +421,49 @@ int gr_pack_gate_up(const void* src, void* dst, int intermediate, int hidden, vo
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ attention without a caller workspace
+// The split scratch of gr_bd_attention_noalloc: one array per loaded device, zero at module load.  Host code may not use
+// the name as a device address; it asks the runtime for the address once per device (below).
+static __device__ __align__(256) uint8_t g_noalloc_attn_scratch[GR_NOALLOC_SCRATCH_BYTES];
+
+namespace gr {
+constexpr int kMaxDevices = 64;
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of this device's scratch array; looked up on the device's first call (with that device current).
+static int noalloc_scratch(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GR_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return GR_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> g(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_attn_scratch) != cudaSuccess || !p) return GR_ERR_CUDA;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return GR_OK;
+}
+}  // namespace gr
+
+extern "C" int gr_bd_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, int64_t n_pages,
+                                       const int32_t* page_table, int pt_stride, const int64_t* seq_lens, int bs, int K,
+                                       int draft, int base_add, int n_q_heads, int n_kv_heads, int page_size, int chunk,
+                                       int max_splits, void* out, int32_t* status, void* stream) {
+  if (bs <= 0 || K <= 0 || n_kv_heads <= 0 || max_splits <= 0) return GR_ERR_ARG;
+  const size_t need = gr_attention_workspace_bytes(bs, K, n_q_heads, n_kv_heads, max_splits);
+  if (need > GR_NOALLOC_SCRATCH_BYTES) return GR_ERR_SCRATCH_LIMIT;
+  void* ws = nullptr;
+  int rc = gr::noalloc_scratch(&ws);
+  if (rc) return rc;
+  // the array keeps whatever the last call left; the tickets this call counts on must start at zero
+  if (max_splits > 1 &&
+      cudaMemsetAsync(ws, 0, static_cast<size_t>(bs) * n_kv_heads * sizeof(int), static_cast<cudaStream_t>(stream)) !=
+          cudaSuccess)
+    return GR_ERR_CUDA;
+  return gr_bd_attention(q, k_cache, v_cache, n_pages, page_table, pt_stride, seq_lens, bs, K, draft, base_add,
+                         n_q_heads, n_kv_heads, page_size, chunk, max_splits, out, ws, GR_NOALLOC_SCRATCH_BYTES, status,
+                         stream);
+}

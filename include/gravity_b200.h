@@ -26,7 +26,8 @@ enum gr_status_code {
   GR_ERR_TIMEOUT = 4,     /* device: a bounded wait ran out (written to the status word) */
   GR_ERR_BAD_ID = 5,      /* device: a token id outside [0, vocab) */
   GR_ERR_BAD_PAGE = 6,    /* device: a position beyond the request's page-table capacity */
-  GR_ERR_UNSUPPORTED = 7  /* the build does not support this configuration */
+  GR_ERR_UNSUPPORTED = 7, /* the build does not support this configuration */
+  GR_ERR_SCRATCH_LIMIT = 8 /* the call needs more scratch than gr_bd_attention_noalloc's fixed array holds */
 };
 
 /* Epilogues of gr_linear. */
@@ -124,6 +125,22 @@ int gr_bd_attention(const void* q, const void* k_cache, const void* v_cache, int
                     int pt_stride, const int64_t* seq_lens, int bs, int K, int draft, int base_add, int n_q_heads,
                     int n_kv_heads, int page_size, int chunk, int max_splits, void* out, void* workspace,
                     size_t workspace_bytes, int32_t* status, void* stream);
+
+/* gr_bd_attention without a caller-provided workspace.  No counterpart in the reference: it exists for callers that
+ * cannot allocate device memory -- a host that owns the whole device-memory budget (a serving framework whose
+ * allocator accounts for every byte, so a private cudaMalloc would break its bookkeeping or fail under pressure), or
+ * code that issues the call while a CUDA stream is being captured, where cudaMalloc is not permitted.
+ * The split scratch lives in one file-scope __device__ array of GR_NOALLOC_SCRATCH_BYTES (8 MiB) that every GPU which
+ * loads the library keeps until the process exits.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current); make that first call before any stream capture.  Calls whose
+ * scratch (gr_attention_workspace_bytes of the same arguments) exceeds the array return GR_ERR_SCRATCH_LIMIT.  The call
+ * allocates nothing: it clears the tickets it uses with cudaMemsetAsync on `stream`, then runs the same kernel.  All
+ * calls share the array, so two calls that can overlap on the GPU (different streams, no ordering) race. */
+#define GR_NOALLOC_SCRATCH_BYTES (8u << 20)
+int gr_bd_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, int64_t n_pages,
+                            const int32_t* page_table, int pt_stride, const int64_t* seq_lens, int bs, int K, int draft,
+                            int base_add, int n_q_heads, int n_kv_heads, int page_size, int chunk, int max_splits,
+                            void* out, int32_t* status, void* stream);
 
 /* Accept and commit (one CTA): acc = leading d_j == v[j-1] matches (linear-chain greedy verify); packed[b] =
  * (a0, acc, v[0..acc], zeros); seeds[rpi[b]] = out_next[b] = v[acc]; seq_lens[b] += acc + 1 (+1 more when
