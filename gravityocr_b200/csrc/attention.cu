@@ -19,6 +19,9 @@ constexpr int kTile = 64;                       // tokens per pipeline stage
 constexpr int kHalfBytes = kTile * 128;         // 64 rows x 64 dims bf16
 constexpr int kStageBytes = 4 * kHalfBytes;     // K lo, K hi, V lo, V hi
 constexpr int kStages = 3;
+constexpr int kMaxChunkPages = 4096 / 16;  // chunk <= 4096 tokens
+constexpr int kMaxMergeSplits = 16;        // splits per (request, kv head); the host enforces it
+constexpr int kMinWarps = 8;               // extra warps idle in the main loop and help the split merge
 
 __device__ __forceinline__ int row_limit(const AttnParams& p, int j, int base) {
   if (p.draft) return j == 0 ? base + 1 : base + p.K;
@@ -39,6 +42,7 @@ __global__ void __launch_bounds__(288, 1) attention_kernel(const __grid_constant
   uint64_t* full = reinterpret_cast<uint64_t*>(q_smem + 2 * R_pad * 128);
   uint64_t* empty = full + kStages;
   int* flag = reinterpret_cast<int*>(empty + kStages);
+  int* pages = flag + 4;  // physical page ids of this split's cache range (chunk / page_size entries)
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -68,19 +72,23 @@ __global__ void __launch_bounds__(288, 1) attention_kernel(const __grid_constant
   const int* pt = p.page_table + (size_t)b * p.pt_stride;
   if (warp == n_mt) {
     // ------------------------------------------------------------ producer
+    // the whole split's page ids in one coalesced pass (pages past the request's last page hold no visible token:
+    // they are replaced by its last page, whose contents are finite)
+    const int last_page = (L - 1) / p.page_size;
+    const int pg_beg = kv_beg / p.page_size;
+    const int n_pg = n_tiles * (kTile / 16);
+    for (int i = lane; i < n_pg; i += 32) pages[i] = pt[min(pg_beg + i, last_page)];
+    __syncwarp();
     if (lane == 0) {
-      const int last_page = (L - 1) / p.page_size;
       int issued = 0;
       for (int i = 0; i < n_tiles; ++i) {
         const int s = i % kStages;
         if (i >= kStages && !mbar_wait(empty + s, ((i / kStages) - 1) & 1, p.status, GR_ERR_TIMEOUT)) break;
         mbar_arrive_expect_tx(full + s, kStageBytes);
         uint8_t* st = kv_smem + s * kStageBytes;
-        const int page0 = (kv_beg + i * kTile) / p.page_size;
 #pragma unroll
         for (int pg = 0; pg < 4; ++pg) {
-          const int lp = page0 + pg;
-          const int phys = pt[min(lp, last_page)];  // pages past the request's last hold no visible token
+          const int phys = pages[i * 4 + pg];
           const int y = (phys * p.n_kv_heads + kvh) * p.page_size;
           tma_load_2d(st + 0 * kHalfBytes + pg * 2048, &tmk, full + s, 0, y);
           tma_load_2d(st + 1 * kHalfBytes + pg * 2048, &tmk, full + s, 64, y);
@@ -92,7 +100,7 @@ __global__ void __launch_bounds__(288, 1) attention_kernel(const __grid_constant
       for (int i = max(0, issued - kStages); i < issued; ++i)
         mbar_wait(full + (i % kStages), (i / kStages) & 1, p.status, GR_ERR_TIMEOUT);
     }
-  } else {
+  } else if (warp < n_mt) {
     // ------------------------------------------------------------ compute warps
     // stage this warp's 16 query rows into shared memory (128-byte swizzle, two 64-dim halves)
     const size_t q_row_stride = (size_t)p.n_q_heads * 128;
@@ -274,40 +282,66 @@ __global__ void __launch_bounds__(288, 1) attention_kernel(const __grid_constant
   __threadfence();
   const size_t slot0 = ((size_t)b * p.n_kv_heads + kvh) * p.max_splits;
   const size_t q_row_stride = (size_t)p.n_q_heads * 128;
-  // one warp per row; lane l owns dims 4l..4l+3; splits merged in split order
-  const int n_warps = blockDim.x >> 5;
-  for (int r = warp; r < R; r += n_warps) {
+  // phase A: per (row, split) weights exp2(m_s - M) / L into shared memory (the stage ring is idle now)
+  float* wgt = reinterpret_cast<float*>(kv_smem);  // [R][kMaxMergeSplits]
+  for (int r = threadIdx.x; r < R; r += blockDim.x) {
     float M = -INFINITY;
-    for (int s = lane; s < n_active; s += 32) M = fmaxf(M, __ldcg(p.ws_ml + ((slot0 + s) * R_pad + r) * 2));
+    float ms[kMaxMergeSplits], ls[kMaxMergeSplits];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    for (int s = 0; s < kMaxMergeSplits; ++s) {
+      if (s < n_active) {
+        const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + ((slot0 + s) * R_pad + r) * 2));
+        ms[s] = ml.x;
+        ls[s] = ml.y;
+        M = fmaxf(M, ml.x);
+      }
+    }
     const float Ms = (M == -INFINITY) ? 0.f : M;
     float Lsum = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-    for (int s = 0; s < n_active; ++s) {
-      const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + ((slot0 + s) * R_pad + r) * 2));
-      const float4 os = __ldcg(reinterpret_cast<const float4*>(p.ws_o + ((slot0 + s) * R_pad + r) * 128) + lane);
-      const float w = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - Ms);
-      Lsum += ml.y * w;
-      acc.x += os.x * w;
-      acc.y += os.y * w;
-      acc.z += os.z * w;
-      acc.w += os.w * w;
+#pragma unroll
+    for (int s = 0; s < kMaxMergeSplits; ++s) {
+      if (s < n_active) {
+        const float w = (ms[s] == -INFINITY) ? 0.f : exp2f(ms[s] - Ms);
+        ms[s] = w;
+        Lsum += ls[s] * w;
+      }
     }
     const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+#pragma unroll
+    for (int s = 0; s < kMaxMergeSplits; ++s)
+      if (s < n_active) wgt[r * kMaxMergeSplits + s] = ms[s] * inv;
+  }
+  __syncthreads();
+  // phase B: (row, 4 dims) items; every split's loads of an item are issued together, summed in split order
+  for (int it = threadIdx.x; it < R * 32; it += blockDim.x) {
+    const int r = it >> 5, q4 = it & 31;
+    float4 os[kMaxMergeSplits];
+#pragma unroll
+    for (int s = 0; s < kMaxMergeSplits; ++s)
+      if (s < n_active) os[s] = __ldcg(reinterpret_cast<const float4*>(p.ws_o + ((slot0 + s) * R_pad + r) * 128) + q4);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int s = 0; s < kMaxMergeSplits; ++s) {
+      if (s < n_active) {
+        const float w = wgt[r * kMaxMergeSplits + s];
+        acc.x += os[s].x * w;
+        acc.y += os[s].y * w;
+        acc.z += os[s].z * w;
+        acc.w += os[s].w * w;
+      }
+    }
     const int g = r / p.K, j = r % p.K;
-    __nv_bfloat16* dst = p.out + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128 + lane * 4;
+    __nv_bfloat16* dst = p.out + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128 + q4 * 4;
     uint2 pk;
-    pk.x = pack_bf16(acc.x * inv, acc.y * inv);
-    pk.y = pack_bf16(acc.z * inv, acc.w * inv);
+    pk.x = pack_bf16(acc.x, acc.y);
+    pk.y = pack_bf16(acc.z, acc.w);
     *reinterpret_cast<uint2*>(dst) = pk;
   }
 }
 
 size_t attention_smem_bytes(int K, int G) {
   const int R_pad = ((G * K + 15) / 16) * 16;
-  return 1024 + kStages * kStageBytes + 2 * R_pad * 128 + 2 * kStages * 8 + 16;
+  return 1024 + kStages * kStageBytes + 2 * R_pad * 128 + 2 * kStages * 8 + 16 + kMaxChunkPages * 4;
 }
 
 cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p,
@@ -322,7 +356,9 @@ cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, con
   const int n_mt = (G * p.K + 15) / 16;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.max_splits, p.n_kv_heads, p.bs);
-  cfg.blockDim = dim3(32 * (n_mt + 1));
+  // idle extra warps help the split merge; unsplit launches keep small CTAs (register-limited occupancy)
+  const int warps = (p.max_splits > 1 && n_mt + 1 < kMinWarps) ? kMinWarps : n_mt + 1;
+  cfg.blockDim = dim3(32 * warps);
   cfg.dynamicSmemBytes = attention_smem_bytes(p.K, G);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];

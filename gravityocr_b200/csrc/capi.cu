@@ -81,7 +81,7 @@ struct LinearShape {
 };
 static LinearShape linear_shape(int n_out, int k_in, int m) {
   LinearShape s;
-  s.m_tiles = (m + 255) / 256;
+  s.m_tiles = (m + GR_MAX_NT - 1) / GR_MAX_NT;
   const int per = (m + s.m_tiles - 1) / s.m_tiles;
   s.nt = ((per + 15) / 16) * 16;
   if (s.nt < 16) s.nt = 16;
@@ -90,19 +90,42 @@ static LinearShape linear_shape(int n_out, int k_in, int m) {
   return s;
 }
 
-static int default_splits(const LinearShape& s, int epi) {
-  const int units = s.n_tiles * s.m_tiles;
-  const int target = (num_sms() * 9) / 10;
-  if (units >= target || epi == GR_EPI_ARGMAX) return 1;
-  for (int sp = 2; sp <= s.kc; ++sp) {
-    if (s.kc % sp) continue;
-    if (s.kc / sp < 2) break;
-    if (units * sp >= target) return sp;
-  }
-  // largest divisor keeping >= 2 chunks per split
+static int acc_cols_for(int nt) { return nt <= 32 ? 32 : (nt <= 64 ? 64 : (nt <= 128 ? 128 : 256)); }
+
+// Pipeline depth and resident CTAs of the persistent projection kernel for a token tile of nt rows.
+static void linear_launch_shape(int nt, int kc, int* stages, int* ctas_per_sm) {
+  int st = GR_MAX_STAGES;
+  while (st > 2 && linear_smem_bytes(nt, st) > 220 * 1024) --st;
+  if (st > kc) st = kc < 2 ? 2 : kc;
+  while (st > 1 && linear_smem_bytes(nt, st) > 220 * 1024) --st;
+  const int by_smem = static_cast<int>(233472 / (linear_smem_bytes(nt, st) + 1024));
+  const int by_tmem = 512 / (2 * acc_cols_for(nt));
+  *stages = st;
+  *ctas_per_sm = by_smem < by_tmem ? (by_smem < 1 ? 1 : by_smem) : by_tmem;
+}
+
+// Split-K count for the persistent schedule: minimise (units per CTA, rounded up) x (K chunks per unit); ties go to
+// fewer splits (less partial traffic).  The argmax epilogue runs unsplit.
+static int default_splits(const LinearShape& s, int epi, int m) {
+  if (epi == GR_EPI_ARGMAX) return 1;
+  int stages, per_sm;
+  linear_launch_shape(s.nt, s.kc, &stages, &per_sm);
+  const long long cap = static_cast<long long>(num_sms()) * per_sm;
+  const long long units = static_cast<long long>(s.n_tiles) * s.m_tiles;
+  if (units >= cap) return 1;  // the grid is already full: split partials would only add traffic
   int best = 1;
-  for (int sp = 2; sp <= s.kc / 2; ++sp)
-    if (s.kc % sp == 0) best = sp;
+  long long best_cost = ((units + cap - 1) / cap) * s.kc;
+  for (int sp = 2; sp <= s.kc / 2; ++sp) {
+    if (s.kc % sp) continue;
+    const long long u = units * sp;
+    // fp32 partials (s x m x n_out) must stay a small, L2-resident fraction of the traffic
+    if (static_cast<double>(sp) * m * s.n_tiles * 128 * 4 > 32.0 * (1 << 20)) break;
+    const long long cost = ((u + cap - 1) / cap) * (s.kc / sp);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = sp;
+    }
+  }
   return best;
 }
 
@@ -166,7 +189,7 @@ int gr_num_sms(void) { return num_sms(); }
 
 int gr_linear_default_splits(int n_out, int k_in, int m) {
   if (n_out <= 0 || k_in <= 0 || m <= 0) return 1;
-  return default_splits(linear_shape(n_out, k_in, m), GR_EPI_STORE_F32);
+  return default_splits(linear_shape(n_out, k_in, m), GR_EPI_STORE_F32, m);
 }
 
 size_t gr_linear_workspace_bytes(int n_out, int m, int splits) {
@@ -182,7 +205,7 @@ int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr
   if (!w || !x || !epi || m <= 0 || n_out <= 0 || (n_out % 128) || k_in <= 0 || (k_in % 64)) return GR_ERR_ARG;
   if (epi->mode < GR_EPI_STORE_F32 || epi->mode > GR_EPI_PARTIAL_F32) return GR_ERR_ARG;
   LinearShape s = linear_shape(n_out, k_in, m);
-  if (splits <= 0) splits = default_splits(s, epi->mode);
+  if (splits <= 0) splits = default_splits(s, epi->mode, m);
   if (s.kc % splits) return GR_ERR_ARG;
   const size_t ws_splits = epi->mode == GR_EPI_PARTIAL_F32 ? 1 : static_cast<size_t>(splits);
   const int kc = s.kc / splits;
@@ -193,19 +216,19 @@ int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr
   if (epi->mode == GR_EPI_QKV_ROPE) {
     if (!epi->q_out || !epi->k_cache || !epi->v_cache || !epi->row_pos || !epi->row_slot || !epi->inv_freq ||
         epi->rotary_dim % 32 || epi->rotary_dim > 128 || n_out != (epi->n_q_heads + 2 * epi->n_kv_heads) * 128 ||
-        epi->page_size <= 0)
+        epi->page_size != 16)
       return GR_ERR_ARG;
   } else if (epi->mode == GR_EPI_ARGMAX) {
     if (!epi->out_idx) return GR_ERR_ARG;
   } else if (!epi->out || epi->ld_out <= 0) {
     return GR_ERR_ARG;
   }
-  // stages: deep enough to cover latency; keep two CTAs per SM when the grid has more units than SMs
+  // persistent grid: every resident CTA walks units c, c + grid, ...
   const int units = s.n_tiles * s.m_tiles * splits;
-  int stages = kc < 6 ? kc : 6;
-  while (stages > 1 && linear_smem_bytes(s.nt, stages) > 220 * 1024) --stages;
-  if (units > num_sms())
-    while (stages > 2 && linear_smem_bytes(s.nt, stages) > 112 * 1024) --stages;
+  int stages, per_sm;
+  linear_launch_shape(s.nt, kc, &stages, &per_sm);
+  const int cap = num_sms() * per_sm;
+  const int grid = units < cap ? units : cap;
   CUtensorMap tmw, tmx;
   int rc = tensor_map_2d(w, static_cast<uint64_t>(n_out), static_cast<uint64_t>(k_in), 128, 64, &tmw);
   if (rc) return rc;
@@ -244,7 +267,8 @@ int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr
   p.prefetch = static_cast<const uint8_t*>(prefetch);
   p.prefetch_bytes = prefetch ? prefetch_bytes : 0;
   p.status = status;
-  cudaError_t e = launch_linear(epi->mode, tmw, tmx, p, units, linear_smem_bytes(s.nt, stages),
+  p.rope_cs = reinterpret_cast<const float2*>(epi->rope_cs);
+  cudaError_t e = launch_linear(epi->mode, tmw, tmx, p, grid, linear_smem_bytes(s.nt, stages),
                                 static_cast<cudaStream_t>(stream), g_pdl);
   return e == cudaSuccess ? GR_OK : GR_ERR_CUDA;
 }
@@ -263,10 +287,12 @@ int gr_bd_attention(const void* q, const void* k_cache, const void* v_cache, int
                     size_t workspace_bytes, int32_t* status, void* stream) {
   if (!q || !k_cache || !v_cache || !page_table || !seq_lens || !out || bs <= 0 || K <= 0 || n_pages <= 0)
     return GR_ERR_ARG;
-  if (n_kv_heads <= 0 || n_q_heads % n_kv_heads || page_size != 16 || chunk <= 0 || chunk % 64 || max_splits <= 0)
+  if (n_kv_heads <= 0 || n_q_heads % n_kv_heads || page_size != 16 || chunk <= 0 || chunk % 64 || chunk > 4096 ||
+      max_splits <= 0)
     return GR_ERR_ARG;
   const int G = n_q_heads / n_kv_heads;
   if (G * K > 128 || static_cast<size_t>(bs) * n_kv_heads * sizeof(int) > kAttnTicketBytes) return GR_ERR_UNSUPPORTED;
+  if (max_splits > 16) return GR_ERR_ARG;  // the split merge handles up to 16 splits per (request, kv head)
   const size_t need = gr_attention_workspace_bytes(bs, K, n_q_heads, n_kv_heads, max_splits);
   if (max_splits > 1 && (!workspace || workspace_bytes < need)) return GR_ERR_ARG;
   const uint64_t rows = static_cast<uint64_t>(n_pages) * n_kv_heads * page_size;
@@ -311,7 +337,8 @@ int gr_embed_rows(int mode, int bs, int K, const int64_t* seeds, const int64_t* 
                   const int64_t* ids64, const float* row_embeds, const int64_t* seq_lens, const int32_t* page_table,
                   int pt_stride, int page_size, int pages_per_req, const void* embed, int vocab, int mask_id,
                   const void* norm_w, float eps, int hidden, float* h_out, void* x_out, int32_t* row_pos,
-                  int64_t* row_slot, int32_t* row_ids, int32_t* status, void* stream) {
+                  int64_t* row_slot, int32_t* row_ids, const float* inv_freq, int rotary_dim, float* rope_cs,
+                  int32_t* status, void* stream) {
   if (bs <= 0 || K <= 0 || !seq_lens || !page_table || !embed || !norm_w || !h_out || !x_out || !row_pos || !row_slot)
     return GR_ERR_ARG;
   if (hidden <= 0 || hidden % 8 || page_size <= 0 || pages_per_req <= 0) return GR_ERR_ARG;
@@ -319,6 +346,7 @@ int gr_embed_rows(int mode, int bs, int K, const int64_t* seeds, const int64_t* 
   if (mode == GR_ROWS_VERIFY && !ids32) return GR_ERR_ARG;
   if (mode == GR_ROWS_EXPLICIT && !ids64) return GR_ERR_ARG;
   if (mode < GR_ROWS_DRAFT || mode > GR_ROWS_EXPLICIT) return GR_ERR_ARG;
+  if (rope_cs && (!inv_freq || rotary_dim <= 0 || rotary_dim % 2 || rotary_dim / 2 > 192)) return GR_ERR_ARG;
   EmbedParams p;
   std::memset(&p, 0, sizeof(p));
   p.mode = mode;
@@ -346,6 +374,9 @@ int gr_embed_rows(int mode, int bs, int K, const int64_t* seeds, const int64_t* 
   p.row_slot = row_slot;
   p.row_ids = row_ids;
   p.status = status;
+  p.inv_freq = inv_freq;
+  p.rotary_dim = rotary_dim;
+  p.rope_cs = reinterpret_cast<float2*>(rope_cs);
   return launch_embed_rows(p, static_cast<cudaStream_t>(stream), g_pdl) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
 }
 

@@ -15,6 +15,16 @@
 #ifndef GR_WAIT_NS
 #define GR_WAIT_NS 2000000000ull  // 2 s
 #endif
+// Tuning knobs of the projection kernel (compile-time; the defaults are the measured best).
+#ifndef GR_W_EVICT_FIRST
+#define GR_W_EVICT_FIRST 1  // weight tiles loaded with an L2 evict-first hint
+#endif
+#ifndef GR_MAX_STAGES
+#define GR_MAX_STAGES 8     // deepest TMA ring
+#endif
+#ifndef GR_MAX_NT
+#define GR_MAX_NT 256       // widest token tile (MMA N)
+#endif
 
 namespace gr {
 

@@ -21,10 +21,14 @@
 
 namespace gr {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue (two per TMEM lane quadrant)
 constexpr uint32_t kWStageBytes = 128 * 128;  // 128 rows x 64 bf16
+constexpr uint32_t kEpiScratchBytes = 16384;  // argmax transpose: two halves x [16 tokens][128 rows] fp32
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// all 8 epilogue warps
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// the 4 epilogue warps of one column half (one warp per TMEM lane quadrant)
+__device__ __forceinline__ void half_bar(int half) { asm volatile("bar.sync %0, 128;" ::"r"(2 + half) : "memory"); }
 
 struct Top2 {
   float v1;
@@ -78,24 +82,19 @@ __device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, in
       }
     }
   } else if constexpr (EPI == GR_EPI_SWIGLU) {
-    // rows 0..63 of the tile are gate features 64*n_tile + j, rows 64..127 the matching up features
-    if (f_local >= 64) {
+    // rows 2j / 2j+1 of the tile are gate / up of feature 64*n_tile + j (gr_pack_gate_up): the pair sits in adjacent
+    // lanes, so one shuffle brings the up value to the gate lane
+    const int f = n_tile * 64 + (f_local >> 1);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) scratch[i * 64 + (f_local - 64)] = v[i];
-    }
-    epi_bar();
-    if (f_local < 64) {
-      const int f = n_tile * 64 + f_local;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int t = t0 + i;
+    for (int i = 0; i < 16; ++i) {
+      const float u = __shfl_xor_sync(0xffffffffu, v[i], 1);
+      const int t = t0 + i;
+      if (!(lane & 1) && t < t_end) {
         const float g = v[i];
-        const float u = scratch[i * 64 + f_local];
-        const float a = u * (g / (1.0f + expf(-g)));
-        if (t < t_end) static_cast<__nv_bfloat16*>(p.out)[(size_t)t * p.ld_out + f] = __float2bfloat16_rn(a);
+        const float a = u * __fdividef(g, 1.0f + __expf(-g));
+        static_cast<__nv_bfloat16*>(p.out)[(size_t)t * p.ld_out + f] = __float2bfloat16_rn(a);
       }
     }
-    epi_bar();
   } else if constexpr (EPI == GR_EPI_QKV_ROPE) {
     // tile = one head: [0, nq) query heads, [nq, nq+nkv) key heads, then value heads; f_local = head dim
     const int head = n_tile;
@@ -105,14 +104,19 @@ __device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, in
     const bool rot = !is_v && (d & ~31) < p.rotary_dim;  // warp-uniform: rotary_dim is a multiple of 32
     float o[16];
     if (rot) {
-      const float fr = p.inv_freq[d >> 1];
+      const int half = p.rotary_dim >> 1;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const float partner = __shfl_xor_sync(0xffffffffu, v[i], 1);
         const int t = min(t0 + i, t_end - 1);
-        const float ang = static_cast<float>(p.row_pos[t]) * fr;
         float s, c;
-        sincosf(ang, &s, &c);
+        if (p.rope_cs) {
+          const float2 cs = p.rope_cs[(size_t)t * half + (d >> 1)];
+          c = cs.x;
+          s = cs.y;
+        } else {
+          sincosf(static_cast<float>(p.row_pos[t]) * p.inv_freq[d >> 1], &s, &c);
+        }
         o[i] = (d & 1) ? (v[i] * c + partner * s) : (v[i] * c - partner * s);
       }
     } else {
@@ -127,38 +131,42 @@ __device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, in
       if (is_q) {
         p.q_out[(size_t)t * (p.n_q_heads * 128) + head * 128 + d] = b;
       } else {
+        // page size 16 (the host checks): page = slot >> 4, offset = slot & 15
         const int kvh = is_v ? head - p.n_q_heads - p.n_kv_heads : head - p.n_q_heads;
-        const int64_t slot = p.row_slot[t];
-        const int64_t page = slot / p.page_size, off = slot % p.page_size;
-        const size_t idx = (((size_t)page * p.n_kv_heads + kvh) * p.page_size + off) * 128 + d;
+        const uint64_t slot = static_cast<uint64_t>(p.row_slot[t]);
+        const size_t idx = ((((slot >> 4) * p.n_kv_heads + kvh) << 4) + (slot & 15)) * 128 + d;
         (is_v ? p.v_cache : p.k_cache)[idx] = b;
       }
     }
   } else if constexpr (EPI == GR_EPI_ARGMAX) {
-    const int warp = (threadIdx.x >> 5) - 2;
-    const int f = n_tile * 128 + f_local;
-    Top2* sm = reinterpret_cast<Top2*>(scratch);  // [4 warps][16 tokens]
+    // transpose through shared memory: [16 tokens][128 vocab rows]; then 8 threads per token scan 16 rows each and
+    // merge with 3 shuffle rounds (ties: lowest vocab index)
+    const int half = (((threadIdx.x >> 5) - 2) >> 2);
+    const int tid = threadIdx.x & 127;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      Top2 x{v[i], f, -INFINITY};
-      x = top2_warp(x);
-      if (lane == 0) sm[warp * 16 + i] = x;
-    }
-    epi_bar();
-    if (threadIdx.x < 64 + 16) {
-      const int i = threadIdx.x - 64;
-      Top2 x = sm[i];
+    for (int i = 0; i < 16; ++i) scratch[i * 128 + f_local] = v[i];
+    half_bar(half);
+    const int tok = tid >> 3, part = tid & 7;
+    const float* row = scratch + tok * 128 + part * 16;
+    Top2 x{-INFINITY, 0x7fffffff, -INFINITY};
 #pragma unroll
-      for (int w = 1; w < 4; ++w) x = top2_merge(x, sm[w * 16 + i]);
-      const int t = t0 + i;
-      if (t < t_end) {
-        float* dst = p.ws_arg + ((size_t)n_tile * p.m + t) * 3;
-        dst[0] = x.v1;
-        dst[1] = __int_as_float(x.i1);
-        dst[2] = x.v2;
-      }
+    for (int j = 0; j < 16; ++j) x = top2_merge(x, Top2{row[j], n_tile * 128 + part * 16 + j, -INFINITY});
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+      Top2 y;
+      y.v1 = __shfl_xor_sync(0xffffffffu, x.v1, o);
+      y.i1 = __shfl_xor_sync(0xffffffffu, x.i1, o);
+      y.v2 = __shfl_xor_sync(0xffffffffu, x.v2, o);
+      x = top2_merge(x, y);
     }
-    epi_bar();
+    const int t = t0 + tok;
+    if (part == 0 && t < t_end) {
+      float* dst = p.ws_arg + ((size_t)n_tile * p.m + t) * 3;
+      dst[0] = x.v1;
+      dst[1] = __int_as_float(x.i1);
+      dst[2] = x.v2;
+    }
+    half_bar(half);
   }
 }
 
@@ -175,7 +183,7 @@ __device__ void argmax_finish(const LinearParams& p, int m_tile, int* flag) {
   __threadfence();
   const int warp = (threadIdx.x >> 5) - 2, lane = threadIdx.x & 31;
   const int t_beg = m_tile * p.nt, t_end = min(p.m, t_beg + p.nt);
-  for (int t = t_beg + warp; t < t_end; t += 4) {
+  for (int t = t_beg + warp; t < t_end; t += 8) {
     Top2 x{-INFINITY, 0x7fffffff, -INFINITY};
     for (int n = lane; n < p.n_tiles; n += 32) {
       const float* s = p.ws_arg + ((size_t)n * p.m + t) * 3;
@@ -196,33 +204,39 @@ template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
                   const LinearParams p) {
+  // Persistent: CTA c processes units c, c + gridDim.x, ...  The producer and the MMA issuer walk the same global
+  // sequence of (unit, K chunk) through one S-stage ring, so the next unit's weights stream while the current unit's
+  // epilogue runs; the accumulator is double-buffered in TMEM (acc_full / acc_empty per buffer).
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = p.stages;
   const uint32_t x_stage_bytes = static_cast<uint32_t>(p.nt) * 128u;
   uint8_t* w_smem = smem;
   uint8_t* x_smem = smem + S * kWStageBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(x_smem + S * x_stage_bytes);
+  float* scratch = reinterpret_cast<float*>(x_smem + S * x_stage_bytes);  // epilogue exchange, kEpiScratchBytes
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(scratch) + kEpiScratchBytes);
   uint64_t* empty = full + S;
-  uint64_t* accum = empty + S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
-  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] abort, [1] last-split, [2] last-argmax
+  uint64_t* acc_full = empty + S;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] abort, [1] last split, [2] last argmax tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int u = blockIdx.x;
-  const int m_tile = u % p.m_tiles;
-  u /= p.m_tiles;
-  const int split = u % p.splits;
-  const int n_tile = u / p.splits;
-  const int kc = p.kc_per_split, kc0 = split * kc;
-  const uint32_t tmem_cols = p.nt <= 32 ? 32u : (p.nt <= 64 ? 64u : (p.nt <= 128 ? 128u : 256u));
+  const int kc = p.kc_per_split;
+  const int n_units = p.n_tiles * p.m_tiles * p.splits;
+  const int n_my = blockIdx.x < n_units ? (n_units - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  const uint32_t acc_cols = p.nt <= 32 ? 32u : (p.nt <= 64 ? 64u : (p.nt <= 128 ? 128u : 256u));
+  const uint32_t tmem_cols = 2 * acc_cols;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full + b, 1);
+      mbar_init(acc_empty + b, 8);  // one arrival per epilogue warp
+    }
     flags[0] = flags[1] = flags[2] = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmw);
@@ -241,117 +255,162 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (threadIdx.x == 0) pdl_trigger();
+  pdl_trigger();
+
+  // unit u -> (m_tile fastest, then split, then n_tile): the token tiles of one weight slab run side by side (L2 reuse)
+  auto decode = [&](int u, int& m_tile, int& split, int& n_tile) {
+    m_tile = u % p.m_tiles;
+    u /= p.m_tiles;
+    split = u % p.splits;
+    n_tile = u / p.splits;
+  };
 
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
-      const int pre = min(S, kc);
-      for (int c = 0; c < pre; ++c) {
-        mbar_arrive_expect_tx(full + c, kWStageBytes + x_stage_bytes);
-        tma_load_2d_hint(w_smem + c * kWStageBytes, &tmw, full + c, (kc0 + c) * 64, n_tile * 128, pol);
+      const int total = n_my * kc;
+      auto issue = [&](int g, bool w_part, bool x_part) {
+        const int s = g % S;
+        const int k = g / kc, c = g % kc;
+        int m_tile, split, n_tile;
+        decode(blockIdx.x + k * gridDim.x, m_tile, split, n_tile);
+        const int xk = (split * kc + c) * 64;
+        if (w_part) {
+          if (GR_W_EVICT_FIRST)
+            tma_load_2d_hint(w_smem + s * kWStageBytes, &tmw, full + s, xk, n_tile * 128, pol);
+          else
+            tma_load_2d(w_smem + s * kWStageBytes, &tmw, full + s, xk, n_tile * 128);
+        }
+        if (x_part) tma_load_2d(x_smem + s * x_stage_bytes, &tmx, full + s, xk, m_tile * p.nt);
+      };
+      // weights do not depend on the previous kernel: the first S stages' weight tiles go out before the wait
+      const int pre = min(S, total);
+      for (int g = 0; g < pre; ++g) {
+        mbar_arrive_expect_tx(full + g, kWStageBytes + x_stage_bytes);
+        issue(g, true, false);
       }
       pdl_wait();
-      for (int c = 0; c < pre; ++c)
-        tma_load_2d(x_smem + c * x_stage_bytes, &tmx, full + c, (kc0 + c) * 64, m_tile * p.nt);
+      for (int g = 0; g < pre; ++g) issue(g, false, true);
       int issued = pre;
-      for (int c = pre; c < kc; ++c) {
-        const int s = c % S;
-        if (!mbar_wait(empty + s, ((c / S) - 1) & 1, p.status, GR_ERR_TIMEOUT)) {
+      for (int g = pre; g < total; ++g) {
+        const int s = g % S;
+        if (!mbar_wait(empty + s, ((g / S) - 1) & 1, p.status, GR_ERR_TIMEOUT)) {
           flags[0] = 1;
           break;
         }
         mbar_arrive_expect_tx(full + s, kWStageBytes + x_stage_bytes);
-        tma_load_2d_hint(w_smem + s * kWStageBytes, &tmw, full + s, (kc0 + c) * 64, n_tile * 128, pol);
-        tma_load_2d(x_smem + s * x_stage_bytes, &tmx, full + s, (kc0 + c) * 64, m_tile * p.nt);
-        issued = c + 1;
+        issue(g, true, true);
+        issued = g + 1;
       }
       // no copy may still be landing in shared memory when the CTA exits
-      for (int c = max(0, issued - S); c < issued; ++c) mbar_wait(full + (c % S), (c / S) & 1, p.status, GR_ERR_TIMEOUT);
+      for (int g = max(0, issued - S); g < issued; ++g) mbar_wait(full + (g % S), (g / S) & 1, p.status, GR_ERR_TIMEOUT);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(128, p.nt);
-      for (int c = 0; c < kc; ++c) {
-        const int s = c % S;
-        if (!mbar_wait(full + s, (c / S) & 1, p.status, GR_ERR_TIMEOUT)) {
+      int g = 0;
+      bool ok = true;
+      for (int k = 0; k < n_my && ok; ++k) {
+        const int b = k & 1;
+        if (k >= 2 && !mbar_wait(acc_empty + b, ((k >> 1) - 1) & 1, p.status, GR_ERR_TIMEOUT)) {
           flags[0] = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t wa = smem_u32(w_smem + s * kWStageBytes);
-        const uint32_t xa = smem_u32(x_smem + s * x_stage_bytes);
+        const uint32_t acc = tmem + b * acc_cols;
+        for (int c = 0; c < kc; ++c, ++g) {
+          const int s = g % S;
+          if (!mbar_wait(full + s, (g / S) & 1, p.status, GR_ERR_TIMEOUT)) {
+            flags[0] = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t wa = smem_u32(w_smem + s * kWStageBytes);
+          const uint32_t xa = smem_u32(x_smem + s * x_stage_bytes);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          tc_mma_bf16(tmem, smem_desc_sw128(wa + kk * 32), smem_desc_sw128(xa + kk * 32), idesc, (c | kk) != 0);
-        tc_commit(empty + s);
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_bf16(acc, smem_desc_sw128(wa + kk * 32), smem_desc_sw128(xa + kk * 32), idesc, (c | kk) != 0);
+          tc_commit(empty + s);
+        }
+        tc_commit(acc_full + b);
       }
-      tc_commit(accum);
     }
   } else {
-    // ---------------------------------------------------------------- epilogue warps 2..5
+    // ---------------------------------------------------------------- epilogue warps 2..9
+    // warp w reads TMEM lanes 32*(w%4).. (its quadrant); the two warps of a quadrant take alternate 16-token chunks
     pdl_wait();
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int f_local = quad * 32 + lane;
-    const bool ok = mbar_wait(accum, 0, p.status, GR_ERR_TIMEOUT);
-    tc_fence_after();
-    float* scratch = reinterpret_cast<float*>(w_smem);  // the stage ring is idle once the accumulator is final
-    const uint32_t t_lane = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    const int t_beg = m_tile * p.nt;
-    const int rows = min(p.nt, p.m - t_beg);
-    bool run = ok && !flags[0];
-    epi_bar();
-    run = run && !flags[0];
-    if (p.splits == 1 || EPI == GR_EPI_PARTIAL_F32) {
-      if (run) {
-        for (int c0 = 0; c0 < p.nt; c0 += 16) {
-          float v[16];
-          tmem_ld16(t_lane + c0, v);
-          epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, scratch, split);
-        }
-      }
-    } else {
-      const int tile = n_tile * p.m_tiles + m_tile;
-      float* part = p.ws_partial + ((size_t)tile * p.splits + split) * p.nt * 128;
-      if (run) {
-        for (int c0 = 0; c0 < p.nt; c0 += 16) {
-          float v[16];
-          tmem_ld16(t_lane + c0, v);
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            if (c0 + i < rows) part[(c0 + i) * 128 + f_local] = v[i];
-        }
-      }
-      __threadfence();
+    float* my_scratch = scratch + half * 2048;
+    for (int k = 0; k < n_my; ++k) {
+      const int b = k & 1;
+      int m_tile, split, n_tile;
+      decode(blockIdx.x + k * gridDim.x, m_tile, split, n_tile);
+      const bool ok = mbar_wait(acc_full + b, (k >> 1) & 1, p.status, GR_ERR_TIMEOUT);
+      tc_fence_after();
+      const uint32_t t_lane = tmem + b * acc_cols + (static_cast<uint32_t>(quad * 32) << 16);
+      const int t_beg = m_tile * p.nt;
+      const int rows = min(p.nt, p.m - t_beg);
       epi_bar();
-      if (threadIdx.x == 64) {
-        const int prev = atomicAdd(&p.ws_ticket[tile], 1);
-        flags[1] = (prev == p.splits - 1);
-      }
-      epi_bar();
-      if (flags[1]) {
-        __threadfence();
-        const float* base = p.ws_partial + (size_t)tile * p.splits * p.nt * 128;
-        for (int c0 = 0; c0 < p.nt; c0 += 16) {
-          // split order is fixed (deterministic sums); the 16 rows' loads of one split are independent
-          float v[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = 0.f;
-          for (int s = 0; s < p.splits; ++s) {
-            const float* src = base + ((size_t)s * p.nt + c0) * 128 + f_local;
-            float x[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) x[i] = (c0 + i < rows) ? __ldcg(src + i * 128) : 0.f;
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] += x[i];
+      const bool run = ok && !flags[0];
+      if (p.splits == 1 || EPI == GR_EPI_PARTIAL_F32) {
+        if (run) {
+          for (int c0 = half * 16; c0 < p.nt; c0 += 32) {
+            float v[16];
+            tmem_ld16(t_lane + c0, v);
+            epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, my_scratch, split);
           }
-          epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, scratch, split);
         }
-        if (threadIdx.x == 64) p.ws_ticket[tile] = 0;
+        tc_fence_before();
+        if (lane == 0) mbar_arrive(acc_empty + b);
+      } else {
+        const int tile = n_tile * p.m_tiles + m_tile;
+        float* part = p.ws_partial + ((size_t)tile * p.splits + split) * p.nt * 128;
+        if (run) {
+          for (int c0 = half * 16; c0 < p.nt; c0 += 32) {
+            float v[16];
+            tmem_ld16(t_lane + c0, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (c0 + i < rows) part[(c0 + i) * 128 + f_local] = v[i];
+          }
+        }
+        tc_fence_before();
+        if (lane == 0) mbar_arrive(acc_empty + b);  // the accumulator is free again; the rest reads global memory
+        __threadfence();
+        epi_bar();
+        if (threadIdx.x == 64) {
+          const int prev = atomicAdd(&p.ws_ticket[tile], 1);
+          flags[1] = (prev == p.splits - 1);
+        }
+        epi_bar();
+        if (flags[1]) {
+          __threadfence();
+          const float* base = p.ws_partial + (size_t)tile * p.splits * p.nt * 128;
+          for (int c0 = half * 16; c0 < p.nt; c0 += 32) {
+            // split order is fixed (deterministic sums); the 16 rows' loads of one split are independent
+            float v[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = 0.f;
+            for (int s = 0; s < p.splits; ++s) {
+              const float* src = base + ((size_t)s * p.nt + c0) * 128 + f_local;
+              float x[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) x[i] = (c0 + i < rows) ? __ldcg(src + i * 128) : 0.f;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) v[i] += x[i];
+            }
+            epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, my_scratch, split);
+          }
+          if (threadIdx.x == 64) p.ws_ticket[tile] = 0;
+        }
       }
-    }
-    if constexpr (EPI == GR_EPI_ARGMAX) {
-      if (p.splits == 1 || flags[1]) argmax_finish(p, m_tile, &flags[2]);
+      if constexpr (EPI == GR_EPI_ARGMAX) {
+        if (p.splits == 1 || flags[1]) argmax_finish(p, m_tile, &flags[2]);
+      }
+      epi_bar();  // flags / scratch are reused by the next unit
     }
   }
   tc_fence_before();
@@ -364,8 +423,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ------------------------------------------------------------------ host side
 size_t linear_smem_bytes(int nt, int stages) {
-  return 1024 + static_cast<size_t>(stages) * (kWStageBytes + static_cast<size_t>(nt) * 128) +
-         (2 * stages + 1) * 8 + 16;
+  return 1024 + static_cast<size_t>(stages) * (kWStageBytes + static_cast<size_t>(nt) * 128) + kEpiScratchBytes +
+         (2 * stages + 4) * 8 + 32;
 }
 
 template <int EPI>

@@ -23,6 +23,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 __global__ void __launch_bounds__(kRowThreads) embed_rows_kernel(const EmbedParams p) {
   __shared__ float red[32];
   __shared__ int64_t s_id;
+  __shared__ int s_pos;
   if (threadIdx.x == 0) pdl_trigger();
   pdl_wait();
   const int t = blockIdx.x;
@@ -55,8 +56,15 @@ __global__ void __launch_bounds__(kRowThreads) embed_rows_kernel(const EmbedPara
     p.row_slot[t] = phys * p.page_size + (pos % p.page_size);
     if (p.row_ids) p.row_ids[t] = static_cast<int32_t>(id);
     s_id = id;
+    s_pos = static_cast<int>(pos);
   }
   __syncthreads();
+  if (p.rope_cs && threadIdx.x < (p.rotary_dim >> 1)) {
+    // RoPE table of this row: the same fp32 product pos * inv_freq[i] as transformers, then accurate sincos
+    float s, c;
+    sincosf(static_cast<float>(s_pos) * p.inv_freq[threadIdx.x], &s, &c);
+    p.rope_cs[(size_t)t * (p.rotary_dim >> 1) + threadIdx.x] = make_float2(c, s);
+  }
   const int64_t id = s_id;
   float v[8];
   float ss = 0.f;
@@ -245,10 +253,10 @@ __global__ void draft_override_kernel(const OverrideParams p) {
 }
 
 // ------------------------------------------------------------------ gate/up interleave (load time)
+// destination row 2j = gate row j, 2j + 1 = up row j (the SwiGLU epilogue pairs adjacent TMEM lanes)
 __global__ void pack_gate_up_kernel(const __nv_bfloat16* src, __nv_bfloat16* dst, int I, int H) {
-  const int r = blockIdx.x;  // destination row
-  const int tile = r / 128, within = r % 128;
-  const int srow = within < 64 ? tile * 64 + within : I + tile * 64 + (within - 64);
+  const int r = blockIdx.x;
+  const int srow = (r & 1) ? I + (r >> 1) : (r >> 1);
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
     *reinterpret_cast<uint4*>(dst + (size_t)r * H + c) = *reinterpret_cast<const uint4*>(src + (size_t)srow * H + c);
 }

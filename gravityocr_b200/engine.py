@@ -3,7 +3,7 @@ kernels, the draft / verify / accept-commit round and its CUDA-graph capture per
 
 Data layout in HBM (bf16 unless noted):
   * weights per layer: ``qkv`` [q_dim + 2 kv_dim, H] (q, k, v rows stacked), ``o`` [H, q_dim], ``gate_up`` [2I, H]
-    re-tiled so every 128-row tile holds 64 gate rows and the matching 64 up rows, ``down`` [H, I], 4 norm vectors;
+    with gate and up rows interleaved pairwise (row 2j = gate j, 2j+1 = up j), ``down`` [H, I], 4 norm vectors;
     ``embed`` [V, H], ``norm`` [H], ``lm_head`` [V, H].
   * K/V cache: two tensors [layers, pages, kv_heads, page_size=16, head_dim] -- one (page, head) block of a layer is
     4 KiB contiguous, the TMA box of the attention kernel; requests own fixed page tables [bs, pages_per_req] int32.
@@ -91,13 +91,19 @@ class PagePool:
 
 
 def attention_split(bs: int, K: int, max_len: int, avg_len: int, n_kv: int, sms: int) -> Tuple[int, int]:
-    """Cache tokens per split and the split-grid extent: enough (request, head, split) units to fill the SMs a few
-    times over, never less than one 64-token tile per split."""
-    work = max(1, avg_len) * bs * n_kv
-    chunk = int(math.ceil(work / (2 * sms) / 64.0)) * 64
-    chunk = max(256, min(chunk, 4096))  # >= 4 pipeline tiles per split: the split merge is not free
-    max_splits = max(1, int(math.ceil((max_len + K + 1) / chunk)))
-    return chunk, max_splits
+    """Cache tokens per split and the split-grid extent.  With enough (request, head) pairs to fill the GPU twice the
+    requests run unsplit (no merge); otherwise each pair is cut into up to 16 splits of >= 256 tokens so that about
+    2 x SMs CTAs stream in parallel.  At most 16 splits per pair (the merge's limit)."""
+    L = max_len + K + 1
+    units = max(1, bs * n_kv)
+    if units >= 2 * sms:
+        chunk = 4096
+    else:
+        want = min(16, -(-2 * sms // units))
+        chunk = max(256, -(-max(1, avg_len) // want))
+    chunk = max(chunk, -(-L // 16))
+    chunk = min(4096, -(-chunk // 64) * 64)
+    return chunk, max(1, -(-L // chunk))
 
 
 @dataclass
@@ -164,6 +170,7 @@ class Engine:
         self.row_pos = torch.zeros((max_rows,), dtype=torch.int32, device=dev)
         self.row_slot = torch.zeros((max_rows,), dtype=torch.int64, device=dev)
         self.row_ids = torch.zeros((max_rows,), dtype=torch.int32, device=dev)
+        self.rope_cs = torch.zeros((max_rows, cfg.rotary_dim // 2, 2), dtype=torch.float32, device=dev)
         self.status = torch.zeros((4,), dtype=torch.int32, device=dev)
         self.lin_ws = torch.zeros((self.linear_ws_bytes(max_rows),), dtype=torch.uint8, device=dev)
         self.attn_ws: Optional[torch.Tensor] = None
@@ -225,7 +232,8 @@ class Engine:
         L.embed_rows(rows_mode, bs, K, seeds=seeds, rpi=rpi, ids32=ids32, ids64=ids64, row_embeds=row_embeds,
                      seq_lens=seq_lens, page_table=page_table, page_size=self.page_size, embed=w.embed, vocab=cfg.vocab,
                      mask_id=cfg.mask_id, norm_w=w.layers[0]["in"], eps=cfg.rms_eps, h_out=self.h[0], x_out=self.x,
-                     row_pos=self.row_pos, row_slot=self.row_slot, row_ids=self.row_ids, status=st)
+                     row_pos=self.row_pos, row_slot=self.row_slot, row_ids=self.row_ids, inv_freq=w.inv_freq,
+                     rotary_dim=cfg.rotary_dim, rope_cs=self.rope_cs, status=st)
         ws_attn = self._attn_workspace(bs, K, attn_splits) if attn_splits > 1 else None
         cur = 0
         for l, d in enumerate(w.layers):
@@ -242,6 +250,7 @@ class Engine:
             e.n_q_heads = cfg.n_q_heads
             e.n_kv_heads = cfg.n_kv_heads
             e.page_size = self.page_size
+            e.rope_cs = self.rope_cs.data_ptr()
             L.linear(d["qkv"], self.x, M, e, self.lin_ws, prefetch=d["o"], status=st)
             L.bd_attention(self.q, self.pool.k[l], self.pool.v[l], page_table, seq_lens, bs, K, draft, base_add,
                            cfg.n_q_heads, cfg.n_kv_heads, self.page_size, attn_chunk, attn_splits, self.attn, ws_attn,

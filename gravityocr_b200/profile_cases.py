@@ -48,9 +48,10 @@ def case_attention(a):
     seq = torch.tensor(S, dtype=torch.int64, device="cuda")
     q = torch.randn((bs * K, nq, D), generator=g).to("cuda", torch.bfloat16)
     out = torch.empty_like(q)
-    work = a.seq * bs * nkv
-    chunk = a.chunk or max(256, min(4096, int(math.ceil(work / (2 * L.num_sms()) / 64.0)) * 64))
-    splits = int(math.ceil((a.seq + K + 1) / chunk))
+    from .engine import attention_split
+    chunk, splits = attention_split(bs, K, a.seq, a.seq, nkv, L.num_sms())
+    if a.chunk:
+        chunk, splits = a.chunk, int(math.ceil((a.seq + K + 1) / a.chunk))
     ws = torch.zeros((L.attention_workspace_bytes(bs, K, nq, nkv, splits),), dtype=torch.uint8, device="cuda")
     fn = lambda: L.bd_attention(q, kc, vc, pt, seq, bs, K, a.draft, 0 if a.draft else 1, nq, nkv, ps, chunk, splits,
                                 out, ws)
@@ -94,7 +95,10 @@ def case_linear(a):
         e.q_out, e.k_cache, e.v_cache = q.data_ptr(), kc.data_ptr(), vc.data_ptr()
         e.row_pos, e.row_slot, e.inv_freq = pos.data_ptr(), slot.data_ptr(), inv.data_ptr()
         e.rotary_dim, e.n_q_heads, e.n_kv_heads, e.page_size = cfg.rotary_dim, cfg.n_q_heads, cfg.n_kv_heads, 16
-        keep += [q, kc, vc, pos, slot, inv]
+        f = pos.float()[:, None] * inv[None, :]
+        cs = torch.stack([f.cos(), f.sin()], -1).contiguous()  # the per-row table gr_embed_rows writes
+        e.rope_cs = cs.data_ptr()
+        keep += [q, kc, vc, pos, slot, inv, cs]
     ws_sp = 1 if mode == L.EPI_PARTIAL_F32 else sp
     ws = torch.zeros((L.linear_workspace_bytes(n_out, m, ws_sp),), dtype=torch.uint8, device="cuda")
     ms = _time(lambda: L.linear(w, x, m, e, ws, splits=sp), a.reps)

@@ -91,14 +91,14 @@ def _rope_ref(x, pos, inv_freq, rd):
     return out
 
 
-@pytest.mark.parametrize("m", [17, 170])
-def test_linear_qkv_rope_kvwrite(m):
+@pytest.mark.parametrize("m,table", [(17, False), (170, False), (17, True), (1088, True)])
+def test_linear_qkv_rope_kvwrite(m, table):
     cfg = ModelConfig()
     g = torch.Generator().manual_seed(11 + m)
     H, nq, nkv, D = cfg.hidden, cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim
     w = _rand((cfg.qkv_dim, H), g, 0.02)
     x = _rand((m, H), g)
-    n_pages, ps = 64, 16
+    n_pages, ps = m // 16 + 64, 16
     pos = torch.randint(0, 8000, (m,), generator=g, dtype=torch.int32)
     perm = torch.randperm(n_pages * ps, generator=g)[:m]
     slots = perm.to(torch.int64)
@@ -112,6 +112,10 @@ def test_linear_qkv_rope_kvwrite(m):
     e.q_out, e.k_cache, e.v_cache = q.data_ptr(), kc.data_ptr(), vc.data_ptr()
     e.row_pos, e.row_slot, e.inv_freq = pos_d.data_ptr(), slots_d.data_ptr(), inv.data_ptr()
     e.rotary_dim, e.n_q_heads, e.n_kv_heads, e.page_size = cfg.rotary_dim, nq, nkv, ps
+    if table:
+        f = pos_d.float()[:, None] * inv[None, :]
+        cs = torch.stack([f.cos(), f.sin()], -1).contiguous()
+        e.rope_cs = cs.data_ptr()
     L.linear(w, x, m, e, _ws(cfg.qkv_dim, H, m))
     torch.cuda.synchronize()
     y = x.float() @ w.float().T
@@ -200,8 +204,10 @@ def test_bd_attention(bs, K, draft):
     q = _rand((bs * K, nq, D), g)
     pt_d, seq_d = pt.to(DEV), S.to(DEV)
     ref = _attn_ref(q, kc, vc, pt_d, seq_d, K, draft, base_add, nq, nkv)
-    for chunk in (64, 256, 4096):
-        max_splits = int(math.ceil((int(S.max()) + base_add + K) / chunk))
+    Lmax = int(S.max()) + base_add + K
+    min_chunk = max(64, -(-(-(-Lmax // 16)) // 64) * 64)   # the merge takes at most 16 splits
+    for chunk in sorted({min_chunk, max(min_chunk, 512), 4096}):
+        max_splits = int(math.ceil(Lmax / chunk))
         ws = torch.zeros((max(256, L.attention_workspace_bytes(bs, K, nq, nkv, max_splits)),), dtype=torch.uint8,
                          device=DEV)
         out = torch.full((bs * K, nq, D), float("nan"), dtype=torch.bfloat16, device=DEV)
@@ -232,11 +238,13 @@ def test_embed_rows_and_residual_norm():
     slot = torch.zeros((M,), dtype=torch.int64, device=DEV)
     ids = torch.zeros((M,), dtype=torch.int32, device=DEV)
     st = torch.zeros((1,), dtype=torch.int32, device=DEV)
+    inv = rope_inv_freq(cfg).to(DEV)
+    cs = torch.zeros((M, cfg.rotary_dim // 2, 2), device=DEV)
     for mode in (L.ROWS_DRAFT, L.ROWS_VERIFY):
         am = torch.randint(0, V, (M,), generator=g, dtype=torch.int32).to(DEV)
         L.embed_rows(mode, bs, K, seeds=seeds, rpi=rpi, ids32=am, seq_lens=seq, page_table=pt, page_size=16,
                      embed=E, vocab=V, mask_id=cfg.mask_id, norm_w=nw, eps=cfg.rms_eps, h_out=h, x_out=x, row_pos=pos,
-                     row_slot=slot, row_ids=ids, status=st)
+                     row_slot=slot, row_ids=ids, inv_freq=inv, rotary_dim=cfg.rotary_dim, rope_cs=cs, status=st)
         torch.cuda.synchronize()
         assert int(st.item()) == 0
         j = torch.arange(K, device=DEV).repeat(bs)
@@ -249,6 +257,9 @@ def test_embed_rows_and_residual_norm():
             want_pos = seq[b] + 1 + j
         assert torch.equal(ids.long(), want_ids)
         assert torch.equal(pos.long(), want_pos)
+        f = want_pos.float()[:, None] * inv[None, :]
+        torch.testing.assert_close(cs[..., 0], f.cos(), rtol=0, atol=2e-6)
+        torch.testing.assert_close(cs[..., 1], f.sin(), rtol=0, atol=2e-6)
         want_slot = pt[b, want_pos // 16].long() * 16 + want_pos % 16
         assert torch.equal(slot, want_slot)
         hr = E[want_ids].float()
@@ -401,8 +412,8 @@ def test_attention_shared_workspace_across_batches():
     g = torch.Generator().manual_seed(9)
     n_pages = 900
     kc, vc = _rand((n_pages, nkv, ps, D), g), _rand((n_pages, nkv, ps, D), g)
-    ws = torch.zeros((L.attention_workspace_bytes(64, 64, nq, nkv, 40),), dtype=torch.uint8, device=DEV)
-    for bs, K, draft, chunk in [(1, 64, False, 64), (8, 17, True, 64), (1, 17, False, 128), (6, 33, True, 64)]:
+    ws = torch.zeros((L.attention_workspace_bytes(64, 64, nq, nkv, 16),), dtype=torch.uint8, device=DEV)
+    for bs, K, draft, chunk in [(1, 64, False, 128), (8, 17, True, 128), (1, 17, False, 256), (6, 33, True, 128)]:
         S = torch.randint(0, 1500, (bs,), generator=g)
         base_add = 0 if draft else 1
         P = (1600 + K) // ps + 2

@@ -40,7 +40,7 @@ def _setup(n_layers=2, n_image=64, n_prompt=16, new=64, bs=1, seed=0):
     eng.reserve(bs * K)
     ppr = (cap + 15) // 16
     rb = eng.new_round_buffers(bs, K, ppr, max_len=cap, avg_len=P)
-    rb.attn_chunk, rb.attn_splits = 64, int(math.ceil((cap + K + 1) / 64))  # same split points at every batch size
+    rb.attn_chunk, rb.attn_splits = 128, int(math.ceil((cap + K + 1) / 128))  # same split points at every batch size
     for b in range(bs):
         rb.page_table[b] = torch.tensor(eng.pool.alloc(ppr), dtype=torch.int32, device=DEV)
     return cfg, w32, reqs, eng, rb, cap
@@ -155,7 +155,7 @@ def test_graph_replay_equals_eager():
 def test_batched_rounds_match_single_requests():
     """Requests are independent: a batch of 3 commits exactly what each request commits alone."""
     cfg, w32, reqs, eng, rb, cap = _setup(bs=3)
-    eng.prefill(rb, [r[0] for r in reqs], [r[1] for r in reqs], attn_chunk=64)
+    eng.prefill(rb, [r[0] for r in reqs], [r[1] for r in reqs], attn_chunk=128)
     batched = [[] for _ in range(3)]
     for _ in range(3):
         eng.round_launch(rb)
@@ -165,7 +165,7 @@ def test_batched_rounds_match_single_requests():
     for b in range(3):
         cfg1, _, reqs1, eng1, rb1, _ = _setup(bs=1)
         x, ids = reqs[b]
-        eng1.prefill(rb1, [x], [ids], attn_chunk=64)
+        eng1.prefill(rb1, [x], [ids], attn_chunk=128)
         single = []
         for _ in range(3):
             eng1.round_launch(rb1)
