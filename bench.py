@@ -292,7 +292,8 @@ def main():
             ev0.record(st)
         l = i % cfg.n_layers  # rotate layers: each launch reads K/V that is not in L2
         L.bd_attention(eng.q, eng.pool.k[l], eng.pool.v[l], rb.page_table, rb.seq_lens, bs, K, False, 1,
-                       cfg.n_q_heads, cfg.n_kv_heads, 16, rb.attn_chunk, rb.attn_splits, eng.attn, ws, status=rb.status)
+                       cfg.n_q_heads, cfg.n_kv_heads, 16, rb.attn_chunk, rb.attn_splits, eng.attn, ws, status=rb.status,
+                       order=rb.order)
     ev1.record(st)
     torch.cuda.synchronize()
     attn_ms = ev0.elapsed_time(ev1) / n_rep

@@ -24,7 +24,7 @@ ROWS_DRAFT, ROWS_VERIFY, ROWS_EXPLICIT = range(3)
 EXPORTS = ("gr_version", "gr_status_string", "gr_set_pdl", "gr_num_sms", "gr_linear_workspace_bytes",
            "gr_attention_workspace_bytes", "gr_linear_default_splits", "gr_linear", "gr_embed_rows",
            "gr_residual_norm", "gr_bd_attention", "gr_accept_commit", "gr_draft_override", "gr_pack_gate_up",
-           "gr_bd_attention_noalloc")
+           "gr_bd_attention_noalloc", "gr_bd_attention_ordered")
 
 
 class Epilogue(ctypes.Structure):
@@ -70,6 +70,8 @@ _SIGS = {
     "gr_draft_override": (_I, [_I, _I, _P, _P, _I, _P, _P, _I, _P, _I, _I, _P]),
     "gr_pack_gate_up": (_I, [_P, _P, _I, _I, _P]),
     "gr_bd_attention_noalloc": (_I, [_P, _P, _P, _L, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
+    "gr_bd_attention_ordered": (_I, [_P, _P, _P, _L, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _Z, _P,
+                                     _P]),
 }
 GR_ERR_SCRATCH_LIMIT = 8
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -172,10 +174,11 @@ def residual_norm(m: int, h_in, y, w_a, w_b, eps: float, h_out, x_out, y_parts: 
 
 def bd_attention(q, k_cache, v_cache, page_table, seq_lens, bs: int, K: int, draft: bool, base_add: int,
                  n_q_heads: int, n_kv_heads: int, page_size: int, chunk: int, max_splits: int, out, workspace,
-                 status=None, stream=None) -> None:
+                 status=None, stream=None, order=None) -> None:
     n_pages = k_cache.shape[0]
-    rc = load().gr_bd_attention(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), n_pages, page_table.data_ptr(),
-                                page_table.shape[1], seq_lens.data_ptr(), bs, K, 1 if draft else 0, base_add,
+    rc = load().gr_bd_attention_ordered(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), n_pages,
+                                page_table.data_ptr(), page_table.shape[1], seq_lens.data_ptr(), _ptr(order),
+                                bs, K, 1 if draft else 0, base_add,
                                 n_q_heads, n_kv_heads, page_size, chunk, max_splits, out.data_ptr(),
                                 _ptr(workspace), 0 if workspace is None else workspace.numel() * workspace.element_size(),
                                 _ptr(status), _stream(stream))

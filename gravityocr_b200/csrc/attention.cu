@@ -28,15 +28,20 @@ __device__ __forceinline__ int row_limit(const AttnParams& p, int j, int base) {
   return base + j + 1;
 }
 
-__global__ void __launch_bounds__(288, 1) attention_kernel(const __grid_constant__ CUtensorMap tmk,
-                                                           const __grid_constant__ CUtensorMap tmv,
-                                                           const AttnParams p) {
+// Two instantiations: <224, 2> (two warp groups of <= 3 row tiles + producer, two CTAs per SM) and <288, 1>
+// (up to 8 row tiles, one group).
+template <int MAXT, int MINB>
+__global__ void __launch_bounds__(MAXT, MINB) attention_kernel(const __grid_constant__ CUtensorMap tmk,
+                                                               const __grid_constant__ CUtensorMap tmv,
+                                                               const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int G = p.n_q_heads / p.n_kv_heads;
   const int R = G * p.K;
   const int n_mt = (R + 15) / 16;
   const int R_pad = n_mt * 16;
+  const int NG = p.groups;                                    // warp groups taking alternate KV tiles
+  const int n_cw = NG * n_mt;                                 // compute warps
   uint8_t* kv_smem = smem;                                    // kStages x kStageBytes
   uint8_t* q_smem = smem + kStages * kStageBytes;             // 2 halves x R_pad x 128 B
   uint64_t* full = reinterpret_cast<uint64_t*>(q_smem + 2 * R_pad * 128);
@@ -44,7 +49,8 @@ __global__ void __launch_bounds__(288, 1) attention_kernel(const __grid_constant
   int* flag = reinterpret_cast<int*>(empty + kStages);
   int* pages = flag + 4;  // physical page ids of this split's cache range (chunk / page_size entries)
 
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  // blocks launch in z-major order: a longest-first request order shortens the tail of a mixed-length batch
+  const int split = blockIdx.x, kvh = blockIdx.y, b = p.order ? p.order[blockIdx.z] : blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t seq = p.seq_lens[b];
   const int base = static_cast<int>(seq) + p.base_add;
@@ -58,7 +64,7 @@ __global__ void __launch_bounds__(288, 1) attention_kernel(const __grid_constant
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(full + s, 1);
-      mbar_init(empty + s, n_mt);
+      mbar_init(empty + s, n_mt);  // one warp group consumes each tile
     }
     *flag = 0;
     fence_mbar_init();
@@ -70,7 +76,8 @@ __global__ void __launch_bounds__(288, 1) attention_kernel(const __grid_constant
   pdl_wait();
 
   const int* pt = p.page_table + (size_t)b * p.pt_stride;
-  if (warp == n_mt) {
+  const size_t q_row_stride = (size_t)p.n_q_heads * 128;
+  if (warp == n_cw) {
     // ------------------------------------------------------------ producer
     // the whole split's page ids in one coalesced pass (pages past the request's last page hold no visible token:
     // they are replaced by its last page, whose contents are finite)
@@ -100,35 +107,30 @@ __global__ void __launch_bounds__(288, 1) attention_kernel(const __grid_constant
       for (int i = max(0, issued - kStages); i < issued; ++i)
         mbar_wait(full + (i % kStages), (i / kStages) & 1, p.status, GR_ERR_TIMEOUT);
     }
-  } else if (warp < n_mt) {
+  } else if (warp < n_cw) {
     // ------------------------------------------------------------ compute warps
-    // stage this warp's 16 query rows into shared memory (128-byte swizzle, two 64-dim halves)
-    const size_t q_row_stride = (size_t)p.n_q_heads * 128;
-    for (int e = lane; e < 16 * 16; e += 32) {
-      const int rr = e >> 4, chunk = e & 15;
-      const int r = warp * 16 + rr;
-      uint4 val = make_uint4(0, 0, 0, 0);
-      if (r < R) {
-        const int g = r / p.K, j = r % p.K;
-        const __nv_bfloat16* src = p.q + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128 + chunk * 8;
-        val = *reinterpret_cast<const uint4*>(src);
+    const int mt = warp % n_mt, grp = warp / n_mt;
+    // group 0 stages the query rows into shared memory (128-byte swizzle, two 64-dim halves)
+    if (grp == 0) {
+      for (int e = lane; e < 16 * 16; e += 32) {
+        const int rr = e >> 4, chunk = e & 15;
+        const int r = mt * 16 + rr;
+        uint4 val = make_uint4(0, 0, 0, 0);
+        if (r < R) {
+          const int g = r / p.K, j = r % p.K;
+          const __nv_bfloat16* src = p.q + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128 + chunk * 8;
+          val = *reinterpret_cast<const uint4*>(src);
+        }
+        *reinterpret_cast<uint4*>(q_smem + (chunk >> 3) * (R_pad * 128) + sw128(r, chunk & 7)) = val;
       }
-      *reinterpret_cast<uint4*>(q_smem + (chunk >> 3) * (R_pad * 128) + sw128(r, chunk & 7)) = val;
     }
-    __syncwarp();
-    uint32_t qf[8][4];
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const uint32_t a = smem_u32(q_smem + (ks >> 2) * (R_pad * 128) +
-                                  sw128(warp * 16 + (lane & 15), 2 * (ks & 3) + (lane >> 4)));
-      ldsm_x4(a, qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
-    }
+    asm volatile("bar.sync 2, %0;" ::"r"(n_cw * 32) : "memory");
     const int g4 = lane >> 2, t4 = lane & 3;
     int lim[2];
     bool live[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const int r = warp * 16 + g4 + 8 * h;
+      const int r = mt * 16 + g4 + 8 * h;
       live[h] = r < R;
       lim[h] = live[h] ? min(row_limit(p, r % p.K, base), kv_end) : 0;
     }
@@ -137,7 +139,7 @@ __global__ void __launch_bounds__(288, 1) attention_kernel(const __grid_constant
 #pragma unroll
     for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
 
-    for (int i = 0; i < n_tiles; ++i) {
+    for (int i = grp; i < n_tiles; i += NG) {
       const int s = i % kStages;
       if (!mbar_wait(full + s, (i / kStages) & 1, p.status, GR_ERR_TIMEOUT)) {
         *flag = 1;
@@ -145,12 +147,15 @@ __global__ void __launch_bounds__(288, 1) attention_kernel(const __grid_constant
       }
       const uint8_t* st = kv_smem + s * kStageBytes;
       const int tok0 = kv_beg + i * kTile;
-      // S = Q K^T for 16 rows x 64 tokens
+      // S = Q K^T for 16 rows x 64 tokens (query fragments re-read from shared memory: fewer live registers)
       float sc[8][4];
 #pragma unroll
       for (int n = 0; n < 8; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
+        uint32_t qf[4];
+        ldsm_x4(smem_u32(q_smem + (ks >> 2) * (R_pad * 128) + sw128(mt * 16 + (lane & 15), 2 * (ks & 3) + (lane >> 4))),
+                qf[0], qf[1], qf[2], qf[3]);
         const uint8_t* kh = st + (ks >> 2) * kHalfBytes;
 #pragma unroll
         for (int np = 0; np < 4; ++np) {
@@ -158,8 +163,8 @@ __global__ void __launch_bounds__(288, 1) attention_kernel(const __grid_constant
           const int ch = 2 * (ks & 3) + ((lane >> 3) & 1);
           uint32_t b0, b1, b2, b3;
           ldsm_x4(smem_u32(kh + sw128(trow, ch)), b0, b1, b2, b3);
-          mma_16816(sc[2 * np], qf[ks], b0, b1);
-          mma_16816(sc[2 * np + 1], qf[ks], b2, b3);
+          mma_16816(sc[2 * np], qf, b0, b1);
+          mma_16816(sc[2 * np + 1], qf, b2, b3);
         }
       }
       // mask + online softmax (rows g4 and g4+8 of this warp's tile)
@@ -232,36 +237,70 @@ __global__ void __launch_bounds__(288, 1) attention_kernel(const __grid_constant
       if (lane == 0) mbar_arrive(empty + s);
     }
 
-    // ------------------------------------------------------------ write / merge
-    if (n_active == 1) {
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        if (!live[h]) continue;
-        const int r = warp * 16 + g4 + 8 * h;
-        const int g = r / p.K, j = r % p.K;
-        const float inv = l_run[h] > 0.f ? 1.f / l_run[h] : 0.f;
-        __nv_bfloat16* dst = p.out + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128;
+    // ------------------------------------------------------------ combine the warp groups (group 1 -> group 0)
+    if (NG > 1) {
+      float* xch = reinterpret_cast<float*>(kv_smem) + (size_t)(mt * 32 + lane) * 68;  // every tile is consumed
+      asm volatile("bar.sync 2, %0;" ::"r"(n_cw * 32) : "memory");
+      if (grp == 1) {
+        xch[0] = m_run[0]; xch[1] = m_run[1]; xch[2] = l_run[0]; xch[3] = l_run[1];
 #pragma unroll
         for (int n = 0; n < 16; ++n) {
-          const int d = n * 8 + 2 * t4;
-          *reinterpret_cast<uint32_t*>(dst + d) = pack_bf16(o[n][2 * h] * inv, o[n][2 * h + 1] * inv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) xch[4 + n * 4 + e] = o[n][e];
         }
       }
-    } else {
-      const size_t slot = ((size_t)b * p.n_kv_heads + kvh) * p.max_splits + split;
+      asm volatile("bar.sync 2, %0;" ::"r"(n_cw * 32) : "memory");
+      if (grp == 0) {
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int r = warp * 16 + g4 + 8 * h;
-        float* dst = p.ws_o + (slot * R_pad + r) * 128;
+        for (int h = 0; h < 2; ++h) {
+          const float m1 = xch[h], l1 = xch[2 + h];
+          const float mn = fmaxf(m_run[h], m1);
+          const float ms = (mn == -INFINITY) ? 0.f : mn;
+          const float a0 = (m_run[h] == -INFINITY) ? 0.f : exp2f(m_run[h] - ms);
+          const float a1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - ms);
+          m_run[h] = mn;
+          l_run[h] = l_run[h] * a0 + l1 * a1;
 #pragma unroll
-        for (int n = 0; n < 16; ++n) {
-          const int d = n * 8 + 2 * t4;
-          *reinterpret_cast<float2*>(dst + d) = make_float2(o[n][2 * h], o[n][2 * h + 1]);
+          for (int n = 0; n < 16; ++n) {
+            o[n][2 * h] = o[n][2 * h] * a0 + xch[4 + n * 4 + 2 * h] * a1;
+            o[n][2 * h + 1] = o[n][2 * h + 1] * a0 + xch[4 + n * 4 + 2 * h + 1] * a1;
+          }
         }
-        if (t4 == 0) {
-          float* ml = p.ws_ml + (slot * R_pad + r) * 2;
-          ml[0] = m_run[h];
-          ml[1] = l_run[h];
+      }
+    }
+
+    // ------------------------------------------------------------ write / merge (group 0)
+    if (grp == 0) {
+      if (n_active == 1) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (!live[h]) continue;
+          const int r = mt * 16 + g4 + 8 * h;
+          const int g = r / p.K, j = r % p.K;
+          const float inv = l_run[h] > 0.f ? 1.f / l_run[h] : 0.f;
+          __nv_bfloat16* dst = p.out + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128;
+#pragma unroll
+          for (int n = 0; n < 16; ++n) {
+            const int d = n * 8 + 2 * t4;
+            *reinterpret_cast<uint32_t*>(dst + d) = pack_bf16(o[n][2 * h] * inv, o[n][2 * h + 1] * inv);
+          }
+        }
+      } else {
+        const size_t slot = ((size_t)b * p.n_kv_heads + kvh) * p.max_splits + split;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = mt * 16 + g4 + 8 * h;
+          float* dst = p.ws_o + (slot * R_pad + r) * 128;
+#pragma unroll
+          for (int n = 0; n < 16; ++n) {
+            const int d = n * 8 + 2 * t4;
+            *reinterpret_cast<float2*>(dst + d) = make_float2(o[n][2 * h], o[n][2 * h + 1]);
+          }
+          if (t4 == 0) {
+            float* ml = p.ws_ml + (slot * R_pad + r) * 2;
+            ml[0] = m_run[h];
+            ml[1] = l_run[h];
+          }
         }
       }
     }
@@ -281,7 +320,6 @@ __global__ void __launch_bounds__(288, 1) attention_kernel(const __grid_constant
   if (*flag != 2) return;
   __threadfence();
   const size_t slot0 = ((size_t)b * p.n_kv_heads + kvh) * p.max_splits;
-  const size_t q_row_stride = (size_t)p.n_q_heads * 128;
   // phase A: per (row, split) weights exp2(m_s - M) / L into shared memory (the stage ring is idle now)
   float* wgt = reinterpret_cast<float*>(kv_smem);  // [R][kMaxMergeSplits]
   for (int r = threadIdx.x; r < R; r += blockDim.x) {
@@ -344,20 +382,37 @@ size_t attention_smem_bytes(int K, int G) {
   return 1024 + kStages * kStageBytes + 2 * R_pad * 128 + 2 * kStages * 8 + 16 + kMaxChunkPages * 4;
 }
 
+template <int MAXT, int MINB>
+static cudaError_t configure_attention() {
+  static bool configured = false;
+  if (configured) return cudaSuccess;
+  cudaError_t e =
+      cudaFuncSetAttribute(attention_kernel<MAXT, MINB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(attention_kernel<MAXT, MINB>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e != cudaSuccess) return e;
+  configured = true;
+  return cudaSuccess;
+}
+
 cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p,
                              cudaStream_t stream, bool pdl) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
   const int G = p.n_q_heads / p.n_kv_heads;
   const int n_mt = (G * p.K + 15) / 16;
+  // One warp group.  Two groups on alternate tiles would need an even stage count (a group may only ever wait for
+  // the next phase of a stage it owns: with shared stages a fast group can meet a stage two phases ahead, where the
+  // parity wait sees the older completed phase); 4 stages do not leave room for two CTAs per SM.  Idle extra warps
+  // help the split merge of small batches (large batches keep small CTAs: 2 per SM).
+  AttnParams q = p;
+  q.groups = 1;
+  const bool small = p.bs * p.n_kv_heads < 2 * 148;
+  int warps = q.groups * n_mt + 1;
+  if (small && p.max_splits > 1 && warps < kMinWarps) warps = kMinWarps;
+  const bool narrow = q.groups == 2 && warps * 32 <= 224;
+  cudaError_t e = narrow ? configure_attention<224, 2>() : configure_attention<288, 1>();
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.max_splits, p.n_kv_heads, p.bs);
-  // idle extra warps help the split merge; unsplit launches keep small CTAs (register-limited occupancy)
-  const int warps = (p.max_splits > 1 && n_mt + 1 < kMinWarps) ? kMinWarps : n_mt + 1;
   cfg.blockDim = dim3(32 * warps);
   cfg.dynamicSmemBytes = attention_smem_bytes(p.K, G);
   cfg.stream = stream;
@@ -366,7 +421,8 @@ cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, con
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, attention_kernel, tmk, tmv, p);
+  return narrow ? cudaLaunchKernelEx(&cfg, attention_kernel<224, 2>, tmk, tmv, q)
+                : cudaLaunchKernelEx(&cfg, attention_kernel<288, 1>, tmk, tmv, q);
 }
 
 }  // namespace gr

@@ -281,10 +281,11 @@ size_t gr_attention_workspace_bytes(int bs, int K, int n_q_heads, int n_kv_heads
   return kAttnTicketBytes + align256(slots * R_pad * 128 * sizeof(float)) + align256(slots * R_pad * 2 * sizeof(float));
 }
 
-int gr_bd_attention(const void* q, const void* k_cache, const void* v_cache, int64_t n_pages, const int32_t* page_table,
-                    int pt_stride, const int64_t* seq_lens, int bs, int K, int draft, int base_add, int n_q_heads,
-                    int n_kv_heads, int page_size, int chunk, int max_splits, void* out, void* workspace,
-                    size_t workspace_bytes, int32_t* status, void* stream) {
+int gr_bd_attention_ordered(const void* q, const void* k_cache, const void* v_cache, int64_t n_pages,
+                            const int32_t* page_table, int pt_stride, const int64_t* seq_lens, const int32_t* req_order,
+                            int bs, int K, int draft, int base_add, int n_q_heads, int n_kv_heads, int page_size,
+                            int chunk, int max_splits, void* out, void* workspace, size_t workspace_bytes,
+                            int32_t* status, void* stream) {
   if (!q || !k_cache || !v_cache || !page_table || !seq_lens || !out || bs <= 0 || K <= 0 || n_pages <= 0)
     return GR_ERR_ARG;
   if (n_kv_heads <= 0 || n_q_heads % n_kv_heads || page_size != 16 || chunk <= 0 || chunk % 64 || chunk > 4096 ||
@@ -329,8 +330,18 @@ int gr_bd_attention(const void* q, const void* k_cache, const void* v_cache, int
     p.ws_ml = reinterpret_cast<float*>(b);
   }
   p.status = status;
+  p.order = req_order;
   cudaError_t e = launch_attention(tmk, tmv, p, static_cast<cudaStream_t>(stream), g_pdl);
   return e == cudaSuccess ? GR_OK : GR_ERR_CUDA;
+}
+
+int gr_bd_attention(const void* q, const void* k_cache, const void* v_cache, int64_t n_pages, const int32_t* page_table,
+                    int pt_stride, const int64_t* seq_lens, int bs, int K, int draft, int base_add, int n_q_heads,
+                    int n_kv_heads, int page_size, int chunk, int max_splits, void* out, void* workspace,
+                    size_t workspace_bytes, int32_t* status, void* stream) {
+  return gr_bd_attention_ordered(q, k_cache, v_cache, n_pages, page_table, pt_stride, seq_lens, nullptr, bs, K, draft,
+                                 base_add, n_q_heads, n_kv_heads, page_size, chunk, max_splits, out, workspace,
+                                 workspace_bytes, status, stream);
 }
 
 int gr_embed_rows(int mode, int bs, int K, const int64_t* seeds, const int64_t* req_pool_idx, const int32_t* ids32,

@@ -435,6 +435,8 @@ cudaError_t launch_linear_t(const CUtensorMap& tmw, const CUtensorMap& tmx, cons
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
     configured = true;
   }
   cudaLaunchConfig_t cfg = {};

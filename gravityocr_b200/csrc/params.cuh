@@ -36,7 +36,8 @@ struct AttnParams {
   const int64_t* seq_lens;
   int bs, K, draft, base_add;
   int n_q_heads, n_kv_heads, page_size;
-  int chunk, max_splits;
+  int chunk, max_splits, groups;
+  const int32_t* order;  // optional: grid z -> request (longest first), NULL = identity
   float scale_log2;
   float* ws_o;
   float* ws_ml;

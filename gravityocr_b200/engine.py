@@ -128,6 +128,7 @@ class RoundBuffers:
     accept_len: torch.Tensor    # int32 [bs]
     attn_chunk: int
     attn_splits: int
+    order: Optional[torch.Tensor] = None            # int32 [bs] attention launch order (longest first)
     override_g: Optional[torch.Tensor] = None      # int32 [bs, g_len] forced-accept replay stream
     override_plan: Optional[torch.Tensor] = None   # int32 [bs, max_rounds]
 
@@ -214,7 +215,8 @@ class Engine:
     def forward(self, rows_mode: int, bs: int, K: int, seq_lens: torch.Tensor, page_table: torch.Tensor, *,
                 out_idx: torch.Tensor, out_top1: Optional[torch.Tensor] = None, out_gap: Optional[torch.Tensor] = None,
                 seeds=None, rpi=None, ids32=None, ids64=None, row_embeds=None, attn_chunk: int = 64,
-                attn_splits: int = 1, status: Optional[torch.Tensor] = None, head: bool = True) -> None:
+                attn_splits: int = 1, status: Optional[torch.Tensor] = None, head: bool = True,
+                order: Optional[torch.Tensor] = None) -> None:
         """One pass of the decoder over M = bs*K rows; writes each row's argmax (and top-1 / gap) to out_idx.
         head=False stops before lm_head (the normed final hidden rows stay in ``self.x``)."""
         cfg, w, M = self.cfg, self.w, bs * K
@@ -254,7 +256,7 @@ class Engine:
             L.linear(d["qkv"], self.x, M, e, self.lin_ws, prefetch=d["o"], status=st)
             L.bd_attention(self.q, self.pool.k[l], self.pool.v[l], page_table, seq_lens, bs, K, draft, base_add,
                            cfg.n_q_heads, cfg.n_kv_heads, self.page_size, attn_chunk, attn_splits, self.attn, ws_attn,
-                           status=st)
+                           status=st, order=order)
             e = L.Epilogue()
             e.mode = L.EPI_PARTIAL_F32
             e.out = self.y.data_ptr()
@@ -364,11 +366,21 @@ class Engine:
                 for k, (b, _) in enumerate(ends):
                     first[b] = int(res[k])
         rb.seq_lens.copy_(torch.tensor(lens, dtype=torch.int64))
+        self.refresh_order(rb)
         rb.seeds[rb.rpi] = torch.tensor(first, dtype=torch.int64, device=dev)
         rb.n_committed.fill_(1)
         rb.rounds.zero_()
         self.check_status(rb)
         return first
+
+    def refresh_order(self, rb: RoundBuffers) -> None:
+        """Longest-first attention launch order from the current lengths (scheduling only; results do not depend on
+        it).  The buffer is updated in place, so captured graphs pick it up."""
+        order = torch.argsort(rb.seq_lens, descending=True, stable=True).to(torch.int32)
+        if rb.order is None:
+            rb.order = order.contiguous()
+        else:
+            rb.order.copy_(order)
 
     def check_status(self, rb: RoundBuffers) -> None:
         s = int(rb.status.item())
@@ -381,7 +393,7 @@ class Engine:
         bs, K = rb.bs, rb.K
         self.forward(L.ROWS_DRAFT, bs, K, rb.seq_lens, rb.page_table, out_idx=rb.am, out_top1=rb.top_d,
                      out_gap=rb.gap_d, seeds=rb.seeds, rpi=rb.rpi, attn_chunk=rb.attn_chunk,
-                     attn_splits=rb.attn_splits, status=rb.status)
+                     attn_splits=rb.attn_splits, status=rb.status, order=rb.order)
         if override:
             L.draft_override(bs, K, rb.am, rb.override_g, rb.n_committed, rb.override_plan, rb.rounds,
                              self.cfg.vocab, self.cfg.mask_id)
@@ -391,7 +403,7 @@ class Engine:
         bs, K = rb.bs, rb.K
         self.forward(L.ROWS_VERIFY, bs, K, rb.seq_lens, rb.page_table, out_idx=rb.v, out_top1=rb.top_v,
                      out_gap=rb.gap_v, ids32=rb.am, attn_chunk=rb.attn_chunk, attn_splits=rb.attn_splits,
-                     status=rb.status)
+                     status=rb.status, order=rb.order)
         L.accept_commit(bs, K, rb.am, rb.v, rb.seeds, rb.rpi, rb.seq_lens, rb.packed, rb.released, rb.out_next,
                         x0_committed=False, n_released=rb.n_released, n_committed=rb.n_committed, rounds=rb.rounds,
                         accept_len=rb.accept_len)

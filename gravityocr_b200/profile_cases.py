@@ -39,25 +39,33 @@ def case_attention(a):
     bs, K = a.bs, a.bd + 1
     g = torch.Generator().manual_seed(1)
     nq, nkv, D, ps = cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, 16
-    S = [a.seq] * bs
-    ppr = (a.seq + K + 2 + ps - 1) // ps
+    if a.mixed:
+        # the config-3 mix: prefixes U[256, 4096] image tokens + 32 prompt tokens (seed 3)
+        S = (torch.randint(256, 4097, (bs,), generator=torch.Generator().manual_seed(3)) + 32).tolist()
+    else:
+        S = [a.seq] * bs
+    seq_max = max(S)
+    ppr = (seq_max + K + 2 + ps - 1) // ps
     n_pages = bs * ppr
     kc = torch.randn((n_pages, nkv, ps, D), generator=g).to("cuda", torch.bfloat16)
     vc = torch.randn((n_pages, nkv, ps, D), generator=g).to("cuda", torch.bfloat16)
     pt = torch.randperm(n_pages, generator=g).to(torch.int32).view(bs, ppr).cuda()
     seq = torch.tensor(S, dtype=torch.int64, device="cuda")
+    avg = sum(S) // len(S)
     q = torch.randn((bs * K, nq, D), generator=g).to("cuda", torch.bfloat16)
     out = torch.empty_like(q)
     from .engine import attention_split
-    chunk, splits = attention_split(bs, K, a.seq, a.seq, nkv, L.num_sms())
+    chunk, splits = attention_split(bs, K, seq_max, avg, nkv, L.num_sms())
     if a.chunk:
-        chunk, splits = a.chunk, int(math.ceil((a.seq + K + 1) / a.chunk))
+        chunk, splits = a.chunk, int(math.ceil((seq_max + K + 1) / a.chunk))
     ws = torch.zeros((L.attention_workspace_bytes(bs, K, nq, nkv, splits),), dtype=torch.uint8, device="cuda")
+    order = torch.argsort(seq, descending=True, stable=True).to(torch.int32) if a.mixed else None
     fn = lambda: L.bd_attention(q, kc, vc, pt, seq, bs, K, a.draft, 0 if a.draft else 1, nq, nkv, ps, chunk, splits,
-                                out, ws)
+                                out, ws, order=order)
     ms = _time(fn, a.reps)
     b = attention_bytes(cfg, S, K, 0 if a.draft else 1)
-    return {"kernel": "attention_kernel", "bs": bs, "seq": a.seq, "K": K, "chunk": chunk, "splits": splits, "ms": ms,
+    return {"kernel": "attention_kernel", "bs": bs, "seq": "mixed" if a.mixed else a.seq, "K": K, "chunk": chunk,
+            "splits": splits, "ms": ms,
             "bytes": b, "GBps": b / ms / 1e6}
 
 
@@ -117,6 +125,7 @@ def main():
     at.add_argument("--bd", type=int, default=16)
     at.add_argument("--draft", action="store_true")
     at.add_argument("--chunk", type=int, default=0)
+    at.add_argument("--mixed", action="store_true", help="config-3 prefix lengths instead of --seq")
     at.add_argument("--reps", type=int, default=3)
     li = sub.add_parser("linear")
     li.add_argument("--n-out", type=int, default=9216)

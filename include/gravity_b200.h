@@ -131,6 +131,14 @@ int gr_bd_attention(const void* q, const void* k_cache, const void* v_cache, int
                     int n_kv_heads, int page_size, int chunk, int max_splits, void* out, void* workspace,
                     size_t workspace_bytes, int32_t* status, void* stream);
 
+/* gr_bd_attention with a scheduling order: req_order (int32 [bs], a permutation of 0..bs-1, e.g. longest committed
+ * length first) is the order in which requests' blocks are launched; results do not depend on it. */
+int gr_bd_attention_ordered(const void* q, const void* k_cache, const void* v_cache, int64_t n_pages,
+                            const int32_t* page_table, int pt_stride, const int64_t* seq_lens, const int32_t* req_order,
+                            int bs, int K, int draft, int base_add, int n_q_heads, int n_kv_heads, int page_size,
+                            int chunk, int max_splits, void* out, void* workspace, size_t workspace_bytes,
+                            int32_t* status, void* stream);
+
 /* gr_bd_attention without a caller-provided workspace.  No counterpart in the reference: it exists for callers that
  * cannot allocate device memory -- a host that owns the whole device-memory budget (a serving framework whose
  * allocator accounts for every byte, so a private cudaMalloc would break its bookkeeping or fail under pressure), or

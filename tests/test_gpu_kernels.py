@@ -218,6 +218,13 @@ def test_bd_attention(bs, K, draft):
         torch.cuda.synchronize()
         assert int(st.item()) == 0
         torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=1.5e-2)
+        # a launch order (longest request first) changes scheduling only
+        order = torch.argsort(seq_d, descending=True).to(torch.int32)
+        out2 = torch.full_like(out, float("nan"))
+        L.bd_attention(q, kc, vc, pt_d, seq_d, bs, K, draft, base_add, nq, nkv, ps, chunk, max_splits, out2, ws,
+                       status=st, order=order)
+        torch.cuda.synchronize()
+        assert torch.equal(out2, out)
 
 
 # ---------------------------------------------------------------------- row-wise kernels
