@@ -35,6 +35,9 @@ sys.path.insert(0, ROOT)
 METRIC = "self-spec decode tokens/s & tokens/forward @bs1/bs64, %HBM roofline, 1/2/4/8 B200"
 K_BD = 16
 SEED = 3
+# DRAM bytes / algorithmic bytes of the verify attention on the config-3 mix, from the ncu capture recorded in
+# profiles/attention_kernel_config3_bs64.md (dram__bytes_read + dram__bytes_write of one launch)
+ATTN_TRAFFIC_RATIO = (584.617984e6 + 5.966592e6) / 586.93632e6
 
 
 def _args():
@@ -317,7 +320,8 @@ def main():
                                      "bytes_draft": bd, "bytes_verify": bv},
         "roofline": {"kernel": "attention_kernel (verify, one layer)", "bound": "hbm",
                      "achieved": round(attn_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(attn_gbs / hbm_peak, 4), "traffic": None,
+                     "frac": round(attn_gbs / hbm_peak, 4), "traffic": int(attn_b * ATTN_TRAFFIC_RATIO),
+                     "traffic_source": "ncu dram bytes of the same kernel on the config-3 mix, scaled to this launch",
                      "algorithmic_bytes": attn_b, "avg_launch_ms": round(attn_ms, 5), "peak_source": peak_src},
         "gpu_launches": launches,
         "prefill_s": round(t_pf, 2),
