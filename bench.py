@@ -52,6 +52,8 @@ def _args():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile-small", action="store_true", help="short run for ncu captures (no extras)")
+    ap.add_argument("--config4", action="store_true",
+                    help="config-4 sweep instead: prefix 4096 + 64, B in {4, 8, 16, 32}, batch 1 and 128")
     return ap.parse_args()
 
 
@@ -208,6 +210,8 @@ def main():
     a = _args()
     if a.impl == "reference":
         return run_reference(a)
+    if a.config4:
+        return config4_sweep(a)
     from gravityocr_b200 import _lib as L
     from gravityocr_b200 import dp
     from gravityocr_b200.config import ModelConfig
@@ -331,7 +335,11 @@ def main():
 
     # ---- end to end through the served worker API (rank 0's replica, same batch, from its current state)
     if not a.no_e2e and not a.profile_small:
-        line["e2e"] = e2e_worker(eng, rb, cfg, K, min(a.steps, 50), dev)
+        e2e = e2e_worker(eng, rb, cfg, K, min(a.steps, 50), dev)
+        tok_all = dp.sum_over_ranks(float(e2e.pop("tokens")), dev)
+        ms_max = dp.max_over_ranks(e2e.pop("ms"), dev)
+        e2e["value"] = round(tok_all / (ms_max / 1000.0), 2)
+        line["e2e"] = e2e
 
     if rank == 0 and world == 1 and not a.profile_small:
         if not a.no_bs1:
@@ -387,9 +395,9 @@ def e2e_worker(eng, rb, cfg, K, steps, dev):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
-    return {"value": round(toks / (ms / 1000.0), 2), "unit": "tokens/s", "h2d_bytes_per_step": bs * 8,
+    return {"value": None, "unit": "tokens/s", "h2d_bytes_per_step": bs * 8,
             "d2h_bytes_per_step": int(rb.readback.numel() * 4), "steps": steps,
-            "api": "SelfSpecDiffusionWorker.forward_batch_generation"}
+            "api": "SelfSpecDiffusionWorker.forward_batch_generation", "tokens": toks, "ms": ms}
 
 
 def bs1_crop(eng, cfg, w, K, dev, hbm_peak):
@@ -482,6 +490,72 @@ def bs1_crop(eng, cfg, w, K, dev, hbm_peak):
     eng.pool.release(pages)
     out["workload"] = "config2-bs1-crop (prefix 256 + 32, 1024 tokens), weights of the config-3 replica"
     return out
+
+
+def config4_sweep(a):
+    """Config 4 (full-page long output): prefix 4096 image + 64 prompt tokens, B in {4, 8, 16, 32}, batch 1 and
+    128 on one GPU; steady-state rounds after prefill (each B starts from the same post-prefill state).  Prints one
+    JSON line with tokens/forward and % of the measured HBM roofline per draft and verify forward for each (B, batch).
+    Bounded sample: `--steps` rounds per point instead of the full 4096 generated tokens."""
+    from gravityocr_b200 import dp
+    from gravityocr_b200.config import ModelConfig
+    from gravityocr_b200.engine import Engine
+    from gravityocr_b200.metrics import forward_bytes
+    from gravityocr_b200.weights import random_weights
+    rank, world, local = dp.dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    hbm_peak, _, peak_src = peaks()
+    cfg = ModelConfig()
+    w = random_weights(cfg, 4, torch.bfloat16)
+    P = 4096 + 64
+    steps = max(4, min(a.steps, 40))
+    out = {"metric": METRIC, "config": {"workload": "config4-fullpage-sweep", "prefix": P, "steps_per_point": steps,
+                                        "seed": 4, "peak_gbs": hbm_peak, "peak": peak_src}, "points": []}
+    for bs in (1, 128):
+        cap = P + (a.warmup + steps + 4) * 34 + 2 * 33 + 64
+        ppr = (cap + 15) // 16
+        eng = Engine(cfg, w, max_rows=max(bs * 33, bs * 64), n_pages=bs * ppr + 8, device=dev)
+        rbs = {}
+        pages = [eng.pool.alloc(ppr) for _ in range(bs)]
+        xs, ids = zip(*[request_rows(cfg, w, 4, i, 4096, 64) for i in range(bs)])
+        base = None
+        for B in (4, 8, 16, 32):
+            K = B + 1
+            eng.reserve(bs * K)
+            rb = eng.new_round_buffers(bs, K, ppr, max_len=cap, avg_len=P + 200)
+            for b in range(bs):
+                rb.page_table[b] = torch.tensor(pages[b], dtype=torch.int32, device=dev)
+            if base is None:
+                eng.prefill(rb, list(xs), list(ids))
+                base = (rb.seq_lens.clone(), rb.seeds.clone())
+            rb.seq_lens.copy_(base[0]); rb.seeds.copy_(base[1]); rb.n_committed.fill_(1)
+            eng.refresh_order(rb)
+            eng.round_launch(rb)
+            torch.cuda.synchronize()
+            rb.seq_lens.copy_(base[0]); rb.seeds.copy_(base[1]); rb.n_committed.fill_(1)
+            gd, gv = eng.capture_split(rb)
+            for _ in range(a.warmup):
+                gd.replay(); gv.replay()
+            torch.cuda.synchronize()
+            c0 = rb.n_committed.clone()
+            s0 = rb.seq_lens.cpu().tolist()
+            total, dms, vms = time_graphs(gd, gv, steps)
+            eng.check_status(rb)
+            toks = int((rb.n_committed - c0).sum())
+            s1 = rb.seq_lens.cpu().tolist()
+            mid = [(x + y) / 2 for x, y in zip(s0, s1)]
+            out["points"].append({
+                "B": B, "batch": bs, "tokens_per_s": round(toks / (total / 1000.0), 1),
+                "tokens_per_forward": round(toks / (2 * steps * bs), 4),
+                "draft_ms": round(dms / steps, 4), "verify_ms": round(vms / steps, 4),
+                "hbm_frac_draft": round(forward_bytes(cfg, mid, K, False) / (dms / steps / 1e3) / (hbm_peak * 1e9), 4),
+                "hbm_frac_verify": round(forward_bytes(cfg, mid, K, True) / (vms / steps / 1e3) / (hbm_peak * 1e9), 4)})
+            del gd, gv
+        del eng
+        torch.cuda.empty_cache()
+    print(json.dumps(out), flush=True)
+    return 0
 
 
 if __name__ == "__main__":
