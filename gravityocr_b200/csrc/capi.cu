@@ -79,14 +79,34 @@ static int num_sms() {
 struct LinearShape {
   int nt, m_tiles, n_tiles, kc;
 };
+static int round16(int x) { return ((x + 15) / 16) * 16; }
+
+// Token tiling: among the tile counts whose tile fits one MMA (nt <= GR_MAX_NT), pick the one minimising the critical
+// path of the persistent schedule, (units per CTA, rounded up) x (per-unit cost ~ weight-tile overhead + nt).  Tiles
+// narrower than 128 tokens only where the rows need no more (small batches stream weights: a second token tile
+// would read every weight tile twice).
 static LinearShape linear_shape(int n_out, int k_in, int m) {
   LinearShape s;
-  s.m_tiles = (m + GR_MAX_NT - 1) / GR_MAX_NT;
-  const int per = (m + s.m_tiles - 1) / s.m_tiles;
-  s.nt = ((per + 15) / 16) * 16;
-  if (s.nt < 16) s.nt = 16;
   s.n_tiles = n_out / 128;
   s.kc = k_in / 64;
+  const int min_tiles = (m + GR_MAX_NT - 1) / GR_MAX_NT;
+  const long long cap = num_sms();
+  long long best = -1;
+  s.m_tiles = min_tiles;
+  s.nt = round16((m + min_tiles - 1) / min_tiles);
+  for (int mt = min_tiles; mt <= min_tiles * 4 && mt <= m; ++mt) {
+    const int nt = round16((m + mt - 1) / mt);
+    if (mt > min_tiles && nt < 128) break;
+    const long long units = static_cast<long long>(s.n_tiles) * mt;
+    const long long cost = ((units + cap - 1) / cap) * (64 + nt);
+    if (best < 0 || cost < best) {
+      best = cost;
+      s.m_tiles = mt;
+      s.nt = nt;
+    }
+    if (units >= cap * 4) break;
+  }
+  if (s.nt < 16) s.nt = 16;
   return s;
 }
 
@@ -131,29 +151,26 @@ static int default_splits(const LinearShape& s, int epi, int m) {
 
 struct LinearWs {
   int* ticket;
-  int* arg_ticket;
   float* partial;
-  float* arg;
+  float4* arg;
   size_t bytes;
 };
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // Every call shares one scratch buffer, whatever its shape: the tickets live in a fixed region at its head (so a
 // later call of another shape never finds another call's partial sums where its tickets are), then the fp32
-// split-K partials, then the per-tile argmax records.
-constexpr size_t kMaxTiles = 16384;    // feature tiles x token tiles of one call (lm_head at 8192 rows)
-constexpr size_t kMaxArgTiles = 1024;  // token tiles of one lm_head call
-constexpr size_t kTicketBytes = kMaxTiles * sizeof(int) + kMaxArgTiles * sizeof(int);
+// split-K partials, then the per-(token, feature tile) argmax records.
+constexpr size_t kMaxTiles = 16384;  // feature tiles x token tiles of one call (lm_head at 8192 rows)
+constexpr size_t kTicketBytes = kMaxTiles * sizeof(int);
 static LinearWs linear_ws_layout(void* base, const LinearShape& s, int m, int splits) {
   LinearWs w;
   uint8_t* p = static_cast<uint8_t*>(base);
   const size_t tiles = static_cast<size_t>(s.n_tiles) * s.m_tiles;
   w.ticket = reinterpret_cast<int*>(p);
-  w.arg_ticket = reinterpret_cast<int*>(p + kMaxTiles * sizeof(int));
   size_t off = kTicketBytes;
   w.partial = reinterpret_cast<float*>(p + off);
   off += splits > 1 ? align256(tiles * splits * s.nt * 128 * sizeof(float)) : 0;
-  w.arg = reinterpret_cast<float*>(p + off);
-  off += align256(static_cast<size_t>(s.n_tiles) * m * 3 * sizeof(float));
+  w.arg = reinterpret_cast<float4*>(p + off);
+  off += align256(static_cast<size_t>(s.n_tiles) * m * sizeof(float4));
   w.bytes = off;
   return w;
 }
@@ -211,8 +228,7 @@ int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr
   const int kc = s.kc / splits;
   LinearWs ws = linear_ws_layout(workspace, s, m, static_cast<int>(ws_splits));
   if (!workspace || workspace_bytes < ws.bytes) return GR_ERR_ARG;
-  if (static_cast<size_t>(s.n_tiles) * s.m_tiles > kMaxTiles || static_cast<size_t>(s.m_tiles) > kMaxArgTiles)
-    return GR_ERR_UNSUPPORTED;
+  if (static_cast<size_t>(s.n_tiles) * s.m_tiles > kMaxTiles) return GR_ERR_UNSUPPORTED;
   if (epi->mode == GR_EPI_QKV_ROPE) {
     if (!epi->q_out || !epi->k_cache || !epi->v_cache || !epi->row_pos || !epi->row_slot || !epi->inv_freq ||
         epi->rotary_dim % 32 || epi->rotary_dim > 128 || n_out != (epi->n_q_heads + 2 * epi->n_kv_heads) * 128 ||
@@ -263,13 +279,13 @@ int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr
   p.ws_partial = ws.partial;
   p.ws_ticket = ws.ticket;
   p.ws_arg = ws.arg;
-  p.ws_arg_ticket = ws.arg_ticket;
   p.prefetch = static_cast<const uint8_t*>(prefetch);
   p.prefetch_bytes = prefetch ? prefetch_bytes : 0;
   p.status = status;
   p.rope_cs = reinterpret_cast<const float2*>(epi->rope_cs);
   cudaError_t e = launch_linear(epi->mode, tmw, tmx, p, grid, linear_smem_bytes(s.nt, stages),
                                 static_cast<cudaStream_t>(stream), g_pdl);
+  if (e == cudaSuccess && epi->mode == GR_EPI_ARGMAX) e = launch_argmax_reduce(p, static_cast<cudaStream_t>(stream), g_pdl);
   return e == cudaSuccess ? GR_OK : GR_ERR_CUDA;
 }
 

@@ -11,12 +11,14 @@
 //               kernel drains.
 //   warp 1      allocates TMEM (NT fp32 columns), one thread issues tcgen05.mma (M=128, N=NT, K=16) x 4 per stage,
 //               tcgen05.commit frees the stage and finally signals the accumulator.
-//   warps 2-5   epilogue: tcgen05.ld of their TMEM lane quadrant (lane = output feature, column = token).
+//   warps 2-9   epilogue: tcgen05.ld of their TMEM lane quadrant (lane = output feature, column = token); the two
+//               warps of a quadrant take alternate 16-token chunks.
 // Split-K: each split writes an fp32 partial tile to the workspace; the last CTA of a tile to arrive (atomic ticket)
 // sums the partials in split order (deterministic) and runs the epilogue, then re-arms the ticket for the next launch.
 // Epilogues: fp32 / bf16 store, SwiGLU (gate and up rows interleaved per 64 features by the host), Q/K/V with
 // interleaved-pair partial RoPE and the paged K/V cache write, and lm_head's vocab-wide argmax (top-1 index, top-1
-// value and top-2 gap; logits are never written).
+// value and top-2 gap; logits are never written): each feature tile leaves one top-2 record per token and
+// argmax_reduce_kernel, launched right after, reduces a token's records with one warp.
 #include "params.cuh"
 
 namespace gr {
@@ -160,44 +162,39 @@ __device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, in
       x = top2_merge(x, y);
     }
     const int t = t0 + tok;
-    if (part == 0 && t < t_end) {
-      float* dst = p.ws_arg + ((size_t)n_tile * p.m + t) * 3;
-      dst[0] = x.v1;
-      dst[1] = __int_as_float(x.i1);
-      dst[2] = x.v2;
-    }
+    if (part == 0 && t < t_end)
+      p.ws_arg[(size_t)t * p.n_tiles + n_tile] = make_float4(x.v1, __int_as_float(x.i1), x.v2, 0.f);
     half_bar(half);
   }
 }
 
-// lm_head: after every feature tile of a token tile has written its per-token top-2, the last one reduces them.
-__device__ void argmax_finish(const LinearParams& p, int m_tile, int* flag) {
-  __threadfence();
-  epi_bar();
-  if (threadIdx.x == 64) {
-    const int prev = atomicAdd(&p.ws_arg_ticket[m_tile], 1);
-    *flag = (prev == p.n_tiles - 1);
-  }
-  epi_bar();
-  if (!*flag) return;
-  __threadfence();
-  const int warp = (threadIdx.x >> 5) - 2, lane = threadIdx.x & 31;
-  const int t_beg = m_tile * p.nt, t_end = min(p.m, t_beg + p.nt);
-  for (int t = t_beg + warp; t < t_end; t += 8) {
-    Top2 x{-INFINITY, 0x7fffffff, -INFINITY};
-    for (int n = lane; n < p.n_tiles; n += 32) {
-      const float* s = p.ws_arg + ((size_t)n * p.m + t) * 3;
-      Top2 y{__ldcg(s), __float_as_int(__ldcg(s + 1)), __ldcg(s + 2)};
-      x = top2_merge(x, y);
+// lm_head, second step: one warp per token merges the token's n_tiles top-2 records (ties: lowest vocab index).  The
+// records of a token are contiguous; every lane issues all its loads before merging (up to 16 x 16 B in flight).
+constexpr int kReduceWarps = 8;
+__global__ void __launch_bounds__(kReduceWarps * 32) argmax_reduce_kernel(const LinearParams p) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x * kReduceWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= p.m) return;
+  const float4* rec = p.ws_arg + (size_t)t * p.n_tiles;
+  Top2 x{-INFINITY, 0x7fffffff, -INFINITY};
+  for (int n0 = 0; n0 < p.n_tiles; n0 += 32 * 16) {
+    float4 r[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = n0 + j * 32 + lane;
+      r[j] = n < p.n_tiles ? __ldcg(rec + n) : make_float4(-INFINITY, __int_as_float(0x7fffffff), -INFINITY, 0.f);
     }
-    x = top2_warp(x);
-    if (lane == 0) {
-      p.out_idx[t] = x.i1;
-      if (p.out_top1) p.out_top1[t] = x.v1;
-      if (p.out_gap) p.out_gap[t] = x.v1 - x.v2;
-    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) x = top2_merge(x, Top2{r[j].x, __float_as_int(r[j].y), r[j].z});
   }
-  if (threadIdx.x == 64) p.ws_arg_ticket[m_tile] = 0;
+  x = top2_warp(x);
+  if (lane == 0) {
+    p.out_idx[t] = x.i1;
+    if (p.out_top1) p.out_top1[t] = x.v1;
+    if (p.out_gap) p.out_gap[t] = x.v1 - x.v2;
+  }
 }
 
 template <int EPI>
@@ -219,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + S;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] abort, [1] last split, [2] last argmax tile
+  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] abort, [1] last split
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kc = p.kc_per_split;
@@ -237,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(acc_full + b, 1);
       mbar_init(acc_empty + b, 8);  // one arrival per epilogue warp
     }
-    flags[0] = flags[1] = flags[2] = 0;
+    flags[0] = flags[1] = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmw);
     tma_prefetch_desc(&tmx);
@@ -407,9 +404,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (threadIdx.x == 64) p.ws_ticket[tile] = 0;
         }
       }
-      if constexpr (EPI == GR_EPI_ARGMAX) {
-        if (p.splits == 1 || flags[1]) argmax_finish(p, m_tile, &flags[2]);
-      }
       epi_bar();  // flags / scratch are reused by the next unit
     }
   }
@@ -450,6 +444,19 @@ cudaError_t launch_linear_t(const CUtensorMap& tmw, const CUtensorMap& tmx, cons
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, tmw, tmx, p);
+}
+
+cudaError_t launch_argmax_reduce(const LinearParams& p, cudaStream_t stream, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((p.m + kReduceWarps - 1) / kReduceWarps);
+  cfg.blockDim = dim3(kReduceWarps * 32);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, argmax_reduce_kernel, p);
 }
 
 cudaError_t launch_linear(int epi, const CUtensorMap& tmw, const CUtensorMap& tmx, const LinearParams& p, int grid,

@@ -21,8 +21,7 @@ struct LinearParams {
   float* out_gap;
   float* ws_partial;
   int* ws_ticket;
-  float* ws_arg;
-  int* ws_arg_ticket;
+  float4* ws_arg;  // lm_head: per (token, feature tile) top-2 record {v1, i1 bits, v2, 0}, token-major
   const uint8_t* prefetch;
   unsigned long long prefetch_bytes;
   int* status;
@@ -104,6 +103,7 @@ struct OverrideParams {
 size_t linear_smem_bytes(int nt, int stages);
 cudaError_t launch_linear(int epi, const CUtensorMap& tmw, const CUtensorMap& tmx, const LinearParams& p, int grid,
                           size_t smem, cudaStream_t stream, bool pdl);
+cudaError_t launch_argmax_reduce(const LinearParams& p, cudaStream_t stream, bool pdl);
 size_t attention_smem_bytes(int K, int G);
 cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p, cudaStream_t stream,
                              bool pdl);

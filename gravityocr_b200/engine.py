@@ -414,8 +414,9 @@ class Engine:
         self.verify_launch(rb)
 
     def kernels_per_forward(self) -> int:
-        """Kernel launches of one forward: embed + per layer (4 projections, attention, 2 residual norms) + lm_head."""
-        return 2 + 7 * self.cfg.n_layers
+        """Kernel launches of one forward: embed + per layer (4 projections, attention, 2 residual norms) + lm_head
+        (projection + per-token argmax reduction)."""
+        return 3 + 7 * self.cfg.n_layers
 
     def capture(self, rb: RoundBuffers, override: bool = False, warmup: int = 0) -> torch.cuda.CUDAGraph:
         """Capture one round (both forwards and the commit) into a CUDA graph; replays read the device-resident
