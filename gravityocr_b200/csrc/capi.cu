@@ -405,7 +405,6 @@ int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr
   p.prefetch = static_cast<const uint8_t*>(prefetch);
   p.prefetch_bytes = prefetch ? prefetch_bytes : 0;
   p.status = status;
-  p.rope_cs = reinterpret_cast<const float2*>(epi->rope_cs);
   cudaError_t e = pair ? launch_linear_pair(epi->mode, tmw, tmx, p, grid, linear_smem_bytes(x_rows, stages),
                                             static_cast<cudaStream_t>(stream), g_pdl)
                        : launch_linear(epi->mode, tmw, tmx, p, grid, linear_smem_bytes(x_rows, stages),
@@ -489,8 +488,7 @@ int gr_embed_rows(int mode, int bs, int K, const int64_t* seeds, const int64_t* 
                   const int64_t* ids64, const float* row_embeds, const int64_t* seq_lens, const int32_t* page_table,
                   int pt_stride, int page_size, int pages_per_req, const void* embed, int vocab, int mask_id,
                   const void* norm_w, float eps, int hidden, float* h_out, void* x_out, int32_t* row_pos,
-                  int64_t* row_slot, int32_t* row_ids, const float* inv_freq, int rotary_dim, float* rope_cs,
-                  int32_t* status, void* stream) {
+                  int64_t* row_slot, int32_t* row_ids, int32_t* status, void* stream) {
   if (bs <= 0 || K <= 0 || !seq_lens || !page_table || !embed || !norm_w || !h_out || !x_out || !row_pos || !row_slot)
     return GR_ERR_ARG;
   if (hidden <= 0 || hidden % 8 || page_size <= 0 || pages_per_req <= 0) return GR_ERR_ARG;
@@ -498,7 +496,6 @@ int gr_embed_rows(int mode, int bs, int K, const int64_t* seeds, const int64_t* 
   if (mode == GR_ROWS_VERIFY && !ids32) return GR_ERR_ARG;
   if (mode == GR_ROWS_EXPLICIT && !ids64) return GR_ERR_ARG;
   if (mode < GR_ROWS_DRAFT || mode > GR_ROWS_EXPLICIT) return GR_ERR_ARG;
-  if (rope_cs && (!inv_freq || rotary_dim <= 0 || rotary_dim % 2 || rotary_dim / 2 > 192)) return GR_ERR_ARG;
   EmbedParams p;
   std::memset(&p, 0, sizeof(p));
   p.mode = mode;
@@ -526,9 +523,6 @@ int gr_embed_rows(int mode, int bs, int K, const int64_t* seeds, const int64_t* 
   p.row_slot = row_slot;
   p.row_ids = row_ids;
   p.status = status;
-  p.inv_freq = inv_freq;
-  p.rotary_dim = rotary_dim;
-  p.rope_cs = reinterpret_cast<float2*>(rope_cs);
   return launch_embed_rows(p, static_cast<cudaStream_t>(stream), g_pdl) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
 }
 

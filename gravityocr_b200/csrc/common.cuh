@@ -324,6 +324,32 @@ __device__ __forceinline__ uint32_t sw128(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
+// ------------------------------------------------------------------ RoPE angles
+// sin and cos of an fp32 angle, |x| < 2^22, to about 1 ulp absolute, in registers (no table, no local memory):
+// Cody-Waite reduction by pi/2 with a three-part split of pi/2 (each product subtracted by one fma), then the Taylor
+// series of sin (to r^9) and cos (to r^10) on |r| <= pi/4, whose truncation error is below 2e-9.
+__device__ __forceinline__ void rope_sincos(float x, float* s_out, float* c_out) {
+  const float q = rintf(x * 0.636619747f);  // x * 2/pi
+  float r = fmaf(q, -1.57079637f, x);       // pi/2 = 1.57079637f - 4.37113883e-8f - 1.71512451e-15f
+  r = fmaf(q, 4.37113883e-8f, r);
+  r = fmaf(q, 1.71512451e-15f, r);
+  const float r2 = r * r;
+  float ps = fmaf(r2, 2.75573188e-6f, -1.98412701e-4f);  // 1/9!, -1/7!
+  ps = fmaf(r2, ps, 8.33333377e-3f);                        // 1/5!
+  ps = fmaf(r2, ps, -0.166666672f);                         // -1/3!
+  const float sn = fmaf(r2 * r, ps, r);
+  float pc = fmaf(r2, -2.75573200e-7f, 2.48015876e-5f);   // -1/10!, 1/8!
+  pc = fmaf(r2, pc, -1.38888892e-3f);                       // -1/6!
+  pc = fmaf(r2, pc, 4.16666679e-2f);                        // 1/4!
+  pc = fmaf(r2, pc, -0.5f);                                 // -1/2!
+  const float cs = fmaf(r2, pc, 1.0f);
+  const int qi = static_cast<int>(q) & 3;
+  const float s1 = (qi & 1) ? cs : sn;
+  const float c1 = (qi & 1) ? sn : cs;
+  *s_out = (qi & 2) ? -s1 : s1;
+  *c_out = ((qi + 1) & 2) ? -c1 : c1;
+}
+
 // ------------------------------------------------------------------ misc
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

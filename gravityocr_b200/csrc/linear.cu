@@ -109,40 +109,40 @@ __device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, in
     const bool is_q = head < p.n_q_heads;
     const bool is_v = head >= p.n_q_heads + p.n_kv_heads;
     const bool rot = !is_v && (d & ~31) < p.rotary_dim;  // warp-uniform: rotary_dim is a multiple of 32
+    // The chunk's 16 positions / cache slots take one coalesced load per warp (lanes l and l + 16 fetch token l) and
+    // reach every lane by shuffles; cos / sin are computed in registers.  Per-token loads here would share the SM's
+    // L1 / shared-memory bandwidth with the tensor core's operand reads of the next unit.
+    const int tl = min(t0 + (lane & 15), t_end - 1);
     float o[16];
     if (rot) {
-      const int half = p.rotary_dim >> 1;
+      const int pos_l = p.row_pos[tl];
+      const float fr = p.inv_freq[d >> 1];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const float partner = __shfl_xor_sync(0xffffffffu, v[i], 1);
-        const int t = min(t0 + i, t_end - 1);
-        float s, c;
-        if (p.rope_cs) {
-          const float2 cs = p.rope_cs[(size_t)t * half + (d >> 1)];
-          c = cs.x;
-          s = cs.y;
-        } else {
-          sincosf(static_cast<float>(p.row_pos[t]) * p.inv_freq[d >> 1], &s, &c);
-        }
-        o[i] = (d & 1) ? (v[i] * c + partner * s) : (v[i] * c - partner * s);
+        const int pos = __shfl_sync(0xffffffffu, pos_l, i);
+        float sn, cs;
+        rope_sincos(__fmul_rn(static_cast<float>(pos), fr), &sn, &cs);  // the reference's fp32 pos * inv_freq
+        o[i] = (d & 1) ? (v[i] * cs + partner * sn) : (v[i] * cs - partner * sn);
       }
     } else {
 #pragma unroll
       for (int i = 0; i < 16; ++i) o[i] = v[i];
     }
+    if (is_q) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int t = t0 + i;
-      if (t >= t_end) continue;
-      const __nv_bfloat16 b = __float2bfloat16_rn(o[i]);
-      if (is_q) {
-        p.q_out[(size_t)t * (p.n_q_heads * 128) + head * 128 + d] = b;
-      } else {
-        // page size 16 (the host checks): page = slot >> 4, offset = slot & 15
-        const int kvh = is_v ? head - p.n_q_heads - p.n_kv_heads : head - p.n_q_heads;
-        const uint64_t slot = static_cast<uint64_t>(p.row_slot[t]);
-        const size_t idx = ((((slot >> 4) * p.n_kv_heads + kvh) << 4) + (slot & 15)) * 128 + d;
-        (is_v ? p.v_cache : p.k_cache)[idx] = b;
+      for (int i = 0; i < 16; ++i)
+        if (t0 + i < t_end) p.q_out[(size_t)(t0 + i) * (p.n_q_heads * 128) + head * 128 + d] = __float2bfloat16_rn(o[i]);
+    } else {
+      // page size 16 (the host checks): page = slot >> 4, offset = slot & 15
+      const int kvh = is_v ? head - p.n_q_heads - p.n_kv_heads : head - p.n_q_heads;
+      __nv_bfloat16* cache = is_v ? p.v_cache : p.k_cache;
+      const long long slot_l = p.row_slot[tl];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint64_t slot = static_cast<uint64_t>(__shfl_sync(0xffffffffu, slot_l, i));
+        if (t0 + i < t_end)
+          cache[((((slot >> 4) * p.n_kv_heads + kvh) << 4) + (slot & 15)) * 128 + d] = __float2bfloat16_rn(o[i]);
       }
     }
   } else if constexpr (EPI == GR_EPI_ARGMAX) {

@@ -25,7 +25,6 @@ struct LinearParams {
   const uint8_t* prefetch;
   unsigned long long prefetch_bytes;
   int* status;
-  const float2* rope_cs;
 };
 struct AttnParams {
   const __nv_bfloat16* q;
@@ -61,9 +60,6 @@ struct EmbedParams {
   int64_t* row_slot;
   int32_t* row_ids;
   int32_t* status;
-  const float* inv_freq;
-  int rotary_dim;
-  float2* rope_cs;
 };
 struct ResNormParams {
   int m, hidden, y_parts;

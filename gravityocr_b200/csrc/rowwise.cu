@@ -59,12 +59,6 @@ __global__ void __launch_bounds__(kRowThreads) embed_rows_kernel(const EmbedPara
     s_pos = static_cast<int>(pos);
   }
   __syncthreads();
-  if (p.rope_cs && threadIdx.x < (p.rotary_dim >> 1)) {
-    // RoPE table of this row: the same fp32 product pos * inv_freq[i] as transformers, then accurate sincos
-    float s, c;
-    sincosf(static_cast<float>(s_pos) * p.inv_freq[threadIdx.x], &s, &c);
-    p.rope_cs[(size_t)t * (p.rotary_dim >> 1) + threadIdx.x] = make_float2(c, s);
-  }
   const int64_t id = s_id;
   float v[8];
   float ss = 0.f;

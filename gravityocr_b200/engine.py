@@ -171,7 +171,6 @@ class Engine:
         self.row_pos = torch.zeros((max_rows,), dtype=torch.int32, device=dev)
         self.row_slot = torch.zeros((max_rows,), dtype=torch.int64, device=dev)
         self.row_ids = torch.zeros((max_rows,), dtype=torch.int32, device=dev)
-        self.rope_cs = torch.zeros((max_rows, cfg.rotary_dim // 2, 2), dtype=torch.float32, device=dev)
         self.status = torch.zeros((4,), dtype=torch.int32, device=dev)
         self.lin_ws = torch.zeros((self.linear_ws_bytes(max_rows),), dtype=torch.uint8, device=dev)
         self.attn_ws: Optional[torch.Tensor] = None
@@ -234,8 +233,7 @@ class Engine:
         L.embed_rows(rows_mode, bs, K, seeds=seeds, rpi=rpi, ids32=ids32, ids64=ids64, row_embeds=row_embeds,
                      seq_lens=seq_lens, page_table=page_table, page_size=self.page_size, embed=w.embed, vocab=cfg.vocab,
                      mask_id=cfg.mask_id, norm_w=w.layers[0]["in"], eps=cfg.rms_eps, h_out=self.h[0], x_out=self.x,
-                     row_pos=self.row_pos, row_slot=self.row_slot, row_ids=self.row_ids, inv_freq=w.inv_freq,
-                     rotary_dim=cfg.rotary_dim, rope_cs=self.rope_cs, status=st)
+                     row_pos=self.row_pos, row_slot=self.row_slot, row_ids=self.row_ids, status=st)
         ws_attn = self._attn_workspace(bs, K, attn_splits) if attn_splits > 1 else None
         cur = 0
         for l, d in enumerate(w.layers):
@@ -252,7 +250,6 @@ class Engine:
             e.n_q_heads = cfg.n_q_heads
             e.n_kv_heads = cfg.n_kv_heads
             e.page_size = self.page_size
-            e.rope_cs = self.rope_cs.data_ptr()
             L.linear(d["qkv"], self.x, M, e, self.lin_ws, prefetch=d["o"], status=st)
             L.bd_attention(self.q, self.pool.k[l], self.pool.v[l], page_table, seq_lens, bs, K, draft, base_add,
                            cfg.n_q_heads, cfg.n_kv_heads, self.page_size, attn_chunk, attn_splits, self.attn, ws_attn,

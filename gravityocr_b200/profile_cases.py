@@ -103,10 +103,7 @@ def case_linear(a):
         e.q_out, e.k_cache, e.v_cache = q.data_ptr(), kc.data_ptr(), vc.data_ptr()
         e.row_pos, e.row_slot, e.inv_freq = pos.data_ptr(), slot.data_ptr(), inv.data_ptr()
         e.rotary_dim, e.n_q_heads, e.n_kv_heads, e.page_size = cfg.rotary_dim, cfg.n_q_heads, cfg.n_kv_heads, 16
-        f = pos.float()[:, None] * inv[None, :]
-        cs = torch.stack([f.cos(), f.sin()], -1).contiguous()  # the per-row table gr_embed_rows writes
-        e.rope_cs = cs.data_ptr()
-        keep += [q, kc, vc, pos, slot, inv, cs]
+        keep += [q, kc, vc, pos, slot, inv]
     ws_sp = 1 if mode == L.EPI_PARTIAL_F32 else sp
     ws = torch.zeros((L.linear_workspace_bytes(n_out, m, ws_sp),), dtype=torch.uint8, device="cuda")
     ms = _time(lambda: L.linear(w, x, m, e, ws, splits=sp), a.reps)

@@ -64,9 +64,6 @@ typedef struct gr_epilogue {
   int32_t* out_idx;       /* [M] */
   float* out_top1;        /* [M] or NULL */
   float* out_gap;         /* [M] top-1 minus top-2 logit, or NULL */
-  /* QKV_ROPE: optional per-row (cos, sin) table [M][rotary_dim / 2] from gr_embed_rows; NULL = compute from
-   * row_pos and inv_freq */
-  const float* rope_cs;
 } gr_epilogue;
 
 /* Library identity / diagnostics. */
@@ -98,8 +95,7 @@ int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr
               void* stream);
 
 /* Layer-0 input rows of a forward and the window plan: for each row its token id, RoPE position and cache slot;
- * h_out[t] = embedding row (fp32), x_out[t] = RMSNorm(h_out[t]) * norm_w (bf16); when rope_cs != NULL also the row's
- * RoPE table rope_cs[t][i] = (cos, sin)(pos * inv_freq[i]), i < rotary_dim / 2, shared by every layer's QKV epilogue.
+ * h_out[t] = embedding row (fp32), x_out[t] = RMSNorm(h_out[t]) * norm_w (bf16).
  * Replaces the draft window build of selfspec_diffusion_worker.py:689-706 (_draft_block: [seed | mask x (K-1)],
  * positions seq_lens + j), the verify ids/positions of :849-884 (_fulldraft_verify: am[:, :K], seq_lens + 1 + j),
  * the embedding lookup with image-embedding injection of src/fast_sampling.py:483-488, and the first
@@ -108,8 +104,7 @@ int gr_embed_rows(int mode, int bs, int K, const int64_t* seeds, const int64_t* 
                   const int64_t* ids64, const float* row_embeds, const int64_t* seq_lens, const int32_t* page_table,
                   int pt_stride, int page_size, int pages_per_req, const void* embed, int vocab, int mask_id,
                   const void* norm_w, float eps, int hidden, float* h_out, void* x_out, int32_t* row_pos,
-                  int64_t* row_slot, int32_t* row_ids, const float* inv_freq, int rotary_dim, float* rope_cs,
-                  int32_t* status, void* stream);
+                  int64_t* row_slot, int32_t* row_ids, int32_t* status, void* stream);
 
 /* Sandwich-norm step: h_out = h_in + w_a * RMSNorm(y); x_out = w_b * RMSNorm(h_out) (bf16).  y may arrive as
  * y_parts split-K partials (y[p * m * hidden + t * hidden + f], summed in order p = 0, 1, ...).  The decoder layer's
