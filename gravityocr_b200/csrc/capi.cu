@@ -113,108 +113,16 @@ static LinearShape linear_shape(int n_out, int k_in, int m) {
 static int acc_cols_for(int nt) { return nt <= 32 ? 32 : (nt <= 64 ? 64 : (nt <= 128 ? 128 : 256)); }
 
 // Pipeline depth and resident CTAs of the persistent projection kernel for a token tile of nt rows.
-static void linear_launch_shape(int nt, int kc, int* stages, int* ctas_per_sm) {
+static void linear_launch_shape(int nt, int kc, int epi, int* stages, int* ctas_per_sm) {
+  const size_t cap = 220 * 1024;
   int st = GR_MAX_STAGES;
-  while (st > 2 && linear_smem_bytes(nt, st) > 220 * 1024) --st;
+  while (st > 2 && linear_smem_bytes(nt, st, epi) > cap) --st;
   if (st > kc) st = kc < 2 ? 2 : kc;
-  while (st > 1 && linear_smem_bytes(nt, st) > 220 * 1024) --st;
-  const int by_smem = static_cast<int>(233472 / (linear_smem_bytes(nt, st) + 1024));
+  while (st > 1 && linear_smem_bytes(nt, st, epi) > cap) --st;
+  const int by_smem = static_cast<int>(233472 / (linear_smem_bytes(nt, st, epi) + 1024));
   const int by_tmem = 512 / (2 * acc_cols_for(nt));
   *stages = st;
   *ctas_per_sm = by_smem < by_tmem ? (by_smem < 1 ? 1 : by_smem) : by_tmem;
-}
-
-// ------------------------------------------------------------------ CTA-pair projections (large token counts)
-// GR_LINEAR_PAIR: 0 = never, 1 = where the token tile is at least 128 rows (the single-CTA kernel is then bound by
-// its per-SM operand stream), 2 = wherever the shape allows.
-#ifndef GR_LINEAR_PAIR
-#define GR_LINEAR_PAIR 1
-#endif
-static int round32(int x) { return ((x + 31) / 32) * 32; }
-
-static int pair_clusters(size_t smem) {
-  static std::mutex mu;
-  static size_t keys[16];
-  static int vals[16];
-  static int n = 0;
-  std::lock_guard<std::mutex> lock(mu);
-  for (int i = 0; i < n; ++i)
-    if (keys[i] == smem) return vals[i];
-  int c = linear_pair_max_clusters(smem);
-  if (c <= 0) c = num_sms() / 2;
-  if (n < 16) {
-    keys[n] = smem;
-    vals[n++] = c;
-  }
-  return c;
-}
-
-// Token tiling of the pair kernel: tiles of a multiple of 32 rows (16 per CTA), same cost model as linear_shape over
-// the pairs the device holds at once.
-static LinearShape pair_shape(int n_out, int k_in, int m, int pairs) {
-  LinearShape s;
-  s.n_tiles = n_out / 128;
-  s.kc = k_in / 64;
-  const int min_tiles = (m + 255) / 256;
-  s.m_tiles = min_tiles;
-  s.nt = round32((m + min_tiles - 1) / min_tiles);
-  long long best = -1;
-  for (int mt = min_tiles; mt <= min_tiles * 4 && mt <= m; ++mt) {
-    const int nt = round32((m + mt - 1) / mt);
-    if (mt > min_tiles && nt < 128) break;
-    const long long units = static_cast<long long>(s.n_tiles / 2) * mt;
-    const long long cost = ((units + pairs - 1) / pairs) * (64 + nt);
-    if (best < 0 || cost < best) {
-      best = cost;
-      s.m_tiles = mt;
-      s.nt = nt;
-    }
-    if (units >= 4ll * pairs) break;
-  }
-  return s;
-}
-
-static bool pair_eligible(int n_out, int m) {
-  if (GR_LINEAR_PAIR == 0 || n_out % 256) return false;
-  if (GR_LINEAR_PAIR == 2) return m >= 32;
-  return linear_shape(n_out, 64, m).nt >= 128;
-}
-
-static void pair_launch_shape(int nt, int kc, int* stages) {
-  int st = GR_MAX_STAGES;
-  while (st > 2 && linear_smem_bytes(nt / 2, st) > 220 * 1024) --st;
-  if (st > kc) st = kc < 2 ? 2 : kc;
-  *stages = st;
-}
-
-// Split-K of the pair kernel (PARTIAL_F32 only: each split writes its own slice, no tickets).
-static int pair_default_splits(const LinearShape& s, int epi, int pairs, int m) {
-  if (epi != GR_EPI_PARTIAL_F32 && epi != -1) return 1;
-  const long long units = static_cast<long long>(s.n_tiles / 2) * s.m_tiles;
-  if (units >= pairs) return 1;
-  int best = 1;
-  long long best_cost = ((units + pairs - 1) / pairs) * s.kc;
-  for (int sp = 2; sp <= s.kc / 2; ++sp) {
-    if (s.kc % sp) continue;
-    if (static_cast<double>(sp) * m * s.n_tiles * 128 * 4 > 32.0 * (1 << 20)) break;
-    const long long u = units * sp;
-    const long long cost = ((u + pairs - 1) / pairs) * (s.kc / sp);
-    if (cost < best_cost) {
-      best_cost = cost;
-      best = sp;
-    }
-  }
-  return best;
-}
-
-static int pair_clusters_for(int n_out, int k_in, int m, LinearShape* ps, int* stages) {
-  // the stage count and so the shared memory depend on the tile; the tile on the pairs: settle with the widest tile
-  int st;
-  pair_launch_shape(256, k_in / 64, &st);
-  const int pairs = pair_clusters(linear_smem_bytes(128, st));
-  *ps = pair_shape(n_out, k_in, m, pairs);
-  pair_launch_shape(ps->nt, ps->kc, stages);
-  return pair_clusters(linear_smem_bytes(ps->nt / 2, *stages));
 }
 
 // Split-K count for the persistent schedule: minimise (units per CTA, rounded up) x (K chunks per unit); ties go to
@@ -222,7 +130,7 @@ static int pair_clusters_for(int n_out, int k_in, int m, LinearShape* ps, int* s
 static int default_splits(const LinearShape& s, int epi, int m) {
   if (epi == GR_EPI_ARGMAX) return 1;
   int stages, per_sm;
-  linear_launch_shape(s.nt, s.kc, &stages, &per_sm);
+  linear_launch_shape(s.nt, s.kc, epi, &stages, &per_sm);
   const long long cap = static_cast<long long>(num_sms()) * per_sm;
   const long long units = static_cast<long long>(s.n_tiles) * s.m_tiles;
   if (units >= cap) return 1;  // the grid is already full: split partials would only add traffic
@@ -299,12 +207,6 @@ int gr_num_sms(void) { return num_sms(); }
 
 int gr_linear_default_splits(int n_out, int k_in, int m) {
   if (n_out <= 0 || k_in <= 0 || m <= 0 || (k_in % 64)) return 1;
-  if (pair_eligible(n_out, m)) {
-    LinearShape ps;
-    int st;
-    const int pairs = pair_clusters_for(n_out, k_in, m, &ps, &st);
-    return pair_default_splits(ps, -1, pairs, m);
-  }
   return default_splits(linear_shape(n_out, k_in, m), GR_EPI_STORE_F32, m);
 }
 
@@ -321,26 +223,11 @@ int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr
   if (!w || !x || !epi || m <= 0 || n_out <= 0 || (n_out % 128) || k_in <= 0 || (k_in % 64)) return GR_ERR_ARG;
   if (epi->mode < GR_EPI_STORE_F32 || epi->mode > GR_EPI_PARTIAL_F32) return GR_ERR_ARG;
   LinearShape s = linear_shape(n_out, k_in, m);
-  // the workspace layout always follows the single-CTA tiling (gr_linear_workspace_bytes sizes it so)
-  const LinearShape s_ws = s;
-  bool pair = pair_eligible(n_out, m);
-  int pair_stages = 0, pairs = 0;
-  if (pair) {
-    LinearShape ps;
-    pairs = pair_clusters_for(n_out, k_in, m, &ps, &pair_stages);
-    const int sp = splits > 0 ? splits : pair_default_splits(ps, epi->mode, pairs, m);
-    if (sp == 1 || epi->mode == GR_EPI_PARTIAL_F32) {
-      s = ps;
-      splits = sp;
-    } else {
-      pair = false;  // split-K with a ticketed reduction: single-CTA kernel
-    }
-  }
   if (splits <= 0) splits = default_splits(s, epi->mode, m);
   if (s.kc % splits) return GR_ERR_ARG;
-  const size_t ws_splits = (pair || epi->mode == GR_EPI_PARTIAL_F32) ? 1 : static_cast<size_t>(splits);
+  const size_t ws_splits = epi->mode == GR_EPI_PARTIAL_F32 ? 1 : static_cast<size_t>(splits);
   const int kc = s.kc / splits;
-  LinearWs ws = linear_ws_layout(workspace, s_ws, m, static_cast<int>(ws_splits));
+  LinearWs ws = linear_ws_layout(workspace, s, m, static_cast<int>(ws_splits));
   if (!workspace || workspace_bytes < ws.bytes) return GR_ERR_ARG;
   if (static_cast<size_t>(s.n_tiles) * s.m_tiles > kMaxTiles) return GR_ERR_UNSUPPORTED;
   if (epi->mode == GR_EPI_QKV_ROPE) {
@@ -353,25 +240,16 @@ int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr
   } else if (!epi->out || epi->ld_out <= 0) {
     return GR_ERR_ARG;
   }
-  // persistent grid: every resident CTA (pair) walks units c, c + grid, ...
-  int stages, grid;
-  if (pair) {
-    const int units = (s.n_tiles / 2) * s.m_tiles * splits;
-    stages = pair_stages;
-    if (stages > kc) stages = kc < 2 ? 2 : kc;
-    grid = 2 * (units < pairs ? units : pairs);
-  } else {
-    const int units = s.n_tiles * s.m_tiles * splits;
-    int per_sm;
-    linear_launch_shape(s.nt, kc, &stages, &per_sm);
-    const int cap = num_sms() * per_sm;
-    grid = units < cap ? units : cap;
-  }
-  const int x_rows = pair ? s.nt / 2 : s.nt;
+  // persistent grid: every resident CTA walks units c, c + grid, ...
+  const int units = s.n_tiles * s.m_tiles * splits;
+  int stages, per_sm;
+  linear_launch_shape(s.nt, kc, epi->mode, &stages, &per_sm);
+  const int cap = num_sms() * per_sm;
+  const int grid = units < cap ? units : cap;
   CUtensorMap tmw, tmx;
   int rc = tensor_map_2d(w, static_cast<uint64_t>(n_out), static_cast<uint64_t>(k_in), 128, 64, &tmw);
   if (rc) return rc;
-  rc = tensor_map_2d(x, static_cast<uint64_t>(m), static_cast<uint64_t>(k_in), static_cast<uint32_t>(x_rows), 64, &tmx);
+  rc = tensor_map_2d(x, static_cast<uint64_t>(m), static_cast<uint64_t>(k_in), static_cast<uint32_t>(s.nt), 64, &tmx);
   if (rc) return rc;
   LinearParams p;
   std::memset(&p, 0, sizeof(p));
@@ -405,10 +283,8 @@ int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr
   p.prefetch = static_cast<const uint8_t*>(prefetch);
   p.prefetch_bytes = prefetch ? prefetch_bytes : 0;
   p.status = status;
-  cudaError_t e = pair ? launch_linear_pair(epi->mode, tmw, tmx, p, grid, linear_smem_bytes(x_rows, stages),
-                                            static_cast<cudaStream_t>(stream), g_pdl)
-                       : launch_linear(epi->mode, tmw, tmx, p, grid, linear_smem_bytes(x_rows, stages),
-                                       static_cast<cudaStream_t>(stream), g_pdl);
+  cudaError_t e = launch_linear(epi->mode, tmw, tmx, p, grid, linear_smem_bytes(s.nt, stages, epi->mode),
+                                static_cast<cudaStream_t>(stream), g_pdl);
   if (e == cudaSuccess && epi->mode == GR_EPI_ARGMAX) e = launch_argmax_reduce(p, static_cast<cudaStream_t>(stream), g_pdl);
   return e == cudaSuccess ? GR_OK : GR_ERR_CUDA;
 }

@@ -25,9 +25,6 @@
 #ifndef GR_MAX_NT
 #define GR_MAX_NT 256       // widest token tile (MMA N)
 #endif
-#ifndef GR_SPIN_WAIT
-#define GR_SPIN_WAIT 0      // projection producer / MMA loops poll their stage barriers without suspending
-#endif
 
 namespace gr {
 
@@ -73,33 +70,6 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
-}
-// Non-suspending probe (mbarrier.test_wait): for the single-thread producer / MMA loops, where a suspended thread's
-// wake-up latency would stall the pipeline.
-__device__ __forceinline__ bool mbar_probe(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded spin on mbar_probe.  Returns false (and records `code`) on timeout.
-__device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity, int* status, int code) {
-  if (mbar_probe(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 64; ++i)
-      if (mbar_probe(bar, parity)) return true;
-    if (globaltimer() - t0 > GR_WAIT_NS) {
-      report(status, code);
-      return false;
-    }
-  }
 }
 // Bounded wait for the phase with the given parity to complete.  Returns false (and records `code`) on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
@@ -197,6 +167,23 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Split form for software pipelining: issue a 16-column load, later wait for it.  The wait names the destination
+// registers as operands so that no use of them can be scheduled before it.
+__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld16_wait(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+
 // Shared-memory matrix descriptor, K-major operand in the 128-byte-swizzle canonical layout (8 rows x 128 B atoms,
 // 1024 B between 8-row groups), sm100 descriptor version 1.  `addr` is the shared-space byte address.
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
@@ -212,88 +199,6 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
          (static_cast<uint32_t>(M >> 4) << 24);
-}
-
-// ------------------------------------------------------------------ CTA pairs (cluster of 2, tcgen05 cta_group::2)
-// The two CTAs of a pair run one 256-row MMA: each holds 128 rows of A and half of B's columns in its own shared
-// memory and receives its 128 rows of D in its own TMEM.  The even CTA (rank 0) owns the load barriers and issues
-// the MMAs; every tcgen05 instruction of such a kernel uses cta_group::2.
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// shared::cluster address of the variable at the same offset in CTA `rank` of this cluster
-__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
-}
-__device__ __forceinline__ bool mbar_test_acq_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait on a barrier that the peer CTA also arrives on (cluster-scope acquire).
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* status, int code) {
-  if (mbar_test_acq_cluster(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  while (true) {
-    if (mbar_test_acq_cluster(bar, parity)) return true;
-    if (globaltimer() - t0 > GR_WAIT_NS) {
-      report(status, code);
-      return false;
-    }
-  }
-}
-// Tiled 2-D load into this CTA's shared memory whose completion is counted on a barrier of either CTA of the pair
-// (`cluster_bar`, a shared::cluster address).  No multicast.
-__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t cluster_bar, int x, int y,
-                                                 uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
-      "[%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(cluster_bar), "r"(x), "r"(y), "l"(policy)
-      : "memory");
-}
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-// D[tmem of both CTAs] (+)= A * B^T over the pair (M = 256), issued by one thread of the even CTA.
-__device__ __forceinline__ void tc_mma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                                 uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Arrive once on the barrier at this offset in both CTAs of the pair when all prior pair MMAs have completed.
-__device__ __forceinline__ void tc_commit_pair(uint64_t* bar) {
-  const uint16_t mask = 3;
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
-      "h"(mask)
-      : "memory");
 }
 
 // ------------------------------------------------------------------ warp-level mma.sync (attention)

@@ -25,12 +25,8 @@ namespace gr {
 
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue (two per TMEM lane quadrant)
 constexpr uint32_t kWStageBytes = 128 * 128;  // 128 rows x 64 bf16
-constexpr uint32_t kEpiScratchBytes = 16384;  // argmax transpose: two halves x [16 tokens][128 rows] fp32
-
-// stage-ring waits of the single-thread producer and MMA loops
-__device__ __forceinline__ bool stage_wait(uint64_t* bar, uint32_t parity, int* status) {
-  return GR_SPIN_WAIT ? mbar_spin(bar, parity, status, GR_ERR_TIMEOUT) : mbar_wait(bar, parity, status, GR_ERR_TIMEOUT);
-}
+// argmax transpose: two halves x [16 tokens][128 rows] fp32 (the other epilogues need no shared memory)
+__host__ __device__ constexpr uint32_t epi_scratch_bytes(int epi) { return epi == GR_EPI_ARGMAX ? 16384u : 0u; }
 
 // all 8 epilogue warps
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
@@ -215,8 +211,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t x_stage_bytes = static_cast<uint32_t>(p.nt) * 128u;
   uint8_t* w_smem = smem;
   uint8_t* x_smem = smem + S * kWStageBytes;
-  float* scratch = reinterpret_cast<float*>(x_smem + S * x_stage_bytes);  // epilogue exchange, kEpiScratchBytes
-  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(scratch) + kEpiScratchBytes);
+  float* scratch = reinterpret_cast<float*>(x_smem + S * x_stage_bytes);  // epilogue exchange
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(scratch) + epi_scratch_bytes(EPI));
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;
   uint64_t* acc_empty = acc_full + 2;
@@ -309,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int st = 0;
       uint32_t par = 0;  // parity of the empty phase that frees stage st
       for (int g = pre; g < total; ++g) {
-        if (!stage_wait(empty + st, par, p.status)) {
+        if (!mbar_wait(empty + st, par, p.status, GR_ERR_TIMEOUT)) {
           flags[0] = 1;
           break;
         }
@@ -343,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t acc = tmem + b * acc_cols;
         for (int c = 0; c < kc; ++c) {
-          if (!stage_wait(full + st, par, p.status)) {
+          if (!mbar_wait(full + st, par, p.status, GR_ERR_TIMEOUT)) {
             flags[0] = 1;
             ok = false;
             break;
@@ -383,10 +379,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool run = ok && !flags[0];
       if (p.splits == 1 || EPI == GR_EPI_PARTIAL_F32) {
         if (run) {
-          for (int c0 = half * 16; c0 < p.nt; c0 += 32) {
+          // the next chunk's TMEM load is in flight while this chunk's epilogue runs
+          uint32_t ra[16], rb[16];
+          int c0 = half * 16;
+          if (c0 < p.nt) tmem_ld16_issue(t_lane + c0, ra);
+          while (c0 < p.nt) {
             float v[16];
-            tmem_ld16(t_lane + c0, v);
+            tmem_ld16_wait(ra);
+            const int c1 = c0 + 32;
+            if (c1 < p.nt) tmem_ld16_issue(t_lane + c1, rb);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(ra[i]);
             epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, my_scratch, split);
+            if (c1 >= p.nt) break;
+            tmem_ld16_wait(rb);
+            c0 = c1 + 32;
+            if (c0 < p.nt) tmem_ld16_issue(t_lane + c0, ra);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(rb[i]);
+            epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c1, v, my_scratch, split);
           }
         }
         tc_fence_before();
@@ -444,205 +455,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Pair variant for large token counts: a cluster of two CTAs runs one 256-feature x NT-token unit with
-// tcgen05.mma.cta_group::2 (M = 256).  CTA r loads features [256 u + 128 r, +128) and tokens [NT t + NT/2 r, +NT/2);
-// each token tile is thus read once per 256 features instead of once per 128, and every CTA streams half the bytes
-// per MMA of the single-CTA kernel.  Roles per CTA as in linear_kernel; only the even CTA's warp 1 issues MMAs.
-//   full[s]       even CTA only: one arrive (with both CTAs' byte count) + both CTAs' TMA bytes
-//   empty[s]      both CTAs: the MMA commit arrives on both (multicast commit)
-//   acc_full[b]   both CTAs: the unit's final commit arrives on both
-//   acc_empty[b]  even CTA only: 16 arrivals, one per epilogue warp of either CTA
-// The epilogue of CTA r is the single-CTA epilogue for feature tile 2u + r.  Split-K only in PARTIAL_F32 mode
-// (no tickets).
-template <int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
-    linear_pair_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
-                       const LinearParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int S = p.stages;
-  const uint32_t x_stage_bytes = static_cast<uint32_t>(p.nt / 2) * 128u;
-  uint8_t* w_smem = smem;
-  uint8_t* x_smem = smem + S * kWStageBytes;
-  float* scratch = reinterpret_cast<float*>(x_smem + S * x_stage_bytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(scratch) + kEpiScratchBytes);
-  uint64_t* empty = full + S;
-  uint64_t* acc_full = empty + S;
-  uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] abort
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_rank();
-  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
-  const int kc = p.kc_per_split;
-  const int n_pair_tiles = p.n_tiles >> 1;
-  const int n_units = n_pair_tiles * p.m_tiles * p.splits;
-  const int n_my = pair < n_units ? (n_units - pair + n_pairs - 1) / n_pairs : 0;
-  const uint32_t acc_cols = p.nt <= 32 ? 32u : (p.nt <= 64 ? 64u : (p.nt <= 128 ? 128u : 256u));
-  const uint32_t tmem_cols = 2 * acc_cols;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(full + s, 1);
-      mbar_init(empty + s, 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(acc_full + b, 1);
-      mbar_init(acc_empty + b, 16);
-    }
-    flags[0] = 0;
-    fence_mbar_init();
-    tma_prefetch_desc(&tmw);
-    tma_prefetch_desc(&tmx);
-  }
-  if (warp == 1) tmem_alloc_pair(tmem_slot, tmem_cols);
-  tc_fence_before();
-  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA signal
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  pdl_trigger();
-
-  auto decode = [&](int u, int& m_tile, int& split, int& n_pt) {
-    m_tile = u % p.m_tiles;
-    u /= p.m_tiles;
-    split = u % p.splits;
-    n_pt = u / p.splits;
-  };
-
-  if (warp == 0) {
-    if (lane == 0) {
-      const uint64_t pol = policy_evict_first();
-      const uint64_t pol_x = policy_evict_last();
-      const uint32_t full0 = cluster_addr(full, 0);
-      const int total = n_my * kc;
-      const uint32_t stage_tx = 2u * (kWStageBytes + x_stage_bytes);  // both CTAs' bytes land on the even CTA's barrier
-      const int w_off = static_cast<int>(rank) * 128, x_off = static_cast<int>(rank) * (p.nt / 2);
-      int k = 0, c = 0, m_tile = 0, split = 0, n_pt = 0, xk = 0;
-      auto start_unit = [&]() {
-        decode(pair + k * n_pairs, m_tile, split, n_pt);
-        xk = split * kc * 64;
-      };
-      auto advance = [&]() {
-        if (++c == kc) {
-          c = 0;
-          if (++k < n_my) start_unit();
-        } else {
-          xk += 64;
-        }
-      };
-      if (n_my > 0) start_unit();
-      const int pre = min(S, total);
-      int pre_xk[GR_MAX_STAGES], pre_row[GR_MAX_STAGES];
-      for (int g = 0; g < pre; ++g) {
-        if (rank == 0) mbar_arrive_expect_tx(full + g, stage_tx);
-        tma_load_2d_pair(w_smem + g * kWStageBytes, &tmw, full0 + 8u * g, xk, n_pt * 256 + w_off, pol);
-        pre_xk[g] = xk;
-        pre_row[g] = m_tile * p.nt + x_off;
-        advance();
-      }
-      pdl_wait();
-      for (int g = 0; g < pre; ++g)
-        tma_load_2d_pair(x_smem + g * x_stage_bytes, &tmx, full0 + 8u * g, pre_xk[g], pre_row[g], pol_x);
-      int st = 0;
-      uint32_t par = 0;
-      for (int g = pre; g < total; ++g) {
-        if (!stage_wait(empty + st, par, p.status)) {
-          flags[0] = 1;
-          break;
-        }
-        if (rank == 0) mbar_arrive_expect_tx(full + st, stage_tx);
-        tma_load_2d_pair(w_smem + st * kWStageBytes, &tmw, full0 + 8u * st, xk, n_pt * 256 + w_off, pol);
-        tma_load_2d_pair(x_smem + st * x_stage_bytes, &tmx, full0 + 8u * st, xk, m_tile * p.nt + x_off, pol_x);
-        advance();
-        if (++st == S) {
-          st = 0;
-          par ^= 1u;
-        }
-      }
-      // Every copy this CTA issued has landed once the MMAs that read it completed: the last units' empty commits.
-      for (int g = max(0, total - S); g < total && !flags[0]; ++g)
-        if (!mbar_wait(empty + (g % S), (g / S) & 1, p.status, GR_ERR_TIMEOUT)) break;
-    }
-  } else if (warp == 1) {
-    if (lane == 0 && rank == 0) {
-      const uint32_t idesc = idesc_bf16_f32(256, p.nt);
-      const uint64_t a0 = smem_desc_sw128(smem_u32(w_smem)), b0 = smem_desc_sw128(smem_u32(x_smem));
-      int st = 0;
-      uint32_t par = 0;
-      bool ok = true;
-      for (int k = 0; k < n_my && ok; ++k) {
-        const int b = k & 1;
-        if (k >= 2 && !mbar_wait_cluster(acc_empty + b, ((k >> 1) - 1) & 1, p.status, GR_ERR_TIMEOUT)) {
-          flags[0] = 1;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t acc = tmem + b * acc_cols;
-        for (int c = 0; c < kc; ++c) {
-          if (!stage_wait(full + st, par, p.status)) {
-            flags[0] = 1;
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint64_t ad = a0 + ((static_cast<uint32_t>(st) * kWStageBytes) >> 4);
-          const uint64_t bd = b0 + ((static_cast<uint32_t>(st) * x_stage_bytes) >> 4);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) tc_mma_bf16_pair(acc, ad + 2 * kk, bd + 2 * kk, idesc, (c | kk) != 0);
-          tc_commit_pair(empty + st);
-          if (++st == S) {
-            st = 0;
-            par ^= 1u;
-          }
-        }
-        if (ok) tc_commit_pair(acc_full + b);
-      }
-      // the last accumulators are read by both CTAs' epilogues before TMEM is released
-      for (int k = max(0, n_my - 2); k < n_my && ok; ++k)
-        mbar_wait_cluster(acc_empty + (k & 1), (k >> 1) & 1, p.status, GR_ERR_TIMEOUT);
-    }
-  } else {
-    // ---------------------------------------------------------------- epilogue warps 2..9
-    pdl_wait();
-    const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int f_local = quad * 32 + lane;
-    float* my_scratch = scratch + half * 2048;
-    const uint32_t acc_empty0 = cluster_addr(acc_empty, 0);
-    for (int k = 0; k < n_my; ++k) {
-      const int b = k & 1;
-      int m_tile, split, n_pt;
-      decode(pair + k * n_pairs, m_tile, split, n_pt);
-      const bool ok = mbar_wait(acc_full + b, (k >> 1) & 1, p.status, GR_ERR_TIMEOUT);
-      tc_fence_after();
-      const uint32_t t_lane = tmem + b * acc_cols + (static_cast<uint32_t>(quad * 32) << 16);
-      const int n_tile = n_pt * 2 + static_cast<int>(rank);
-      if (ok) {
-        for (int c0 = half * 16; c0 < p.nt; c0 += 32) {
-          float v[16];
-          tmem_ld16(t_lane + c0, v);
-          epilogue16<EPI>(p, n_tile, m_tile, f_local, m_tile * p.nt + c0, v, my_scratch, split);
-        }
-      }
-      tc_fence_before();
-      if (lane == 0) mbar_arrive_cluster(acc_empty0 + static_cast<uint32_t>(b) * 8u);
-      if (!ok) break;
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();  // neither CTA releases TMEM or exits while the pair's MMAs or copies may still touch it
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc_pair(tmem, tmem_cols);
-  }
-}
-
 // ------------------------------------------------------------------ host side
-// dynamic shared memory of either kernel; `x_rows` = token rows per stage (NT, or NT/2 for the pair kernel)
-size_t linear_smem_bytes(int x_rows, int stages) {
-  return 1024 + static_cast<size_t>(stages) * (kWStageBytes + static_cast<size_t>(x_rows) * 128) + kEpiScratchBytes +
+size_t linear_smem_bytes(int nt, int stages, int epi) {
+  return 1024 + static_cast<size_t>(stages) * (kWStageBytes + static_cast<size_t>(nt) * 128) + epi_scratch_bytes(epi) +
          (2 * stages + 4) * 8 + 32;
 }
 
@@ -682,68 +497,6 @@ cudaError_t launch_argmax_reduce(const LinearParams& p, cudaStream_t stream, boo
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, argmax_reduce_kernel, p);
-}
-
-template <int EPI>
-cudaError_t launch_linear_pair_t(const CUtensorMap& tmw, const CUtensorMap& tmx, const LinearParams& p, int grid,
-                                 size_t smem, cudaStream_t stream, bool pdl) {
-  auto kern = linear_pair_kernel<EPI>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-  attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = 2;
-  attr[1].val.clusterDim.y = 1;
-  attr[1].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, kern, tmw, tmx, p);
-}
-
-// CTA pairs of the pair kernel that fit on the device at once with `smem` bytes each (0 if the query fails).
-int linear_pair_max_clusters(size_t smem) {
-  auto kern = linear_pair_kernel<GR_EPI_STORE_F32>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess) return 0;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) return 0;
-  return n;
-}
-
-cudaError_t launch_linear_pair(int epi, const CUtensorMap& tmw, const CUtensorMap& tmx, const LinearParams& p,
-                               int grid, size_t smem, cudaStream_t stream, bool pdl) {
-  switch (epi) {
-    case GR_EPI_STORE_F32: return launch_linear_pair_t<GR_EPI_STORE_F32>(tmw, tmx, p, grid, smem, stream, pdl);
-    case GR_EPI_STORE_BF16: return launch_linear_pair_t<GR_EPI_STORE_BF16>(tmw, tmx, p, grid, smem, stream, pdl);
-    case GR_EPI_SWIGLU: return launch_linear_pair_t<GR_EPI_SWIGLU>(tmw, tmx, p, grid, smem, stream, pdl);
-    case GR_EPI_QKV_ROPE: return launch_linear_pair_t<GR_EPI_QKV_ROPE>(tmw, tmx, p, grid, smem, stream, pdl);
-    case GR_EPI_ARGMAX: return launch_linear_pair_t<GR_EPI_ARGMAX>(tmw, tmx, p, grid, smem, stream, pdl);
-    case GR_EPI_PARTIAL_F32: return launch_linear_pair_t<GR_EPI_PARTIAL_F32>(tmw, tmx, p, grid, smem, stream, pdl);
-    default: return cudaErrorInvalidValue;
-  }
 }
 
 cudaError_t launch_linear(int epi, const CUtensorMap& tmw, const CUtensorMap& tmx, const LinearParams& p, int grid,

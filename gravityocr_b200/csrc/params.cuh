@@ -96,13 +96,11 @@ struct OverrideParams {
   const int32_t* rounds;
 };
 
-size_t linear_smem_bytes(int x_rows, int stages);
+size_t linear_smem_bytes(int nt, int stages, int epi);
 cudaError_t launch_linear(int epi, const CUtensorMap& tmw, const CUtensorMap& tmx, const LinearParams& p, int grid,
                           size_t smem, cudaStream_t stream, bool pdl);
 cudaError_t launch_argmax_reduce(const LinearParams& p, cudaStream_t stream, bool pdl);
-cudaError_t launch_linear_pair(int epi, const CUtensorMap& tmw, const CUtensorMap& tmx, const LinearParams& p,
-                               int grid, size_t smem, cudaStream_t stream, bool pdl);
-int linear_pair_max_clusters(size_t smem);
+
 size_t attention_smem_bytes(int K, int G);
 cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p, cudaStream_t stream,
                              bool pdl);

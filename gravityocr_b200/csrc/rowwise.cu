@@ -23,7 +23,6 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 __global__ void __launch_bounds__(kRowThreads) embed_rows_kernel(const EmbedParams p) {
   __shared__ float red[32];
   __shared__ int64_t s_id;
-  __shared__ int s_pos;
   if (threadIdx.x == 0) pdl_trigger();
   pdl_wait();
   const int t = blockIdx.x;
@@ -56,7 +55,6 @@ __global__ void __launch_bounds__(kRowThreads) embed_rows_kernel(const EmbedPara
     p.row_slot[t] = phys * p.page_size + (pos % p.page_size);
     if (p.row_ids) p.row_ids[t] = static_cast<int32_t>(id);
     s_id = id;
-    s_pos = static_cast<int>(pos);
   }
   __syncthreads();
   const int64_t id = s_id;

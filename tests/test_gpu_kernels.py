@@ -25,7 +25,7 @@ def _rand(shape, g, scale=1.0, dtype=torch.bfloat16):
     return (torch.randn(shape, generator=g) * scale).to(DEV, dtype)
 
 
-# m >= ~128 runs the CTA-pair kernel (256-row MMA over two CTAs) where n_out is a multiple of 256
+# large m: several token tiles per weight tile (cost-model tiling); odd m: a ragged last token tile
 SHAPES = [(1536, 2048, 17), (4096, 1536, 17), (9216, 1536, 34), (1536, 4608, 17), (1536, 1536, 5),
           (4096, 1536, 1088), (1536, 2048, 300), (1536, 4608, 2176), (256, 128, 1), (1536, 4608, 64),
           (4096, 1536, 129), (9216, 1536, 513), (1152, 1536, 300)]
