@@ -18,7 +18,6 @@ namespace gr {
 constexpr int kTile = 64;                       // tokens per pipeline stage
 constexpr int kHalfBytes = kTile * 128;         // 64 rows x 64 dims bf16
 constexpr int kStageBytes = 4 * kHalfBytes;     // K lo, K hi, V lo, V hi
-constexpr int kStages = 3;
 constexpr int kMaxChunkPages = 4096 / 16;  // chunk <= 4096 tokens
 constexpr int kMaxMergeSplits = 16;        // splits per (request, kv head); the host enforces it
 constexpr int kMinWarps = 8;               // extra warps idle in the main loop and help the split merge
@@ -28,9 +27,12 @@ __device__ __forceinline__ int row_limit(const AttnParams& p, int j, int base) {
   return base + j + 1;
 }
 
-// Two instantiations: <224, 2> (two warp groups of <= 3 row tiles + producer, two CTAs per SM) and <288, 1>
-// (up to 8 row tiles, one group).
-template <int MAXT, int MINB>
+// Two instantiations (ST = pipeline stages):
+//   <288, 1, 3>  one warp group (the row tiles of a request's GQA group) + producer; large batches, two CTAs per SM;
+//   <288, 1, 4>  two warp groups on alternate 64-token tiles + producer; small batches, where a CTA's latency is the
+//                forward's.  Tile i uses stage i % 4 and group i % 2, so each stage has one consuming group and its
+//                phases stay in order.
+template <int MAXT, int MINB, int ST>
 __global__ void __launch_bounds__(MAXT, MINB) attention_kernel(const __grid_constant__ CUtensorMap tmk,
                                                                const __grid_constant__ CUtensorMap tmv,
                                                                const AttnParams p) {
@@ -42,11 +44,11 @@ __global__ void __launch_bounds__(MAXT, MINB) attention_kernel(const __grid_cons
   const int R_pad = n_mt * 16;
   const int NG = p.groups;                                    // warp groups taking alternate KV tiles
   const int n_cw = NG * n_mt;                                 // compute warps
-  uint8_t* kv_smem = smem;                                    // kStages x kStageBytes
-  uint8_t* q_smem = smem + kStages * kStageBytes;             // 2 halves x R_pad x 128 B
+  uint8_t* kv_smem = smem;                                    // ST x kStageBytes
+  uint8_t* q_smem = smem + ST * kStageBytes;             // 2 halves x R_pad x 128 B
   uint64_t* full = reinterpret_cast<uint64_t*>(q_smem + 2 * R_pad * 128);
-  uint64_t* empty = full + kStages;
-  int* flag = reinterpret_cast<int*>(empty + kStages);
+  uint64_t* empty = full + ST;
+  int* flag = reinterpret_cast<int*>(empty + ST);
   int* pages = flag + 4;  // physical page ids of this split's cache range (chunk / page_size entries)
 
   // blocks launch in z-major order: a longest-first request order shortens the tail of a mixed-length batch
@@ -62,7 +64,7 @@ __global__ void __launch_bounds__(MAXT, MINB) attention_kernel(const __grid_cons
   const int n_tiles = (kv_end - kv_beg + kTile - 1) / kTile;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < ST; ++s) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, n_mt);  // one warp group consumes each tile
     }
@@ -89,8 +91,8 @@ __global__ void __launch_bounds__(MAXT, MINB) attention_kernel(const __grid_cons
     if (lane == 0) {
       int issued = 0;
       for (int i = 0; i < n_tiles; ++i) {
-        const int s = i % kStages;
-        if (i >= kStages && !mbar_wait(empty + s, ((i / kStages) - 1) & 1, p.status, GR_ERR_TIMEOUT)) break;
+        const int s = i % ST;
+        if (i >= ST && !mbar_wait(empty + s, ((i / ST) - 1) & 1, p.status, GR_ERR_TIMEOUT)) break;
         mbar_arrive_expect_tx(full + s, kStageBytes);
         uint8_t* st = kv_smem + s * kStageBytes;
 #pragma unroll
@@ -104,24 +106,32 @@ __global__ void __launch_bounds__(MAXT, MINB) attention_kernel(const __grid_cons
         }
         issued = i + 1;
       }
-      for (int i = max(0, issued - kStages); i < issued; ++i)
-        mbar_wait(full + (i % kStages), (i / kStages) & 1, p.status, GR_ERR_TIMEOUT);
+      for (int i = max(0, issued - ST); i < issued; ++i)
+        mbar_wait(full + (i % ST), (i / ST) & 1, p.status, GR_ERR_TIMEOUT);
     }
   } else if (warp < n_cw) {
     // ------------------------------------------------------------ compute warps
     const int mt = warp % n_mt, grp = warp / n_mt;
     // group 0 stages the query rows into shared memory (128-byte swizzle, two 64-dim halves)
     if (grp == 0) {
-      for (int e = lane; e < 16 * 16; e += 32) {
-        const int rr = e >> 4, chunk = e & 15;
-        const int r = mt * 16 + rr;
-        uint4 val = make_uint4(0, 0, 0, 0);
+      // all eight 16-byte loads of a lane in flight together
+      uint4 val[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int e = lane + 32 * k;
+        const int r = mt * 16 + (e >> 4), chunk = e & 15;
+        val[k] = make_uint4(0, 0, 0, 0);
         if (r < R) {
           const int g = r / p.K, j = r % p.K;
-          const __nv_bfloat16* src = p.q + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128 + chunk * 8;
-          val = *reinterpret_cast<const uint4*>(src);
+          val[k] = *reinterpret_cast<const uint4*>(p.q + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128 +
+                                                   chunk * 8);
         }
-        *reinterpret_cast<uint4*>(q_smem + (chunk >> 3) * (R_pad * 128) + sw128(r, chunk & 7)) = val;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int e = lane + 32 * k;
+        const int r = mt * 16 + (e >> 4), chunk = e & 15;
+        *reinterpret_cast<uint4*>(q_smem + (chunk >> 3) * (R_pad * 128) + sw128(r, chunk & 7)) = val[k];
       }
     }
     asm volatile("bar.sync 2, %0;" ::"r"(n_cw * 32) : "memory");
@@ -140,8 +150,8 @@ __global__ void __launch_bounds__(MAXT, MINB) attention_kernel(const __grid_cons
     for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
 
     for (int i = grp; i < n_tiles; i += NG) {
-      const int s = i % kStages;
-      if (!mbar_wait(full + s, (i / kStages) & 1, p.status, GR_ERR_TIMEOUT)) {
+      const int s = i % ST;
+      if (!mbar_wait(full + s, (i / ST) & 1, p.status, GR_ERR_TIMEOUT)) {
         *flag = 1;
         break;
       }
@@ -350,7 +360,49 @@ __global__ void __launch_bounds__(MAXT, MINB) attention_kernel(const __grid_cons
       if (s < n_active) wgt[r * kMaxMergeSplits + s] = ms[s] * inv;
   }
   __syncthreads();
-  // phase B: (row, 4 dims) items; every split's loads of an item are issued together, summed in split order
+  // phase B: (row, 4 dims) items; every split's loads of an item are issued together, summed in split order.  With
+  // at most 4 splits, four items' loads go out together.
+  auto store4 = [&](int it, float4 acc) {
+    const int r = it >> 5, q4 = it & 31;
+    const int g = r / p.K, j = r % p.K;
+    __nv_bfloat16* dst = p.out + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128 + q4 * 4;
+    uint2 pk;
+    pk.x = pack_bf16(acc.x, acc.y);
+    pk.y = pack_bf16(acc.z, acc.w);
+    *reinterpret_cast<uint2*>(dst) = pk;
+  };
+  if (n_active <= 4) {
+    for (int it0 = threadIdx.x; it0 < R * 32; it0 += 4 * blockDim.x) {
+      float4 os[4][4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int it = it0 + u * blockDim.x;
+#pragma unroll
+        for (int sp = 0; sp < 4; ++sp)
+          if (it < R * 32 && sp < n_active)
+            os[u][sp] = __ldcg(reinterpret_cast<const float4*>(p.ws_o + ((slot0 + sp) * R_pad + (it >> 5)) * 128) +
+                               (it & 31));
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int it = it0 + u * blockDim.x;
+        if (it >= R * 32) break;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int sp = 0; sp < 4; ++sp) {
+          if (sp < n_active) {
+            const float w = wgt[(it >> 5) * kMaxMergeSplits + sp];
+            acc.x += os[u][sp].x * w;
+            acc.y += os[u][sp].y * w;
+            acc.z += os[u][sp].z * w;
+            acc.w += os[u][sp].w * w;
+          }
+        }
+        store4(it, acc);
+      }
+    }
+    return;
+  }
   for (int it = threadIdx.x; it < R * 32; it += blockDim.x) {
     const int r = it >> 5, q4 = it & 31;
     float4 os[kMaxMergeSplits];
@@ -368,28 +420,23 @@ __global__ void __launch_bounds__(MAXT, MINB) attention_kernel(const __grid_cons
         acc.w += os[s].w * w;
       }
     }
-    const int g = r / p.K, j = r % p.K;
-    __nv_bfloat16* dst = p.out + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128 + q4 * 4;
-    uint2 pk;
-    pk.x = pack_bf16(acc.x, acc.y);
-    pk.y = pack_bf16(acc.z, acc.w);
-    *reinterpret_cast<uint2*>(dst) = pk;
+    store4(it, acc);
   }
 }
 
-size_t attention_smem_bytes(int K, int G) {
+size_t attention_smem_bytes(int K, int G, int stages) {
   const int R_pad = ((G * K + 15) / 16) * 16;
-  return 1024 + kStages * kStageBytes + 2 * R_pad * 128 + 2 * kStages * 8 + 16 + kMaxChunkPages * 4;
+  return 1024 + stages * kStageBytes + 2 * R_pad * 128 + 2 * stages * 8 + 16 + kMaxChunkPages * 4;
 }
 
-template <int MAXT, int MINB>
+template <int MAXT, int MINB, int ST>
 static cudaError_t configure_attention() {
   static bool configured = false;
   if (configured) return cudaSuccess;
   cudaError_t e =
-      cudaFuncSetAttribute(attention_kernel<MAXT, MINB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      cudaFuncSetAttribute(attention_kernel<MAXT, MINB, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(attention_kernel<MAXT, MINB>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  e = cudaFuncSetAttribute(attention_kernel<MAXT, MINB, ST>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   if (e != cudaSuccess) return e;
   configured = true;
   return cudaSuccess;
@@ -399,30 +446,29 @@ cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, con
                              cudaStream_t stream, bool pdl) {
   const int G = p.n_q_heads / p.n_kv_heads;
   const int n_mt = (G * p.K + 15) / 16;
-  // One warp group.  Two groups on alternate tiles would need an even stage count (a group may only ever wait for
-  // the next phase of a stage it owns: with shared stages a fast group can meet a stage two phases ahead, where the
-  // parity wait sees the older completed phase); 4 stages do not leave room for two CTAs per SM.  Idle extra warps
-  // help the split merge of small batches (large batches keep small CTAs: 2 per SM).
+  // Large batches: one warp group, 3 stages, small CTAs (two per SM).  Small batches (fewer (request, head) pairs
+  // than two per SM): two groups on alternate tiles over 4 stages, and at least kMinWarps warps for the split merge.
   AttnParams q = p;
-  q.groups = 1;
   const bool small = p.bs * p.n_kv_heads < 2 * 148;
+  q.groups = (small && 2 * n_mt + 1 <= 9) ? 2 : 1;  // up to 288 threads
   int warps = q.groups * n_mt + 1;
   if (small && p.max_splits > 1 && warps < kMinWarps) warps = kMinWarps;
-  const bool narrow = q.groups == 2 && warps * 32 <= 224;
-  cudaError_t e = narrow ? configure_attention<224, 2>() : configure_attention<288, 1>();
+  if (warps * 32 > 288) return cudaErrorInvalidValue;  // more than 8 row tiles: the host rejects G*K > 128
+  const int stages = small ? 4 : 3;
+  cudaError_t e = small ? configure_attention<288, 1, 4>() : configure_attention<288, 1, 3>();
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.max_splits, p.n_kv_heads, p.bs);
   cfg.blockDim = dim3(32 * warps);
-  cfg.dynamicSmemBytes = attention_smem_bytes(p.K, G);
+  cfg.dynamicSmemBytes = attention_smem_bytes(p.K, G, stages);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return narrow ? cudaLaunchKernelEx(&cfg, attention_kernel<224, 2>, tmk, tmv, q)
-                : cudaLaunchKernelEx(&cfg, attention_kernel<288, 1>, tmk, tmv, q);
+  return small ? cudaLaunchKernelEx(&cfg, attention_kernel<288, 1, 4>, tmk, tmv, q)
+               : cudaLaunchKernelEx(&cfg, attention_kernel<288, 1, 3>, tmk, tmv, q);
 }
 
 }  // namespace gr

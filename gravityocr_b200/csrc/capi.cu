@@ -240,6 +240,11 @@ int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr
   } else if (!epi->out || epi->ld_out <= 0) {
     return GR_ERR_ARG;
   }
+  // the bf16 epilogues store 16-byte vectors
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  if ((epi->mode == GR_EPI_SWIGLU || epi->mode == GR_EPI_STORE_BF16) && (!a16(epi->out) || epi->ld_out % 8))
+    return GR_ERR_ARG;
+  if (epi->mode == GR_EPI_QKV_ROPE && (!a16(epi->q_out) || !a16(epi->k_cache) || !a16(epi->v_cache))) return GR_ERR_ARG;
   // persistent grid: every resident CTA walks units c, c + grid, ...
   const int units = s.n_tiles * s.m_tiles * splits;
   int stages, per_sm;

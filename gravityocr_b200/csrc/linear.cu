@@ -25,8 +25,12 @@ namespace gr {
 
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue (two per TMEM lane quadrant)
 constexpr uint32_t kWStageBytes = 128 * 128;  // 128 rows x 64 bf16
-// argmax transpose: two halves x [16 tokens][128 rows] fp32 (the other epilogues need no shared memory)
-__host__ __device__ constexpr uint32_t epi_scratch_bytes(int epi) { return epi == GR_EPI_ARGMAX ? 16384u : 0u; }
+// Epilogue shared memory: the argmax transpose (two halves x [16 tokens][128 rows] fp32); the bf16 epilogues stage
+// each warp's 16 tokens x 32 rows (1 KB per warp) so that global stores go out as 16-byte vectors per lane.
+__host__ __device__ constexpr uint32_t epi_scratch_bytes(int epi) {
+  return epi == GR_EPI_ARGMAX ? 16384u
+                              : ((epi == GR_EPI_SWIGLU || epi == GR_EPI_QKV_ROPE || epi == GR_EPI_STORE_BF16) ? 8192u : 0u);
+}
 
 // all 8 epilogue warps
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
@@ -64,40 +68,58 @@ __device__ __forceinline__ Top2 top2_warp(Top2 x) {
   return x;
 }
 
-// Apply the epilogue to 16 consecutive tokens [t0, t0+16) of feature row f_local of this tile.  Called by all 128
-// epilogue threads together (it may use warp shuffles, the epilogue barrier and `scratch` shared memory).
+// Apply the epilogue to 16 consecutive tokens [t0, t0+16) of feature row f_local of this tile.  Called by the 128
+// epilogue threads of one column half together (it may use warp shuffles, the half's barrier and the CTA's
+// epilogue shared memory `scratch`).
 template <int EPI>
 __device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, int m_tile, int f_local, int t0,
                                            const float* v, float* scratch, int split) {
   const int lane = threadIdx.x & 31;
   const int t_end = min(p.m, (m_tile + 1) * p.nt);
-  if constexpr (EPI == GR_EPI_STORE_F32 || EPI == GR_EPI_STORE_BF16 || EPI == GR_EPI_PARTIAL_F32) {
+  // bf16 staging area of this warp: [16 tokens][32 rows]
+  __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(scratch) + (((threadIdx.x >> 5) - 2) << 9);
+  if constexpr (EPI == GR_EPI_STORE_F32 || EPI == GR_EPI_PARTIAL_F32) {
     const int f = n_tile * 128 + f_local;
     const size_t base = EPI == GR_EPI_PARTIAL_F32 ? (size_t)split * p.m * p.ld_out : 0;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const int t = t0 + i;
-      if (t < t_end) {
-        if constexpr (EPI == GR_EPI_STORE_BF16)
-          static_cast<__nv_bfloat16*>(p.out)[(size_t)t * p.ld_out + f] = __float2bfloat16_rn(v[i]);
-        else
-          static_cast<float*>(p.out)[base + (size_t)t * p.ld_out + f] = v[i];
-      }
+      if (t < t_end) static_cast<float*>(p.out)[base + (size_t)t * p.ld_out + f] = v[i];
     }
+  } else if constexpr (EPI == GR_EPI_STORE_BF16) {
+    // stage [token][32 rows], then lane l writes 16 rows (32 B) of token l / 2
+#pragma unroll
+    for (int i = 0; i < 16; ++i) stage[i * 32 + lane] = __float2bfloat16_rn(v[i]);
+    __syncwarp();
+    const int tok = lane >> 1, hh = lane & 1;
+    const uint4 a = *reinterpret_cast<const uint4*>(stage + tok * 32 + hh * 16);
+    const uint4 c = *reinterpret_cast<const uint4*>(stage + tok * 32 + hh * 16 + 8);
+    if (t0 + tok < t_end) {
+      __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + (size_t)(t0 + tok) * p.ld_out + n_tile * 128 +
+                           (f_local & ~31) + hh * 16;
+      reinterpret_cast<uint4*>(dst)[0] = a;
+      reinterpret_cast<uint4*>(dst)[1] = c;
+    }
+    __syncwarp();
   } else if constexpr (EPI == GR_EPI_SWIGLU) {
     // rows 2j / 2j+1 of the tile are gate / up of feature 64*n_tile + j (gr_pack_gate_up): the pair sits in adjacent
-    // lanes, so one shuffle brings the up value to the gate lane
-    const int f = n_tile * 64 + (f_local >> 1);
+    // lanes, so one shuffle brings the up value to the gate lane.  The warp's 16 features x 16 tokens are staged
+    // [token][16 features] and written as one 16-byte vector per lane (token lane / 2, features 8 * (lane & 1) + 0..7).
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const float u = __shfl_xor_sync(0xffffffffu, v[i], 1);
-      const int t = t0 + i;
-      if (!(lane & 1) && t < t_end) {
+      if (!(lane & 1)) {
         const float g = v[i];
-        const float a = u * __fdividef(g, 1.0f + __expf(-g));
-        static_cast<__nv_bfloat16*>(p.out)[(size_t)t * p.ld_out + f] = __float2bfloat16_rn(a);
+        stage[i * 16 + (lane >> 1)] = __float2bfloat16_rn(u * __fdividef(g, 1.0f + __expf(-g)));
       }
     }
+    __syncwarp();
+    const int tok = lane >> 1, hh = lane & 1;
+    const uint4 a = *reinterpret_cast<const uint4*>(stage + tok * 16 + hh * 8);
+    if (t0 + tok < t_end)
+      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + (size_t)(t0 + tok) * p.ld_out + n_tile * 64 +
+                                ((f_local >> 1) & ~15) + hh * 8) = a;
+    __syncwarp();
   } else if constexpr (EPI == GR_EPI_QKV_ROPE) {
     // tile = one head: [0, nq) query heads, [nq, nq+nkv) key heads, then value heads; f_local = head dim
     const int head = n_tile;
@@ -109,6 +131,7 @@ __device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, in
     // reach every lane by shuffles; cos / sin are computed in registers.  Per-token loads here would share the SM's
     // L1 / shared-memory bandwidth with the tensor core's operand reads of the next unit.
     const int tl = min(t0 + (lane & 15), t_end - 1);
+    const long long slot_l = is_q ? 0ll : p.row_slot[tl];
     float o[16];
     if (rot) {
       const int pos_l = p.row_pos[tl];
@@ -125,32 +148,39 @@ __device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, in
 #pragma unroll
       for (int i = 0; i < 16; ++i) o[i] = v[i];
     }
-    if (is_q) {
+    // stage [token][32 dims]; lane l then writes 16 dims (32 B) of token l / 2
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
-        if (t0 + i < t_end) p.q_out[(size_t)(t0 + i) * (p.n_q_heads * 128) + head * 128 + d] = __float2bfloat16_rn(o[i]);
+    for (int i = 0; i < 16; ++i) stage[i * 32 + lane] = __float2bfloat16_rn(o[i]);
+    __syncwarp();
+    const int tok = lane >> 1, hh = lane & 1;
+    const uint4 a = *reinterpret_cast<const uint4*>(stage + tok * 32 + hh * 16);
+    const uint4 c = *reinterpret_cast<const uint4*>(stage + tok * 32 + hh * 16 + 8);
+    const int d0 = (d & ~31) + hh * 16;
+    __nv_bfloat16* dst;
+    if (is_q) {
+      dst = p.q_out + (size_t)(t0 + tok) * (p.n_q_heads * 128) + head * 128 + d0;
     } else {
       // page size 16 (the host checks): page = slot >> 4, offset = slot & 15
       const int kvh = is_v ? head - p.n_q_heads - p.n_kv_heads : head - p.n_q_heads;
-      __nv_bfloat16* cache = is_v ? p.v_cache : p.k_cache;
-      const long long slot_l = p.row_slot[tl];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint64_t slot = static_cast<uint64_t>(__shfl_sync(0xffffffffu, slot_l, i));
-        if (t0 + i < t_end)
-          cache[((((slot >> 4) * p.n_kv_heads + kvh) << 4) + (slot & 15)) * 128 + d] = __float2bfloat16_rn(o[i]);
-      }
+      const uint64_t slot = static_cast<uint64_t>(__shfl_sync(0xffffffffu, slot_l, tok));
+      dst = (is_v ? p.v_cache : p.k_cache) + ((((slot >> 4) * p.n_kv_heads + kvh) << 4) + (slot & 15)) * 128 + d0;
     }
+    if (t0 + tok < t_end) {
+      reinterpret_cast<uint4*>(dst)[0] = a;
+      reinterpret_cast<uint4*>(dst)[1] = c;
+    }
+    __syncwarp();
   } else if constexpr (EPI == GR_EPI_ARGMAX) {
     // transpose through shared memory: [16 tokens][128 vocab rows]; then 8 threads per token scan 16 rows each and
     // merge with 3 shuffle rounds (ties: lowest vocab index)
     const int half = (((threadIdx.x >> 5) - 2) >> 2);
     const int tid = threadIdx.x & 127;
+    float* xs = scratch + half * 2048;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) scratch[i * 128 + f_local] = v[i];
+    for (int i = 0; i < 16; ++i) xs[i * 128 + f_local] = v[i];
     half_bar(half);
     const int tok = tid >> 3, part = tid & 7;
-    const float* row = scratch + tok * 128 + part * 16;
+    const float* row = xs + tok * 128 + part * 16;
     Top2 x{-INFINITY, 0x7fffffff, -INFINITY};
 #pragma unroll
     for (int j = 0; j < 16; ++j) x = top2_merge(x, Top2{row[j], n_tile * 128 + part * 16 + j, -INFINITY});
@@ -365,7 +395,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
     const int f_local = quad * 32 + lane;
-    float* my_scratch = scratch + half * 2048;
     for (int k = 0; k < n_my; ++k) {
       const int b = k & 1;
       int m_tile, split, n_tile;
@@ -390,14 +419,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (c1 < p.nt) tmem_ld16_issue(t_lane + c1, rb);
 #pragma unroll
             for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(ra[i]);
-            epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, my_scratch, split);
+            epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, scratch, split);
             if (c1 >= p.nt) break;
             tmem_ld16_wait(rb);
             c0 = c1 + 32;
             if (c0 < p.nt) tmem_ld16_issue(t_lane + c0, ra);
 #pragma unroll
             for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(rb[i]);
-            epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c1, v, my_scratch, split);
+            epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c1, v, scratch, split);
           }
         }
         tc_fence_before();
@@ -439,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int i = 0; i < 16; ++i) v[i] += x[i];
             }
-            epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, my_scratch, split);
+            epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, scratch, split);
           }
           if (threadIdx.x == 64) p.ws_ticket[tile] = 0;
         }

@@ -101,7 +101,7 @@ cudaError_t launch_linear(int epi, const CUtensorMap& tmw, const CUtensorMap& tm
                           size_t smem, cudaStream_t stream, bool pdl);
 cudaError_t launch_argmax_reduce(const LinearParams& p, cudaStream_t stream, bool pdl);
 
-size_t attention_smem_bytes(int K, int G);
+size_t attention_smem_bytes(int K, int G, int stages);
 cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p, cudaStream_t stream,
                              bool pdl);
 cudaError_t launch_embed_rows(const EmbedParams& p, cudaStream_t s, bool pdl);

@@ -50,9 +50,9 @@ enum gr_rows_mode {
 
 typedef struct gr_epilogue {
   int mode;               /* gr_epilogue_mode */
-  void* out;              /* STORE_*, SWIGLU: [M, ld_out] */
+  void* out;              /* STORE_*, SWIGLU: [M, ld_out]; bf16 outputs 16-byte aligned with ld_out % 8 == 0 */
   int ld_out;
-  /* QKV_ROPE: weight rows are [q heads | k heads | v heads] x head_dim 128 */
+  /* QKV_ROPE: weight rows are [q heads | k heads | v heads] x head_dim 128; q_out and the caches 16-byte aligned */
   void* q_out;            /* bf16 [M, n_q_heads*128] */
   void* k_cache;          /* bf16 [pages, n_kv_heads, page_size, 128] of this layer */
   void* v_cache;

@@ -48,6 +48,24 @@ def test_linear_store_f32(n_out, k_in, m):
     torch.testing.assert_close(out, ref, rtol=1e-3, atol=2e-4 * math.sqrt(k_in))
 
 
+@pytest.mark.parametrize("n_out,k_in,m,ld_extra", [(1536, 2048, 17, 0), (4096, 1536, 300, 8), (1536, 1536, 1088, 0)])
+def test_linear_store_bf16(n_out, k_in, m, ld_extra):
+    """bf16 store epilogue (16-byte vector stores through shared memory), also into a wider row (ld_out > n_out)."""
+    g = torch.Generator().manual_seed(n_out + m)
+    w = _rand((n_out, k_in), g, 0.02)
+    x = _rand((m, k_in), g)
+    ld = n_out + ld_extra
+    out = torch.full((m, ld), float("nan"), dtype=torch.bfloat16, device=DEV)
+    e = L.Epilogue()
+    e.mode, e.out, e.ld_out = L.EPI_STORE_BF16, out.data_ptr(), ld
+    L.linear(w, x, m, e, _ws(n_out, k_in, m))
+    torch.cuda.synchronize()
+    ref = x.float() @ w.float().T
+    torch.testing.assert_close(out[:, :n_out].float(), ref, rtol=1e-2, atol=1e-2)
+    if ld_extra:
+        assert torch.isnan(out[:, n_out:].float()).all()  # nothing written past the tile
+
+
 @pytest.mark.parametrize("splits", [1, 2, 4, 8])
 def test_linear_splits_agree(splits):
     n_out, k_in, m = 1536, 2048, 17
