@@ -306,7 +306,7 @@ def main():
     attn_ms = ev0.elapsed_time(ev1) / n_rep
     attn_b = attention_bytes(cfg, seq_now, K, 1)
     attn_gbs = attn_b / (attn_ms / 1000.0) / 1e9
-    launches = a.steps * (2 * eng.kernels_per_forward() + 1)
+    launches = a.steps * (2 * eng.kernels_per_forward(bs * K) + 1)
 
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": a.steps,

@@ -5,6 +5,8 @@
 #include <map>
 #include <mutex>
 #include <tuple>
+#include <vector>
+#include <new>
 
 #include "params.cuh"
 
@@ -217,9 +219,16 @@ size_t gr_linear_workspace_bytes(int n_out, int m, int splits) {
   return linear_ws_layout(nullptr, s, m, splits).bytes;
 }
 
-int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr_epilogue* epi, int splits,
-              void* workspace, size_t workspace_bytes, const void* prefetch, size_t prefetch_bytes, int32_t* status,
-              void* stream) {
+// Checks, tiling, tensor maps and kernel parameters of one projection; shared by gr_linear and the small-batch plan.
+struct LinearLaunch {
+  LinearParams p;
+  CUtensorMap tmw, tmx;
+  int grid, stages;
+  size_t smem;
+};
+static int build_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr_epilogue* epi, int splits,
+                        void* workspace, size_t workspace_bytes, const void* prefetch, size_t prefetch_bytes,
+                        int32_t* status, LinearLaunch* out) {
   if (!w || !x || !epi || m <= 0 || n_out <= 0 || (n_out % 128) || k_in <= 0 || (k_in % 64)) return GR_ERR_ARG;
   if (epi->mode < GR_EPI_STORE_F32 || epi->mode > GR_EPI_PARTIAL_F32) return GR_ERR_ARG;
   LinearShape s = linear_shape(n_out, k_in, m);
@@ -251,12 +260,13 @@ int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr
   linear_launch_shape(s.nt, kc, epi->mode, &stages, &per_sm);
   const int cap = num_sms() * per_sm;
   const int grid = units < cap ? units : cap;
-  CUtensorMap tmw, tmx;
+  CUtensorMap& tmw = out->tmw;
+  CUtensorMap& tmx = out->tmx;
   int rc = tensor_map_2d(w, static_cast<uint64_t>(n_out), static_cast<uint64_t>(k_in), 128, 64, &tmw);
   if (rc) return rc;
   rc = tensor_map_2d(x, static_cast<uint64_t>(m), static_cast<uint64_t>(k_in), static_cast<uint32_t>(s.nt), 64, &tmx);
   if (rc) return rc;
-  LinearParams p;
+  LinearParams& p = out->p;
   std::memset(&p, 0, sizeof(p));
   p.n_out = n_out;
   p.k_in = k_in;
@@ -288,9 +298,23 @@ int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr
   p.prefetch = static_cast<const uint8_t*>(prefetch);
   p.prefetch_bytes = prefetch ? prefetch_bytes : 0;
   p.status = status;
-  cudaError_t e = launch_linear(epi->mode, tmw, tmx, p, grid, linear_smem_bytes(s.nt, stages, epi->mode),
-                                static_cast<cudaStream_t>(stream), g_pdl);
-  if (e == cudaSuccess && epi->mode == GR_EPI_ARGMAX) e = launch_argmax_reduce(p, static_cast<cudaStream_t>(stream), g_pdl);
+  out->grid = grid;
+  out->stages = stages;
+  out->smem = linear_smem_bytes(s.nt, stages, epi->mode);
+  return GR_OK;
+}
+
+int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr_epilogue* epi, int splits,
+              void* workspace, size_t workspace_bytes, const void* prefetch, size_t prefetch_bytes, int32_t* status,
+              void* stream) {
+  LinearLaunch ll;
+  const int rc = build_linear(w, n_out, k_in, x, m, epi, splits, workspace, workspace_bytes, prefetch, prefetch_bytes,
+                              status, &ll);
+  if (rc) return rc;
+  cudaError_t e = launch_linear(epi->mode, ll.tmw, ll.tmx, ll.p, ll.grid, ll.smem, static_cast<cudaStream_t>(stream),
+                                g_pdl);
+  if (e == cudaSuccess && epi->mode == GR_EPI_ARGMAX)
+    e = launch_argmax_reduce(ll.p, static_cast<cudaStream_t>(stream), g_pdl);
   return e == cudaSuccess ? GR_OK : GR_ERR_CUDA;
 }
 
@@ -302,11 +326,16 @@ size_t gr_attention_workspace_bytes(int bs, int K, int n_q_heads, int n_kv_heads
   return kAttnTicketBytes + align256(slots * R_pad * 128 * sizeof(float)) + align256(slots * R_pad * 2 * sizeof(float));
 }
 
-int gr_bd_attention_ordered(const void* q, const void* k_cache, const void* v_cache, int64_t n_pages,
-                            const int32_t* page_table, int pt_stride, const int64_t* seq_lens, const int32_t* req_order,
-                            int bs, int K, int draft, int base_add, int n_q_heads, int n_kv_heads, int page_size,
-                            int chunk, int max_splits, void* out, void* workspace, size_t workspace_bytes,
-                            int32_t* status, void* stream) {
+// Checks, tensor maps and kernel parameters of one attention call; shared by the entry points and the plan.
+struct AttnLaunch {
+  AttnParams p;
+  CUtensorMap tmk, tmv;
+};
+static int build_attention(const void* q, const void* k_cache, const void* v_cache, int64_t n_pages,
+                           const int32_t* page_table, int pt_stride, const int64_t* seq_lens, const int32_t* req_order,
+                           int bs, int K, int draft, int base_add, int n_q_heads, int n_kv_heads, int page_size,
+                           int chunk, int max_splits, void* out, void* workspace, size_t workspace_bytes,
+                           int32_t* status, AttnLaunch* al) {
   if (!q || !k_cache || !v_cache || !page_table || !seq_lens || !out || bs <= 0 || K <= 0 || n_pages <= 0)
     return GR_ERR_ARG;
   if (n_kv_heads <= 0 || n_q_heads % n_kv_heads || page_size != 16 || chunk <= 0 || chunk % 64 || chunk > 4096 ||
@@ -318,12 +347,13 @@ int gr_bd_attention_ordered(const void* q, const void* k_cache, const void* v_ca
   const size_t need = gr_attention_workspace_bytes(bs, K, n_q_heads, n_kv_heads, max_splits);
   if (max_splits > 1 && (!workspace || workspace_bytes < need)) return GR_ERR_ARG;
   const uint64_t rows = static_cast<uint64_t>(n_pages) * n_kv_heads * page_size;
-  CUtensorMap tmk, tmv;
+  CUtensorMap& tmk = al->tmk;
+  CUtensorMap& tmv = al->tmv;
   int rc = tensor_map_2d(k_cache, rows, 128, static_cast<uint32_t>(page_size), 64, &tmk);
   if (rc) return rc;
   rc = tensor_map_2d(v_cache, rows, 128, static_cast<uint32_t>(page_size), 64, &tmv);
   if (rc) return rc;
-  AttnParams p;
+  AttnParams& p = al->p;
   std::memset(&p, 0, sizeof(p));
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.out = static_cast<__nv_bfloat16*>(out);
@@ -352,7 +382,20 @@ int gr_bd_attention_ordered(const void* q, const void* k_cache, const void* v_ca
   }
   p.status = status;
   p.order = req_order;
-  cudaError_t e = launch_attention(tmk, tmv, p, static_cast<cudaStream_t>(stream), g_pdl);
+  return GR_OK;
+}
+
+int gr_bd_attention_ordered(const void* q, const void* k_cache, const void* v_cache, int64_t n_pages,
+                            const int32_t* page_table, int pt_stride, const int64_t* seq_lens, const int32_t* req_order,
+                            int bs, int K, int draft, int base_add, int n_q_heads, int n_kv_heads, int page_size,
+                            int chunk, int max_splits, void* out, void* workspace, size_t workspace_bytes,
+                            int32_t* status, void* stream) {
+  AttnLaunch al;
+  const int rc = build_attention(q, k_cache, v_cache, n_pages, page_table, pt_stride, seq_lens, req_order, bs, K, draft,
+                                 base_add, n_q_heads, n_kv_heads, page_size, chunk, max_splits, out, workspace,
+                                 workspace_bytes, status, &al);
+  if (rc) return rc;
+  cudaError_t e = launch_attention(al.tmk, al.tmv, al.p, static_cast<cudaStream_t>(stream), g_pdl);
   return e == cudaSuccess ? GR_OK : GR_ERR_CUDA;
 }
 
@@ -423,6 +466,161 @@ int gr_residual_norm(int m, int hidden, const float* h_in, const float* y, int y
   p.h_out = h_out;
   p.x_out = static_cast<__nv_bfloat16*>(x_out);
   return launch_residual_norm(p, static_cast<cudaStream_t>(stream), g_pdl) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
+}
+
+// ------------------------------------------------------------------ persistent small-batch forward (plan)
+namespace {
+struct SmallPlan {
+  std::vector<CUtensorMap> maps;
+  std::vector<SmallPhase> phases;
+  int nt = -1;
+  int attn_row_tiles = -1;
+  int stages = 0;
+  int grid = 0;
+  int device = -1;
+  uint8_t* dev = nullptr;  // tensor maps | phases | grid-barrier counters
+  size_t phases_off = 0, sync_off = 0;
+  bool finalized = false;
+};
+int plan_add_map(SmallPlan* pl, const CUtensorMap& m) {
+  pl->maps.push_back(m);
+  return static_cast<int>(pl->maps.size()) - 1;
+}
+}  // namespace
+
+void* gr_small_create(void) { return new (std::nothrow) SmallPlan(); }
+
+void gr_small_destroy(void* plan) {
+  SmallPlan* pl = static_cast<SmallPlan*>(plan);
+  if (!pl) return;
+  if (pl->dev) cudaFree(pl->dev);
+  delete pl;
+}
+
+int gr_small_add_linear(void* plan, const void* w, int n_out, int k_in, const void* x, int m, const gr_epilogue* epi,
+                        int splits, void* workspace, size_t workspace_bytes) {
+  SmallPlan* pl = static_cast<SmallPlan*>(plan);
+  if (!pl || pl->finalized || !epi) return GR_ERR_ARG;
+  if (m <= 0 || m > 64) return GR_ERR_UNSUPPORTED;  // one token tile of at most 64 rows
+  LinearLaunch ll;
+  const int rc = build_linear(w, n_out, k_in, x, m, epi, splits, workspace, workspace_bytes, nullptr, 0, nullptr, &ll);
+  if (rc) return rc;
+  if (ll.p.m_tiles != 1 || (pl->nt >= 0 && pl->nt != ll.p.nt)) return GR_ERR_UNSUPPORTED;
+  pl->nt = ll.p.nt;
+  SmallPhase ph;
+  std::memset(&ph, 0, sizeof(ph));
+  ph.type = SP_LINEAR;
+  ph.epi = epi->mode;
+  ph.map_a = plan_add_map(pl, ll.tmw);
+  ph.map_b = plan_add_map(pl, ll.tmx);
+  ph.lin = ll.p;
+  pl->phases.push_back(ph);
+  if (epi->mode == GR_EPI_ARGMAX) {  // the per-token reduction of the records is a phase of its own
+    ph.type = SP_ARGREDUCE;
+    pl->phases.push_back(ph);
+  }
+  return GR_OK;
+}
+
+int gr_small_add_attention(void* plan, const void* q, const void* k_cache, const void* v_cache, int64_t n_pages,
+                           const int32_t* page_table, int pt_stride, const int64_t* seq_lens, const int32_t* req_order,
+                           int bs, int K, int draft, int base_add, int n_q_heads, int n_kv_heads, int page_size,
+                           int chunk, int max_splits, void* out, void* workspace, size_t workspace_bytes) {
+  SmallPlan* pl = static_cast<SmallPlan*>(plan);
+  if (!pl || pl->finalized) return GR_ERR_ARG;
+  AttnLaunch al;
+  const int rc = build_attention(q, k_cache, v_cache, n_pages, page_table, pt_stride, seq_lens, req_order, bs, K, draft,
+                                 base_add, n_q_heads, n_kv_heads, page_size, chunk, max_splits, out, workspace,
+                                 workspace_bytes, nullptr, &al);
+  if (rc) return rc;
+  const int n_mt = (n_q_heads / n_kv_heads * K + 15) / 16;
+  if (pl->attn_row_tiles >= 0 && pl->attn_row_tiles != n_mt) return GR_ERR_UNSUPPORTED;
+  // eight worker warps: two groups of n_mt compute warps plus a producer, else one group
+  al.p.groups = 2 * n_mt + 1 <= 8 ? 2 : 1;
+  if (al.p.groups * n_mt + 1 > 8) return GR_ERR_UNSUPPORTED;
+  pl->attn_row_tiles = n_mt;
+  SmallPhase ph;
+  std::memset(&ph, 0, sizeof(ph));
+  ph.type = SP_ATTENTION;
+  ph.map_a = plan_add_map(pl, al.tmk);
+  ph.map_b = plan_add_map(pl, al.tmv);
+  ph.att = al.p;
+  pl->phases.push_back(ph);
+  return GR_OK;
+}
+
+int gr_small_add_residual_norm(void* plan, int m, int hidden, const float* h_in, const float* y, int y_parts,
+                               const void* w_a, const void* w_b, float eps, float* h_out, void* x_out) {
+  SmallPlan* pl = static_cast<SmallPlan*>(plan);
+  if (!pl || pl->finalized) return GR_ERR_ARG;
+  if (m <= 0 || hidden <= 0 || hidden % 8 || !h_in || !y || !w_a || !w_b || !h_out || !x_out) return GR_ERR_ARG;
+  if (h_in == h_out || y_parts < 1 || hidden > 8 * 192 * 4) return GR_ERR_ARG;
+  SmallPhase ph;
+  std::memset(&ph, 0, sizeof(ph));
+  ph.type = SP_RESNORM;
+  ResNormParams& p = ph.rn;
+  p.m = m;
+  p.hidden = hidden;
+  p.y_parts = y_parts;
+  p.h_in = h_in;
+  p.y = y;
+  p.w_a = static_cast<const __nv_bfloat16*>(w_a);
+  p.w_b = static_cast<const __nv_bfloat16*>(w_b);
+  p.eps = eps;
+  p.h_out = h_out;
+  p.x_out = static_cast<__nv_bfloat16*>(x_out);
+  pl->phases.push_back(ph);
+  return GR_OK;
+}
+
+int gr_small_finalize(void* plan, int32_t* status) {
+  SmallPlan* pl = static_cast<SmallPlan*>(plan);
+  if (!pl || pl->finalized || pl->phases.empty() || pl->nt < 0) return GR_ERR_ARG;
+  for (SmallPhase& ph : pl->phases) {
+    ph.lin.status = status;
+    ph.att.status = status;
+  }
+  const int rows_pad = 16 * (pl->attn_row_tiles > 0 ? pl->attn_row_tiles : 1);
+  int st = GR_MAX_STAGES;
+  while (st > 2 && small_smem_bytes(pl->nt, st, rows_pad) > 227 * 1024) --st;
+  if (small_smem_bytes(pl->nt, st, rows_pad) > 227 * 1024) return GR_ERR_UNSUPPORTED;
+  pl->stages = st;
+  cudaGetDevice(&pl->device);
+  pl->grid = num_sms();
+  const size_t maps_bytes = pl->maps.size() * sizeof(CUtensorMap);
+  pl->phases_off = align256(maps_bytes);
+  pl->sync_off = pl->phases_off + align256(pl->phases.size() * sizeof(SmallPhase));
+  const size_t bytes = pl->sync_off + (pl->phases.size() + 2) * sizeof(int);
+  if (cudaMalloc(&pl->dev, bytes) != cudaSuccess) return GR_ERR_CUDA;
+  if (cudaMemcpy(pl->dev, pl->maps.data(), maps_bytes, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(pl->dev + pl->phases_off, pl->phases.data(), pl->phases.size() * sizeof(SmallPhase),
+                 cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemset(pl->dev + pl->sync_off, 0, (pl->phases.size() + 2) * sizeof(int)) != cudaSuccess)
+    return GR_ERR_CUDA;
+  pl->finalized = true;
+  return GR_OK;
+}
+
+int gr_small_launch(void* plan, void* stream) {
+  SmallPlan* pl = static_cast<SmallPlan*>(plan);
+  if (!pl || !pl->finalized) return GR_ERR_ARG;
+  SmallArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.maps = reinterpret_cast<const CUtensorMap*>(pl->dev);
+  a.phases = reinterpret_cast<const SmallPhase*>(pl->dev + pl->phases_off);
+  a.n_phases = static_cast<int>(pl->phases.size());
+  a.nt = pl->nt;
+  a.stages = pl->stages;
+  a.attn_rows_pad = 16 * (pl->attn_row_tiles > 0 ? pl->attn_row_tiles : 1);
+  a.attn_row_tiles = pl->attn_row_tiles > 0 ? pl->attn_row_tiles : 1;
+  int* sync = reinterpret_cast<int*>(pl->dev + pl->sync_off);
+  a.done = sync;
+  a.exited = sync + pl->phases.size();
+  a.abort = sync + pl->phases.size() + 1;
+  a.status = pl->phases[0].lin.status ? pl->phases[0].lin.status : pl->phases[0].att.status;
+  for (const SmallPhase& ph : pl->phases)
+    if (!a.status) a.status = ph.lin.status ? ph.lin.status : ph.att.status;
+  return launch_small_forward(a, pl->grid, static_cast<cudaStream_t>(stream)) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
 }
 
 int gr_accept_commit(int bs, int K, const int32_t* am, const int32_t* v, int64_t* seeds, const int64_t* req_pool_idx,

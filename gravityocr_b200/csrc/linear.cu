@@ -19,213 +19,18 @@
 // interleaved-pair partial RoPE and the paged K/V cache write, and lm_head's vocab-wide argmax (top-1 index, top-1
 // value and top-2 gap; logits are never written): each feature tile leaves one top-2 record per token and
 // argmax_reduce_kernel, launched right after, reduces a token's records with one warp.
-#include "params.cuh"
+#include "linear_dev.cuh"
 
 namespace gr {
 
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue (two per TMEM lane quadrant)
-constexpr uint32_t kWStageBytes = 128 * 128;  // 128 rows x 64 bf16
-// Epilogue shared memory: the argmax transpose (two halves x [16 tokens][128 rows] fp32); the bf16 epilogues stage
-// each warp's 16 tokens x 32 rows (1 KB per warp) so that global stores go out as 16-byte vectors per lane.
-__host__ __device__ constexpr uint32_t epi_scratch_bytes(int epi) {
-  return epi == GR_EPI_ARGMAX ? 16384u
-                              : ((epi == GR_EPI_SWIGLU || epi == GR_EPI_QKV_ROPE || epi == GR_EPI_STORE_BF16) ? 8192u : 0u);
-}
-
-// all 8 epilogue warps
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-// the 4 epilogue warps of one column half (one warp per TMEM lane quadrant)
-__device__ __forceinline__ void half_bar(int half) { asm volatile("bar.sync %0, 128;" ::"r"(2 + half) : "memory"); }
-
-struct Top2 {
-  float v1;
-  int i1;
-  float v2;
-};
-__device__ __forceinline__ Top2 top2_merge(Top2 a, Top2 b) {
-  const bool bw = (b.v1 > a.v1) || (b.v1 == a.v1 && b.i1 < a.i1);
-  Top2 r;
-  if (bw) {
-    r.v1 = b.v1;
-    r.i1 = b.i1;
-    r.v2 = fmaxf(a.v1, b.v2);
-  } else {
-    r.v1 = a.v1;
-    r.i1 = a.i1;
-    r.v2 = fmaxf(a.v2, b.v1);
-  }
-  return r;
-}
-__device__ __forceinline__ Top2 top2_warp(Top2 x) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    Top2 y;
-    y.v1 = __shfl_xor_sync(0xffffffffu, x.v1, o);
-    y.i1 = __shfl_xor_sync(0xffffffffu, x.i1, o);
-    y.v2 = __shfl_xor_sync(0xffffffffu, x.v2, o);
-    x = top2_merge(x, y);
-  }
-  return x;
-}
-
-// Apply the epilogue to 16 consecutive tokens [t0, t0+16) of feature row f_local of this tile.  Called by the 128
-// epilogue threads of one column half together (it may use warp shuffles, the half's barrier and the CTA's
-// epilogue shared memory `scratch`).
-template <int EPI>
-__device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, int m_tile, int f_local, int t0,
-                                           const float* v, float* scratch, int split) {
-  const int lane = threadIdx.x & 31;
-  const int t_end = min(p.m, (m_tile + 1) * p.nt);
-  // bf16 staging area of this warp: [16 tokens][32 rows]
-  __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(scratch) + (((threadIdx.x >> 5) - 2) << 9);
-  if constexpr (EPI == GR_EPI_STORE_F32 || EPI == GR_EPI_PARTIAL_F32) {
-    const int f = n_tile * 128 + f_local;
-    const size_t base = EPI == GR_EPI_PARTIAL_F32 ? (size_t)split * p.m * p.ld_out : 0;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int t = t0 + i;
-      if (t < t_end) static_cast<float*>(p.out)[base + (size_t)t * p.ld_out + f] = v[i];
-    }
-  } else if constexpr (EPI == GR_EPI_STORE_BF16) {
-    // stage [token][32 rows], then lane l writes 16 rows (32 B) of token l / 2
-#pragma unroll
-    for (int i = 0; i < 16; ++i) stage[i * 32 + lane] = __float2bfloat16_rn(v[i]);
-    __syncwarp();
-    const int tok = lane >> 1, hh = lane & 1;
-    const uint4 a = *reinterpret_cast<const uint4*>(stage + tok * 32 + hh * 16);
-    const uint4 c = *reinterpret_cast<const uint4*>(stage + tok * 32 + hh * 16 + 8);
-    if (t0 + tok < t_end) {
-      __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + (size_t)(t0 + tok) * p.ld_out + n_tile * 128 +
-                           (f_local & ~31) + hh * 16;
-      reinterpret_cast<uint4*>(dst)[0] = a;
-      reinterpret_cast<uint4*>(dst)[1] = c;
-    }
-    __syncwarp();
-  } else if constexpr (EPI == GR_EPI_SWIGLU) {
-    // rows 2j / 2j+1 of the tile are gate / up of feature 64*n_tile + j (gr_pack_gate_up): the pair sits in adjacent
-    // lanes, so one shuffle brings the up value to the gate lane.  The warp's 16 features x 16 tokens are staged
-    // [token][16 features] and written as one 16-byte vector per lane (token lane / 2, features 8 * (lane & 1) + 0..7).
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float u = __shfl_xor_sync(0xffffffffu, v[i], 1);
-      if (!(lane & 1)) {
-        const float g = v[i];
-        stage[i * 16 + (lane >> 1)] = __float2bfloat16_rn(u * __fdividef(g, 1.0f + __expf(-g)));
-      }
-    }
-    __syncwarp();
-    const int tok = lane >> 1, hh = lane & 1;
-    const uint4 a = *reinterpret_cast<const uint4*>(stage + tok * 16 + hh * 8);
-    if (t0 + tok < t_end)
-      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + (size_t)(t0 + tok) * p.ld_out + n_tile * 64 +
-                                ((f_local >> 1) & ~15) + hh * 8) = a;
-    __syncwarp();
-  } else if constexpr (EPI == GR_EPI_QKV_ROPE) {
-    // tile = one head: [0, nq) query heads, [nq, nq+nkv) key heads, then value heads; f_local = head dim
-    const int head = n_tile;
-    const int d = f_local;
-    const bool is_q = head < p.n_q_heads;
-    const bool is_v = head >= p.n_q_heads + p.n_kv_heads;
-    const bool rot = !is_v && (d & ~31) < p.rotary_dim;  // warp-uniform: rotary_dim is a multiple of 32
-    // The chunk's 16 positions / cache slots take one coalesced load per warp (lanes l and l + 16 fetch token l) and
-    // reach every lane by shuffles; cos / sin are computed in registers.  Per-token loads here would share the SM's
-    // L1 / shared-memory bandwidth with the tensor core's operand reads of the next unit.
-    const int tl = min(t0 + (lane & 15), t_end - 1);
-    const long long slot_l = is_q ? 0ll : p.row_slot[tl];
-    float o[16];
-    if (rot) {
-      const int pos_l = p.row_pos[tl];
-      const float fr = p.inv_freq[d >> 1];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float partner = __shfl_xor_sync(0xffffffffu, v[i], 1);
-        const int pos = __shfl_sync(0xffffffffu, pos_l, i);
-        float sn, cs;
-        rope_sincos(__fmul_rn(static_cast<float>(pos), fr), &sn, &cs);  // the reference's fp32 pos * inv_freq
-        o[i] = (d & 1) ? (v[i] * cs + partner * sn) : (v[i] * cs - partner * sn);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) o[i] = v[i];
-    }
-    // stage [token][32 dims]; lane l then writes 16 dims (32 B) of token l / 2
-#pragma unroll
-    for (int i = 0; i < 16; ++i) stage[i * 32 + lane] = __float2bfloat16_rn(o[i]);
-    __syncwarp();
-    const int tok = lane >> 1, hh = lane & 1;
-    const uint4 a = *reinterpret_cast<const uint4*>(stage + tok * 32 + hh * 16);
-    const uint4 c = *reinterpret_cast<const uint4*>(stage + tok * 32 + hh * 16 + 8);
-    const int d0 = (d & ~31) + hh * 16;
-    __nv_bfloat16* dst;
-    if (is_q) {
-      dst = p.q_out + (size_t)(t0 + tok) * (p.n_q_heads * 128) + head * 128 + d0;
-    } else {
-      // page size 16 (the host checks): page = slot >> 4, offset = slot & 15
-      const int kvh = is_v ? head - p.n_q_heads - p.n_kv_heads : head - p.n_q_heads;
-      const uint64_t slot = static_cast<uint64_t>(__shfl_sync(0xffffffffu, slot_l, tok));
-      dst = (is_v ? p.v_cache : p.k_cache) + ((((slot >> 4) * p.n_kv_heads + kvh) << 4) + (slot & 15)) * 128 + d0;
-    }
-    if (t0 + tok < t_end) {
-      reinterpret_cast<uint4*>(dst)[0] = a;
-      reinterpret_cast<uint4*>(dst)[1] = c;
-    }
-    __syncwarp();
-  } else if constexpr (EPI == GR_EPI_ARGMAX) {
-    // transpose through shared memory: [16 tokens][128 vocab rows]; then 8 threads per token scan 16 rows each and
-    // merge with 3 shuffle rounds (ties: lowest vocab index)
-    const int half = (((threadIdx.x >> 5) - 2) >> 2);
-    const int tid = threadIdx.x & 127;
-    float* xs = scratch + half * 2048;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) xs[i * 128 + f_local] = v[i];
-    half_bar(half);
-    const int tok = tid >> 3, part = tid & 7;
-    const float* row = xs + tok * 128 + part * 16;
-    Top2 x{-INFINITY, 0x7fffffff, -INFINITY};
-#pragma unroll
-    for (int j = 0; j < 16; ++j) x = top2_merge(x, Top2{row[j], n_tile * 128 + part * 16 + j, -INFINITY});
-#pragma unroll
-    for (int o = 4; o > 0; o >>= 1) {
-      Top2 y;
-      y.v1 = __shfl_xor_sync(0xffffffffu, x.v1, o);
-      y.i1 = __shfl_xor_sync(0xffffffffu, x.i1, o);
-      y.v2 = __shfl_xor_sync(0xffffffffu, x.v2, o);
-      x = top2_merge(x, y);
-    }
-    const int t = t0 + tok;
-    if (part == 0 && t < t_end)
-      p.ws_arg[(size_t)t * p.n_tiles + n_tile] = make_float4(x.v1, __int_as_float(x.i1), x.v2, 0.f);
-    half_bar(half);
-  }
-}
-
-// lm_head, second step: one warp per token merges the token's n_tiles top-2 records (ties: lowest vocab index).  The
-// records of a token are contiguous; every lane issues all its loads before merging (up to 16 x 16 B in flight).
+// lm_head, second step: one warp per token (argmax_reduce_token).
 constexpr int kReduceWarps = 8;
 __global__ void __launch_bounds__(kReduceWarps * 32) argmax_reduce_kernel(const LinearParams p) {
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x * kReduceWarps + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (t >= p.m) return;
-  const float4* rec = p.ws_arg + (size_t)t * p.n_tiles;
-  Top2 x{-INFINITY, 0x7fffffff, -INFINITY};
-  for (int n0 = 0; n0 < p.n_tiles; n0 += 32 * 16) {
-    float4 r[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const int n = n0 + j * 32 + lane;
-      r[j] = n < p.n_tiles ? __ldcg(rec + n) : make_float4(-INFINITY, __int_as_float(0x7fffffff), -INFINITY, 0.f);
-    }
-#pragma unroll
-    for (int j = 0; j < 16; ++j) x = top2_merge(x, Top2{r[j].x, __float_as_int(r[j].y), r[j].z});
-  }
-  x = top2_warp(x);
-  if (lane == 0) {
-    p.out_idx[t] = x.i1;
-    if (p.out_top1) p.out_top1[t] = x.v1;
-    if (p.out_gap) p.out_gap[t] = x.v1 - x.v2;
-  }
+  if (t < p.m) argmax_reduce_token(p, t);
 }
 
 template <int EPI>
@@ -393,8 +198,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // warp w reads TMEM lanes 32*(w%4).. (its quadrant); the two warps of a quadrant take alternate 16-token chunks
     pdl_wait();
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int f_local = quad * 32 + lane;
     for (int k = 0; k < n_my; ++k) {
       const int b = k & 1;
       int m_tile, split, n_tile;
@@ -402,77 +205,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool ok = mbar_wait(acc_full + b, (k >> 1) & 1, p.status, GR_ERR_TIMEOUT);
       tc_fence_after();
       const uint32_t t_lane = tmem + b * acc_cols + (static_cast<uint32_t>(quad * 32) << 16);
-      const int t_beg = m_tile * p.nt;
-      const int rows = min(p.nt, p.m - t_beg);
       epi_bar();
-      const bool run = ok && !flags[0];
-      if (p.splits == 1 || EPI == GR_EPI_PARTIAL_F32) {
-        if (run) {
-          // the next chunk's TMEM load is in flight while this chunk's epilogue runs
-          uint32_t ra[16], rb[16];
-          int c0 = half * 16;
-          if (c0 < p.nt) tmem_ld16_issue(t_lane + c0, ra);
-          while (c0 < p.nt) {
-            float v[16];
-            tmem_ld16_wait(ra);
-            const int c1 = c0 + 32;
-            if (c1 < p.nt) tmem_ld16_issue(t_lane + c1, rb);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(ra[i]);
-            epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, scratch, split);
-            if (c1 >= p.nt) break;
-            tmem_ld16_wait(rb);
-            c0 = c1 + 32;
-            if (c0 < p.nt) tmem_ld16_issue(t_lane + c0, ra);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(rb[i]);
-            epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c1, v, scratch, split);
-          }
-        }
-        tc_fence_before();
-        if (lane == 0) mbar_arrive(acc_empty + b);
-      } else {
-        const int tile = n_tile * p.m_tiles + m_tile;
-        float* part = p.ws_partial + ((size_t)tile * p.splits + split) * p.nt * 128;
-        if (run) {
-          for (int c0 = half * 16; c0 < p.nt; c0 += 32) {
-            float v[16];
-            tmem_ld16(t_lane + c0, v);
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              if (c0 + i < rows) part[(c0 + i) * 128 + f_local] = v[i];
-          }
-        }
-        tc_fence_before();
-        if (lane == 0) mbar_arrive(acc_empty + b);  // the accumulator is free again; the rest reads global memory
-        __threadfence();
-        epi_bar();
-        if (threadIdx.x == 64) {
-          const int prev = atomicAdd(&p.ws_ticket[tile], 1);
-          flags[1] = (prev == p.splits - 1);
-        }
-        epi_bar();
-        if (flags[1]) {
-          __threadfence();
-          const float* base = p.ws_partial + (size_t)tile * p.splits * p.nt * 128;
-          for (int c0 = half * 16; c0 < p.nt; c0 += 32) {
-            // split order is fixed (deterministic sums); the 16 rows' loads of one split are independent
-            float v[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = 0.f;
-            for (int s = 0; s < p.splits; ++s) {
-              const float* src = base + ((size_t)s * p.nt + c0) * 128 + f_local;
-              float x[16];
-#pragma unroll
-              for (int i = 0; i < 16; ++i) x[i] = (c0 + i < rows) ? __ldcg(src + i * 128) : 0.f;
-#pragma unroll
-              for (int i = 0; i < 16; ++i) v[i] += x[i];
-            }
-            epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, scratch, split);
-          }
-          if (threadIdx.x == 64) p.ws_ticket[tile] = 0;
-        }
-      }
+      unit_epilogue<EPI>(p, t_lane, n_tile, m_tile, split, ok && !flags[0], scratch, &flags[1], acc_empty + b);
       epi_bar();  // flags / scratch are reused by the next unit
     }
   }

@@ -96,6 +96,29 @@ struct OverrideParams {
   const int32_t* rounds;
 };
 
+// Persistent small-batch forward (small.cu): a device-resident phase list.
+enum SmallPhaseType { SP_LINEAR = 0, SP_ATTENTION = 1, SP_RESNORM = 2, SP_ARGREDUCE = 3 };
+struct SmallPhase {
+  int type, epi;     // SP_LINEAR: epilogue mode
+  int map_a, map_b;  // tensor maps: SP_LINEAR weights / activations, SP_ATTENTION K / V cache
+  LinearParams lin;  // SP_LINEAR, SP_ARGREDUCE
+  AttnParams att;    // SP_ATTENTION
+  ResNormParams rn;  // SP_RESNORM
+};
+struct SmallArgs {
+  const CUtensorMap* maps;
+  const SmallPhase* phases;
+  int n_phases;
+  int nt, stages;                       // token tile (every projection phase) and TMA ring depth
+  int attn_rows_pad, attn_row_tiles;    // attention rows (G * K) padded to 16, and their 16-row tiles
+  int* done;                            // [n_phases] grid-barrier counters, then `exited`, then `abort`
+  int* exited;
+  int* abort;
+  int* status;
+};
+size_t small_smem_bytes(int nt, int stages, int attn_rows_pad);
+cudaError_t launch_small_forward(const SmallArgs& a, int grid, cudaStream_t stream);
+
 size_t linear_smem_bytes(int nt, int stages, int epi);
 cudaError_t launch_linear(int epi, const CUtensorMap& tmw, const CUtensorMap& tmx, const LinearParams& p, int grid,
                           size_t smem, cudaStream_t stream, bool pdl);

@@ -1,7 +1,7 @@
 // Row-wise kernels of the round: window planning + embedding + input norm, the sandwich residual norm, the
 // accept-and-commit step and the forced-accept draft override.  All HBM-bound on a few KB per row; one CTA per row
 // (192 threads x 8 bf16 lanes = one 1536-wide row per pass).
-#include "params.cuh"
+#include "rowwise_dev.cuh"
 
 namespace gr {
 
@@ -98,70 +98,11 @@ __global__ void __launch_bounds__(kRowThreads) embed_rows_kernel(const EmbedPara
 
 // ------------------------------------------------------------------ residual + sandwich norm
 // One CTA per row; each thread owns up to kMaxChunks groups of 8 features, kept in registers between the passes.
-constexpr int kMaxChunks = 4;
-
 __global__ void __launch_bounds__(kRowThreads) residual_norm_kernel(const ResNormParams p) {
   __shared__ float red[32];
   if (threadIdx.x == 0) pdl_trigger();
   pdl_wait();
-  const int t = blockIdx.x;
-  const int H = p.hidden;
-  const size_t part = (size_t)p.m * H;
-  const float* yrow = p.y + (size_t)t * H;
-  const float* hin = p.h_in + (size_t)t * H;
-  float* hout = p.h_out + (size_t)t * H;
-  __nv_bfloat16* xrow = p.x_out + (size_t)t * H;
-  float yv[kMaxChunks][8];
-  float ss = 0.f;
-#pragma unroll
-  for (int k = 0; k < kMaxChunks; ++k) {
-    const int c = (threadIdx.x + k * kRowThreads) * 8;
-    if (c >= H) break;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) yv[k][i] = 0.f;
-    for (int s = 0; s < p.y_parts; ++s) {  // split-K partials summed in split order
-      const float4 a = __ldcg(reinterpret_cast<const float4*>(yrow + s * part + c));
-      const float4 b = __ldcg(reinterpret_cast<const float4*>(yrow + s * part + c + 4));
-      yv[k][0] += a.x; yv[k][1] += a.y; yv[k][2] += a.z; yv[k][3] += a.w;
-      yv[k][4] += b.x; yv[k][5] += b.y; yv[k][6] += b.z; yv[k][7] += b.w;
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) ss += yv[k][i] * yv[k][i];
-  }
-  const float ra = rsqrtf(block_sum(ss, red) / H + p.eps);
-  float s2 = 0.f;
-#pragma unroll
-  for (int k = 0; k < kMaxChunks; ++k) {
-    const int c = (threadIdx.x + k * kRowThreads) * 8;
-    if (c >= H) break;
-    const float4 ha = *reinterpret_cast<const float4*>(hin + c);
-    const float4 hb = *reinterpret_cast<const float4*>(hin + c + 4);
-    const float hv[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
-    const uint4 wraw = *reinterpret_cast<const uint4*>(p.w_a + c);
-    const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(&wraw);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      yv[k][i] = hv[i] + __bfloat162float(w[i]) * (yv[k][i] * ra);  // now the new residual
-      s2 += yv[k][i] * yv[k][i];
-    }
-    *reinterpret_cast<float4*>(hout + c) = make_float4(yv[k][0], yv[k][1], yv[k][2], yv[k][3]);
-    *reinterpret_cast<float4*>(hout + c + 4) = make_float4(yv[k][4], yv[k][5], yv[k][6], yv[k][7]);
-  }
-  const float rb = rsqrtf(block_sum(s2, red) / H + p.eps);
-#pragma unroll
-  for (int k = 0; k < kMaxChunks; ++k) {
-    const int c = (threadIdx.x + k * kRowThreads) * 8;
-    if (c >= H) break;
-    const uint4 wraw = *reinterpret_cast<const uint4*>(p.w_b + c);
-    const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(&wraw);
-    uint4 out;
-    uint32_t* o = reinterpret_cast<uint32_t*>(&out);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      o[i] = pack_bf16(__bfloat162float(w[2 * i]) * (yv[k][2 * i] * rb),
-                       __bfloat162float(w[2 * i + 1]) * (yv[k][2 * i + 1] * rb));
-    *reinterpret_cast<uint4*>(xrow + c) = out;
-  }
+  resnorm_row(p, blockIdx.x, threadIdx.x, blockDim.x, 1, red);
 }
 
 // ------------------------------------------------------------------ accept and commit

@@ -106,6 +106,13 @@ def attention_split(bs: int, K: int, max_len: int, avg_len: int, n_kv: int, sms:
     return chunk, max(1, -(-L // chunk))
 
 
+class _LAUNCH:
+    """Per-launch issue of the forward's kernels (the interface L.SmallPlan records)."""
+    linear = staticmethod(L.linear)
+    bd_attention = staticmethod(L.bd_attention)
+    residual_norm = staticmethod(L.residual_norm)
+
+
 @dataclass
 class RoundBuffers:
     bs: int
@@ -149,7 +156,8 @@ class Engine:
     """One model replica on one GPU: the forward, the round and graph capture."""
 
     def __init__(self, cfg: ModelConfig, weights: Dict[str, torch.Tensor], *, max_rows: int, n_pages: int,
-                 page_size: int = 16, device: Optional[torch.device] = None, pdl: bool = True):
+                 page_size: int = 16, device: Optional[torch.device] = None, pdl: bool = True,
+                 small_rows: int = 64):
         L.load()
         if page_size != 16:
             raise ValueError("the attention kernel's TMA box is one 16-token page")
@@ -176,6 +184,10 @@ class Engine:
         self.attn_ws: Optional[torch.Tensor] = None
         self.sms = L.num_sms()
         self.graphs: Dict[Tuple[int, int], torch.cuda.CUDAGraph] = {}
+        # forwards of at most small_rows rows (with lm_head) run as one persistent kernel (L.SmallPlan), built on
+        # first use for each set of buffers; 0 disables it
+        self.small_rows = small_rows
+        self._small: Dict[tuple, "L.SmallPlan"] = {}
 
     # ------------------------------------------------------------------ workspace
     def gemm_shapes(self) -> List[Tuple[int, int]]:
@@ -228,13 +240,35 @@ class Engine:
             if torch.cuda.is_current_stream_capturing():
                 raise RuntimeError(f"scratch too small for M={M}; call reserve() before capture")
             self.reserve(M)
-        draft = rows_mode == L.ROWS_DRAFT
-        base_add = 1 if rows_mode == L.ROWS_VERIFY else 0
         L.embed_rows(rows_mode, bs, K, seeds=seeds, rpi=rpi, ids32=ids32, ids64=ids64, row_embeds=row_embeds,
                      seq_lens=seq_lens, page_table=page_table, page_size=self.page_size, embed=w.embed, vocab=cfg.vocab,
                      mask_id=cfg.mask_id, norm_w=w.layers[0]["in"], eps=cfg.rms_eps, h_out=self.h[0], x_out=self.x,
                      row_pos=self.row_pos, row_slot=self.row_slot, row_ids=self.row_ids, status=st)
         ws_attn = self._attn_workspace(bs, K, attn_splits) if attn_splits > 1 else None
+        args = (rows_mode, bs, K, seq_lens, page_table, out_idx, out_top1, out_gap, attn_chunk, attn_splits, st, head,
+                order, ws_attn)
+        if head and 0 < M <= self.small_rows:
+            key = tuple(t.data_ptr() if isinstance(t, torch.Tensor) else t for t in args) + (
+                self.y.data_ptr(), self.lin_ws.data_ptr(), self.y.numel())
+            plan = self._small.get(key)
+            if plan is None:
+                if torch.cuda.is_current_stream_capturing():
+                    raise RuntimeError("no persistent plan for this forward yet: run it once eagerly before capture")
+                plan = L.SmallPlan()
+                self._forward_body(plan, *args)
+                plan.finalize(st)
+                self._small[key] = plan
+            plan.launch()
+            return
+        self._forward_body(_LAUNCH, *args)
+
+    def _forward_body(self, ops, rows_mode, bs, K, seq_lens, page_table, out_idx, out_top1, out_gap, attn_chunk,
+                      attn_splits, st, head, order, ws_attn) -> None:
+        """The layers and lm_head after the embedding rows, issued through ``ops``: the library's per-launch calls
+        (_LAUNCH) or a persistent plan recording them (L.SmallPlan)."""
+        cfg, w, M = self.cfg, self.w, bs * K
+        draft = rows_mode == L.ROWS_DRAFT
+        base_add = 1 if rows_mode == L.ROWS_VERIFY else 0
         cur = 0
         for l, d in enumerate(w.layers):
             nxt = w.layers[l + 1] if l + 1 < len(w.layers) else None
@@ -250,8 +284,8 @@ class Engine:
             e.n_q_heads = cfg.n_q_heads
             e.n_kv_heads = cfg.n_kv_heads
             e.page_size = self.page_size
-            L.linear(d["qkv"], self.x, M, e, self.lin_ws, prefetch=d["o"], status=st)
-            L.bd_attention(self.q, self.pool.k[l], self.pool.v[l], page_table, seq_lens, bs, K, draft, base_add,
+            ops.linear(d["qkv"], self.x, M, e, self.lin_ws, prefetch=d["o"], status=st)
+            ops.bd_attention(self.q, self.pool.k[l], self.pool.v[l], page_table, seq_lens, bs, K, draft, base_add,
                            cfg.n_q_heads, cfg.n_kv_heads, self.page_size, attn_chunk, attn_splits, self.attn, ws_attn,
                            status=st, order=order)
             e = L.Epilogue()
@@ -259,23 +293,23 @@ class Engine:
             e.out = self.y.data_ptr()
             e.ld_out = cfg.hidden
             sp_o = self.splits(cfg.hidden, cfg.q_dim, M)
-            L.linear(d["o"], self.attn, M, e, self.lin_ws, splits=sp_o, prefetch=d["gate_up"], status=st)
-            L.residual_norm(M, self.h[cur], self.y, d["psa"], d["pa"], cfg.rms_eps, self.h[1 - cur], self.x,
+            ops.linear(d["o"], self.attn, M, e, self.lin_ws, splits=sp_o, prefetch=d["gate_up"], status=st)
+            ops.residual_norm(M, self.h[cur], self.y, d["psa"], d["pa"], cfg.rms_eps, self.h[1 - cur], self.x,
                             y_parts=sp_o)
             cur ^= 1
             e = L.Epilogue()
             e.mode = L.EPI_SWIGLU
             e.out = self.act.data_ptr()
             e.ld_out = cfg.intermediate
-            L.linear(d["gate_up"], self.x, M, e, self.lin_ws, prefetch=d["down"], status=st)
+            ops.linear(d["gate_up"], self.x, M, e, self.lin_ws, prefetch=d["down"], status=st)
             e = L.Epilogue()
             e.mode = L.EPI_PARTIAL_F32
             e.out = self.y.data_ptr()
             e.ld_out = cfg.hidden
             sp_d = self.splits(cfg.hidden, cfg.intermediate, M)
             pf = nxt["qkv"] if nxt is not None else w.lm_head[: min(w.lm_head.shape[0], 16384)]
-            L.linear(d["down"], self.act, M, e, self.lin_ws, splits=sp_d, prefetch=pf, status=st)
-            L.residual_norm(M, self.h[cur], self.y, d["pm"], nxt["in"] if nxt is not None else w.norm, cfg.rms_eps,
+            ops.linear(d["down"], self.act, M, e, self.lin_ws, splits=sp_d, prefetch=pf, status=st)
+            ops.residual_norm(M, self.h[cur], self.y, d["pm"], nxt["in"] if nxt is not None else w.norm, cfg.rms_eps,
                             self.h[1 - cur], self.x, y_parts=sp_d)
             cur ^= 1
         if not head:
@@ -285,7 +319,7 @@ class Engine:
         e.out_idx = out_idx.data_ptr()
         e.out_top1 = 0 if out_top1 is None else out_top1.data_ptr()
         e.out_gap = 0 if out_gap is None else out_gap.data_ptr()
-        L.linear(w.lm_head, self.x, M, e, self.lin_ws, status=st)
+        ops.linear(w.lm_head, self.x, M, e, self.lin_ws, status=st)
 
     def final_hidden(self) -> torch.Tensor:
         """Normed input of lm_head of the last forward (bf16 [max_rows, H]); for logits checks in tests."""
@@ -410,9 +444,11 @@ class Engine:
         self.draft_launch(rb, override)
         self.verify_launch(rb)
 
-    def kernels_per_forward(self) -> int:
-        """Kernel launches of one forward: embed + per layer (4 projections, attention, 2 residual norms) + lm_head
-        (projection + per-token argmax reduction)."""
+    def kernels_per_forward(self, rows: int = 0) -> int:
+        """Kernel launches of one forward of `rows` rows: embed + per layer (4 projections, attention, 2 residual
+        norms) + lm_head (projection + per-token argmax reduction); embed + the persistent kernel for small forwards."""
+        if 0 < rows <= self.small_rows:
+            return 2
         return 3 + 7 * self.cfg.n_layers
 
     def capture(self, rb: RoundBuffers, override: bool = False, warmup: int = 0) -> torch.cuda.CUDAGraph:
