@@ -85,15 +85,17 @@ __device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, in
     __syncwarp();
   } else if constexpr (EPI == GR_EPI_SWIGLU) {
     // rows 2j / 2j+1 of the tile are gate / up of feature 64*n_tile + j (gr_pack_gate_up): the pair sits in adjacent
-    // lanes, so one shuffle brings the up value to the gate lane.  The warp's 16 features x 16 tokens are staged
-    // [token][16 features] and written as one 16-byte vector per lane (token lane / 2, features 8 * (lane & 1) + 0..7).
+    // lanes.  The gate lane computes tokens 0-7 and the up lane tokens 8-15 of the chunk: one shuffle per token pair
+    // swaps the gate lane's gates 8-15 for the up lane's ups 0-7, so both lanes do half the math.  The warp's
+    // 16 features x 16 tokens are staged [token][16 features] and written as one 16-byte vector per lane (token
+    // lane / 2, features 8 * (lane & 1) + 0..7).
+    const bool up_lane = lane & 1;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float u = __shfl_xor_sync(0xffffffffu, v[i], 1);
-      if (!(lane & 1)) {
-        const float g = v[i];
-        stage[i * 16 + (lane >> 1)] = __float2bfloat16_rn(u * __fdividef(g, 1.0f + __expf(-g)));
-      }
+    for (int i = 0; i < 8; ++i) {
+      const float other = __shfl_xor_sync(0xffffffffu, up_lane ? v[i] : v[8 + i], 1);
+      const float g = up_lane ? other : v[i];     // gate of token (up_lane ? 8 + i : i)
+      const float u = up_lane ? v[8 + i] : other;  // up of the same token
+      stage[(up_lane ? 8 + i : i) * 16 + (lane >> 1)] = __float2bfloat16_rn(u * __fdividef(g, 1.0f + __expf(-g)));
     }
     __syncwarp();
     const int tok = lane >> 1, hh = lane & 1;
@@ -116,15 +118,24 @@ __device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, in
     const long long slot_l = is_q ? 0ll : p.row_slot[tl];
     float o[16];
     if (rot) {
+      // Lanes d and d ^ 1 rotate the same pair and need the same angles: the even lane computes cos / sin for
+      // tokens 0-7 and the odd lane for tokens 8-15, and they swap the results.
       const int pos_l = p.row_pos[tl];
       const float fr = p.inv_freq[d >> 1];
+      const bool odd = d & 1;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float partner = __shfl_xor_sync(0xffffffffu, v[i], 1);
-        const int pos = __shfl_sync(0xffffffffu, pos_l, i);
+      for (int i = 0; i < 8; ++i) {
+        const int pos = __shfl_sync(0xffffffffu, pos_l, odd ? 8 + i : i);
         float sn, cs;
         rope_sincos(__fmul_rn(static_cast<float>(pos), fr), &sn, &cs);  // the reference's fp32 pos * inv_freq
-        o[i] = (d & 1) ? (v[i] * cs + partner * sn) : (v[i] * cs - partner * sn);
+        const float cs_o = __shfl_xor_sync(0xffffffffu, cs, 1);
+        const float sn_o = __shfl_xor_sync(0xffffffffu, sn, 1);
+        const float ca = odd ? cs_o : cs, sa = odd ? sn_o : sn;  // token i
+        const float cb = odd ? cs : cs_o, sb = odd ? sn : sn_o;  // token 8 + i
+        const float pa = __shfl_xor_sync(0xffffffffu, v[i], 1);
+        const float pb = __shfl_xor_sync(0xffffffffu, v[8 + i], 1);
+        o[i] = odd ? (v[i] * ca + pa * sa) : (v[i] * ca - pa * sa);
+        o[8 + i] = odd ? (v[8 + i] * cb + pb * sb) : (v[8 + i] * cb - pb * sb);
       }
     } else {
 #pragma unroll
