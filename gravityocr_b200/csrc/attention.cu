@@ -64,6 +64,32 @@ static cudaError_t configure_attention() {
   return cudaSuccess;
 }
 
+// Whether clusters of `size` CTAs of the small-batch configuration fit on the device (cached per size).
+static bool attention_cluster_ok(int size, int threads, size_t smem) {
+  static int known[17] = {0};  // 0 unknown, 1 yes, 2 no
+  if (known[size]) return known[size] == 1;
+  bool ok = false;
+  auto kern = attention_kernel<288, 1, 4>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(size);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = size;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    ok = cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n >= 1;
+  }
+  cudaGetLastError();  // a refused query leaves no sticky error
+  known[size] = ok ? 1 : 2;
+  return ok;
+}
+
 cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p,
                              cudaStream_t stream, bool pdl) {
   const int G = p.n_q_heads / p.n_kv_heads;
@@ -84,11 +110,23 @@ cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, con
   cfg.blockDim = dim3(32 * warps);
   cfg.dynamicSmemBytes = attention_smem_bytes(p.K, G, stages);
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  // Small batches with split KV: the splits of a (request, kv head) form one thread-block cluster and merge their
+  // partials through distributed shared memory (no global round trip, no ticket), where the device can hold such
+  // clusters.
+  q.cluster = (small && p.max_splits >= 2 && p.max_splits <= 16 &&
+               attention_cluster_ok(p.max_splits, 32 * warps, cfg.dynamicSmemBytes)) ? 1 : 0;
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (q.cluster) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = p.max_splits;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
   return small ? cudaLaunchKernelEx(&cfg, attention_kernel<288, 1, 4>, tmk, tmv, q)
                : cudaLaunchKernelEx(&cfg, attention_kernel<288, 1, 3>, tmk, tmv, q);
 }

@@ -19,6 +19,27 @@ __device__ __forceinline__ int row_limit(const AttnParams& p, int j, int base) {
 __device__ __forceinline__ void named_bar(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
+// All threads of every CTA of the cluster (release / acquire: shared-memory writes before it are visible to the
+// cluster's DSMEM reads after it).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ float2 ld_dsmem_f2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+  return v;
+}
 
 // Shared-memory state of a CTA's attention ring, kept across the units it runs: ST stages of kStageBytes, the query
 // staging area, the stage barriers (full: one arrival + bytes; empty: one per consuming warp), a flag word and the
@@ -76,16 +97,22 @@ __device__ void attention_unit(const CUtensorMap* tmk_p, const CUtensorMap* tmv_
   const int base = static_cast<int>(seq) + p.base_add;
   const int L = base + p.K;  // the last row's limit
   const int n_active = (L + p.chunk - 1) / p.chunk;
-  if (split >= n_active) return;
+  const bool active = split < n_active;
+  if (!active && !p.cluster) return;  // a cluster's idle splits still join its barriers (and the merge)
   const int kv_beg = split * p.chunk;
   const int kv_end = min(L, kv_beg + p.chunk);
-  const int n_tiles = (kv_end - kv_beg + kTile - 1) / kTile;
+  const int n_tiles = active ? (kv_end - kv_beg + kTile - 1) / kTile : 0;
+  // cluster merge: each split's (O, m, l) partial in its own shared memory, past the group exchange area
+  float* part_o = reinterpret_cast<float*>(kv_smem + 32768);  // [R_pad][128]
+  float* part_ml = part_o + R_pad * 128;                      // [R_pad][2]
   const int tb = c.tile_base;  // this unit streams the ring's tiles tb .. tb + n_tiles - 1
   c.tile_base += n_tiles;
 
   const int* pt = p.page_table + (size_t)b * p.pt_stride;
   const size_t q_row_stride = (size_t)p.n_q_heads * 128;
-  if (warp == n_cw) {
+  if (!active) {
+    // idle split of a cluster: no tiles, no partial
+  } else if (warp == n_cw) {
     // ------------------------------------------------------------ producer
     // the whole split's page ids in one coalesced pass (pages past the request's last page hold no visible token:
     // they are replaced by its last page, whose contents are finite)
@@ -287,6 +314,8 @@ __device__ void attention_unit(const CUtensorMap* tmk_p, const CUtensorMap* tmv_
     }
 
     // ------------------------------------------------------------ write / merge (group 0)
+    // the cluster partials overwrite the stage ring: every compute warp must be done with its last tile
+    if (p.cluster && n_active > 1) named_bar(bar_cw, n_cw * 32);
     if (grp == 0) {
       if (n_active == 1) {
 #pragma unroll
@@ -301,6 +330,17 @@ __device__ void attention_unit(const CUtensorMap* tmk_p, const CUtensorMap* tmv_
             const int d = n * 8 + 2 * t4;
             *reinterpret_cast<uint32_t*>(dst + d) = pack_bf16(o[n][2 * h] * inv, o[n][2 * h + 1] * inv);
           }
+        }
+      } else if (p.cluster) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = mt * 16 + g4 + 8 * h;
+#pragma unroll
+          for (int n = 0; n < 16; ++n) {
+            const int d = n * 8 + 2 * t4;
+            *reinterpret_cast<float2*>(part_o + r * 128 + d) = make_float2(o[n][2 * h], o[n][2 * h + 1]);
+          }
+          if (t4 == 0) *reinterpret_cast<float2*>(part_ml + r * 2) = make_float2(m_run[h], l_run[h]);
         }
       } else {
         const size_t slot = ((size_t)b * p.n_kv_heads + kvh) * p.max_splits + split;
@@ -321,6 +361,59 @@ __device__ void attention_unit(const CUtensorMap* tmk_p, const CUtensorMap* tmv_
         }
       }
     }
+  }
+  if (p.cluster) {
+    // Every split of the (request, kv head) is a CTA of this cluster (rank = split).  After the barrier each CTA
+    // merges a share of the rows, reading the splits' partials from their shared memory in split order with the
+    // same arithmetic as the global-memory merge below; the second barrier keeps the partials alive until read.
+    cluster_sync_all();
+    if (n_active > 1) {
+      const int cs = p.max_splits, n_warps = nthr >> 5;
+      for (int r = split * n_warps + warp; r < R; r += cs * n_warps) {
+        float M = -INFINITY;
+        float ms[kMaxMergeSplits], ls[kMaxMergeSplits];
+#pragma unroll
+        for (int s2 = 0; s2 < kMaxMergeSplits; ++s2) {
+          if (s2 < n_active) {
+            const float2 ml = ld_dsmem_f2(dsmem_addr(part_ml + r * 2, s2));
+            ms[s2] = ml.x;
+            ls[s2] = ml.y;
+            M = fmaxf(M, ml.x);
+          }
+        }
+        const float Ms = (M == -INFINITY) ? 0.f : M;
+        float Lsum = 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < kMaxMergeSplits; ++s2) {
+          if (s2 < n_active) {
+            const float w = (ms[s2] == -INFINITY) ? 0.f : exp2f(ms[s2] - Ms);
+            ms[s2] = w;
+            Lsum += ls[s2] * w;
+          }
+        }
+        const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int s2 = 0; s2 < kMaxMergeSplits; ++s2) {
+          if (s2 < n_active) {
+            const float w = ms[s2] * inv;
+            const float4 ov = ld_dsmem_f4(dsmem_addr(part_o + r * 128 + lane * 4, s2));
+            acc.x += ov.x * w;
+            acc.y += ov.y * w;
+            acc.z += ov.z * w;
+            acc.w += ov.w * w;
+          }
+        }
+        const int g = r / p.K, j = r % p.K;
+        __nv_bfloat16* dst = p.out + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128 + lane * 4;
+        uint2 pk;
+        pk.x = pack_bf16(acc.x, acc.y);
+        pk.y = pack_bf16(acc.z, acc.w);
+        *reinterpret_cast<uint2*>(dst) = pk;
+      }
+    }
+    cluster_sync_all();
+    return;
   }
   if (n_active == 1) return;
 

@@ -92,16 +92,17 @@ class PagePool:
 
 def attention_split(bs: int, K: int, max_len: int, avg_len: int, n_kv: int, sms: int) -> Tuple[int, int]:
     """Cache tokens per split and the split-grid extent.  With enough (request, head) pairs to fill the GPU twice the
-    requests run unsplit (no merge); otherwise each pair is cut into up to 16 splits of >= 256 tokens so that about
-    2 x SMs CTAs stream in parallel.  At most 16 splits per pair (the merge's limit)."""
+    requests run unsplit (no merge); otherwise each pair is cut into splits of >= 128 tokens so that about 2 x SMs
+    CTAs stream in parallel.  A small batch's splits merge inside one thread-block cluster, so there are at most 8
+    (a portable cluster); larger batches allow up to 16 (the global merge's limit)."""
     L = max_len + K + 1
     units = max(1, bs * n_kv)
     if units >= 2 * sms:
         chunk = 4096
     else:
         want = min(16, -(-2 * sms // units))
-        chunk = max(256, -(-max(1, avg_len) // want))
-    chunk = max(chunk, -(-L // 16))
+        chunk = max(128, -(-max(1, avg_len) // want))
+    chunk = max(chunk, -(-L // (8 if units < 2 * sms else 16)))
     chunk = min(4096, -(-chunk // 64) * 64)
     return chunk, max(1, -(-L // chunk))
 
