@@ -94,10 +94,10 @@ cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, con
                              cudaStream_t stream, bool pdl) {
   const int G = p.n_q_heads / p.n_kv_heads;
   const int n_mt = (G * p.K + 15) / 16;
-  // Large batches: one warp group, 3 stages, small CTAs (two per SM).  Small batches (fewer (request, head) pairs
-  // than two per SM): two groups on alternate tiles over 4 stages, and at least kMinWarps warps for the split merge.
+  // Large grids: one warp group, 3 stages, small CTAs (two per SM).  Grids of at most one CTA per SM: two groups on
+  // alternate tiles over 4 stages (a CTA's latency is the launch's), and at least kMinWarps warps for the merge.
   AttnParams q = p;
-  const bool small = p.bs * p.n_kv_heads < 2 * 148;
+  const bool small = p.bs * p.n_kv_heads * p.max_splits <= 148;
   q.groups = (small && 2 * n_mt + 1 <= 9) ? 2 : 1;  // up to 288 threads
   int warps = q.groups * n_mt + 1;
   if (small && p.max_splits > 1 && warps < kMinWarps) warps = kMinWarps;
