@@ -21,7 +21,7 @@ EPI_STORE_F32, EPI_STORE_BF16, EPI_SWIGLU, EPI_QKV_ROPE, EPI_ARGMAX, EPI_PARTIAL
 ROWS_DRAFT, ROWS_VERIFY, ROWS_EXPLICIT = range(3)
 
 # every symbol include/gravity_b200.h declares
-EXPORTS = ("gr_version", "gr_status_string", "gr_set_pdl", "gr_num_sms", "gr_linear_workspace_bytes",
+EXPORTS = ("gr_version", "gr_status_string", "gr_set_pdl", "gr_set_attention_tc", "gr_num_sms", "gr_linear_workspace_bytes",
            "gr_attention_workspace_bytes", "gr_linear_default_splits", "gr_linear", "gr_embed_rows",
            "gr_residual_norm", "gr_bd_attention", "gr_accept_commit", "gr_draft_override", "gr_pack_gate_up",
            "gr_bd_attention_noalloc", "gr_bd_attention_ordered", "gr_small_create", "gr_small_destroy",
@@ -58,6 +58,7 @@ _SIGS = {
     "gr_version": (_I, []),
     "gr_status_string": (ctypes.c_char_p, [_I]),
     "gr_set_pdl": (None, [_I]),
+    "gr_set_attention_tc": (None, [_I]),
     "gr_num_sms": (_I, []),
     "gr_linear_workspace_bytes": (_Z, [_I, _I, _I]),
     "gr_attention_workspace_bytes": (_Z, [_I, _I, _I, _I, _I]),
@@ -130,6 +131,11 @@ def _need(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
 # ---------------------------------------------------------------------- wrappers
 def set_pdl(enable: bool) -> None:
     load().gr_set_pdl(1 if enable else 0)
+
+
+def set_attention_tc(enable: bool) -> None:
+    """Large attention grids on the tcgen05 kernel (default) or on the mma.sync kernel."""
+    load().gr_set_attention_tc(1 if enable else 0)
 
 
 def num_sms() -> int:

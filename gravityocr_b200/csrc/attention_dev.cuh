@@ -72,6 +72,121 @@ __device__ __forceinline__ AttnCta attn_cta_layout(uint8_t* region, int R_pad) {
   return c;
 }
 
+// Split merge through global memory: every split of (request b, kv head kvh) has written its (O, m, l) partial to
+// ws_o / ws_ml; the last split to arrive merges them in split order.  Called by all nthr participating threads of
+// each split's CTA (named barrier bar_all); `flag` is a shared int, `wgt` shared scratch of R * kMaxMergeSplits
+// floats.
+__device__ inline void attention_merge_global(const AttnParams& p, int b, int kvh, int n_active, int wt, int nthr,
+                                              int bar_all, int* flag, float* wgt) {
+  const int G = p.n_q_heads / p.n_kv_heads;
+  const int R = G * p.K;
+  const int R_pad = attn_rows_pad(G, p.K);
+  const size_t q_row_stride = (size_t)p.n_q_heads * 128;
+  __threadfence();
+  named_bar(bar_all, nthr);
+  if (wt == 0) {
+    int* tk = p.ws_ticket + (size_t)b * p.n_kv_heads + kvh;
+    const int prev = atomicAdd(tk, 1);
+    *flag = (prev == n_active - 1) ? 2 : 0;
+    if (*flag) *tk = 0;
+  }
+  named_bar(bar_all, nthr);
+  if (*flag != 2) return;
+  __threadfence();
+  const size_t slot0 = ((size_t)b * p.n_kv_heads + kvh) * p.max_splits;
+  // phase A: per (row, split) weights exp2(m_s - M) / L into shared memory (the stage ring is idle now)
+  for (int r = wt; r < R; r += nthr) {
+    float M = -INFINITY;
+    float ms[kMaxMergeSplits], ls[kMaxMergeSplits];
+#pragma unroll
+    for (int s = 0; s < kMaxMergeSplits; ++s) {
+      if (s < n_active) {
+        const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + ((slot0 + s) * R_pad + r) * 2));
+        ms[s] = ml.x;
+        ls[s] = ml.y;
+        M = fmaxf(M, ml.x);
+      }
+    }
+    const float Ms = (M == -INFINITY) ? 0.f : M;
+    float Lsum = 0.f;
+#pragma unroll
+    for (int s = 0; s < kMaxMergeSplits; ++s) {
+      if (s < n_active) {
+        const float w = (ms[s] == -INFINITY) ? 0.f : exp2f(ms[s] - Ms);
+        ms[s] = w;
+        Lsum += ls[s] * w;
+      }
+    }
+    const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+#pragma unroll
+    for (int s = 0; s < kMaxMergeSplits; ++s)
+      if (s < n_active) wgt[r * kMaxMergeSplits + s] = ms[s] * inv;
+  }
+  named_bar(bar_all, nthr);
+  // phase B: (row, 4 dims) items; every split's loads of an item are issued together, summed in split order.  With
+  // at most 4 splits, four items' loads go out together.
+  auto store4 = [&](int it, float4 acc) {
+    const int r = it >> 5, q4 = it & 31;
+    const int g = r / p.K, j = r % p.K;
+    __nv_bfloat16* dst = p.out + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128 + q4 * 4;
+    uint2 pk;
+    pk.x = pack_bf16(acc.x, acc.y);
+    pk.y = pack_bf16(acc.z, acc.w);
+    *reinterpret_cast<uint2*>(dst) = pk;
+  };
+  if (n_active <= 4) {
+    for (int it0 = wt; it0 < R * 32; it0 += 4 * nthr) {
+      float4 os[4][4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int it = it0 + u * nthr;
+#pragma unroll
+        for (int sp = 0; sp < 4; ++sp)
+          if (it < R * 32 && sp < n_active)
+            os[u][sp] = __ldcg(reinterpret_cast<const float4*>(p.ws_o + ((slot0 + sp) * R_pad + (it >> 5)) * 128) +
+                               (it & 31));
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int it = it0 + u * nthr;
+        if (it >= R * 32) break;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int sp = 0; sp < 4; ++sp) {
+          if (sp < n_active) {
+            const float w = wgt[(it >> 5) * kMaxMergeSplits + sp];
+            acc.x += os[u][sp].x * w;
+            acc.y += os[u][sp].y * w;
+            acc.z += os[u][sp].z * w;
+            acc.w += os[u][sp].w * w;
+          }
+        }
+        store4(it, acc);
+      }
+    }
+    return;
+  }
+  for (int it = wt; it < R * 32; it += nthr) {
+    const int r = it >> 5, q4 = it & 31;
+    float4 os[kMaxMergeSplits];
+#pragma unroll
+    for (int s = 0; s < kMaxMergeSplits; ++s)
+      if (s < n_active) os[s] = __ldcg(reinterpret_cast<const float4*>(p.ws_o + ((slot0 + s) * R_pad + r) * 128) + q4);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int s = 0; s < kMaxMergeSplits; ++s) {
+      if (s < n_active) {
+        const float w = wgt[r * kMaxMergeSplits + s];
+        acc.x += os[s].x * w;
+        acc.y += os[s].y * w;
+        acc.z += os[s].z * w;
+        acc.w += os[s].w * w;
+      }
+    }
+    store4(it, acc);
+  }
+}
+
 // One unit.  Participating threads: wt in [0, nthr), warp aw = wt / 32; warps aw < groups * n_mt compute, warp
 // aw == groups * n_mt is the TMA producer, the rest only help the split merge.  bar_all / bar_cw are named barrier
 // ids for all participants / the compute warps.  Every participant calls with the same arguments.
@@ -416,112 +531,7 @@ __device__ void attention_unit(const CUtensorMap* tmk_p, const CUtensorMap* tmv_
     return;
   }
   if (n_active == 1) return;
-
-  // last split to arrive merges every split's partial in split order
-  __threadfence();
-  named_bar(bar_all, nthr);
-  if (wt == 0) {
-    int* tk = p.ws_ticket + (size_t)b * p.n_kv_heads + kvh;
-    const int prev = atomicAdd(tk, 1);
-    *flag = (prev == n_active - 1) ? 2 : 0;
-    if (*flag) *tk = 0;
-  }
-  named_bar(bar_all, nthr);
-  if (*flag != 2) return;
-  __threadfence();
-  const size_t slot0 = ((size_t)b * p.n_kv_heads + kvh) * p.max_splits;
-  // phase A: per (row, split) weights exp2(m_s - M) / L into shared memory (the stage ring is idle now)
-  float* wgt = reinterpret_cast<float*>(kv_smem);  // [R][kMaxMergeSplits]
-  for (int r = wt; r < R; r += nthr) {
-    float M = -INFINITY;
-    float ms[kMaxMergeSplits], ls[kMaxMergeSplits];
-#pragma unroll
-    for (int s = 0; s < kMaxMergeSplits; ++s) {
-      if (s < n_active) {
-        const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + ((slot0 + s) * R_pad + r) * 2));
-        ms[s] = ml.x;
-        ls[s] = ml.y;
-        M = fmaxf(M, ml.x);
-      }
-    }
-    const float Ms = (M == -INFINITY) ? 0.f : M;
-    float Lsum = 0.f;
-#pragma unroll
-    for (int s = 0; s < kMaxMergeSplits; ++s) {
-      if (s < n_active) {
-        const float w = (ms[s] == -INFINITY) ? 0.f : exp2f(ms[s] - Ms);
-        ms[s] = w;
-        Lsum += ls[s] * w;
-      }
-    }
-    const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
-#pragma unroll
-    for (int s = 0; s < kMaxMergeSplits; ++s)
-      if (s < n_active) wgt[r * kMaxMergeSplits + s] = ms[s] * inv;
-  }
-  named_bar(bar_all, nthr);
-  // phase B: (row, 4 dims) items; every split's loads of an item are issued together, summed in split order.  With
-  // at most 4 splits, four items' loads go out together.
-  auto store4 = [&](int it, float4 acc) {
-    const int r = it >> 5, q4 = it & 31;
-    const int g = r / p.K, j = r % p.K;
-    __nv_bfloat16* dst = p.out + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128 + q4 * 4;
-    uint2 pk;
-    pk.x = pack_bf16(acc.x, acc.y);
-    pk.y = pack_bf16(acc.z, acc.w);
-    *reinterpret_cast<uint2*>(dst) = pk;
-  };
-  if (n_active <= 4) {
-    for (int it0 = wt; it0 < R * 32; it0 += 4 * nthr) {
-      float4 os[4][4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int it = it0 + u * nthr;
-#pragma unroll
-        for (int sp = 0; sp < 4; ++sp)
-          if (it < R * 32 && sp < n_active)
-            os[u][sp] = __ldcg(reinterpret_cast<const float4*>(p.ws_o + ((slot0 + sp) * R_pad + (it >> 5)) * 128) +
-                               (it & 31));
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int it = it0 + u * nthr;
-        if (it >= R * 32) break;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int sp = 0; sp < 4; ++sp) {
-          if (sp < n_active) {
-            const float w = wgt[(it >> 5) * kMaxMergeSplits + sp];
-            acc.x += os[u][sp].x * w;
-            acc.y += os[u][sp].y * w;
-            acc.z += os[u][sp].z * w;
-            acc.w += os[u][sp].w * w;
-          }
-        }
-        store4(it, acc);
-      }
-    }
-    return;
-  }
-  for (int it = wt; it < R * 32; it += nthr) {
-    const int r = it >> 5, q4 = it & 31;
-    float4 os[kMaxMergeSplits];
-#pragma unroll
-    for (int s = 0; s < kMaxMergeSplits; ++s)
-      if (s < n_active) os[s] = __ldcg(reinterpret_cast<const float4*>(p.ws_o + ((slot0 + s) * R_pad + r) * 128) + q4);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int s = 0; s < kMaxMergeSplits; ++s) {
-      if (s < n_active) {
-        const float w = wgt[r * kMaxMergeSplits + s];
-        acc.x += os[s].x * w;
-        acc.y += os[s].y * w;
-        acc.z += os[s].z * w;
-        acc.w += os[s].w * w;
-      }
-    }
-    store4(it, acc);
-  }
+  attention_merge_global(p, b, kvh, n_active, wt, nthr, bar_all, flag, reinterpret_cast<float*>(kv_smem));
 }
 
 }  // namespace gr

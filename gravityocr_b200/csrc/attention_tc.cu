@@ -1,0 +1,364 @@
+// Verify / draft attention on the 5th-generation tensor cores (tcgen05, TMEM accumulators), sm_100a: the large-batch
+// configuration of the paged attention in attention.cu, with the same unit (split, kv head, request), the same row
+// limits (draft: x0 causal, the block bidirectional; verify: causal), the same split-KV partials and the same merge.
+//
+// Rows of a unit: r = g*K + j (query head g of the GQA group, window row j), R = G*K <= 128, row r = TMEM lane r.
+// One CTA per unit, W + 2 warps with W = ceil(R / 32):
+//   warps 0..W-1  softmax, one thread per row (warp w reads TMEM lane quadrant w);
+//   warp W        TMA producer: 64-token tiles (4 pages, K and V, both 64-dim halves, 128-byte swizzle) into a
+//                 3-stage ring (two CTAs per SM);
+//   warp W + 1    allocates TMEM and issues the MMAs from one thread.
+// Per 64-token tile i (M = 128: rows R..127 are padding whose TMEM lanes no thread reads):
+//   S_i = Q K_i^T   tcgen05.mma, A = Q (K-major, shared memory), B = K tile (K-major), N = 64, D = TMEM S[i % 2];
+//   softmax         each thread loads its row of S_i (64 columns), masks, and exponentiates against its reference
+//                   max m: m moves (and the warp rescales its O rows in TMEM: ld, multiply, st) only when the tile's
+//                   max exceeds m by more than 2^8, so P <= 256; the sum l is kept in fp32 against the same m.  P_i
+//                   (bf16) is written as a K-major operand over the tile's consumed K (dims 0..63) in its stage;
+//   O += P_i V_i    tcgen05.mma, A = P (K-major), B = V tile (MN-major: 64 dims per 128-byte line, the two dim halves
+//                   8 KB apart), N = 128, D = TMEM O.  Its commit frees the stage.
+// The MMA thread issues whichever of S_{i+1} (its K/V landed, S buffer free) and O += P_i V_i (P_i written) is ready,
+// so the next tile's QK^T runs under this tile's softmax and a stage is freed as soon as its PV completes.
+// The result is O / l with O and l taken against the same m: the same quantity as the running-max formulation, up
+// to fp32 / bf16 rounding.
+#include "attention_dev.cuh"
+
+namespace gr {
+
+constexpr int kTcStages = 3;
+constexpr uint32_t kTcTmemCols = 256;  // S[0] 0..63, S[1] 64..127, O 128..255
+constexpr float kTcRescaleLog2 = 8.0f;  // the reference max moves when a row's max exceeds it by more than this
+
+__host__ __device__ constexpr int tc_rows(int G, int K) { return G * K; }
+// one 64-dim atom of the query operand: the rows rounded up to 8-row (1024-byte) swizzle groups
+__host__ __device__ constexpr uint32_t tc_q_atom_bytes(int R) { return static_cast<uint32_t>((R + 7) / 8) * 1024; }
+
+// Shared memory (1024-aligned): Q (two atoms), the ring, barriers, TMEM slot, flag, page ids.  An M = 128 operand
+// read from Q or from a stage's P runs past the rows written (rows that only feed padding lanes); everything it
+// reads stays inside the allocation.
+size_t attention_tc_smem_bytes(int G, int K) {
+  return 1024 + 2 * static_cast<size_t>(tc_q_atom_bytes(tc_rows(G, K))) + kTcStages * kStageBytes +
+         (3 * kTcStages + 4) * 8 + 16 + kMaxChunkPages * 4;
+}
+
+template <int ST>
+__global__ void __launch_bounds__(192) attention_tc_kernel(const __grid_constant__ CUtensorMap tmk,
+                                                           const __grid_constant__ CUtensorMap tmv,
+                                                           const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int G = p.n_q_heads / p.n_kv_heads;
+  const int R = tc_rows(G, p.K);
+  const int W = (R + 31) / 32;
+  const int w_prod = W, w_mma = W + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t qa = tc_q_atom_bytes(R);
+  uint8_t* q_smem = smem;
+  uint8_t* ring = smem + 2 * qa;
+  uint64_t* kv_full = reinterpret_cast<uint64_t*>(ring + ST * kStageBytes);
+  uint64_t* kv_empty = kv_full + ST;  // PV of the stage's tile complete: stage free, O up to date
+  uint64_t* s_full = kv_empty + ST;   // [2] by tile parity
+  uint64_t* p_full = s_full + 2;      // [2] by tile parity
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(p_full + 2);
+  int* flag = reinterpret_cast<int*>(tmem_slot + 2);
+  int* pages = flag + 2;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(kv_full + s, 1);
+      mbar_init(kv_empty + s, 1);
+    }
+    for (int k = 0; k < 2; ++k) {
+      mbar_init(s_full + k, 1);
+      mbar_init(p_full + k, W);  // one arrival per softmax warp
+    }
+    *flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmk);
+    tma_prefetch_desc(&tmv);
+  }
+  // TMEM is taken before the dependent launch is released: a CTA of a later kernel (which may wait for this grid)
+  // can then never hold the columns this CTA is waiting for
+  if (warp == w_mma) tmem_alloc(tmem_slot, kTcTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) pdl_trigger();
+  pdl_wait();
+
+  // blocks launch in z-major order: a longest-first request order shortens the tail of a mixed-length batch
+  const int b = p.order ? p.order[blockIdx.z] : blockIdx.z;
+  const int split = blockIdx.x, kvh = blockIdx.y;
+  const int base = static_cast<int>(p.seq_lens[b]) + p.base_add;
+  const int L = base + p.K;  // the last row's limit
+  const int n_active = (L + p.chunk - 1) / p.chunk;
+  const bool active = split < n_active;  // uniform over the CTA
+  const int kv_beg = split * p.chunk;
+  const int kv_end = min(L, kv_beg + p.chunk);
+  const int n_tiles = active ? (kv_end - kv_beg + kTile - 1) / kTile : 0;
+  const size_t q_row_stride = static_cast<size_t>(p.n_q_heads) * 128;
+  const int r = warp * 32 + lane;  // softmax warps: this thread's row
+  const bool valid = warp < W && r < R;
+  const int g = valid ? r / p.K : 0, j = valid ? r % p.K : 0;
+
+  if (active && warp < W) {
+    // ------------------------------------------------------------ query rows -> shared memory
+    const uint4* src = reinterpret_cast<const uint4*>(p.q + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128);
+    uint4 val[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) val[c] = valid ? src[c] : make_uint4(0, 0, 0, 0);
+    if (r < (R + 7) / 8 * 8) {
+#pragma unroll
+      for (int c = 0; c < 16; ++c) *reinterpret_cast<uint4*>(q_smem + (c >> 3) * qa + sw128(r, c & 7)) = val[c];
+    }
+    fence_proxy_async_smem();
+  }
+  if (active && (warp < W || warp == w_mma)) named_bar(2, (W + 1) * 32);  // Q staged before the first MMA
+
+  if (!active) {
+    // no tiles: straight to the teardown
+  } else if (warp == w_prod) {
+    // ------------------------------------------------------------ producer
+    // the split's page ids in one coalesced pass (pages past the request's last page hold no visible token: they
+    // are replaced by its last page, whose contents are finite)
+    const int* pt = p.page_table + (size_t)b * p.pt_stride;
+    const int last_page = (L - 1) / p.page_size;
+    const int pg_beg = kv_beg / p.page_size;
+    const int n_pg = n_tiles * (kTile / 16);
+    for (int i = lane; i < n_pg; i += 32) pages[i] = pt[min(pg_beg + i, last_page)];
+    __syncwarp();
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < n_tiles; ++i) {
+        const int s = i % ST;
+        if (i >= ST && !mbar_wait(kv_empty + s, ((i / ST) - 1) & 1, p.status, GR_ERR_TIMEOUT)) break;
+        mbar_arrive_expect_tx(kv_full + s, kStageBytes);
+        uint8_t* st = ring + s * kStageBytes;
+#pragma unroll
+        for (int pg = 0; pg < 4; ++pg) {
+          const int y = (pages[i * 4 + pg] * p.n_kv_heads + kvh) * p.page_size;
+          tma_load_2d(st + 0 * kHalfBytes + pg * 2048, &tmk, kv_full + s, 0, y);
+          tma_load_2d(st + 1 * kHalfBytes + pg * 2048, &tmk, kv_full + s, 64, y);
+          tma_load_2d(st + 2 * kHalfBytes + pg * 2048, &tmv, kv_full + s, 0, y);
+          tma_load_2d(st + 3 * kHalfBytes + pg * 2048, &tmv, kv_full + s, 64, y);
+        }
+        issued = i + 1;
+      }
+      // no copy may still be landing in shared memory when the CTA moves on
+      for (int i = max(0, issued - ST); i < issued; ++i)
+        mbar_wait(kv_full + (i % ST), (i / ST) & 1, p.status, GR_ERR_TIMEOUT);
+    }
+  } else if (warp == w_mma) {
+    // ------------------------------------------------------------ MMA issue (one thread)
+    if (lane == 0) {
+      const uint32_t id_s = idesc_bf16_f32(128, kTile);
+      const uint32_t id_pv = idesc_bf16_f32(128, 128) | (1u << 16);  // B (V) MN-major
+      const uint64_t qd0 = smem_desc_sw128(smem_u32(q_smem));
+      const uint64_t qd1 = smem_desc_sw128(smem_u32(q_smem + qa));
+      const uint64_t kd = smem_desc_sw128(smem_u32(ring));  // stage 0: K dims 0..63, later P
+      const uint64_t vd = smem_desc_sw128_mn(smem_u32(ring + 2 * kHalfBytes), kHalfBytes);  // stage 0: V dims 0..63
+      int s_next = 0, pv_next = 0;
+      uint64_t t0 = globaltimer();
+      while (pv_next < n_tiles) {
+        bool progress = false;
+        // O += P_k V_k as soon as P_k is written (frees the stage)
+        if (pv_next < s_next && mbar_test(p_full + (pv_next & 1), (pv_next >> 1) & 1)) {
+          tc_fence_after();
+          const int s = pv_next % ST;
+          const uint32_t so = (static_cast<uint32_t>(s) * kStageBytes) >> 4;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)  // 16 tokens per MMA: 32 bytes of a P row, 2 KB of V lines
+            tc_mma_bf16(tmem + 128, kd + so + 2 * kk, vd + so + 128 * kk, id_pv, (pv_next | kk) != 0);
+          tc_commit(kv_empty + s);
+          ++pv_next;
+          progress = true;
+        }
+        // S_i = Q K_i^T once its tile landed and its S buffer is free (the softmax is done with S_{i-2})
+        if (s_next < n_tiles && s_next <= pv_next + 1 && mbar_test(kv_full + s_next % ST, (s_next / ST) & 1)) {
+          tc_fence_after();
+          const uint32_t so = (static_cast<uint32_t>(s_next % ST) * kStageBytes) >> 4;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)  // 16 dims per MMA
+            tc_mma_bf16(tmem + (s_next & 1) * kTile, (kk < 4 ? qd0 : qd1) + 2 * (kk & 3),
+                        kd + so + (kk >> 2) * (kHalfBytes >> 4) + 2 * (kk & 3), id_s, kk != 0);
+          tc_commit(s_full + (s_next & 1));
+          ++s_next;
+          progress = true;
+        }
+        if (progress) {
+          t0 = globaltimer();
+        } else if (globaltimer() - t0 > GR_WAIT_NS) {
+          report(p.status, GR_ERR_TIMEOUT);
+          break;
+        }
+      }
+    }
+  } else if (warp < W) {
+    // ------------------------------------------------------------ softmax warps
+    const int lim = valid ? min(row_limit(p, j, base), kv_end) : 0;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int i = 0; i < n_tiles; ++i) {
+      ok = __all_sync(0xffffffffu, mbar_wait(s_full + (i & 1), (i >> 1) & 1, p.status, GR_ERR_TIMEOUT));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sr[2][32];
+      tmem_ld32_issue(t_lane + (i & 1) * kTile, sr[0]);
+      tmem_ld32_issue(t_lane + (i & 1) * kTile + 32, sr[1]);
+      tmem_ld32_wait(sr[0]);
+      tmem_ld32_wait(sr[1]);
+      const int tok0 = kv_beg + i * kTile;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float x = (tok0 + c < lim) ? __uint_as_float(sr[c >> 5][c & 31]) * p.scale_log2 : -INFINITY;
+        sr[c >> 5][c & 31] = __float_as_uint(x);
+        mx = fmaxf(mx, x);
+      }
+      // the reference max moves only when the tile's max exceeds it by more than 2^8 (always for the first visible
+      // token); O needs rescaling only if it already holds visible tokens
+      float m_new = m_run;
+      bool resc = false;
+      if (mx > m_run + kTcRescaleLog2) {
+        resc = m_run != -INFINITY;
+        m_new = mx;
+      }
+      const float alpha = resc ? exp2f(m_run - m_new) : 1.f;
+      const float msafe = (m_new == -INFINITY) ? 0.f : m_new;
+      float rs = 0.f;
+      uint32_t pk[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const float p0 = exp2f(__uint_as_float(sr[c >> 4][(2 * c) & 31]) - msafe);
+        const float p1 = exp2f(__uint_as_float(sr[c >> 4][(2 * c + 1) & 31]) - msafe);
+        rs += p0;
+        rs += p1;
+        pk[c] = pack_bf16(p0, p1);
+      }
+      l_run = l_run * alpha + rs;
+      m_run = m_new;
+      if (__any_sync(0xffffffffu, resc)) {
+        // O holds tiles 0..i-1 once the previous tile's PV completed (resc implies i > 0)
+        const int k = i - 1;
+        ok = __all_sync(0xffffffffu, mbar_wait(kv_empty + k % ST, (k / ST) & 1, p.status, GR_ERR_TIMEOUT));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint32_t o[32];
+          tmem_ld32_issue(t_lane + 128 + c4 * 32, o);
+          tmem_ld32_wait(o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(t_lane + 128 + c4 * 32, o);
+        }
+        tmem_wait_st();
+      }
+      // P_i over the stage's consumed K dims 0..63 (S_i, its only reader, has completed)
+      uint8_t* p_smem = ring + (i % ST) * kStageBytes;
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(p_smem + sw128(r, c)) = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2],
+                                                                     pk[4 * c + 3]);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full + (i & 1));
+    }
+    // ------------------------------------------------------------ output rows / split partials
+    if (ok) {
+      const int k = n_tiles - 1;  // the last PV
+      ok = __all_sync(0xffffffffu, mbar_wait(kv_empty + k % ST, (k / ST) & 1, p.status, GR_ERR_TIMEOUT));
+    }
+    if (ok) {
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      const int R_pad = attn_rows_pad(G, p.K);
+      const size_t slot = ((size_t)b * p.n_kv_heads + kvh) * p.max_splits + split;
+      __nv_bfloat16* dst_o = p.out + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128;
+      float* dst_w = p.ws_o + (slot * R_pad + (valid ? r : 0)) * 128;
+#pragma unroll 1
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t o[32];
+        tmem_ld32_issue(t_lane + 128 + c4 * 32, o);
+        tmem_ld32_wait(o);
+        if (!valid) continue;
+        if (n_active == 1) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 v;
+            v.x = pack_bf16(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv);
+            v.y = pack_bf16(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv);
+            v.z = pack_bf16(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv);
+            v.w = pack_bf16(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst_o + c4 * 32 + q * 8) = v;
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(dst_w + c4 * 32 + q * 4) =
+                make_float4(__uint_as_float(o[4 * q]), __uint_as_float(o[4 * q + 1]), __uint_as_float(o[4 * q + 2]),
+                            __uint_as_float(o[4 * q + 3]));
+        }
+      }
+      if (valid && n_active > 1) {
+        float* ml = p.ws_ml + (slot * R_pad + r) * 2;
+        ml[0] = m_run;
+        ml[1] = l_run;
+      }
+    }
+  }
+
+  // every TMEM read done and every MMA complete (the softmax warps waited for the last PV)
+  tc_fence_before();
+  __syncthreads();
+  if (warp == w_mma) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTcTmemCols);
+  }
+  if (active && n_active > 1)  // the ring is idle: the merge's weights go there
+    attention_merge_global(p, b, kvh, n_active, threadIdx.x, blockDim.x, 1, flag, reinterpret_cast<float*>(ring));
+}
+
+static cudaError_t configure_attention_tc() {
+  static bool configured = false;
+  if (configured) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel<kTcStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       227 * 1024);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(attention_tc_kernel<kTcStages>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e != cudaSuccess) return e;
+  configured = true;
+  return cudaSuccess;
+}
+
+bool attention_tc_fits(const AttnParams& p) {
+  const int G = p.n_q_heads / p.n_kv_heads;
+  return G >= 1 && p.K >= 1 && G * p.K <= 128 && p.page_size == 16;
+}
+
+cudaError_t launch_attention_tc(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p,
+                                cudaStream_t stream, bool pdl) {
+  if (!attention_tc_fits(p)) return cudaErrorInvalidValue;
+  const int G = p.n_q_heads / p.n_kv_heads;
+  const int W = (tc_rows(G, p.K) + 31) / 32;
+  cudaError_t e = configure_attention_tc();
+  if (e != cudaSuccess) return e;
+  AttnParams q = p;
+  q.groups = 1;
+  q.cluster = 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.max_splits, p.n_kv_heads, p.bs);
+  cfg.blockDim = dim3(32 * (W + 2));
+  cfg.dynamicSmemBytes = attention_tc_smem_bytes(G, p.K);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attention_tc_kernel<kTcStages>, tmk, tmv, q);
+}
+
+}  // namespace gr

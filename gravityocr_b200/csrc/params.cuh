@@ -126,6 +126,11 @@ cudaError_t launch_linear(int epi, const CUtensorMap& tmw, const CUtensorMap& tm
 cudaError_t launch_argmax_reduce(const LinearParams& p, cudaStream_t stream, bool pdl);
 
 size_t attention_smem_bytes(int K, int G, int stages);
+size_t attention_tc_smem_bytes(int G, int K);
+bool attention_tc_fits(const AttnParams& p);
+cudaError_t launch_attention_tc(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p,
+                                cudaStream_t stream, bool pdl);
+extern bool g_attention_tc;
 cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p, cudaStream_t stream,
                              bool pdl);
 cudaError_t launch_embed_rows(const EmbedParams& p, cudaStream_t s, bool pdl);

@@ -62,9 +62,11 @@ def case_attention(a):
     order = torch.argsort(seq, descending=True, stable=True).to(torch.int32) if a.mixed else None
     fn = lambda: L.bd_attention(q, kc, vc, pt, seq, bs, K, a.draft, 0 if a.draft else 1, nq, nkv, ps, chunk, splits,
                                 out, ws, order=order)
+    L.set_attention_tc(not a.mma)
     ms = _time(fn, a.reps)
     b = attention_bytes(cfg, S, K, 0 if a.draft else 1)
-    return {"kernel": "attention_kernel", "bs": bs, "seq": "mixed" if a.mixed else a.seq, "K": K, "chunk": chunk,
+    tc = not a.mma and bs * nkv * splits > L.num_sms()
+    return {"kernel": "attention_tc_kernel" if tc else "attention_kernel", "bs": bs, "seq": "mixed" if a.mixed else a.seq, "K": K, "chunk": chunk,
             "splits": splits, "ms": ms,
             "bytes": b, "GBps": b / ms / 1e6}
 
@@ -123,6 +125,7 @@ def main():
     at.add_argument("--draft", action="store_true")
     at.add_argument("--chunk", type=int, default=0)
     at.add_argument("--mixed", action="store_true", help="config-3 prefix lengths instead of --seq")
+    at.add_argument("--mma", action="store_true", help="large grids on the mma.sync kernel instead of tcgen05")
     at.add_argument("--reps", type=int, default=3)
     li = sub.add_parser("linear")
     li.add_argument("--n-out", type=int, default=9216)

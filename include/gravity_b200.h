@@ -71,6 +71,9 @@ int gr_version(void);
 const char* gr_status_string(int code);
 /* Programmatic dependent launch on (1, default) / off (0) for every later launch. */
 void gr_set_pdl(int enable);
+/* Attention kernel for large grids (more than one CTA per SM): the tcgen05 / TMEM kernel (1, default) or the
+ * mma.sync kernel (0).  Both compute the same rows; the switch exists to compare them. */
+void gr_set_attention_tc(int enable);
 /* Number of SMs the split heuristics assume (queried from device 0 on first use). */
 int gr_num_sms(void);
 

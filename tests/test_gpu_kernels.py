@@ -477,3 +477,51 @@ def test_linear_partials_summed_by_residual_norm(n_out, k_in, m):
     hr = h + rms(ref_y, wa)
     torch.testing.assert_close(h2, hr, rtol=1e-3, atol=1e-5)
     torch.testing.assert_close(xo.float(), rms(hr, wb), rtol=1e-2, atol=1e-4)
+
+
+@pytest.mark.parametrize("bs,K,draft,chunk,q_scale", [(64, 17, False, 4096, 1.0), (64, 17, True, 4096, 1.0),
+                                                     (24, 17, False, 512, 1.0), (24, 17, True, 256, 4.0),
+                                                     (40, 9, False, 1024, 8.0), (20, 32, True, 4096, 1.0),
+                                                     (12, 33, True, 1024, 1.0), (20, 64, False, 4096, 2.0)])
+def test_attention_tc_matches_mma_kernel(bs, K, draft, chunk, q_scale):
+    """Large grids (more units than SMs): the tcgen05 / TMEM kernel against the fp32 reference and the mma.sync kernel
+    on the same inputs.  Scaled queries make the running max move often (the O rescale in TMEM); small chunks give
+    split partials and the merge.  Prefixes U[0, 3000] (seed 11)."""
+    nq, nkv, D, ps = 16, 8, 128, 16
+    g = torch.Generator().manual_seed(11)
+    S = torch.randint(0, 3001, (bs,), generator=g)
+    base_add = 0 if draft else 1
+    need = [(int(s) + base_add + K + ps - 1) // ps for s in S]
+    P = max(need) + 1
+    n_pages = sum(need) + 4
+    perm = torch.randperm(n_pages, generator=g)
+    pt = torch.zeros((bs, P), dtype=torch.int32)
+    o = 0
+    for b in range(bs):
+        pt[b, : need[b]] = perm[o: o + need[b]].to(torch.int32)
+        pt[b, need[b]:] = perm[o]
+        o += need[b]
+    kc = _rand((n_pages, nkv, ps, D), g)
+    vc = _rand((n_pages, nkv, ps, D), g)
+    q = _rand((bs * K, nq, D), g, scale=q_scale)
+    pt_d, seq_d = pt.to(DEV), S.to(DEV)
+    Lmax = int(S.max()) + base_add + K
+    max_splits = int(math.ceil(Lmax / chunk))
+    assert bs * nkv * max_splits > L.num_sms()
+    ws = torch.zeros((L.attention_workspace_bytes(bs, K, nq, nkv, max_splits),), dtype=torch.uint8, device=DEV)
+    st = torch.zeros((1,), dtype=torch.int32, device=DEV)
+    outs = []
+    try:
+        for tc in (True, False):
+            L.set_attention_tc(tc)
+            out = torch.full((bs * K, nq, D), float("nan"), dtype=torch.bfloat16, device=DEV)
+            L.bd_attention(q, kc, vc, pt_d, seq_d, bs, K, draft, base_add, nq, nkv, ps, chunk, max_splits, out, ws,
+                           status=st)
+            torch.cuda.synchronize()
+            assert int(st.item()) == 0
+            outs.append(out.float())
+    finally:
+        L.set_attention_tc(True)
+    ref = _attn_ref(q, kc, vc, pt_d, seq_d, K, draft, base_add, nq, nkv)
+    torch.testing.assert_close(outs[0], ref, rtol=2e-2, atol=1.5e-2)
+    torch.testing.assert_close(outs[0], outs[1], rtol=2e-2, atol=1.5e-2)
