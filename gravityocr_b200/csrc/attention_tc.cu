@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(192) attention_tc_kernel(const __grid_constant
       while (pv_next < n_tiles) {
         bool progress = false;
         // O += P_k V_k as soon as P_k is written (frees the stage)
-        if (pv_next < s_next && mbar_test(p_full + (pv_next & 1), (pv_next >> 1) & 1)) {
+        if (pv_next < s_next && mbar_poll(p_full + (pv_next & 1), (pv_next >> 1) & 1)) {
           tc_fence_after();
           const int s = pv_next % ST;
           const uint32_t so = (static_cast<uint32_t>(s) * kStageBytes) >> 4;
@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(192) attention_tc_kernel(const __grid_constant
           progress = true;
         }
         // S_i = Q K_i^T once its tile landed and its S buffer is free (the softmax is done with S_{i-2})
-        if (s_next < n_tiles && s_next <= pv_next + 1 && mbar_test(kv_full + s_next % ST, (s_next / ST) & 1)) {
+        if (s_next < n_tiles && s_next <= pv_next + 1 && mbar_poll(kv_full + s_next % ST, (s_next / ST) & 1)) {
           tc_fence_after();
           const uint32_t so = (static_cast<uint32_t>(s_next % ST) * kStageBytes) >> 4;
 #pragma unroll
@@ -195,8 +195,11 @@ __global__ void __launch_bounds__(192) attention_tc_kernel(const __grid_constant
     }
   } else if (warp < W) {
     // ------------------------------------------------------------ softmax warps
-    const int lim = valid ? min(row_limit(p, j, base), kv_end) : 0;
+    // padding lanes (rows >= R) take the unmasked path on whatever their S holds: their P rows only feed O rows
+    // that nobody reads, and they never ask for a rescale
+    const int lim = valid ? min(row_limit(p, j, base), kv_end) : 0x7fffffff;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const float sc = p.scale_log2;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int i = 0; i < n_tiles; ++i) {
@@ -209,34 +212,37 @@ __global__ void __launch_bounds__(192) attention_tc_kernel(const __grid_constant
       tmem_ld32_wait(sr[0]);
       tmem_ld32_wait(sr[1]);
       const int tok0 = kv_beg + i * kTile;
-      float mx = -INFINITY;
+      // raw scores; masked positions become -inf (scale_log2 > 0, so the max of the raw scores scales)
+      if (tok0 + kTile > lim) {
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float x = (tok0 + c < lim) ? __uint_as_float(sr[c >> 5][c & 31]) * p.scale_log2 : -INFINITY;
-        sr[c >> 5][c & 31] = __float_as_uint(x);
-        mx = fmaxf(mx, x);
+        for (int c = 0; c < 64; ++c)
+          if (tok0 + c >= lim) sr[c >> 5][c & 31] = __float_as_uint(-INFINITY);
       }
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < 64; ++c) m4[c & 3] = fmaxf(m4[c & 3], __uint_as_float(sr[c >> 5][c & 31]));
+      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sc;
       // the reference max moves only when the tile's max exceeds it by more than 2^8 (always for the first visible
       // token); O needs rescaling only if it already holds visible tokens
       float m_new = m_run;
       bool resc = false;
       if (mx > m_run + kTcRescaleLog2) {
-        resc = m_run != -INFINITY;
+        resc = valid && m_run != -INFINITY;
         m_new = mx;
       }
-      const float alpha = resc ? exp2f(m_run - m_new) : 1.f;
-      const float msafe = (m_new == -INFINITY) ? 0.f : m_new;
-      float rs = 0.f;
+      const float alpha = resc ? ex2_approx(m_run - m_new) : 1.f;
+      const float nm = (m_new == -INFINITY) ? 0.f : -m_new;
+      float r4[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t pk[32];
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
-        const float p0 = exp2f(__uint_as_float(sr[c >> 4][(2 * c) & 31]) - msafe);
-        const float p1 = exp2f(__uint_as_float(sr[c >> 4][(2 * c + 1) & 31]) - msafe);
-        rs += p0;
-        rs += p1;
+        const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c >> 4][(2 * c) & 31]), sc, nm));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(sr[c >> 4][(2 * c + 1) & 31]), sc, nm));
+        r4[(2 * c) & 3] += p0;
+        r4[(2 * c + 1) & 3] += p1;
         pk[c] = pack_bf16(p0, p1);
       }
-      l_run = l_run * alpha + rs;
+      l_run = l_run * alpha + ((r4[0] + r4[1]) + (r4[2] + r4[3]));
       m_run = m_new;
       if (__any_sync(0xffffffffu, resc)) {
         // O holds tiles 0..i-1 once the previous tile's PV completed (resc implies i > 0)

@@ -69,9 +69,16 @@ def _rounds(eng, rb, n, small):
 
 @pytest.mark.parametrize("bs", [1, 2, 3])
 def test_small_forward_equals_per_launch(bs):
+    """The persistent kernel runs the mma.sync attention body: the per-launch reference uses the same kernel for
+    every grid size (large grids would otherwise take the tcgen05 kernel, equal only to rounding)."""
+    from gravityocr_b200 import _lib as L
     eng, rb = _setup(bs)
     snap = _state(rb)
-    ref = _rounds(eng, rb, 3, small=False)
+    L.set_attention_tc(False)
+    try:
+        ref = _rounds(eng, rb, 3, small=False)
+    finally:
+        L.set_attention_tc(True)
     ref_cache = _cache(eng)
     _restore(rb, snap)
     got = _rounds(eng, rb, 3, small=True)
