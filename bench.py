@@ -35,9 +35,9 @@ sys.path.insert(0, ROOT)
 METRIC = "self-spec decode tokens/s & tokens/forward @bs1/bs64, %HBM roofline, 1/2/4/8 B200"
 K_BD = 16
 SEED = 3
-# DRAM bytes / algorithmic bytes of the verify attention on the config-3 mix, from the ncu capture recorded in
-# profiles/attention_kernel_config3_bs64.md (dram__bytes_read + dram__bytes_write of one launch)
-ATTN_TRAFFIC_RATIO = (584.65664e6 + 5.728e6) / 586.93632e6
+# DRAM bytes / algorithmic bytes of the verify attention (attention_tc_kernel) on the config-3 mix, from the ncu
+# capture recorded in profiles/attention_tc_kernel_config3_bs64.md (dram__bytes_read + dram__bytes_write of one launch)
+ATTN_TRAFFIC_RATIO = (584.57344e6 + 5.767424e6) / 586.93632e6
 
 
 def _args():
@@ -322,7 +322,7 @@ def main():
                                      "peak": peak_src, "draft_ms": round(draft_ms / a.steps, 4),
                                      "verify_ms": round(verify_ms / a.steps, 4),
                                      "bytes_draft": bd, "bytes_verify": bv},
-        "roofline": {"kernel": "attention_kernel (verify, one layer)", "bound": "hbm",
+        "roofline": {"kernel": "attention_tc_kernel (verify, one layer)", "bound": "hbm",
                      "achieved": round(attn_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(attn_gbs / hbm_peak, 4), "traffic": int(attn_b * ATTN_TRAFFIC_RATIO),
                      "traffic_source": "ncu dram bytes of the same kernel on the config-3 mix, scaled to this launch",

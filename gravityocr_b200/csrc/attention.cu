@@ -100,7 +100,7 @@ cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, con
   // alternate tiles over 4 stages (a CTA's latency is the launch's), and at least kMinWarps warps for the merge.
   AttnParams q = p;
   const bool small = p.bs * p.n_kv_heads * p.max_splits <= 148;
-  if (!small && g_attention_tc && attention_tc_fits(p)) return launch_attention_tc(tmk, tmv, p, stream, pdl);
+  if (g_attention_tc && attention_tc_fits(p)) return launch_attention_tc(tmk, tmv, p, small, stream, pdl);
   q.groups = (small && 2 * n_mt + 1 <= 9) ? 2 : 1;  // up to 288 threads
   int warps = q.groups * n_mt + 1;
   if (small && p.max_splits > 1 && warps < kMinWarps) warps = kMinWarps;

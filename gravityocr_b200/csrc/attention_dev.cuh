@@ -187,6 +187,63 @@ __device__ inline void attention_merge_global(const AttnParams& p, int b, int kv
   }
 }
 
+// Split merge through distributed shared memory: the max_splits CTAs of (request b, kv head kvh) form one cluster
+// (rank = split) and each holds its (O, m, l) partial in its own shared memory (part_o [R_pad][128], part_ml
+// [R_pad][2], the same offsets in every CTA).  Called after a cluster barrier by every warp of every CTA; CTA `split`
+// merges rows split*n_warps + warp (stride max_splits*n_warps) in split order with the arithmetic of the global
+// merge.  The caller's second cluster barrier keeps the partials alive until read.
+__device__ inline void attention_merge_cluster(const AttnParams& p, int b, int kvh, int split, int n_active, int warp,
+                                               int lane, int n_warps, const float* part_o, const float* part_ml) {
+  const int G = p.n_q_heads / p.n_kv_heads;
+  const int R = G * p.K;
+  const size_t q_row_stride = (size_t)p.n_q_heads * 128;
+  if (n_active > 1) {
+    const int cs = p.max_splits;
+    for (int r = split * n_warps + warp; r < R; r += cs * n_warps) {
+      float M = -INFINITY;
+      float ms[kMaxMergeSplits], ls[kMaxMergeSplits];
+#pragma unroll
+      for (int s2 = 0; s2 < kMaxMergeSplits; ++s2) {
+        if (s2 < n_active) {
+          const float2 ml = ld_dsmem_f2(dsmem_addr(part_ml + r * 2, s2));
+          ms[s2] = ml.x;
+          ls[s2] = ml.y;
+          M = fmaxf(M, ml.x);
+        }
+      }
+      const float Ms = (M == -INFINITY) ? 0.f : M;
+      float Lsum = 0.f;
+#pragma unroll
+      for (int s2 = 0; s2 < kMaxMergeSplits; ++s2) {
+        if (s2 < n_active) {
+          const float w = (ms[s2] == -INFINITY) ? 0.f : exp2f(ms[s2] - Ms);
+          ms[s2] = w;
+          Lsum += ls[s2] * w;
+        }
+      }
+      const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int s2 = 0; s2 < kMaxMergeSplits; ++s2) {
+        if (s2 < n_active) {
+          const float w = ms[s2] * inv;
+          const float4 ov = ld_dsmem_f4(dsmem_addr(part_o + r * 128 + lane * 4, s2));
+          acc.x += ov.x * w;
+          acc.y += ov.y * w;
+          acc.z += ov.z * w;
+          acc.w += ov.w * w;
+        }
+      }
+      const int g = r / p.K, j = r % p.K;
+      __nv_bfloat16* dst = p.out + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128 + lane * 4;
+      uint2 pk;
+      pk.x = pack_bf16(acc.x, acc.y);
+      pk.y = pack_bf16(acc.z, acc.w);
+      *reinterpret_cast<uint2*>(dst) = pk;
+    }
+  }
+}
+
 // One unit.  Participating threads: wt in [0, nthr), warp aw = wt / 32; warps aw < groups * n_mt compute, warp
 // aw == groups * n_mt is the TMA producer, the rest only help the split merge.  bar_all / bar_cw are named barrier
 // ids for all participants / the compute warps.  Every participant calls with the same arguments.
@@ -482,51 +539,7 @@ __device__ void attention_unit(const CUtensorMap* tmk_p, const CUtensorMap* tmv_
     // merges a share of the rows, reading the splits' partials from their shared memory in split order with the
     // same arithmetic as the global-memory merge below; the second barrier keeps the partials alive until read.
     cluster_sync_all();
-    if (n_active > 1) {
-      const int cs = p.max_splits, n_warps = nthr >> 5;
-      for (int r = split * n_warps + warp; r < R; r += cs * n_warps) {
-        float M = -INFINITY;
-        float ms[kMaxMergeSplits], ls[kMaxMergeSplits];
-#pragma unroll
-        for (int s2 = 0; s2 < kMaxMergeSplits; ++s2) {
-          if (s2 < n_active) {
-            const float2 ml = ld_dsmem_f2(dsmem_addr(part_ml + r * 2, s2));
-            ms[s2] = ml.x;
-            ls[s2] = ml.y;
-            M = fmaxf(M, ml.x);
-          }
-        }
-        const float Ms = (M == -INFINITY) ? 0.f : M;
-        float Lsum = 0.f;
-#pragma unroll
-        for (int s2 = 0; s2 < kMaxMergeSplits; ++s2) {
-          if (s2 < n_active) {
-            const float w = (ms[s2] == -INFINITY) ? 0.f : exp2f(ms[s2] - Ms);
-            ms[s2] = w;
-            Lsum += ls[s2] * w;
-          }
-        }
-        const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int s2 = 0; s2 < kMaxMergeSplits; ++s2) {
-          if (s2 < n_active) {
-            const float w = ms[s2] * inv;
-            const float4 ov = ld_dsmem_f4(dsmem_addr(part_o + r * 128 + lane * 4, s2));
-            acc.x += ov.x * w;
-            acc.y += ov.y * w;
-            acc.z += ov.z * w;
-            acc.w += ov.w * w;
-          }
-        }
-        const int g = r / p.K, j = r % p.K;
-        __nv_bfloat16* dst = p.out + ((size_t)b * p.K + j) * q_row_stride + (kvh * G + g) * 128 + lane * 4;
-        uint2 pk;
-        pk.x = pack_bf16(acc.x, acc.y);
-        pk.y = pack_bf16(acc.z, acc.w);
-        *reinterpret_cast<uint2*>(dst) = pk;
-      }
-    }
+    attention_merge_cluster(p, b, kvh, split, n_active, warp, lane, nthr >> 5, part_o, part_ml);
     cluster_sync_all();
     return;
   }

@@ -126,9 +126,9 @@ cudaError_t launch_linear(int epi, const CUtensorMap& tmw, const CUtensorMap& tm
 cudaError_t launch_argmax_reduce(const LinearParams& p, cudaStream_t stream, bool pdl);
 
 size_t attention_smem_bytes(int K, int G, int stages);
-size_t attention_tc_smem_bytes(int G, int K);
+size_t attention_tc_smem_bytes(int G, int K, int stages);
 bool attention_tc_fits(const AttnParams& p);
-cudaError_t launch_attention_tc(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p,
+cudaError_t launch_attention_tc(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p, bool small,
                                 cudaStream_t stream, bool pdl);
 extern bool g_attention_tc;
 cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p, cudaStream_t stream,

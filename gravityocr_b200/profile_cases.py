@@ -65,7 +65,7 @@ def case_attention(a):
     L.set_attention_tc(not a.mma)
     ms = _time(fn, a.reps)
     b = attention_bytes(cfg, S, K, 0 if a.draft else 1)
-    tc = not a.mma and bs * nkv * splits > L.num_sms()
+    tc = not a.mma and nq // nkv * K <= 128
     return {"kernel": "attention_tc_kernel" if tc else "attention_kernel", "bs": bs, "seq": "mixed" if a.mixed else a.seq, "K": K, "chunk": chunk,
             "splits": splits, "ms": ms,
             "bytes": b, "GBps": b / ms / 1e6}

@@ -482,11 +482,15 @@ def test_linear_partials_summed_by_residual_norm(n_out, k_in, m):
 @pytest.mark.parametrize("bs,K,draft,chunk,q_scale", [(64, 17, False, 4096, 1.0), (64, 17, True, 4096, 1.0),
                                                      (24, 17, False, 512, 1.0), (24, 17, True, 256, 4.0),
                                                      (40, 9, False, 1024, 8.0), (20, 32, True, 4096, 1.0),
-                                                     (12, 33, True, 1024, 1.0), (20, 64, False, 4096, 2.0)])
+                                                     (12, 33, True, 1024, 1.0), (20, 64, False, 4096, 2.0),
+                                                     (1, 17, False, 256, 1.0), (2, 17, True, 512, 4.0),
+                                                     (1, 17, True, 192, 1.0), (4, 33, False, 4096, 1.0),
+                                                     (3, 17, False, 1024, 8.0)])
 def test_attention_tc_matches_mma_kernel(bs, K, draft, chunk, q_scale):
-    """Large grids (more units than SMs): the tcgen05 / TMEM kernel against the fp32 reference and the mma.sync kernel
-    on the same inputs.  Scaled queries make the running max move often (the O rescale in TMEM); small chunks give
-    split partials and the merge.  Prefixes U[0, 3000] (seed 11)."""
+    """The tcgen05 / TMEM kernel against the fp32 reference and the mma.sync kernel on the same inputs: large grids
+    (more units than SMs; global split merge) and small grids (one CTA per SM; the splits of a (request, kv head) as
+    one cluster merging through distributed shared memory).  Scaled queries make the reference max move often (the O
+    rescale in TMEM); small chunks give split partials and the merges.  Prefixes U[0, 3000] (seed 11)."""
     nq, nkv, D, ps = 16, 8, 128, 16
     g = torch.Generator().manual_seed(11)
     S = torch.randint(0, 3001, (bs,), generator=g)
@@ -507,7 +511,7 @@ def test_attention_tc_matches_mma_kernel(bs, K, draft, chunk, q_scale):
     pt_d, seq_d = pt.to(DEV), S.to(DEV)
     Lmax = int(S.max()) + base_add + K
     max_splits = int(math.ceil(Lmax / chunk))
-    assert bs * nkv * max_splits > L.num_sms()
+    assert max_splits <= 16
     ws = torch.zeros((L.attention_workspace_bytes(bs, K, nq, nkv, max_splits),), dtype=torch.uint8, device=DEV)
     st = torch.zeros((1,), dtype=torch.int32, device=DEV)
     outs = []
