@@ -133,9 +133,10 @@ def set_pdl(enable: bool) -> None:
     load().gr_set_pdl(1 if enable else 0)
 
 
-def set_attention_tc(enable: bool) -> None:
-    """Large attention grids on the tcgen05 kernel (default) or on the mma.sync kernel."""
-    load().gr_set_attention_tc(1 if enable else 0)
+def set_attention_tc(mode) -> None:
+    """Attention kernel: 0 / False mma.sync everywhere; 1 / True tcgen05 on grids of more than one CTA per SM (the
+    default); 2 tcgen05 on every grid."""
+    load().gr_set_attention_tc(int(mode))
 
 
 def num_sms() -> int:

@@ -17,7 +17,9 @@ namespace gr {
 
 constexpr int kMinWarps = 8;  // extra warps idle in the main loop and help the split merge
 
-bool g_attention_tc = true;  // large grids on the tcgen05 kernel (attention_tc.cu) where it fits
+// tcgen05 kernel (attention_tc.cu) where it fits: 0 never, 1 large grids (default: on grids of at most one CTA per
+// SM the mma.sync kernel's shorter per-CTA latency wins), 2 every grid
+int g_attention_tc = 1;
 
 // Two instantiations (ST = pipeline stages):
 //   <288, 1, 3>  one warp group (the row tiles of a request's GQA group) + producer; large batches, two CTAs per SM;
@@ -100,7 +102,8 @@ cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, con
   // alternate tiles over 4 stages (a CTA's latency is the launch's), and at least kMinWarps warps for the merge.
   AttnParams q = p;
   const bool small = p.bs * p.n_kv_heads * p.max_splits <= 148;
-  if (g_attention_tc && attention_tc_fits(p)) return launch_attention_tc(tmk, tmv, p, small, stream, pdl);
+  if (g_attention_tc > (small ? 1 : 0) && attention_tc_fits(p))
+    return launch_attention_tc(tmk, tmv, p, small, stream, pdl);
   q.groups = (small && 2 * n_mt + 1 <= 9) ? 2 : 1;  // up to 288 threads
   int warps = q.groups * n_mt + 1;
   if (small && p.max_splits > 1 && warps < kMinWarps) warps = kMinWarps;

@@ -205,7 +205,7 @@ const char* gr_status_string(int code) {
 }
 
 void gr_set_pdl(int enable) { g_pdl = enable != 0; }
-void gr_set_attention_tc(int enable) { g_attention_tc = enable != 0; }
+void gr_set_attention_tc(int mode) { g_attention_tc = mode < 0 ? 0 : (mode > 2 ? 2 : mode); }
 int gr_num_sms(void) { return num_sms(); }
 
 int gr_linear_default_splits(int n_out, int k_in, int m) {

@@ -130,7 +130,7 @@ size_t attention_tc_smem_bytes(int G, int K, int stages);
 bool attention_tc_fits(const AttnParams& p);
 cudaError_t launch_attention_tc(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p, bool small,
                                 cudaStream_t stream, bool pdl);
-extern bool g_attention_tc;
+extern int g_attention_tc;
 cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p, cudaStream_t stream,
                              bool pdl);
 cudaError_t launch_embed_rows(const EmbedParams& p, cudaStream_t s, bool pdl);

@@ -98,11 +98,14 @@ __global__ void __launch_bounds__(kRowThreads) embed_rows_kernel(const EmbedPara
 
 // ------------------------------------------------------------------ residual + sandwich norm
 // One CTA per row; each thread owns up to kMaxChunks groups of 8 features, kept in registers between the passes.
+// MC = 1 when the row fits one 8-feature chunk per thread (hidden <= 1536): a small register footprint, so that a
+// whole batch of rows is resident at once.
+template <int MC>
 __global__ void __launch_bounds__(kRowThreads) residual_norm_kernel(const ResNormParams p) {
   __shared__ float red[32];
   if (threadIdx.x == 0) pdl_trigger();
   pdl_wait();
-  resnorm_row(p, blockIdx.x, threadIdx.x, blockDim.x, 1, red);
+  resnorm_row<MC>(p, blockIdx.x, threadIdx.x, blockDim.x, 1, red);
 }
 
 // ------------------------------------------------------------------ accept and commit
@@ -214,7 +217,8 @@ cudaError_t launch_embed_rows(const EmbedParams& p, cudaStream_t s, bool pdl) {
   return launch_pdl(embed_rows_kernel, dim3(p.bs * p.K), dim3(kRowThreads), p, s, pdl);
 }
 cudaError_t launch_residual_norm(const ResNormParams& p, cudaStream_t s, bool pdl) {
-  return launch_pdl(residual_norm_kernel, dim3(p.m), dim3(kRowThreads), p, s, pdl);
+  if (p.hidden <= 8 * kRowThreads) return launch_pdl(residual_norm_kernel<1>, dim3(p.m), dim3(kRowThreads), p, s, pdl);
+  return launch_pdl(residual_norm_kernel<kMaxChunks>, dim3(p.m), dim3(kRowThreads), p, s, pdl);
 }
 cudaError_t launch_accept_commit(const CommitParams& p, cudaStream_t s, bool pdl) {
   return launch_pdl(accept_commit_kernel, dim3(1), dim3(kCommitThreads), p, s, pdl);

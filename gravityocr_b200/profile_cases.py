@@ -22,10 +22,26 @@ from .engine import rope_inv_freq
 from .metrics import attention_bytes
 
 
+GRAPH = False  # --graph: time `reps` launches captured in one CUDA graph (device-bound, as in the engine)
+
+
 def _time(fn, reps):
     fn()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if GRAPH:
+        s = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(reps):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
     e0.record()
     for _ in range(reps):
         fn()
@@ -62,10 +78,10 @@ def case_attention(a):
     order = torch.argsort(seq, descending=True, stable=True).to(torch.int32) if a.mixed else None
     fn = lambda: L.bd_attention(q, kc, vc, pt, seq, bs, K, a.draft, 0 if a.draft else 1, nq, nkv, ps, chunk, splits,
                                 out, ws, order=order)
-    L.set_attention_tc(not a.mma)
+    L.set_attention_tc(0 if a.mma else (2 if a.tc_all else 1))
     ms = _time(fn, a.reps)
     b = attention_bytes(cfg, S, K, 0 if a.draft else 1)
-    tc = not a.mma and nq // nkv * K <= 128
+    tc = not a.mma and nq // nkv * K <= 128 and (a.tc_all or bs * nkv * splits > L.num_sms())
     return {"kernel": "attention_tc_kernel" if tc else "attention_kernel", "bs": bs, "seq": "mixed" if a.mixed else a.seq, "K": K, "chunk": chunk,
             "splits": splits, "ms": ms,
             "bytes": b, "GBps": b / ms / 1e6}
@@ -125,7 +141,8 @@ def main():
     at.add_argument("--draft", action="store_true")
     at.add_argument("--chunk", type=int, default=0)
     at.add_argument("--mixed", action="store_true", help="config-3 prefix lengths instead of --seq")
-    at.add_argument("--mma", action="store_true", help="large grids on the mma.sync kernel instead of tcgen05")
+    at.add_argument("--mma", action="store_true", help="every grid on the mma.sync kernel")
+    at.add_argument("--tc-all", action="store_true", help="every grid on the tcgen05 kernel (small grids included)")
     at.add_argument("--reps", type=int, default=3)
     li = sub.add_parser("linear")
     li.add_argument("--n-out", type=int, default=9216)
@@ -134,7 +151,10 @@ def main():
     li.add_argument("--epi", default="swiglu", choices=["f32", "partial", "swiglu", "argmax", "qkv"])
     li.add_argument("--splits", type=int, default=0)
     li.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--graph", action="store_true", help="time launches captured in one CUDA graph")
     a = ap.parse_args()
+    global GRAPH
+    GRAPH = a.graph
     r = case_attention(a) if a.case == "attention" else case_linear(a)
     print(json.dumps(r))
 

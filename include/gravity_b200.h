@@ -71,9 +71,10 @@ int gr_version(void);
 const char* gr_status_string(int code);
 /* Programmatic dependent launch on (1, default) / off (0) for every later launch. */
 void gr_set_pdl(int enable);
-/* Attention kernel for large grids (more than one CTA per SM): the tcgen05 / TMEM kernel (1, default) or the
- * mma.sync kernel (0).  Both compute the same rows; the switch exists to compare them. */
-void gr_set_attention_tc(int enable);
+/* Which attention kernel runs: 0 the mma.sync kernel for every grid; 1 (default) the tcgen05 / TMEM kernel for
+ * grids of more than one CTA per SM and the mma.sync kernel below that; 2 the tcgen05 kernel for every grid (small
+ * grids as thread-block clusters).  All compute the same rows; the switch exists to compare them. */
+void gr_set_attention_tc(int mode);
 /* Number of SMs the split heuristics assume (queried from device 0 on first use). */
 int gr_num_sms(void);
 

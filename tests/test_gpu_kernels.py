@@ -516,7 +516,7 @@ def test_attention_tc_matches_mma_kernel(bs, K, draft, chunk, q_scale):
     st = torch.zeros((1,), dtype=torch.int32, device=DEV)
     outs = []
     try:
-        for tc in (True, False):
+        for tc in (2, 0):
             L.set_attention_tc(tc)
             out = torch.full((bs * K, nq, D), float("nan"), dtype=torch.bfloat16, device=DEV)
             L.bd_attention(q, kc, vc, pt_d, seq_d, bs, K, draft, base_add, nq, nkv, ps, chunk, max_splits, out, ws,
