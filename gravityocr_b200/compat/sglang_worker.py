@@ -128,6 +128,7 @@ class SelfSpecDiffusionWorker:
             rb.graph = None
             rb.host = torch.zeros(rb.readback.shape, dtype=torch.int32).pin_memory()
             rb.event = torch.cuda.Event()
+            rb.order = torch.arange(bs, dtype=torch.int32, device=self.device)  # exists before any capture
             self._rb[bs] = rb
         rb.seeds = self._seeds()
         return rb
@@ -176,6 +177,8 @@ class SelfSpecDiffusionWorker:
         rb.rpi.copy_(batch.req_pool_indices)
         rb.page_table.copy_(self.req_to_page.table[batch.req_pool_indices])
         rb.seq_lens.copy_(batch.seq_lens)
+        # longest-first attention launch order for this batch (the captured graph reads it in place)
+        self.engine.refresh_order(rb)
         self._cur = rb
         return None
 
