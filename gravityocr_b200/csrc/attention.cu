@@ -11,6 +11,8 @@
 // run S = Q K^T and O += P V on mma.sync m16n8k16 with an fp32 online softmax (quad shuffles).
 // Split-KV: CTA (split, kv_head, request) covers cache positions [split*chunk, (split+1)*chunk); when a request needs
 // more than one split, each writes (m, l, O) partials and the last split to arrive merges them in split order.
+// launch_attention is the entry of both attention kernels: grids of more than one CTA per SM go to the tcgen05 kernel
+// (attention_tc.cu) when its rows fit (G*K <= 128), smaller grids stay on this one (g_attention_tc selects).
 #include "attention_dev.cuh"
 
 namespace gr {
