@@ -49,10 +49,12 @@ __global__ void __launch_bounds__(MAXT, MINB) attention_kernel(const __grid_cons
   }
   __syncthreads();
   if (threadIdx.x == 0) pdl_trigger();
-  pdl_wait();
   // blocks launch in z-major order: a longest-first request order shortens the tail of a mixed-length batch
   const int b = p.order ? p.order[blockIdx.z] : blockIdx.z;
-  attention_unit<ST>(&tmk, &tmv, p, blockIdx.x, blockIdx.y, b, threadIdx.x, blockDim.x, 1, 2, c);
+  // the producer warp reads the split's page ids while the previous kernel finishes
+  if ((threadIdx.x >> 5) == p.groups * n_mt) attn_preload_pages(p, b, blockIdx.x, threadIdx.x & 31, c.pages);
+  pdl_wait();
+  attention_unit<ST, true>(&tmk, &tmv, p, blockIdx.x, blockIdx.y, b, threadIdx.x, blockDim.x, 1, 2, c);
 }
 
 size_t attention_smem_bytes(int K, int G, int stages) { return 1024 + attn_region_bytes(attn_rows_pad(G, K), stages); }

@@ -72,6 +72,22 @@ __device__ __forceinline__ AttnCta attn_cta_layout(uint8_t* region, int R_pad) {
   return c;
 }
 
+// Page ids of split `split`'s whole chunk of request b, by the 32 lanes of one warp, before the kernel waits for its
+// predecessor: the page table and the launch order are written before a round starts, the lengths are not, so the
+// clamp to the request's last page is applied when a tile is issued (attn_page).  pages[] holds chunk / page_size
+// entries (<= kMaxChunkPages).
+__device__ __forceinline__ void attn_preload_pages(const AttnParams& p, int b, int split, int lane, int* pages) {
+  const int* pt = p.page_table + (size_t)b * p.pt_stride;
+  const int pg_beg = split * p.chunk / p.page_size;
+  const int n = p.chunk / p.page_size;
+  for (int i = lane; i < n; i += 32) pages[i] = pt[min(pg_beg + i, p.pt_stride - 1)];
+}
+// Page of the split's k-th page slot: pages past the request's last page hold no visible token and are replaced by
+// its last page, whose contents are finite.  pre: pages[] from attn_preload_pages (unclamped) or already clamped.
+__device__ __forceinline__ int attn_page(const int* pages, int k, int last_slot, bool pre) {
+  return pages[pre ? min(k, last_slot) : k];
+}
+
 // Split merge through global memory: every split of (request b, kv head kvh) has written its (O, m, l) partial to
 // ws_o / ws_ml; the last split to arrive merges them in split order.  Called by all nthr participating threads of
 // each split's CTA (named barrier bar_all); `flag` is a shared int, `wgt` shared scratch of R * kMaxMergeSplits
@@ -246,8 +262,9 @@ __device__ inline void attention_merge_cluster(const AttnParams& p, int b, int k
 
 // One unit.  Participating threads: wt in [0, nthr), warp aw = wt / 32; warps aw < groups * n_mt compute, warp
 // aw == groups * n_mt is the TMA producer, the rest only help the split merge.  bar_all / bar_cw are named barrier
-// ids for all participants / the compute warps.  Every participant calls with the same arguments.
-template <int ST>
+// ids for all participants / the compute warps.  Every participant calls with the same arguments.  PRE: the
+// producer warp already holds the split's page ids (attn_preload_pages).
+template <int ST, bool PRE = false>
 __device__ void attention_unit(const CUtensorMap* tmk_p, const CUtensorMap* tmv_p, const AttnParams& p, int split,
                                int kvh, int b, int wt, int nthr, int bar_all, int bar_cw, AttnCta& c) {
   const CUtensorMap& tmk = *tmk_p;
@@ -291,7 +308,8 @@ __device__ void attention_unit(const CUtensorMap* tmk_p, const CUtensorMap* tmv_
     const int last_page = (L - 1) / p.page_size;
     const int pg_beg = kv_beg / p.page_size;
     const int n_pg = n_tiles * (kTile / 16);
-    for (int i = lane; i < n_pg; i += 32) pages[i] = pt[min(pg_beg + i, last_page)];
+    if constexpr (!PRE)
+      for (int i = lane; i < n_pg; i += 32) pages[i] = pt[min(pg_beg + i, last_page)];
     __syncwarp();
     if (lane == 0) {
       int issued = 0;
@@ -303,7 +321,7 @@ __device__ void attention_unit(const CUtensorMap* tmk_p, const CUtensorMap* tmv_
         uint8_t* st = kv_smem + s * kStageBytes;
 #pragma unroll
         for (int pg = 0; pg < 4; ++pg) {
-          const int phys = pages[i * 4 + pg];
+          const int phys = attn_page(pages, i * 4 + pg, last_page - pg_beg, PRE);
           const int y = (phys * p.n_kv_heads + kvh) * p.page_size;
           tma_load_2d(st + 0 * kHalfBytes + pg * 2048, &tmk, full + s, 0, y);
           tma_load_2d(st + 1 * kHalfBytes + pg * 2048, &tmk, full + s, 64, y);

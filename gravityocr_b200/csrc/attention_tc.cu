@@ -103,11 +103,13 @@ __global__ void __launch_bounds__(320) attention_tc_kernel(const __grid_constant
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (threadIdx.x == 0) pdl_trigger();
-  pdl_wait();
-
   // blocks launch in z-major order: a longest-first request order shortens the tail of a mixed-length batch
   const int b = p.order ? p.order[blockIdx.z] : blockIdx.z;
   const int split = blockIdx.x, kvh = blockIdx.y;
+  // the producer warp reads the split's page ids while the previous kernel finishes
+  if (warp == w_prod) attn_preload_pages(p, b, split, lane, pages);
+  pdl_wait();
+
   const int base = static_cast<int>(p.seq_lens[b]) + p.base_add;
   const int L = base + p.K;  // the last row's limit
   const int n_active = (L + p.chunk - 1) / p.chunk;
@@ -143,14 +145,8 @@ __global__ void __launch_bounds__(320) attention_tc_kernel(const __grid_constant
   if (!active) {
     // no tiles: straight to the teardown
   } else if (warp == w_prod) {
-    // ------------------------------------------------------------ producer
-    // the split's page ids in one coalesced pass (pages past the request's last page hold no visible token: they
-    // are replaced by its last page, whose contents are finite)
-    const int* pt = p.page_table + (size_t)b * p.pt_stride;
-    const int last_page = (L - 1) / p.page_size;
-    const int pg_beg = kv_beg / p.page_size;
-    const int n_pg = n_tiles * (kTile / 16);
-    for (int i = lane; i < n_pg; i += 32) pages[i] = pt[min(pg_beg + i, last_page)];
+    // ------------------------------------------------------------ producer (page ids preloaded above)
+    const int last_slot = (L - 1) / p.page_size - kv_beg / p.page_size;
     __syncwarp();
     if (lane == 0) {
       int issued = 0;
@@ -161,7 +157,7 @@ __global__ void __launch_bounds__(320) attention_tc_kernel(const __grid_constant
         uint8_t* st = ring + s * kStageBytes;
 #pragma unroll
         for (int pg = 0; pg < 4; ++pg) {
-          const int y = (pages[i * 4 + pg] * p.n_kv_heads + kvh) * p.page_size;
+          const int y = (attn_page(pages, i * 4 + pg, last_slot, true) * p.n_kv_heads + kvh) * p.page_size;
           tma_load_2d(st + 0 * kHalfBytes + pg * 2048, &tmk, kv_full + s, 0, y);
           tma_load_2d(st + 1 * kHalfBytes + pg * 2048, &tmk, kv_full + s, 64, y);
           tma_load_2d(st + 2 * kHalfBytes + pg * 2048, &tmv, kv_full + s, 0, y);
