@@ -98,10 +98,21 @@ __global__ void __launch_bounds__(kRowThreads) embed_rows_kernel(const EmbedPara
 
 // ------------------------------------------------------------------ residual + sandwich norm
 // One CTA per row; each thread owns up to kMaxChunks groups of 8 features, kept in registers between the passes.
-// MC = 1 when the row fits one 8-feature chunk per thread (hidden <= 1536): a small register footprint, so that a
-// whole batch of rows is resident at once.
+// MC = 1 when the row fits one 8-feature chunk per thread (hidden <= 1536); four split partials in flight per thread.
+// Many rows: the default register budget (62 registers at MC = 1, five CTAs resident per SM).  Few rows
+// (<= kNormFewRows): an explicit one-block minimum, under which the compiler keeps more loads in flight (112 registers;
+// batch-1 forward 0.825 -> 0.799 ms).  A cap of 40 registers for eight CTAs per SM spilled and was slower at 1,088
+// rows.
+constexpr int kNormFewRows = 512;
 template <int MC>
 __global__ void __launch_bounds__(kRowThreads) residual_norm_kernel(const ResNormParams p) {
+  __shared__ float red[32];
+  if (threadIdx.x == 0) pdl_trigger();
+  pdl_wait();
+  resnorm_row<MC>(p, blockIdx.x, threadIdx.x, blockDim.x, 1, red);
+}
+template <int MC>
+__global__ void __launch_bounds__(kRowThreads, 1) residual_norm_few_rows_kernel(const ResNormParams p) {
   __shared__ float red[32];
   if (threadIdx.x == 0) pdl_trigger();
   pdl_wait();
@@ -217,7 +228,11 @@ cudaError_t launch_embed_rows(const EmbedParams& p, cudaStream_t s, bool pdl) {
   return launch_pdl(embed_rows_kernel, dim3(p.bs * p.K), dim3(kRowThreads), p, s, pdl);
 }
 cudaError_t launch_residual_norm(const ResNormParams& p, cudaStream_t s, bool pdl) {
-  if (p.hidden <= 8 * kRowThreads) return launch_pdl(residual_norm_kernel<1>, dim3(p.m), dim3(kRowThreads), p, s, pdl);
+  if (p.hidden <= 8 * kRowThreads) {
+    if (p.m <= kNormFewRows)
+      return launch_pdl(residual_norm_few_rows_kernel<1>, dim3(p.m), dim3(kRowThreads), p, s, pdl);
+    return launch_pdl(residual_norm_kernel<1>, dim3(p.m), dim3(kRowThreads), p, s, pdl);
+  }
   return launch_pdl(residual_norm_kernel<kMaxChunks>, dim3(p.m), dim3(kRowThreads), p, s, pdl);
 }
 cudaError_t launch_accept_commit(const CommitParams& p, cudaStream_t s, bool pdl) {
