@@ -83,35 +83,6 @@ struct LinearShape {
 };
 static int round16(int x) { return ((x + 15) / 16) * 16; }
 
-// Token tiling: among the tile counts whose tile fits one MMA (nt <= GR_MAX_NT), pick the one minimising the critical
-// path of the persistent schedule, (units per CTA, rounded up) x (per-unit cost ~ weight-tile overhead + nt).  Tiles
-// narrower than 128 tokens only where the rows need no more (small batches stream weights: a second token tile
-// would read every weight tile twice).
-static LinearShape linear_shape(int n_out, int k_in, int m) {
-  LinearShape s;
-  s.n_tiles = n_out / 128;
-  s.kc = k_in / 64;
-  const int min_tiles = (m + GR_MAX_NT - 1) / GR_MAX_NT;
-  const long long cap = num_sms();
-  long long best = -1;
-  s.m_tiles = min_tiles;
-  s.nt = round16((m + min_tiles - 1) / min_tiles);
-  for (int mt = min_tiles; mt <= min_tiles * 4 && mt <= m; ++mt) {
-    const int nt = round16((m + mt - 1) / mt);
-    if (mt > min_tiles && nt < 128) break;
-    const long long units = static_cast<long long>(s.n_tiles) * mt;
-    const long long cost = ((units + cap - 1) / cap) * (64 + nt);
-    if (best < 0 || cost < best) {
-      best = cost;
-      s.m_tiles = mt;
-      s.nt = nt;
-    }
-    if (units >= cap * 4) break;
-  }
-  if (s.nt < 16) s.nt = 16;
-  return s;
-}
-
 static int acc_cols_for(int nt) { return nt <= 32 ? 32 : (nt <= 64 ? 64 : (nt <= 128 ? 128 : 256)); }
 
 // Pipeline depth and resident CTAs of the persistent projection kernel for a token tile of nt rows.
@@ -127,23 +98,63 @@ static void linear_launch_shape(int nt, int kc, int epi, int* stages, int* ctas_
   *ctas_per_sm = by_smem < by_tmem ? (by_smem < 1 ? 1 : by_smem) : by_tmem;
 }
 
-// Split-K count for the persistent schedule: minimise (units per CTA, rounded up) x (K chunks per unit); ties go to
-// fewer splits (less partial traffic).  The argmax epilogue runs unsplit.
-static int default_splits(const LinearShape& s, int epi, int m) {
+// Candidate token tilings of m rows: tile counts from the fewest whose tile fits one MMA (nt <= GR_MAX_NT) up to 4x
+// that; tiles narrower than 128 tokens only where the rows need no more (small batches stream weights: a second token
+// tile would read every weight tile twice).  Calls f(m_tiles, nt) for each; f returns false to stop.
+template <class F>
+static void for_token_tilings(int m, F f) {
+  const int min_tiles = (m + GR_MAX_NT - 1) / GR_MAX_NT;
+  for (int mt = min_tiles; mt <= min_tiles * 4 && mt <= m; ++mt) {
+    int nt = round16((m + mt - 1) / mt);
+    if (mt > min_tiles && nt < 128) break;
+    if (nt < 16) nt = 16;
+    if (!f(mt, nt)) break;
+  }
+}
+
+// Token tiling for a split-K count `sp`: the candidate minimising the persistent schedule's critical path,
+// (units per CTA, rounded up) x (K chunks per unit) x (per-chunk cost ~ 128 + nt: the 128-row weight tile and the
+// nt-row token tile both pass through shared memory).  The cost goes to *cost_out.
+static LinearShape linear_shape(int n_out, int k_in, int m, int sp = 1, int epi = GR_EPI_STORE_F32,
+                                long long* cost_out = nullptr) {
+  LinearShape s;
+  s.n_tiles = n_out / 128;
+  s.kc = k_in / 64;
+  const int kc = s.kc / sp;
+  long long best = -1;
+  for_token_tilings(m, [&](int mt, int nt) {
+    // resident CTAs as for the full K depth (the deep ring): shallow split rings admit more CTAs per SM, which the
+    // measurements do not reward
+    int stages, per_sm;
+    linear_launch_shape(nt, s.kc, epi, &stages, &per_sm);
+    const long long cap = static_cast<long long>(num_sms()) * per_sm;
+    const long long units = static_cast<long long>(s.n_tiles) * mt * sp;
+    const long long cost = ((units + cap - 1) / cap) * kc * (128 + nt);
+    if (best < 0 || cost < best) {
+      best = cost;
+      s.m_tiles = mt;
+      s.nt = nt;
+    }
+    return units < cap * 4;
+  });
+  if (cost_out) *cost_out = best;
+  return s;
+}
+
+// Split-K count, chosen together with the token tiling: the cost above minimised over the split counts that divide
+// the K chunks (at most half of them) and whose fp32 partials stay a small, L2-resident fraction of the traffic;
+// ties go to fewer splits (less partial traffic).  The argmax epilogue runs unsplit.
+static int default_splits(int n_out, int k_in, int m, int epi) {
   if (epi == GR_EPI_ARGMAX) return 1;
-  int stages, per_sm;
-  linear_launch_shape(s.nt, s.kc, epi, &stages, &per_sm);
-  const long long cap = static_cast<long long>(num_sms()) * per_sm;
-  const long long units = static_cast<long long>(s.n_tiles) * s.m_tiles;
-  if (units >= cap) return 1;  // the grid is already full: split partials would only add traffic
+  const int kc = k_in / 64;
+  long long best_cost = 0;
+  linear_shape(n_out, k_in, m, 1, epi, &best_cost);
   int best = 1;
-  long long best_cost = ((units + cap - 1) / cap) * s.kc;
-  for (int sp = 2; sp <= s.kc / 2; ++sp) {
-    if (s.kc % sp) continue;
-    const long long u = units * sp;
-    // fp32 partials (s x m x n_out) must stay a small, L2-resident fraction of the traffic
-    if (static_cast<double>(sp) * m * s.n_tiles * 128 * 4 > 32.0 * (1 << 20)) break;
-    const long long cost = ((u + cap - 1) / cap) * (s.kc / sp);
+  for (int sp = 2; sp <= kc / 2; ++sp) {
+    if (kc % sp) continue;
+    if (static_cast<double>(sp) * m * (n_out / 128) * 128 * 4 > 32.0 * (1 << 20)) break;
+    long long cost = 0;
+    linear_shape(n_out, k_in, m, sp, epi, &cost);
     if (cost < best_cost) {
       best_cost = cost;
       best = sp;
@@ -210,14 +221,25 @@ int gr_num_sms(void) { return num_sms(); }
 
 int gr_linear_default_splits(int n_out, int k_in, int m) {
   if (n_out <= 0 || k_in <= 0 || m <= 0 || (k_in % 64)) return 1;
-  return default_splits(linear_shape(n_out, k_in, m), GR_EPI_STORE_F32, m);
+  return default_splits(n_out, k_in, m, GR_EPI_STORE_F32);
 }
 
 size_t gr_linear_workspace_bytes(int n_out, int m, int splits) {
   if (n_out <= 0 || m <= 0) return 0;
-  LinearShape s = linear_shape(n_out, 64, m);
   if (splits < 1) splits = 1;
-  return linear_ws_layout(nullptr, s, m, splits).bytes;
+  // the largest layout over every token tiling a call of this shape may use (the tiling also depends on K)
+  size_t bytes = 0;
+  for_token_tilings(m, [&](int mt, int nt) {
+    LinearShape s;
+    s.n_tiles = n_out / 128;
+    s.kc = 1;
+    s.m_tiles = mt;
+    s.nt = nt;
+    const size_t b = linear_ws_layout(nullptr, s, m, splits).bytes;
+    if (b > bytes) bytes = b;
+    return true;
+  });
+  return bytes;
 }
 
 // Checks, tiling, tensor maps and kernel parameters of one projection; shared by gr_linear and the small-batch plan.
@@ -232,9 +254,9 @@ static int build_linear(const void* w, int n_out, int k_in, const void* x, int m
                         int32_t* status, LinearLaunch* out) {
   if (!w || !x || !epi || m <= 0 || n_out <= 0 || (n_out % 128) || k_in <= 0 || (k_in % 64)) return GR_ERR_ARG;
   if (epi->mode < GR_EPI_STORE_F32 || epi->mode > GR_EPI_PARTIAL_F32) return GR_ERR_ARG;
-  LinearShape s = linear_shape(n_out, k_in, m);
-  if (splits <= 0) splits = default_splits(s, epi->mode, m);
-  if (s.kc % splits) return GR_ERR_ARG;
+  if (splits <= 0) splits = default_splits(n_out, k_in, m, epi->mode);
+  if ((k_in / 64) % splits) return GR_ERR_ARG;
+  LinearShape s = linear_shape(n_out, k_in, m, splits, epi->mode);
   const size_t ws_splits = epi->mode == GR_EPI_PARTIAL_F32 ? 1 : static_cast<size_t>(splits);
   const int kc = s.kc / splits;
   LinearWs ws = linear_ws_layout(workspace, s, m, static_cast<int>(ws_splits));
