@@ -13,10 +13,11 @@
 //   MMA           allocates TMEM and issues the MMAs from one thread.
 // Per 64-token tile i (M = 128: rows R..127 are padding whose TMEM lanes no thread reads):
 //   S_i = Q K_i^T   tcgen05.mma, A = Q (K-major, shared memory), B = K tile (K-major), N = 64, D = TMEM S[i % 2];
-//   softmax         each thread loads its half row of S_i (32 columns), masks, and exponentiates against its row's
-//                   reference max m: m moves (and the warps rescale their O columns in TMEM: ld, multiply, st) only
-//                   when the tile's max exceeds m by more than 2^8, so P <= 256; the sums are kept in fp32 against the
-//                   same m.  P_i (bf16) is written as a K-major operand over the tile's consumed K (dims 0..63);
+//   softmax         each thread loads its part of its row of S_i (64/H columns), masks, and exponentiates against
+//                   its row's reference max m: m moves (and the warps rescale their O columns in TMEM: ld, multiply,
+//                   st) only when the tile's max exceeds m by more than 2^8, so P <= 256; the sums are kept in fp32
+//                   against the same m.  P_i (bf16) is written as a K-major operand over the tile's consumed K (dims
+//                   0..63);
 //   O += P_i V_i    tcgen05.mma, A = P (K-major), B = V tile (MN-major: 64 dims per 128-byte line, the two dim halves
 //                   8 KB apart), N = 128, D = TMEM O.  Its commit frees the stage.
 // The MMA thread issues whichever of S_{i+1} (its K/V landed, S buffer free) and O += P_i V_i (P_i written) is ready,
@@ -38,7 +39,9 @@ __host__ __device__ constexpr int tc_rows(int G, int K) { return G * K; }
 __host__ __device__ constexpr int tc_quadrants(int R) { return (R + 31) / 32; }
 // warps: softmax q + 4h, then the producer and the MMA warp (H = 2: in slots 2, 3 when W <= 2)
 __host__ __device__ constexpr int tc_prod_warp(int W, int H) { return H == 1 ? W : (W <= 2 ? 2 : 4 + W); }
-__host__ __device__ constexpr int tc_warps(int W, int H) { return tc_prod_warp(W, H) + 2 > 4 * (H - 1) + W ? tc_prod_warp(W, H) + 2 : 4 * (H - 1) + W; }
+__host__ __device__ constexpr int tc_warps(int W, int H) {
+  return tc_prod_warp(W, H) + 2 > 4 * (H - 1) + W ? tc_prod_warp(W, H) + 2 : 4 * (H - 1) + W;
+}
 // one 64-dim atom of the query operand: the rows rounded up to 8-row (1024-byte) swizzle groups
 __host__ __device__ constexpr uint32_t tc_q_atom_bytes(int R) { return static_cast<uint32_t>((R + 7) / 8) * 1024; }
 constexpr int kTcXchgBytes = (2 * 2 * 128 + 2 * 128) * 4;  // row maxima [tile parity][half][row], sums [half][row]
@@ -424,8 +427,8 @@ bool attention_tc_fits(const AttnParams& p) {
   return G >= 1 && p.K >= 1 && G * p.K <= 128 && p.page_size == 16;
 }
 
-// small: grids of at most one CTA per SM (deeper ring, two column parts; the splits of a (request, kv head) form one cluster where
-// the device holds such clusters, else the global merge).
+// small: grids of at most one CTA per SM (deeper ring, two column parts; the splits of a (request, kv head) form one
+// cluster where the device holds such clusters, else the global merge).
 cudaError_t launch_attention_tc(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p, bool small,
                                 cudaStream_t stream, bool pdl) {
   if (!attention_tc_fits(p)) return cudaErrorInvalidValue;
