@@ -35,8 +35,8 @@ sys.path.insert(0, ROOT)
 METRIC = "self-spec decode tokens/s & tokens/forward @bs1/bs64, %HBM roofline, 1/2/4/8 B200"
 K_BD = 16
 SEED = 3
-# DRAM bytes / algorithmic bytes of the verify attention (attention_tc_kernel) on the config-3 mix, from the ncu
-# capture recorded in profiles/attention_tc_kernel_config3_bs64.md (dram__bytes_read + dram__bytes_write of one launch)
+# DRAM bytes / algorithmic bytes of one verify attention launch (attention_tc_kernel) on the config-3 mix:
+# dram__bytes_read.sum + dram__bytes_write.sum of an ncu capture of that launch over its algorithmic bytes
 ATTN_TRAFFIC_RATIO = (584.648704e6 + 6.316288e6) / 586.93632e6
 
 
@@ -58,11 +58,27 @@ def _args():
 
 
 def peaks():
+    """(HBM GB/s, dense bf16 TF/s burst, dense bf16 TF/s sustained, source)."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         d = json.load(open(p))
-        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
-    return 6650.0, 1590.0, "fallback"
+        return (float(d["hbm_gbs"]), float(d["bf16_tflops"]),
+                float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured")
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def forward_bound(cfg, seqs, K, verify, ms, hbm_peak, tc_sustained):
+    """A forward's time against its roofline: bytes / HBM peak and FLOPs / sustained tensor peak; the bound is the
+    larger of the two (the GEMMs of a large batch are tensor-bound, the attention and small batches HBM-bound)."""
+    from gravityocr_b200.metrics import forward_bytes, forward_flops
+    b = forward_bytes(cfg, seqs, K, verify)
+    f = forward_flops(cfg, seqs, K, verify)
+    t_hbm = b / (hbm_peak * 1e9)
+    t_tc = f / (tc_sustained * 1e12)
+    t = ms / 1e3
+    return {"bytes": b, "flops": f, "hbm_frac": round(t_hbm / t, 4), "tensor_frac": round(t_tc / t, 4),
+            "bound": "hbm" if t_hbm >= t_tc else "tensor", "bound_frac": round(max(t_hbm, t_tc) / t, 4),
+            "ms": round(ms, 4)}
 
 
 # ---------------------------------------------------------------------- workload
@@ -133,26 +149,28 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------- CPU port of the reference round
-def cpu_round_port(cfg, weights, seq_lens, K, rounds, threads=None):
-    """The oracle's restatement of the reference round (fp32, torch CPU, all host threads) on a synthetic K/V prefix
-    of the given lengths; returns (tokens/s, committed tokens, seconds, threads)."""
-    from oracle.decoder_ref import OracleDecoder, SpecState, spec_round
+def cpu_round_port(cfg, weights, x, K, rounds, threads=None):
+    """The oracle's restatement of the reference round (fp32 torch on the CPU, all host threads) on one request: a real
+    causal prefill of its prefix rows x (not timed, as the reference's decode-loop timing excludes prefill), then
+    `rounds` full-draft rounds, timed.  Returns (tokens/s, committed tokens, seconds, threads, tokens per forward)."""
+    from oracle.decoder_ref import OracleDecoder, spec_round, spec_start
     n = threads or os.cpu_count() or 1
     torch.set_num_threads(n)
     m = OracleDecoder(cfg, weights)
-    g = torch.Generator().manual_seed(11)
-    toks, secs = 0, 0.0
-    for S in seq_lens:
-        cache = m.new_cache(S + rounds * (K + 1) + K + 2)
-        cache.k[:, :S].normal_(0, 1, generator=g)
-        cache.v[:, :S].normal_(0, 1, generator=g)
-        st = SpecState(cache, S, 1, [1], S)
-        t0 = time.perf_counter()
-        for _ in range(rounds):
-            spec_round(m, st, K)
-        secs += time.perf_counter() - t0
-        toks += len(st.out) - 1
-    return toks / secs, toks, secs, n
+    st = spec_start(m, x, x.shape[0] + rounds * (K + 1) + K + 2)
+    t0 = time.perf_counter()
+    for _ in range(rounds):
+        spec_round(m, st, K)
+    secs = time.perf_counter() - t0
+    toks = len(st.out) - 1
+    return toks / secs, toks, secs, n, toks / (2 * rounds)
+
+
+def cpu_sample(cfg, w, idx, n_img):
+    """The bounded CPU sample: the shortest request of the shard (its prefill stays within seconds)."""
+    i = min(range(len(idx)), key=lambda k: (n_img[idx[k]], idx[k]))
+    x, _ = request_rows(cfg, w, SEED, idx[i], n_img[idx[i]])
+    return idx[i], x
 
 
 def run_reference(a):
@@ -167,21 +185,23 @@ def run_reference(a):
     w = random_weights(cfg, SEED, torch.bfloat16)
     w32 = {k: v.float() for k, v in w.items()}
     n_img, _ = workload(cfg, a.batch, SEED)
-    S = [n_img[0] + 32]
+    ridx, x = cpu_sample(cfg, w, list(range(a.batch)), n_img)
     rounds = max(1, min(4, a.steps))
-    tps, toks, secs, n = cpu_round_port(cfg, w32, S, K, rounds)
+    tps, toks, secs, n, tpf = cpu_round_port(cfg, w32, x, K, rounds)
     steps_done = a.warmup + a.steps
     line = {"impl": "reference", "metric": METRIC, "value": round(tps, 4), "unit": "tokens/s", "n_gpus": a.gpus,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(1000 * secs / rounds, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-            "config": {"workload": "config3-bs64-serving (CPU sample: request 0)", "batch_per_gpu": a.batch, "K": K,
-                       "prefix": S, "page_size": 16},
+            "config": {"workload": f"config3-bs64-serving (CPU sample: request {ridx})", "batch_per_gpu": a.batch,
+                       "K": K, "prefix": int(x.shape[0]), "page_size": 16},
+            "tokens_per_forward": round(tpf, 4),
             "cpu_baseline": {"value": round(tps, 4), "unit": "tokens/s", "cores": n, "kind": "port",
-                             "sample": f"{rounds} full-draft rounds of request 0 (prefix {S[0]} tokens, synthetic K/V), "
-                                       f"fp32 torch on {n} host threads"},
+                             "sample": f"{rounds} full-draft rounds of request {ridx} after its real prefill "
+                                       f"({int(x.shape[0])} prefix tokens), fp32 torch on {n} host threads"},
             "e2e": {"value": round(tps, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "note": "reference is Python (SGLang / transformers) and cannot run on the GPU box; its round is timed as "
-                    "the oracle's CPU port", "steps_run": steps_done}
+            "note": "the reference's round is Python over SGLang / transformers and its source tree is not on the GPU "
+                    "box, so the arm times the oracle's CPU restatement of that round (pinned to the reference's own "
+                    "outputs in the test suite)", "steps_run": steps_done}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -223,7 +243,7 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dp.init("nccl" if world > 1 else "gloo", timeout_s=600)
-    hbm_peak, tc_peak, peak_src = peaks()
+    hbm_peak, tc_peak, tc_sus, peak_src = peaks()
     cfg = ModelConfig()
     K = a.bd + 1
     bs = a.batch
@@ -234,7 +254,7 @@ def main():
     work = [n_img[i] + 32 + out_len[i] for i in range(bs * world)]
     mine = dp.balanced_shards(work, world)[rank]
     prefix = [n_img[i] + 32 for i in mine]
-    rounds_max = a.warmup + a.steps + (0 if a.no_e2e else min(a.steps, 50)) + 8
+    rounds_max = a.warmup + a.steps + 8   # the end-to-end run rewinds to the pre-warm-up state and replays the same rounds
     cap = max(prefix) + rounds_max * (K + 1) + 2 * K + 64
     ppr = (cap + 15) // 16
     chunk = 64
@@ -278,17 +298,25 @@ def main():
     eng.check_status(rb)
     seq1 = rb.seq_lens.cpu().tolist()
     tokens = int((rb.n_committed - ncom0).sum().item())
+    final_dev = (rb.seq_lens.cpu().tolist(), rb.seeds.cpu().tolist(), (rb.n_committed - state0[2]).cpu().tolist())
     elapsed = dp.max_over_ranks(total_ms, dev)
     tokens_all = dp.sum_over_ranks(float(tokens), dev)
     value = tokens_all / (elapsed / 1000.0)
     fwd = 2 * a.steps
     tok_per_fwd = tokens / (fwd * bs)
-    # per-forward HBM roofline (average over the timed rounds: the lengths grow linearly)
+    # per-forward rooflines (average over the timed rounds: the lengths grow linearly)
     seq_mid = [(x + y) / 2 for x, y in zip(seq0, seq1)]
     bd = forward_bytes(cfg, seq_mid, K, verify=False)
     bv = forward_bytes(cfg, seq_mid, K, verify=True)
     frac_d = bd / (draft_ms / a.steps / 1000.0) / (hbm_peak * 1e9)
     frac_v = bv / (verify_ms / a.steps / 1000.0) / (hbm_peak * 1e9)
+    bound_d = forward_bound(cfg, seq_mid, K, False, draft_ms / a.steps, hbm_peak, tc_sus)
+    bound_v = forward_bound(cfg, seq_mid, K, True, verify_ms / a.steps, hbm_peak, tc_sus)
+    # work-normalised throughput: forward rows (bs x K per forward) per second, independent of how many drafts a
+    # shard's requests happen to accept
+    rows_s = dp.sum_over_ranks(float(2 * a.steps * bs * K), dev) / (elapsed / 1000.0)
+    per_rank = dp.gather_objects({"rank": rank, "tokens": tokens, "tokens_per_forward": round(tok_per_fwd, 4),
+                                  "ms_per_step": round(total_ms / a.steps, 4)})
 
     # ---- dominant kernel at this batch: the verify attention (K/V streaming); timed alone on this stream
     seq_now = rb.seq_lens.cpu().tolist()
@@ -320,10 +348,14 @@ def main():
                    "l2": "inputs larger than L2 (1.16 GB weights + K/V per forward)",
                    "no_finish": "output budgets U[256,2048] exceed the timed rounds"},
         "tokens_per_forward": round(tok_per_fwd, 4),
+        "rows_per_s": round(rows_s, 1),
+        "per_rank": per_rank,
         "hbm_roofline_per_forward": {"draft": round(frac_d, 4), "verify": round(frac_v, 4), "peak_gbs": hbm_peak,
                                      "peak": peak_src, "draft_ms": round(draft_ms / a.steps, 4),
                                      "verify_ms": round(verify_ms / a.steps, 4),
                                      "bytes_draft": bd, "bytes_verify": bv},
+        "bound_per_forward": {"draft": bound_d, "verify": bound_v, "hbm_gbs": hbm_peak, "tensor_tflops": tc_sus,
+                              "peak": f"{peak_src} (HBM copy; bf16 GEMM sustained)"},
         "roofline": {"kernel": "attention_tc_kernel (verify, one layer)", "bound": "hbm",
                      "achieved": round(attn_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(attn_gbs / hbm_peak, 4), "traffic": int(attn_b * ATTN_TRAFFIC_RATIO),
@@ -336,14 +368,20 @@ def main():
         line["clocks"] = clk.summary()
 
     # ---- end to end through the served worker API: the same warm-up and timed rounds as the device-timed run,
-    # replayed from the saved round state (the rounds are deterministic, so they rewrite the same K/V rows)
+    # replayed from the saved round state (the rounds are deterministic, so they rewrite the same K/V rows and must
+    # commit the same tokens)
     if not a.no_e2e and not a.profile_small:
         for t, t0 in zip((rb.seq_lens, rb.seeds, rb.n_committed, rb.rounds), state0):
             t.copy_(t0)
-        e2e = e2e_worker(eng, rb, cfg, K, min(a.steps, 50), dev, max(1, a.warmup))
+        e2e = e2e_worker(eng, rb, cfg, K, a.steps, dev, a.warmup)
+        final_e2e = e2e.pop("final")
+        same = final_e2e == final_dev and e2e["tokens"] == tokens
+        if not same:
+            raise RuntimeError("the end-to-end rounds did not commit what the device-timed rounds committed")
         tok_all = dp.sum_over_ranks(float(e2e.pop("tokens")), dev)
         ms_max = dp.max_over_ranks(e2e.pop("ms"), dev)
         e2e["value"] = round(tok_all / (ms_max / 1000.0), 2)
+        e2e["same_tokens_as_device_run"] = same
         line["e2e"] = e2e
 
     if rank == 0 and world == 1 and not a.profile_small:
@@ -351,11 +389,13 @@ def main():
             line["bs1"] = bs1_crop(eng, cfg, w, K, dev, hbm_peak)
         if not a.no_cpu:
             w32 = {k: v.float() for k, v in w.items()}
-            tps, toks, secs, n = cpu_round_port(cfg, w32, [prefix[0]], K, 4)
+            ridx, x = cpu_sample(cfg, w, mine, n_img)
+            tps, toks, secs, n, tpf = cpu_round_port(cfg, w32, x, K, 4)
             line["cpu_baseline"] = {"value": round(tps, 4), "unit": "tokens/s", "cores": n, "kind": "port",
-                                    "sample": f"4 full-draft rounds of one config-3 request (prefix {prefix[0]}, "
-                                              f"synthetic K/V), fp32 torch on {n} host threads: {toks} tokens in "
-                                              f"{secs:.1f} s"}
+                                    "tokens_per_forward": round(tpf, 4),
+                                    "sample": f"4 full-draft rounds of config-3 request {ridx} after its real prefill "
+                                              f"({int(x.shape[0])} prefix tokens), fp32 torch on {n} host threads: "
+                                              f"{toks} tokens in {secs:.1f} s"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     dp.finish()
@@ -390,6 +430,7 @@ def e2e_worker(eng, rb, cfg, K, steps, dev, warmup):
         rpi_dev.copy_(rpi_host, non_blocking=True)
         wk.forward_batch_generation(batch)
     torch.cuda.synchronize()
+    wrb = wk._rb[bs]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     toks = 0
     e0.record()
@@ -400,9 +441,11 @@ def e2e_worker(eng, rb, cfg, K, steps, dev, warmup):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
+    # the state the rounds leave: K/V lengths, seed pool, committed tokens since the pre-warm-up state
+    final = (wrb.seq_lens.cpu().tolist(), wrb.seeds.cpu().tolist(), wrb.n_committed.cpu().tolist())
     return {"value": None, "unit": "tokens/s", "h2d_bytes_per_step": bs * 8,
             "d2h_bytes_per_step": int(rb.readback.numel() * 4), "steps": steps,
-            "api": "SelfSpecDiffusionWorker.forward_batch_generation", "tokens": toks, "ms": ms}
+            "api": "SelfSpecDiffusionWorker.forward_batch_generation", "tokens": toks, "ms": ms, "final": final}
 
 
 def bs1_crop(eng, cfg, w, K, dev, hbm_peak):

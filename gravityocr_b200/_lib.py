@@ -24,9 +24,7 @@ ROWS_DRAFT, ROWS_VERIFY, ROWS_EXPLICIT = range(3)
 EXPORTS = ("gr_version", "gr_status_string", "gr_set_pdl", "gr_set_attention_tc", "gr_num_sms", "gr_linear_workspace_bytes",
            "gr_attention_workspace_bytes", "gr_linear_default_splits", "gr_linear", "gr_embed_rows",
            "gr_residual_norm", "gr_bd_attention", "gr_accept_commit", "gr_draft_override", "gr_pack_gate_up",
-           "gr_bd_attention_noalloc", "gr_bd_attention_ordered", "gr_small_create", "gr_small_destroy",
-           "gr_small_add_linear", "gr_small_add_attention", "gr_small_add_residual_norm", "gr_small_finalize",
-           "gr_small_launch")
+           "gr_bd_attention_noalloc", "gr_bd_attention_ordered")
 
 
 class Epilogue(ctypes.Structure):
@@ -71,14 +69,6 @@ _SIGS = {
     "gr_accept_commit": (_I, [_I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "gr_draft_override": (_I, [_I, _I, _P, _P, _I, _P, _P, _I, _P, _I, _I, _P]),
     "gr_pack_gate_up": (_I, [_P, _P, _I, _I, _P]),
-    "gr_small_create": (_P, []),
-    "gr_small_destroy": (None, [_P]),
-    "gr_small_add_linear": (_I, [_P, _P, _I, _I, _P, _I, ctypes.POINTER(Epilogue), _I, _P, _Z]),
-    "gr_small_add_attention": (_I, [_P, _P, _P, _P, _L, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P,
-                                    _Z]),
-    "gr_small_add_residual_norm": (_I, [_P, _I, _I, _P, _P, _I, _P, _P, _F, _P, _P]),
-    "gr_small_finalize": (_I, [_P, _P]),
-    "gr_small_launch": (_I, [_P, _P]),
     "gr_bd_attention_noalloc": (_I, [_P, _P, _P, _L, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
     "gr_bd_attention_ordered": (_I, [_P, _P, _P, _L, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _Z, _P,
                                      _P]),
@@ -186,13 +176,13 @@ def residual_norm(m: int, h_in, y, w_a, w_b, eps: float, h_out, x_out, y_parts: 
     _check(rc, "gr_residual_norm")
 
 
-def bd_attention(q, k_cache, v_cache, page_table, seq_lens, bs: int, K: int, draft: bool, base_add: int,
+def bd_attention(q, k_cache, v_cache, page_table, seq_lens, bs: int, K: int, draft, base_add: int,
                  n_q_heads: int, n_kv_heads: int, page_size: int, chunk: int, max_splits: int, out, workspace,
                  status=None, stream=None, order=None) -> None:
     n_pages = k_cache.shape[0]
     rc = load().gr_bd_attention_ordered(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), n_pages,
                                 page_table.data_ptr(), page_table.shape[1], seq_lens.data_ptr(), _ptr(order),
-                                bs, K, 1 if draft else 0, base_add,
+                                bs, K, int(draft), base_add,
                                 n_q_heads, n_kv_heads, page_size, chunk, max_splits, out.data_ptr(),
                                 _ptr(workspace), 0 if workspace is None else workspace.numel() * workspace.element_size(),
                                 _ptr(status), _stream(stream))
@@ -221,66 +211,13 @@ def pack_gate_up(src: torch.Tensor, dst: torch.Tensor, intermediate: int, stream
     _check(rc, "gr_pack_gate_up")
 
 
-def bd_attention_noalloc(q, k_cache, v_cache, page_table, seq_lens, bs: int, K: int, draft: bool, base_add: int,
+def bd_attention_noalloc(q, k_cache, v_cache, page_table, seq_lens, bs: int, K: int, draft, base_add: int,
                          n_q_heads: int, n_kv_heads: int, page_size: int, chunk: int, max_splits: int, out,
                          status=None, stream=None) -> None:
     """``bd_attention`` for callers that cannot allocate device memory: the split scratch is the library's own
     fixed 8 MiB device array (see ``gr_bd_attention_noalloc`` in include/gravity_b200.h for the limits)."""
     rc = load().gr_bd_attention_noalloc(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[0],
                                         page_table.data_ptr(), page_table.shape[1], seq_lens.data_ptr(), bs, K,
-                                        1 if draft else 0, base_add, n_q_heads, n_kv_heads, page_size, chunk,
+                                        int(draft), base_add, n_q_heads, n_kv_heads, page_size, chunk,
                                         max_splits, out.data_ptr(), _ptr(status), _stream(stream))
     _check(rc, "gr_bd_attention_noalloc")
-
-
-class SmallPlan:
-    """A persistent small-batch forward (``gr_small_*``): record the forward's projections, attention calls and
-    residual norms once, with the same arguments as the per-launch calls, then launch the whole phase list as one
-    cooperative kernel.  Every pointer is baked in at record time; lengths, positions and page tables stay device
-    resident and are read at run time.  ``finalize`` allocates the plan's device buffer (not under stream capture)."""
-
-    def __init__(self):
-        self._lib = load()
-        self._h = self._lib.gr_small_create()
-        if not self._h:
-            raise RuntimeError("gr_small_create failed")
-        self.keep = []  # tensors whose pointers the plan holds
-
-    def __del__(self):
-        h, self._h = getattr(self, "_h", None), None
-        if h and _lib is not None:
-            _lib.gr_small_destroy(h)
-
-    def linear(self, w, x, m: int, epi: Epilogue, workspace, splits: int = 0, prefetch=None, status=None) -> None:
-        _need(w, torch.bfloat16, "w")
-        _need(x, torch.bfloat16, "x")
-        n_out, k_in = w.shape
-        rc = self._lib.gr_small_add_linear(self._h, w.data_ptr(), n_out, k_in, x.data_ptr(), m, ctypes.byref(epi),
-                                           splits, workspace.data_ptr(), workspace.numel() * workspace.element_size())
-        _check(rc, "gr_small_add_linear")
-        self.keep += [w, x, workspace]
-
-    def bd_attention(self, q, k_cache, v_cache, page_table, seq_lens, bs: int, K: int, draft: bool, base_add: int,
-                     n_q_heads: int, n_kv_heads: int, page_size: int, chunk: int, max_splits: int, out, workspace,
-                     status=None, order=None) -> None:
-        rc = self._lib.gr_small_add_attention(
-            self._h, q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[0], page_table.data_ptr(),
-            page_table.shape[1], seq_lens.data_ptr(), _ptr(order), bs, K, 1 if draft else 0, base_add, n_q_heads,
-            n_kv_heads, page_size, chunk, max_splits, out.data_ptr(), _ptr(workspace),
-            0 if workspace is None else workspace.numel() * workspace.element_size())
-        _check(rc, "gr_small_add_attention")
-        self.keep += [q, k_cache, v_cache, page_table, seq_lens, out] + [t for t in (workspace, order) if t is not None]
-
-    def residual_norm(self, m: int, h_in, y, w_a, w_b, eps: float, h_out, x_out, y_parts: int = 1) -> None:
-        rc = self._lib.gr_small_add_residual_norm(self._h, m, h_in.shape[-1], h_in.data_ptr(), y.data_ptr(), y_parts,
-                                                  w_a.data_ptr(), w_b.data_ptr(), eps, h_out.data_ptr(),
-                                                  x_out.data_ptr())
-        _check(rc, "gr_small_add_residual_norm")
-        self.keep += [h_in, y, w_a, w_b, h_out, x_out]
-
-    def finalize(self, status) -> None:
-        _check(self._lib.gr_small_finalize(self._h, _ptr(status)), "gr_small_finalize")
-        self.keep.append(status)
-
-    def launch(self, stream=None) -> None:
-        _check(self._lib.gr_small_launch(self._h, _stream(stream)), "gr_small_launch")

@@ -61,24 +61,22 @@ size_t attention_smem_bytes(int K, int G, int stages) { return 1024 + attn_regio
 
 template <int MAXT, int MINB, int ST>
 static cudaError_t configure_attention() {
-  static bool configured = false;
-  if (configured) return cudaSuccess;
-  cudaError_t e =
-      cudaFuncSetAttribute(attention_kernel<MAXT, MINB, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(attention_kernel<MAXT, MINB, ST>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-  if (e != cudaSuccess) return e;
-  configured = true;
-  return cudaSuccess;
+  static PerDeviceOnce configured;
+  return once_per_device(configured, [] {
+    auto kern = attention_kernel<MAXT, MINB, ST>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  });
 }
 
-// Whether clusters of `size` CTAs of the small-batch configuration fit on the device (cached per size).
+// Whether clusters of `size` CTAs of the small-batch configuration fit on the current device (cached per device,
+// size, threads and shared memory).
 static bool attention_cluster_ok(int size, int threads, size_t smem) {
-  static int known[17] = {0};  // 0 unknown, 1 yes, 2 no
-  if (known[size]) return known[size] == 1;
-  bool ok = false;
-  auto kern = attention_kernel<288, 1, 4>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+  static ClusterFitCache cache;
+  return cluster_fit_cached(cache, size, threads, smem, [&] {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(size);
     cfg.blockDim = dim3(threads);
@@ -91,11 +89,10 @@ static bool attention_cluster_ok(int size, int threads, size_t smem) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    ok = cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n >= 1;
-  }
-  cudaGetLastError();  // a refused query leaves no sticky error
-  known[size] = ok ? 1 : 2;
-  return ok;
+    const bool ok = cudaOccupancyMaxActiveClusters(&n, attention_kernel<288, 1, 4>, &cfg) == cudaSuccess && n >= 1;
+    cudaGetLastError();  // a refused query leaves no sticky error
+    return ok;
+  });
 }
 
 cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, const AttnParams& p,

@@ -1,5 +1,5 @@
-// Attention device code shared by the per-launch kernel (attention.cu) and the persistent small-batch forward
-// (small.cu): one (split, kv head, request) unit, run by the CTA's participating warps.
+// Attention device code of the mma.sync kernel (attention.cu), shared in part with the tcgen05 kernel
+// (attention_tc.cu): one (split, kv head, request) unit, run by the CTA's participating warps.
 #pragma once
 
 #include "params.cuh"
@@ -12,8 +12,11 @@ constexpr int kStageBytes = 4 * kHalfBytes;     // K lo, K hi, V lo, V hi
 constexpr int kMaxChunkPages = 4096 / 16;  // chunk <= 4096 tokens
 constexpr int kMaxMergeSplits = 16;        // splits per (request, kv head); the host enforces it
 
+// Cache positions [0, row_limit) that window row j sees: draft 1 (the served round) keeps row 0, the boundary token,
+// causal and lets the mask rows see the whole block; draft 2 (the in-process round's first block, which has no
+// boundary token) lets every row see the whole block; draft 0 is causal.
 __device__ __forceinline__ int row_limit(const AttnParams& p, int j, int base) {
-  if (p.draft) return j == 0 ? base + 1 : base + p.K;
+  if (p.draft) return (j == 0 && p.draft == 1) ? base + 1 : base + p.K;
   return base + j + 1;
 }
 __device__ __forceinline__ void named_bar(int id, int threads) {

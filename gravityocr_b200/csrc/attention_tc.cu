@@ -386,40 +386,39 @@ __global__ void __launch_bounds__(320) attention_tc_kernel(const __grid_constant
 
 template <int ST, int H>
 static cudaError_t configure_attention_tc() {
-  static bool configured = false;
-  if (configured) return cudaSuccess;
-  auto kern = attention_tc_kernel<ST, H>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  if (e != cudaSuccess) return e;
-  configured = true;
-  return cudaSuccess;
+  static PerDeviceOnce configured;
+  return once_per_device(configured, [] {
+    auto kern = attention_tc_kernel<ST, H>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  });
 }
 
-// Whether clusters of `size` CTAs of the small-grid configuration fit on the device (cached per size).
+// Whether clusters of `size` CTAs of the small-grid configuration fit on the current device (cached per device, size,
+// threads and shared memory).
 static bool attention_tc_cluster_ok(int size, int threads, size_t smem) {
-  static int known[17] = {0};  // 0 unknown, 1 yes, 2 no
-  if (known[size]) return known[size] == 1;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(size);
-  cfg.blockDim = dim3(threads);
-  cfg.dynamicSmemBytes = smem;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = size;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  int n = 0;
-  const bool ok =
-      cudaOccupancyMaxActiveClusters(&n, attention_tc_kernel<kTcStagesSmall, 2>, &cfg) == cudaSuccess && n >= 1;
-  cudaGetLastError();  // a refused query leaves no sticky error
-  known[size] = ok ? 1 : 2;
-  return ok;
+  static ClusterFitCache cache;
+  return cluster_fit_cached(cache, size, threads, smem, [&] {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(size);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = size;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    const bool ok =
+        cudaOccupancyMaxActiveClusters(&n, attention_tc_kernel<kTcStagesSmall, 2>, &cfg) == cudaSuccess && n >= 1;
+    cudaGetLastError();  // a refused query leaves no sticky error
+    return ok;
+  });
 }
 
 bool attention_tc_fits(const AttnParams& p) {

@@ -5,8 +5,6 @@
 #include <map>
 #include <mutex>
 #include <tuple>
-#include <vector>
-#include <new>
 
 #include "params.cuh"
 
@@ -66,16 +64,26 @@ static int tensor_map_2d(const void* base, uint64_t rows, uint64_t cols, uint32_
 }
 
 static bool g_pdl = true;
-static int g_sms = 0;
+static std::mutex g_sms_mu;
+static int g_sms[kMaxDevices] = {};
 
+// SM count of the current device (the persistent grids and split heuristics are sized by it); 148 without a device.
 static int num_sms() {
-  if (!g_sms) {
-    int dev = 0, n = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    g_sms = n;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return 148;
   }
-  return g_sms;
+  std::lock_guard<std::mutex> g(g_sms_mu);
+  if (!g_sms[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      return 148;
+    }
+    g_sms[dev] = n;
+  }
+  return g_sms[dev];
 }
 
 struct LinearShape {
@@ -242,7 +250,7 @@ size_t gr_linear_workspace_bytes(int n_out, int m, int splits) {
   return bytes;
 }
 
-// Checks, tiling, tensor maps and kernel parameters of one projection; shared by gr_linear and the small-batch plan.
+// Checks, tiling, tensor maps and kernel parameters of one projection.
 struct LinearLaunch {
   LinearParams p;
   CUtensorMap tmw, tmx;
@@ -349,7 +357,7 @@ size_t gr_attention_workspace_bytes(int bs, int K, int n_q_heads, int n_kv_heads
   return kAttnTicketBytes + align256(slots * R_pad * 128 * sizeof(float)) + align256(slots * R_pad * 2 * sizeof(float));
 }
 
-// Checks, tensor maps and kernel parameters of one attention call; shared by the entry points and the plan.
+// Checks, tensor maps and kernel parameters of one attention call; shared by the entry points.
 struct AttnLaunch {
   AttnParams p;
   CUtensorMap tmk, tmv;
@@ -362,7 +370,7 @@ static int build_attention(const void* q, const void* k_cache, const void* v_cac
   if (!q || !k_cache || !v_cache || !page_table || !seq_lens || !out || bs <= 0 || K <= 0 || n_pages <= 0)
     return GR_ERR_ARG;
   if (n_kv_heads <= 0 || n_q_heads % n_kv_heads || page_size != 16 || chunk <= 0 || chunk % 64 || chunk > 4096 ||
-      max_splits <= 0)
+      max_splits <= 0 || draft < 0 || draft > 2)
     return GR_ERR_ARG;
   const int G = n_q_heads / n_kv_heads;
   if (G * K > 128 || static_cast<size_t>(bs) * n_kv_heads * sizeof(int) > kAttnTicketBytes) return GR_ERR_UNSUPPORTED;
@@ -385,7 +393,7 @@ static int build_attention(const void* q, const void* k_cache, const void* v_cac
   p.seq_lens = seq_lens;
   p.bs = bs;
   p.K = K;
-  p.draft = draft ? 1 : 0;
+  p.draft = draft;
   p.base_add = base_add;
   p.n_q_heads = n_q_heads;
   p.n_kv_heads = n_kv_heads;
@@ -491,161 +499,6 @@ int gr_residual_norm(int m, int hidden, const float* h_in, const float* y, int y
   return launch_residual_norm(p, static_cast<cudaStream_t>(stream), g_pdl) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
 }
 
-// ------------------------------------------------------------------ persistent small-batch forward (plan)
-namespace {
-struct SmallPlan {
-  std::vector<CUtensorMap> maps;
-  std::vector<SmallPhase> phases;
-  int nt = -1;
-  int attn_row_tiles = -1;
-  int stages = 0;
-  int grid = 0;
-  int device = -1;
-  uint8_t* dev = nullptr;  // tensor maps | phases | grid-barrier counters
-  size_t phases_off = 0, sync_off = 0;
-  bool finalized = false;
-};
-int plan_add_map(SmallPlan* pl, const CUtensorMap& m) {
-  pl->maps.push_back(m);
-  return static_cast<int>(pl->maps.size()) - 1;
-}
-}  // namespace
-
-void* gr_small_create(void) { return new (std::nothrow) SmallPlan(); }
-
-void gr_small_destroy(void* plan) {
-  SmallPlan* pl = static_cast<SmallPlan*>(plan);
-  if (!pl) return;
-  if (pl->dev) cudaFree(pl->dev);
-  delete pl;
-}
-
-int gr_small_add_linear(void* plan, const void* w, int n_out, int k_in, const void* x, int m, const gr_epilogue* epi,
-                        int splits, void* workspace, size_t workspace_bytes) {
-  SmallPlan* pl = static_cast<SmallPlan*>(plan);
-  if (!pl || pl->finalized || !epi) return GR_ERR_ARG;
-  if (m <= 0 || m > 64) return GR_ERR_UNSUPPORTED;  // one token tile of at most 64 rows
-  LinearLaunch ll;
-  const int rc = build_linear(w, n_out, k_in, x, m, epi, splits, workspace, workspace_bytes, nullptr, 0, nullptr, &ll);
-  if (rc) return rc;
-  if (ll.p.m_tiles != 1 || (pl->nt >= 0 && pl->nt != ll.p.nt)) return GR_ERR_UNSUPPORTED;
-  pl->nt = ll.p.nt;
-  SmallPhase ph;
-  std::memset(&ph, 0, sizeof(ph));
-  ph.type = SP_LINEAR;
-  ph.epi = epi->mode;
-  ph.map_a = plan_add_map(pl, ll.tmw);
-  ph.map_b = plan_add_map(pl, ll.tmx);
-  ph.lin = ll.p;
-  pl->phases.push_back(ph);
-  if (epi->mode == GR_EPI_ARGMAX) {  // the per-token reduction of the records is a phase of its own
-    ph.type = SP_ARGREDUCE;
-    pl->phases.push_back(ph);
-  }
-  return GR_OK;
-}
-
-int gr_small_add_attention(void* plan, const void* q, const void* k_cache, const void* v_cache, int64_t n_pages,
-                           const int32_t* page_table, int pt_stride, const int64_t* seq_lens, const int32_t* req_order,
-                           int bs, int K, int draft, int base_add, int n_q_heads, int n_kv_heads, int page_size,
-                           int chunk, int max_splits, void* out, void* workspace, size_t workspace_bytes) {
-  SmallPlan* pl = static_cast<SmallPlan*>(plan);
-  if (!pl || pl->finalized) return GR_ERR_ARG;
-  AttnLaunch al;
-  const int rc = build_attention(q, k_cache, v_cache, n_pages, page_table, pt_stride, seq_lens, req_order, bs, K, draft,
-                                 base_add, n_q_heads, n_kv_heads, page_size, chunk, max_splits, out, workspace,
-                                 workspace_bytes, nullptr, &al);
-  if (rc) return rc;
-  const int n_mt = (n_q_heads / n_kv_heads * K + 15) / 16;
-  if (pl->attn_row_tiles >= 0 && pl->attn_row_tiles != n_mt) return GR_ERR_UNSUPPORTED;
-  // eight worker warps: two groups of n_mt compute warps plus a producer, else one group
-  al.p.groups = 2 * n_mt + 1 <= 8 ? 2 : 1;
-  if (al.p.groups * n_mt + 1 > 8) return GR_ERR_UNSUPPORTED;
-  pl->attn_row_tiles = n_mt;
-  SmallPhase ph;
-  std::memset(&ph, 0, sizeof(ph));
-  ph.type = SP_ATTENTION;
-  ph.map_a = plan_add_map(pl, al.tmk);
-  ph.map_b = plan_add_map(pl, al.tmv);
-  ph.att = al.p;
-  pl->phases.push_back(ph);
-  return GR_OK;
-}
-
-int gr_small_add_residual_norm(void* plan, int m, int hidden, const float* h_in, const float* y, int y_parts,
-                               const void* w_a, const void* w_b, float eps, float* h_out, void* x_out) {
-  SmallPlan* pl = static_cast<SmallPlan*>(plan);
-  if (!pl || pl->finalized) return GR_ERR_ARG;
-  if (m <= 0 || hidden <= 0 || hidden % 8 || !h_in || !y || !w_a || !w_b || !h_out || !x_out) return GR_ERR_ARG;
-  if (h_in == h_out || y_parts < 1 || hidden > 8 * 192 * 4) return GR_ERR_ARG;
-  SmallPhase ph;
-  std::memset(&ph, 0, sizeof(ph));
-  ph.type = SP_RESNORM;
-  ResNormParams& p = ph.rn;
-  p.m = m;
-  p.hidden = hidden;
-  p.y_parts = y_parts;
-  p.h_in = h_in;
-  p.y = y;
-  p.w_a = static_cast<const __nv_bfloat16*>(w_a);
-  p.w_b = static_cast<const __nv_bfloat16*>(w_b);
-  p.eps = eps;
-  p.h_out = h_out;
-  p.x_out = static_cast<__nv_bfloat16*>(x_out);
-  pl->phases.push_back(ph);
-  return GR_OK;
-}
-
-int gr_small_finalize(void* plan, int32_t* status) {
-  SmallPlan* pl = static_cast<SmallPlan*>(plan);
-  if (!pl || pl->finalized || pl->phases.empty() || pl->nt < 0) return GR_ERR_ARG;
-  for (SmallPhase& ph : pl->phases) {
-    ph.lin.status = status;
-    ph.att.status = status;
-  }
-  const int rows_pad = 16 * (pl->attn_row_tiles > 0 ? pl->attn_row_tiles : 1);
-  int st = GR_MAX_STAGES;
-  while (st > 2 && small_smem_bytes(pl->nt, st, rows_pad) > 227 * 1024) --st;
-  if (small_smem_bytes(pl->nt, st, rows_pad) > 227 * 1024) return GR_ERR_UNSUPPORTED;
-  pl->stages = st;
-  cudaGetDevice(&pl->device);
-  pl->grid = num_sms();
-  const size_t maps_bytes = pl->maps.size() * sizeof(CUtensorMap);
-  pl->phases_off = align256(maps_bytes);
-  pl->sync_off = pl->phases_off + align256(pl->phases.size() * sizeof(SmallPhase));
-  const size_t bytes = pl->sync_off + (pl->phases.size() + 2) * sizeof(int);
-  if (cudaMalloc(&pl->dev, bytes) != cudaSuccess) return GR_ERR_CUDA;
-  if (cudaMemcpy(pl->dev, pl->maps.data(), maps_bytes, cudaMemcpyHostToDevice) != cudaSuccess ||
-      cudaMemcpy(pl->dev + pl->phases_off, pl->phases.data(), pl->phases.size() * sizeof(SmallPhase),
-                 cudaMemcpyHostToDevice) != cudaSuccess ||
-      cudaMemset(pl->dev + pl->sync_off, 0, (pl->phases.size() + 2) * sizeof(int)) != cudaSuccess)
-    return GR_ERR_CUDA;
-  pl->finalized = true;
-  return GR_OK;
-}
-
-int gr_small_launch(void* plan, void* stream) {
-  SmallPlan* pl = static_cast<SmallPlan*>(plan);
-  if (!pl || !pl->finalized) return GR_ERR_ARG;
-  SmallArgs a;
-  std::memset(&a, 0, sizeof(a));
-  a.maps = reinterpret_cast<const CUtensorMap*>(pl->dev);
-  a.phases = reinterpret_cast<const SmallPhase*>(pl->dev + pl->phases_off);
-  a.n_phases = static_cast<int>(pl->phases.size());
-  a.nt = pl->nt;
-  a.stages = pl->stages;
-  a.attn_rows_pad = 16 * (pl->attn_row_tiles > 0 ? pl->attn_row_tiles : 1);
-  a.attn_row_tiles = pl->attn_row_tiles > 0 ? pl->attn_row_tiles : 1;
-  int* sync = reinterpret_cast<int*>(pl->dev + pl->sync_off);
-  a.done = sync;
-  a.exited = sync + pl->phases.size();
-  a.abort = sync + pl->phases.size() + 1;
-  a.status = pl->phases[0].lin.status ? pl->phases[0].lin.status : pl->phases[0].att.status;
-  for (const SmallPhase& ph : pl->phases)
-    if (!a.status) a.status = ph.lin.status ? ph.lin.status : ph.att.status;
-  return launch_small_forward(a, pl->grid, static_cast<cudaStream_t>(stream)) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
-}
-
 int gr_accept_commit(int bs, int K, const int32_t* am, const int32_t* v, int64_t* seeds, const int64_t* req_pool_idx,
                      int64_t* seq_lens, int x0_committed, const int64_t* loc, int32_t* packed, int64_t* released,
                      int32_t* n_released, int64_t* out_next, int32_t* n_committed, int32_t* rounds,
@@ -707,7 +560,6 @@ int gr_pack_gate_up(const void* src, void* dst, int intermediate, int hidden, vo
 static __device__ __align__(256) uint8_t g_noalloc_attn_scratch[GR_NOALLOC_SCRATCH_BYTES];
 
 namespace gr {
-constexpr int kMaxDevices = 64;
 static std::mutex g_noalloc_mu;
 static void* g_noalloc_addr[kMaxDevices] = {};
 
@@ -737,12 +589,17 @@ extern "C" int gr_bd_attention_noalloc(const void* q, const void* k_cache, const
   void* ws = nullptr;
   int rc = gr::noalloc_scratch(&ws);
   if (rc) return rc;
+  // every argument check runs before anything is queued: a refused call leaves nothing on the stream
+  AttnLaunch al;
+  rc = build_attention(q, k_cache, v_cache, n_pages, page_table, pt_stride, seq_lens, nullptr, bs, K, draft,
+                           base_add, n_q_heads, n_kv_heads, page_size, chunk, max_splits, out, ws,
+                           GR_NOALLOC_SCRATCH_BYTES, status, &al);
+  if (rc) return rc;
   // the array keeps whatever the last call left; the tickets this call counts on must start at zero
   if (max_splits > 1 &&
       cudaMemsetAsync(ws, 0, static_cast<size_t>(bs) * n_kv_heads * sizeof(int), static_cast<cudaStream_t>(stream)) !=
           cudaSuccess)
     return GR_ERR_CUDA;
-  return gr_bd_attention(q, k_cache, v_cache, n_pages, page_table, pt_stride, seq_lens, bs, K, draft, base_add,
-                         n_q_heads, n_kv_heads, page_size, chunk, max_splits, out, ws, GR_NOALLOC_SCRATCH_BYTES, status,
-                         stream);
+  const cudaError_t e = gr::launch_attention(al.tmk, al.tmv, al.p, static_cast<cudaStream_t>(stream), gr::g_pdl);
+  return e == cudaSuccess ? GR_OK : GR_ERR_CUDA;
 }

@@ -1,6 +1,10 @@
 // Parameter blocks of the kernels and their launchers, shared by the kernel files and the C-ABI layer.
 #pragma once
 
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "common.cuh"
 
 namespace gr {
@@ -97,28 +101,42 @@ struct OverrideParams {
   const int32_t* rounds;
 };
 
-// Persistent small-batch forward (small.cu): a device-resident phase list.
-enum SmallPhaseType { SP_LINEAR = 0, SP_ATTENTION = 1, SP_RESNORM = 2, SP_ARGREDUCE = 3 };
-struct SmallPhase {
-  int type, epi;     // SP_LINEAR: epilogue mode
-  int map_a, map_b;  // tensor maps: SP_LINEAR weights / activations, SP_ATTENTION K / V cache
-  LinearParams lin;  // SP_LINEAR, SP_ARGREDUCE
-  AttnParams att;    // SP_ATTENTION
-  ResNormParams rn;  // SP_RESNORM
+// Host-side set-up that belongs to one device context (function attributes, occupancy answers): done once per device,
+// under a lock, by the first launch that runs with that device current.
+constexpr int kMaxDevices = 64;
+struct PerDeviceOnce {
+  std::mutex mu;
+  bool done[kMaxDevices] = {};
 };
-struct SmallArgs {
-  const CUtensorMap* maps;
-  const SmallPhase* phases;
-  int n_phases;
-  int nt, stages;                       // token tile (every projection phase) and TMA ring depth
-  int attn_rows_pad, attn_row_tiles;    // attention rows (G * K) padded to 16, and their 16-row tiles
-  int* done;                            // [n_phases] grid-barrier counters, then `exited`, then `abort`
-  int* exited;
-  int* abort;
-  int* status;
+template <class F>
+inline cudaError_t once_per_device(PerDeviceOnce& o, F f) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> g(o.mu);
+  if (o.done[dev]) return cudaSuccess;
+  e = f();
+  if (e == cudaSuccess) o.done[dev] = true;
+  return e;
+}
+// Cached yes/no answers keyed by (device, cluster size, threads, dynamic shared memory).
+struct ClusterFitCache {
+  std::mutex mu;
+  std::map<std::tuple<int, int, int, size_t>, bool> known;
 };
-size_t small_smem_bytes(int nt, int stages, int attn_rows_pad);
-cudaError_t launch_small_forward(const SmallArgs& a, int grid, cudaStream_t stream);
+template <class F>
+inline bool cluster_fit_cached(ClusterFitCache& c, int size, int threads, size_t smem, F query) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const auto key = std::make_tuple(dev, size, threads, smem);
+  std::lock_guard<std::mutex> g(c.mu);
+  auto it = c.known.find(key);
+  if (it != c.known.end()) return it->second;
+  const bool ok = query();
+  c.known[key] = ok;
+  return ok;
+}
 
 size_t linear_smem_bytes(int nt, int stages, int epi);
 cudaError_t launch_linear(int epi, const CUtensorMap& tmw, const CUtensorMap& tmx, const LinearParams& p, int grid,

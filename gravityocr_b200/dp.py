@@ -60,6 +60,15 @@ def sum_over_ranks(x: float, device=None) -> float:
     return float(t.item())
 
 
+def gather_objects(obj) -> list:
+    """Every rank's `obj`, in rank order (outside the timed region only)."""
+    if not dist.is_initialized():
+        return [obj]
+    out = [None] * dist.get_world_size()
+    dist.all_gather_object(out, obj)
+    return out
+
+
 def finish() -> None:
     if dist.is_initialized():
         dist.destroy_process_group()

@@ -107,13 +107,6 @@ def attention_split(bs: int, K: int, max_len: int, avg_len: int, n_kv: int, sms:
     return chunk, max(1, -(-L // chunk))
 
 
-class _LAUNCH:
-    """Per-launch issue of the forward's kernels (the interface L.SmallPlan records)."""
-    linear = staticmethod(L.linear)
-    bd_attention = staticmethod(L.bd_attention)
-    residual_norm = staticmethod(L.residual_norm)
-
-
 @dataclass
 class RoundBuffers:
     bs: int
@@ -157,8 +150,7 @@ class Engine:
     """One model replica on one GPU: the forward, the round and graph capture."""
 
     def __init__(self, cfg: ModelConfig, weights: Dict[str, torch.Tensor], *, max_rows: int, n_pages: int,
-                 page_size: int = 16, device: Optional[torch.device] = None, pdl: bool = True,
-                 small_rows: int = 0):
+                 page_size: int = 16, device: Optional[torch.device] = None, pdl: bool = True):
         L.load()
         if page_size != 16:
             raise ValueError("the attention kernel's TMA box is one 16-token page")
@@ -185,11 +177,6 @@ class Engine:
         self.attn_ws: Optional[torch.Tensor] = None
         self.sms = L.num_sms()
         self.graphs: Dict[Tuple[int, int], torch.cuda.CUDAGraph] = {}
-        # forwards of at most small_rows rows (with lm_head) run as one persistent kernel (L.SmallPlan), built on
-        # first use for each set of buffers.  Off by default: on B200 it is bit-identical to the per-launch forward
-        # but slower at batch 1 (2.0 vs 0.9 ms per forward).
-        self.small_rows = small_rows
-        self._small: Dict[tuple, "L.SmallPlan"] = {}
 
     # ------------------------------------------------------------------ workspace
     def gemm_shapes(self) -> List[Tuple[int, int]]:
@@ -229,9 +216,10 @@ class Engine:
                 out_idx: torch.Tensor, out_top1: Optional[torch.Tensor] = None, out_gap: Optional[torch.Tensor] = None,
                 seeds=None, rpi=None, ids32=None, ids64=None, row_embeds=None, attn_chunk: int = 64,
                 attn_splits: int = 1, status: Optional[torch.Tensor] = None, head: bool = True,
-                order: Optional[torch.Tensor] = None) -> None:
+                order: Optional[torch.Tensor] = None, attn_draft: Optional[int] = None) -> None:
         """One pass of the decoder over M = bs*K rows; writes each row's argmax (and top-1 / gap) to out_idx.
-        head=False stops before lm_head (the normed final hidden rows stay in ``self.x``)."""
+        head=False stops before lm_head (the normed final hidden rows stay in ``self.x``).  attn_draft overrides the
+        attention mask the row mode implies (1 for draft rows, else causal); 2 = every row sees the whole window."""
         cfg, w, M = self.cfg, self.w, bs * K
         if M > self.max_rows:
             raise ValueError(f"{M} rows > max_rows {self.max_rows}")
@@ -247,29 +235,15 @@ class Engine:
                      mask_id=cfg.mask_id, norm_w=w.layers[0]["in"], eps=cfg.rms_eps, h_out=self.h[0], x_out=self.x,
                      row_pos=self.row_pos, row_slot=self.row_slot, row_ids=self.row_ids, status=st)
         ws_attn = self._attn_workspace(bs, K, attn_splits) if attn_splits > 1 else None
-        args = (rows_mode, bs, K, seq_lens, page_table, out_idx, out_top1, out_gap, attn_chunk, attn_splits, st, head,
-                order, ws_attn)
-        if head and 0 < M <= self.small_rows:
-            key = tuple(t.data_ptr() if isinstance(t, torch.Tensor) else t for t in args) + (
-                self.y.data_ptr(), self.lin_ws.data_ptr(), self.y.numel())
-            plan = self._small.get(key)
-            if plan is None:
-                if torch.cuda.is_current_stream_capturing():
-                    raise RuntimeError("no persistent plan for this forward yet: run it once eagerly before capture")
-                plan = L.SmallPlan()
-                self._forward_body(plan, *args)
-                plan.finalize(st)
-                self._small[key] = plan
-            plan.launch()
-            return
-        self._forward_body(_LAUNCH, *args)
+        draft = int(rows_mode == L.ROWS_DRAFT) if attn_draft is None else int(attn_draft)
+        self._forward_body(rows_mode, bs, K, seq_lens, page_table, out_idx, out_top1, out_gap, attn_chunk,
+                           attn_splits, st, head, order, ws_attn, draft)
 
-    def _forward_body(self, ops, rows_mode, bs, K, seq_lens, page_table, out_idx, out_top1, out_gap, attn_chunk,
-                      attn_splits, st, head, order, ws_attn) -> None:
-        """The layers and lm_head after the embedding rows, issued through ``ops``: the library's per-launch calls
-        (_LAUNCH) or a persistent plan recording them (L.SmallPlan)."""
+    def _forward_body(self, rows_mode, bs, K, seq_lens, page_table, out_idx, out_top1, out_gap, attn_chunk,
+                      attn_splits, st, head, order, ws_attn, draft) -> None:
+        """The layers and lm_head after the embedding rows."""
+        ops = L
         cfg, w, M = self.cfg, self.w, bs * K
-        draft = rows_mode == L.ROWS_DRAFT
         base_add = 1 if rows_mode == L.ROWS_VERIFY else 0
         cur = 0
         for l, d in enumerate(w.layers):
@@ -448,9 +422,7 @@ class Engine:
 
     def kernels_per_forward(self, rows: int = 0) -> int:
         """Kernel launches of one forward of `rows` rows: embed + per layer (4 projections, attention, 2 residual
-        norms) + lm_head (projection + per-token argmax reduction); embed + the persistent kernel for small forwards."""
-        if 0 < rows <= self.small_rows:
-            return 2
+        norms) + lm_head (projection + per-token argmax reduction)."""
         return 3 + 7 * self.cfg.n_layers
 
     def capture(self, rb: RoundBuffers, override: bool = False, warmup: int = 0) -> torch.cuda.CUDAGraph:

@@ -37,15 +37,22 @@ def weight_shapes(cfg: ModelConfig) -> List[Tuple[str, Tuple[int, ...]]]:
     return out
 
 
-def random_weights(cfg: ModelConfig, seed: int, dtype: torch.dtype = torch.bfloat16) -> Dict[str, torch.Tensor]:
+def random_weights(cfg: ModelConfig, seed: int, dtype: torch.dtype = torch.bfloat16,
+                   embed_std: float = INIT_STD) -> Dict[str, torch.Tensor]:
     """N(0, 0.02) for every tensor, drawn in ``weight_shapes`` order from one CPU generator.
 
-    The values are drawn in fp32 and rounded once to ``dtype``; with dtype=float32 nothing is rounded."""
+    The values are drawn in fp32 and rounded once to ``dtype``; with dtype=float32 nothing is rounded.
+    ``embed_std`` scales the token-embedding table only (same draw, multiplied by embed_std / 0.02).  At the baseline's
+    0.02 every sublayer adds a vector of the same size as the token's own embedding, the context dominates and greedy
+    streams settle on one repeated token within a few steps; at 0.25 the token identity carries through the 16 layers
+    and streams stay varied, which the parity fixtures use to exercise rejections and rollbacks."""
     g = torch.Generator().manual_seed(int(seed))
     w: Dict[str, torch.Tensor] = {}
     for name, shape in weight_shapes(cfg):
         t = torch.empty(shape, dtype=torch.float32)
         t.normal_(0.0, INIT_STD, generator=g)
+        if name == "embed_tokens" and embed_std != INIT_STD:
+            t.mul_(embed_std / INIT_STD)
         w[name] = t if dtype == torch.float32 else t.to(dtype)
     return w
 

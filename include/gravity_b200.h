@@ -117,8 +117,9 @@ int gr_embed_rows(int mode, int bs, int K, const int64_t* seeds, const int64_t* 
 int gr_residual_norm(int m, int hidden, const float* h_in, const float* y, int y_parts, const void* w_a,
                      const void* w_b, float eps, float* h_out, void* x_out, void* stream);
 
-/* Block-diffusion draft attention (draft = 1: row 0 causal, mask rows see the whole window) or causal verify /
- * prefill attention (draft = 0) over the paged cache.  q/out: bf16 [bs*K, n_q_heads, 128]; k_cache/v_cache: bf16
+/* Block-diffusion draft attention (draft = 1: row 0 causal, mask rows see the whole window; draft = 2: every row sees
+ * the whole window, the first block of the in-process round of src/fast_sampling.py:508-510 with no pending token) or
+ * causal verify / prefill attention (draft = 0) over the paged cache.  q/out: bf16 [bs*K, n_q_heads, 128]; k_cache/v_cache: bf16
  * [n_pages, n_kv_heads, page_size = 16, 128] of one layer; page_table int32 [bs, pt_stride]; window row j of request b
  * sits at position seq_lens[b] + base_add + j.  chunk: cache tokens per split (multiple of 64); max_splits: grid
  * extent (splits past a request's length exit at once).
@@ -176,30 +177,6 @@ int gr_draft_override(int bs, int K, int32_t* am, const int32_t* g, int g_stride
 /* Load-time helper: reorder gate_up rows [gate(I) | up(I)] so that row 2j is gate j and row 2j+1 is up j (the layout
  * GR_EPI_SWIGLU expects).  src/dst: bf16 [2*I, H] device buffers. */
 int gr_pack_gate_up(const void* src, void* dst, int intermediate, int hidden, void* stream);
-
-/* Persistent small-batch forward.  No counterpart in the reference, whose small-batch decode replays SGLang's CUDA
- * graphs of the per-kernel forward (the target_verify graph shape noted at selfspec_diffusion_worker.py:668).  A plan
- * records the projections, attention calls and residual norms of one forward with the same arguments as
- * gr_linear / gr_bd_attention_ordered / gr_residual_norm (each call appends phases; an ARGMAX projection also appends
- * its per-token reduction), then gr_small_launch runs the whole phase list as one cooperative kernel, one CTA per SM,
- * with a grid barrier between phases.  Every phase runs the per-launch kernels' device code on the same parameters,
- * so the outputs are those of the per-launch forward.  Limits: at most 64 rows per projection (one token tile), the
- * same row count in every projection, and G * K <= 112 attention rows.  Pointers are fixed when recorded; lengths,
- * positions, page tables and ids are read at run time.  gr_small_finalize uploads the plan (one cudaMalloc; not
- * during stream capture) and binds the status word; the plan may then be launched any number of times, also from a
- * captured graph, but not twice at once. */
-void* gr_small_create(void);
-void gr_small_destroy(void* plan);
-int gr_small_add_linear(void* plan, const void* w, int n_out, int k_in, const void* x, int m, const gr_epilogue* epi,
-                        int splits, void* workspace, size_t workspace_bytes);
-int gr_small_add_attention(void* plan, const void* q, const void* k_cache, const void* v_cache, int64_t n_pages,
-                           const int32_t* page_table, int pt_stride, const int64_t* seq_lens, const int32_t* req_order,
-                           int bs, int K, int draft, int base_add, int n_q_heads, int n_kv_heads, int page_size,
-                           int chunk, int max_splits, void* out, void* workspace, size_t workspace_bytes);
-int gr_small_add_residual_norm(void* plan, int m, int hidden, const float* h_in, const float* y, int y_parts,
-                               const void* w_a, const void* w_b, float eps, float* h_out, void* x_out);
-int gr_small_finalize(void* plan, int32_t* status);
-int gr_small_launch(void* plan, void* stream);
 
 #ifdef __cplusplus
 }

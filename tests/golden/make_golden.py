@@ -2,7 +2,7 @@
 
 Run in the build container, where the reference tree is readable (it is never read on the GPU box):
 
-    python tests/golden/make_golden.py [--ref /path/to/GravityOCR] [--only natcache_small,commit_kernel,...]
+    python tests/golden/make_golden.py --ref /path/to/GravityOCR [--only natcache_small,commit_kernel,...]
 
 Outputs (small JSON files next to this script):
   * ``natcache_<case>.json``: the reference's own ``generate_speculative_natcache`` (``src/fast_sampling.py:425``) and
@@ -31,9 +31,14 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 
 NATCACHE_CASES = {
-    # name: (n_layers, n_image, n_prompt, max_new_tokens, bd, weight_seed, input_seed)
-    "small": (2, 64, 16, 48, 16, 0, 0),
-    "config0": (16, 256, 32, 128, 16, 0, 0),
+    # name: (n_layers, n_image, n_prompt, max_new_tokens, bd, weight_seed, input_seed, embed_std)
+    "small": (2, 64, 16, 48, 16, 0, 0, 0.02),
+    "config0": (16, 256, 32, 128, 16, 0, 0, 0.02),
+    # the config-0 model with its token-embedding table drawn at std 0.25: a varied stream (the baseline's 0.02 settles
+    # on one repeated token), drafted at three block sizes -- the committed stream must not depend on B
+    "varied_bd16": (16, 256, 32, 128, 16, 0, 0, 0.25),
+    "varied_bd4": (16, 256, 32, 128, 4, 0, 0, 0.25),
+    "varied_bd32": (16, 256, 32, 128, 32, 0, 0, 0.25),
 }
 
 
@@ -54,7 +59,7 @@ def gen_natcache(ref: str, case: str):
     from gravityocr_b200.config import small_model
     from gravityocr_b200.weights import random_weights, request_inputs, prefix_token_ids
 
-    L, n_img, n_txt, new, bd, wseed, iseed = NATCACHE_CASES[case]
+    L, n_img, n_txt, new, bd, wseed, iseed, estd = NATCACHE_CASES[case]
     cfg = small_model(L)
     hf = GlmOcrConfig()
     tc = hf.text_config
@@ -71,7 +76,7 @@ def gen_natcache(ref: str, case: str):
     hf.vision_config.depth = 1
     torch.manual_seed(0)
     glm = GlmOcrForConditionalGeneration(hf).float().eval()
-    w = random_weights(cfg, wseed, torch.float32)
+    w = random_weights(cfg, wseed, torch.float32, embed_std=estd)
     sd = {}
     for k, t in w.items():
         if k == "lm_head":
@@ -127,7 +132,8 @@ def gen_natcache(ref: str, case: str):
     _dump(f"natcache_{case}.json", {
         "source": "reference src/fast_sampling.py generate_speculative_natcache + teacher_force_argmax (CPU, fp32)",
         "n_layers": L, "n_image": n_img, "n_prompt": n_txt, "max_new_tokens": new, "bd": bd,
-        "weight_seed": wseed, "input_seed": iseed, "mask_id": cfg.mask_id, "prompt_ids": txt.tolist(),
+        "weight_seed": wseed, "input_seed": iseed, "embed_std": estd, "mask_id": cfg.mask_id,
+        "prompt_ids": txt.tolist(),
         "stream": stream, "teacher_force_argmax": tf, "stats": st,
         "trace": [{"k": d["k"], "draft": d["draft"], "ar_pred": d["ar_pred"], "new_tokens": d["new_tokens"]} for d in tr],
         "seconds": round(t1 - t0, 2), "threads": torch.get_num_threads(),
@@ -242,9 +248,12 @@ def gen_commit_rules(ref: str):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("GRAVITYOCR_REF", "/root/reference"))
-    ap.add_argument("--only", default="commit_kernel,commit_rules,natcache_small,natcache_config0")
+    ap.add_argument("--ref", default=os.environ.get("GRAVITYOCR_REF"),
+                    help="path of the GravityOCR source tree (or set GRAVITYOCR_REF)")
+    ap.add_argument("--only", default="commit_kernel,commit_rules," + ",".join(f"natcache_{c}" for c in NATCACHE_CASES))
     a = ap.parse_args()
+    if not a.ref or not os.path.isdir(a.ref):
+        ap.error("--ref (or GRAVITYOCR_REF) must name the GravityOCR source tree")
     only = a.only.split(",")
     if "commit_rules" in only:
         gen_commit_rules(a.ref)

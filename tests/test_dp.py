@@ -55,3 +55,19 @@ def test_gloo_two_ranks_shard_and_reduce():
     assert sorted(res[0][1] + res[1][1]) == list(range(5))
     assert res[0][2] == res[1][2] == 2.0
     assert res[0][3] == res[1][3] == 50.0
+
+
+def test_balanced_shards_equal_counts_cover_and_balance():
+    """The benchmark's sharder: every replica gets the same number of requests (one batch size per GPU), every request
+    lands on exactly one replica, and the expected work per replica stays within one request's work."""
+    from gravityocr_b200.dp import balanced_shards
+    import torch
+    g = torch.Generator().manual_seed(3)
+    work = (torch.randint(256, 4097, (512,), generator=g) + torch.randint(256, 2049, (512,), generator=g)).tolist()
+    for n in (1, 2, 4, 8):
+        sh = balanced_shards(work, n)
+        assert sorted(i for s in sh for i in s) == list(range(len(work)))
+        assert {len(s) for s in sh} == {len(work) // n}
+        loads = [sum(work[i] for i in s) for s in sh]
+        assert max(loads) - min(loads) <= max(work)
+        assert sh == balanced_shards(work, n)          # deterministic

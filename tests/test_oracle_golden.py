@@ -91,3 +91,32 @@ def test_natcache_restatement_reproduces_reference_config0(golden_dir):
     assert tf == g["teacher_force_argmax"]
     s2 = spec_generate(m, x, 32, g["bd"] + 1)
     assert s2 == g["stream"][:32]
+
+
+def _natcache_varied(golden_dir, name):
+    from gravityocr_b200.config import ModelConfig
+    from gravityocr_b200.weights import prefix_embeddings, random_weights, request_inputs
+    g = _load(golden_dir, name)
+    cfg = ModelConfig()
+    w = random_weights(cfg, g["weight_seed"], torch.float32, embed_std=g["embed_std"])
+    img, txt = request_inputs(cfg, g["input_seed"], g["n_image"], g["n_prompt"], 0, torch.float32)
+    assert txt.tolist() == g["prompt_ids"]
+    return g, OracleDecoder(cfg, w), prefix_embeddings(w, cfg, img, txt)
+
+
+def test_reference_stream_does_not_depend_on_block_size(golden_dir):
+    """The reference's own runs at B = 4, 16 and 32 commit one stream (its docs: output invariant to the draft block),
+    and that stream is varied (not one repeated token), so it exercises rejections."""
+    streams = [_load(golden_dir, f"natcache_varied_bd{b}.json")["stream"] for b in (4, 16, 32)]
+    assert streams[0] == streams[1] == streams[2]
+    assert len(set(streams[0])) > 0.9 * len(streams[0])
+
+
+@pytest.mark.slow
+def test_natcache_restatement_reproduces_reference_varied(golden_dir):
+    g, m, x = _natcache_varied(golden_dir, "natcache_varied_bd16.json")
+    tr = []
+    s = natcache_generate(m, x, g["max_new_tokens"], g["bd"], tr)
+    assert s == g["stream"]
+    assert [d["k"] for d in tr] == [d["k"] for d in g["trace"]]
+    assert [d["draft"] for d in tr] == [d["draft"] for d in g["trace"]]

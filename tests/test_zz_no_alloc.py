@@ -42,21 +42,42 @@ def _with_workspace(q, kc, vc, pt, seq, bs, K, draft, base_add, chunk, splits):
     return out
 
 
-def test_noalloc_attention_matches_workspace_version_twice_in_a_row():
-    # two different calls back to back: the second finds the first call's leftovers in the shared array
+def _compare(seed, bs, K, draft, chunk, max_prefix, want_global):
+    q, kc, vc, pt, seq, base_add = _case(seed, bs, K, draft, max_prefix)
+    splits = int(math.ceil((int(seq.max()) + base_add + K) / chunk))
+    assert splits > 1
+    # more CTAs than SMs: the splits merge through the scratch (partials and tickets); at most one CTA per SM, they
+    # merge inside a thread-block cluster and the scratch is not touched
+    assert (bs * NKV * splits > L.num_sms()) == want_global
+    assert L.attention_workspace_bytes(bs, K, NQ, NKV, splits) <= L.NOALLOC_SCRATCH_BYTES
+    ref = _with_workspace(q, kc, vc, pt, seq, bs, K, draft, base_add, chunk, splits)
+    out = torch.full_like(ref, float("nan"))
+    st = torch.zeros((1,), dtype=torch.int32, device=DEV)
+    L.bd_attention_noalloc(q, kc, vc, pt, seq, bs, K, draft, base_add, NQ, NKV, PS, chunk, splits, out, status=st)
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    # same kernel, same split points, same merge order: identical (the attention tests' tolerance would be rtol 2e-2)
+    assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("tc_mode", [1, 0])
+def test_noalloc_attention_matches_workspace_version_twice_in_a_row(tc_mode):
+    """Two calls of different shapes back to back whose splits merge through the fixed array: the second call finds
+    the first call's partials and tickets there.  Mode 1 runs the tcgen05 kernel on these grids, mode 0 the mma.sync
+    kernel; both merge through global scratch."""
+    L.set_attention_tc(tc_mode)
+    try:
+        _compare(5, 5, 17, True, 256, 1700, want_global=True)     # 5 x 8 x 6 = 240 CTAs, 5.8 MiB of scratch
+        _compare(6, 4, 33, False, 192, 1100, want_global=True)    # 4 x 8 x 6 = 192 CTAs, 7.7 MiB
+        _compare(7, 5, 17, False, 192, 1450, want_global=True)    # 240 CTAs, 5.8 MiB
+    finally:
+        L.set_attention_tc(1)
+
+
+def test_noalloc_attention_small_grids():
+    # grids of at most one CTA per SM merge inside a cluster; the call must still match
     for seed, bs, K, draft, chunk in [(5, 3, 17, True, 256), (6, 2, 33, False, 256)]:
-        q, kc, vc, pt, seq, base_add = _case(seed, bs, K, draft, 1500)
-        splits = int(math.ceil((int(seq.max()) + base_add + K) / chunk))
-        assert splits > 1  # the scratch is really used
-        assert L.attention_workspace_bytes(bs, K, NQ, NKV, splits) <= L.NOALLOC_SCRATCH_BYTES
-        ref = _with_workspace(q, kc, vc, pt, seq, bs, K, draft, base_add, chunk, splits)
-        out = torch.full_like(ref, float("nan"))
-        st = torch.zeros((1,), dtype=torch.int32, device=DEV)
-        L.bd_attention_noalloc(q, kc, vc, pt, seq, bs, K, draft, base_add, NQ, NKV, PS, chunk, splits, out, status=st)
-        torch.cuda.synchronize()
-        assert int(st.item()) == 0
-        # same kernel, same split points: identical; the attention tests' tolerance would be rtol 2e-2
-        assert torch.equal(out, ref)
+        _compare(seed, bs, K, draft, chunk, 1500, want_global=False)
 
 
 def test_noalloc_attention_refuses_work_beyond_its_array():
