@@ -68,16 +68,23 @@ def peaks():
 
 
 def forward_bound(cfg, seqs, K, verify, ms, hbm_peak, tc_sustained):
-    """A forward's time against its roofline: bytes / HBM peak and FLOPs / sustained tensor peak; the bound is the
-    larger of the two (the GEMMs of a large batch are tensor-bound, the attention and small batches HBM-bound)."""
+    """A forward's time against its roofline.  hbm_frac / tensor_frac: all bytes / HBM peak and all FLOPs / sustained
+    tensor peak over the forward's time.  serial_bound_frac: the forward runs its phases one after another, so its
+    bound is the sum of the phases' bounds -- the attention launches at K/V bytes / HBM peak plus the projections
+    (weights, lm_head included) at max(weight bytes / HBM peak, GEMM FLOPs / tensor peak)."""
     from gravityocr_b200.metrics import forward_bytes, forward_flops
     b = forward_bytes(cfg, seqs, K, verify)
     f = forward_flops(cfg, seqs, K, verify)
     t_hbm = b / (hbm_peak * 1e9)
     t_tc = f / (tc_sustained * 1e12)
+    w_bytes = cfg.streamed_params() * 2
+    gemm_flops = 2 * cfg.streamed_params() * len(seqs) * K
+    t_attn = (b - w_bytes) / (hbm_peak * 1e9)
+    t_gemm = max(w_bytes / (hbm_peak * 1e9), gemm_flops / (tc_sustained * 1e12))
     t = ms / 1e3
     return {"bytes": b, "flops": f, "hbm_frac": round(t_hbm / t, 4), "tensor_frac": round(t_tc / t, 4),
-            "bound": "hbm" if t_hbm >= t_tc else "tensor", "bound_frac": round(max(t_hbm, t_tc) / t, 4),
+            "serial_bound_ms": round((t_attn + t_gemm) * 1e3, 4), "serial_bound_frac": round((t_attn + t_gemm) / t, 4),
+            "gemm_bound": "tensor" if gemm_flops / (tc_sustained * 1e12) > w_bytes / (hbm_peak * 1e9) else "hbm",
             "ms": round(ms, 4)}
 
 
