@@ -24,7 +24,12 @@ ROWS_DRAFT, ROWS_VERIFY, ROWS_EXPLICIT = range(3)
 EXPORTS = ("gr_version", "gr_status_string", "gr_set_pdl", "gr_set_attention_tc", "gr_num_sms", "gr_linear_workspace_bytes",
            "gr_attention_workspace_bytes", "gr_linear_default_splits", "gr_linear", "gr_embed_rows",
            "gr_residual_norm", "gr_bd_attention", "gr_accept_commit", "gr_draft_override", "gr_pack_gate_up",
-           "gr_bd_attention_noalloc", "gr_bd_attention_ordered")
+           "gr_bd_attention_noalloc", "gr_bd_attention_ordered", "gr_gather_rows", "gr_logits_process",
+           "gr_sample_rows", "gr_commit_sampled", "gr_penalty_cumulate")
+FILTER_JOINT, FILTER_SEQUENTIAL, FILTER_TORCH = range(3)
+PEN_REPETITION, PEN_FREQUENCY, PEN_PRESENCE, PEN_MIN_NEW_TOKENS = range(4)
+COIN_ACCEPT, COIN_FINAL, COIN_FIRST, COIN_PREFILL = range(4)
+GR_ERR_NO_TOKEN = 9
 
 
 class Epilogue(ctypes.Structure):
@@ -45,6 +50,34 @@ class Epilogue(ctypes.Structure):
         ("out_idx", ctypes.c_void_p),
         ("out_top1", ctypes.c_void_p),
         ("out_gap", ctypes.c_void_p),
+    ]
+
+
+class Sampling(ctypes.Structure):
+    """gr_sampling: per-request parameter arrays, penalizer state by pool slot, grammar mask, bias and the coins' rng."""
+    _fields_ = [
+        ("vocab", ctypes.c_int),
+        ("filter", ctypes.c_int),
+        ("temperature", ctypes.c_void_p),
+        ("top_k", ctypes.c_void_p),
+        ("top_p", ctypes.c_void_p),
+        ("min_p", ctypes.c_void_p),
+        ("n_order", ctypes.c_int),
+        ("order", ctypes.c_int * 4),
+        ("repetition", ctypes.c_void_p),
+        ("frequency", ctypes.c_void_p),
+        ("presence", ctypes.c_void_p),
+        ("min_new_tokens", ctypes.c_void_p),
+        ("stop_ids", ctypes.c_void_p),
+        ("n_stop", ctypes.c_int),
+        ("st_rep", ctypes.c_void_p),
+        ("st_freq", ctypes.c_void_p),
+        ("st_pres", ctypes.c_void_p),
+        ("st_len", ctypes.c_void_p),
+        ("req_pool_idx", ctypes.c_void_p),
+        ("allowed", ctypes.c_void_p),
+        ("logit_bias", ctypes.c_void_p),
+        ("rng", ctypes.c_void_p),
     ]
 
 
@@ -70,6 +103,11 @@ _SIGS = {
     "gr_draft_override": (_I, [_I, _I, _P, _P, _I, _P, _P, _I, _P, _I, _I, _P]),
     "gr_pack_gate_up": (_I, [_P, _P, _I, _I, _P]),
     "gr_bd_attention_noalloc": (_I, [_P, _P, _P, _L, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
+    "gr_gather_rows": (_I, [_P, _I, _I, _I, _P, _P]),
+    "gr_logits_process": (_I, [_P, _I, _I, _P, ctypes.POINTER(Sampling), _P]),
+    "gr_sample_rows": (_I, [_P, _I, _I, _P, ctypes.POINTER(Sampling), _I, _P, _P, _P, _P, _I, _P, _P]),
+    "gr_commit_sampled": (_I, [_I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "gr_penalty_cumulate": (_I, [_I, _P, _I, _P, _I, ctypes.POINTER(Sampling), _P]),
     "gr_bd_attention_ordered": (_I, [_P, _P, _P, _L, _P, _I, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _Z, _P,
                                      _P]),
 }
@@ -221,3 +259,37 @@ def bd_attention_noalloc(q, k_cache, v_cache, page_table, seq_lens, bs: int, K: 
                                         int(draft), base_add, n_q_heads, n_kv_heads, page_size, chunk,
                                         max_splits, out.data_ptr(), _ptr(status), _stream(stream))
     _check(rc, "gr_bd_attention_noalloc")
+
+
+# ---------------------------------------------------------------------- non-greedy rounds
+def gather_rows(src: torch.Tensor, n: int, stride_rows: int, dst: torch.Tensor, stream=None) -> None:
+    row_bytes = src.shape[-1] * src.element_size()
+    _check(load().gr_gather_rows(src.data_ptr(), row_bytes, n, stride_rows, dst.data_ptr(), _stream(stream)),
+           "gr_gather_rows")
+
+
+def logits_process(logits: torch.Tensor, bs: int, K: int, cand, smp: Sampling, stream=None) -> None:
+    _need(logits, torch.float32, "logits")
+    _check(load().gr_logits_process(logits.data_ptr(), bs, K, _ptr(cand), ctypes.byref(smp), _stream(stream)),
+           "gr_logits_process")
+
+
+def sample_rows(logits: torch.Tensor, bs: int, K: int, cand, smp: Sampling, first_kind: int, accept, sample,
+                p_next=None, first_out=None, first_stride: int = 1, status=None, stream=None) -> None:
+    _need(logits, torch.float32, "logits")
+    _check(load().gr_sample_rows(logits.data_ptr(), bs, K, _ptr(cand), ctypes.byref(smp), first_kind, _ptr(accept),
+                                 sample.data_ptr(), _ptr(p_next), _ptr(first_out), first_stride, _ptr(status),
+                                 _stream(stream)), "gr_sample_rows")
+
+
+def commit_sampled(bs: int, K: int, am, accept, sample, seeds, rpi, seq_lens, predict, packed, released, out_next, *,
+                   n_released=None, n_committed=None, rounds=None, accept_len=None, rng=None, stream=None) -> None:
+    _check(load().gr_commit_sampled(bs, K, am.data_ptr(), accept.data_ptr(), sample.data_ptr(), seeds.data_ptr(),
+                                    rpi.data_ptr(), seq_lens.data_ptr(), predict.data_ptr(), packed.data_ptr(),
+                                    released.data_ptr(), _ptr(n_released), out_next.data_ptr(), _ptr(n_committed),
+                                    _ptr(rounds), _ptr(accept_len), _ptr(rng), _stream(stream)), "gr_commit_sampled")
+
+
+def penalty_cumulate(bs: int, tokens, stride: int, counts, add: int, smp: Sampling, stream=None) -> None:
+    _check(load().gr_penalty_cumulate(bs, tokens.data_ptr(), stride, _ptr(counts), add, ctypes.byref(smp),
+                                      _stream(stream)), "gr_penalty_cumulate")

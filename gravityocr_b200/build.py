@@ -19,7 +19,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libgravity_b200.so")
-SOURCES = ["linear.cu", "attention.cu", "attention_tc.cu", "rowwise.cu", "capi.cu"]
+SOURCES = ["linear.cu", "attention.cu", "attention_tc.cu", "rowwise.cu", "sampling.cu", "capi.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -10,8 +10,12 @@ device next seeds [bs], ``next_token_ids_cpu`` = the committed tokens per reques
 = j per request, ``num_accepted_tokens`` = sum(j), ``finish_checked=True``.
 
 Ownership as in the reference: the K/V pages and the request -> page table belong to the target worker (an
-``Engine`` plus a ``ReqToPagePool``); the seed pool and the pinned readback buffer belong to this worker.  Greedy
-batches only (non-greedy sampling is a later step; such a batch raises ``ValueError``).
+``Engine`` plus a ``ReqToPagePool``); the seed pool, the penalizer state and the pinned readback buffer belong to this
+worker.  A plain batch (every request greedy; no penalty, logit bias, grammar or custom logit processor: the reference's
+``selfspec_sampling.is_plain``) replays the greedy round's CUDA graph; any other batch runs the sampled round of
+``gravityocr_b200.sampling`` (a0 drawn as AR decode draws it, speculative sampling of the verify rows against AR's
+distribution, penalizer cumulation on the device), with the per-round grammar masks and custom logit processors applied
+on the host side of the launches.
 
 SGLang itself is not a dependency: ``ScheduleBatch``-, ``Req``- and ``GenerationBatchResult``-shaped objects are
 duck typed; ``gravityocr_b200.compat.types`` provides minimal ones for tests and standalone serving.
@@ -25,8 +29,10 @@ from typing import List, Optional
 import torch
 
 from .. import _lib as L
-from ..commit_rules import host_commit
+from ..commit_rules import grammar_accept_or_abort, host_commit, stop_set
 from ..engine import Engine
+from ..sampling import (RequestSampling, SampledRound, SamplerState, current_masks, first_tokens, pack_allowed,
+                        verify_row_masks)
 from .types import GenerationBatchResult
 
 
@@ -96,6 +102,10 @@ class SelfSpecDiffusionWorker:
         self._rb = {}
         self._graphs = bool(int(os.environ.get("GR_GRAPHS", "1")))
         self.n_rounds = 0
+        self._sampler: Optional[SamplerState] = None
+        self._random_seed = int(getattr(server_args, "random_seed", 0) or 0)
+        self._filter = L.FILTER_TORCH if getattr(server_args, "sampling_backend", "flashinfer") == "pytorch" \
+            else L.FILTER_JOINT
 
     # ------------------------------------------------------------------ pools / buffers
     def update_weights_from_tensor(self, recv_req):
@@ -111,6 +121,53 @@ class SelfSpecDiffusionWorker:
 
     def ss_release_stash(self, reason: str = "") -> None:
         return None
+
+    def _sampler_state(self) -> SamplerState:
+        if self._sampler is None:
+            self._sampler = SamplerState(self.engine.cfg.vocab, self.req_to_page.size, self.device,
+                                         seed=self._random_seed, filter=self._filter)
+        return self._sampler
+
+    @staticmethod
+    def _request_sampling(reqs) -> List[RequestSampling]:
+        return [RequestSampling.of(r.sampling_params, stop_ids=sorted(stop_set(r))) for r in reqs]
+
+    def _plain(self, reqs, rs: List[RequestSampling]) -> bool:
+        """selfspec_sampling.is_plain (selfspec_sampling.py:40-70): every request greedy, no penalty, logit bias,
+        grammar or custom logit processor."""
+        return all(x.plain for x in rs) and not any(getattr(r, "grammar", None) is not None for r in reqs) and \
+            not any(getattr(r.sampling_params, "custom_logit_processor", None) for r in reqs)
+
+    @staticmethod
+    def _custom_hook(reqs, K: int, cand: Optional[List[List[int]]]):
+        """Custom logit processors on rows (b, j): one call per (processor, j) over its requests, each with a request
+        view whose output_ids hold the row's prefix (output_ids + cand[b][0..j]; none for first-token rows)."""
+        users = [(i, r.sampling_params.custom_logit_processor) for i, r in enumerate(reqs)
+                 if getattr(r.sampling_params, "custom_logit_processor", None)]
+        if not users:
+            return None
+
+        class _View:
+            def __init__(self, req, extra):
+                self._req, self.output_ids = req, list(req.output_ids) + list(extra)
+
+            def __getattr__(self, n):
+                return getattr(self._req, n)
+
+        def hook(logits: torch.Tensor) -> None:
+            for j in range(K):
+                groups = {}
+                for i, fn in users:
+                    groups.setdefault(id(fn), (fn, []))[1].append(i)
+                for fn, idx in groups.values():
+                    rows = torch.tensor([i * K + j for i in idx], device=logits.device)
+                    params = []
+                    for i in idx:
+                        prm = dict(reqs[i].sampling_params.custom_params or {})
+                        prm["__req__"] = _View(reqs[i], cand[i][: j + 1] if cand is not None else [])
+                        params.append(prm)
+                    logits[rows] = fn(logits[rows], params)
+        return hook
 
     def _seeds(self) -> torch.Tensor:
         if self._seed_pool is None:
@@ -153,12 +210,28 @@ class SelfSpecDiffusionWorker:
             x, pid = req.prefix_rows(eng)
             xs.append(x)
             ids.append(pid)
-        first = eng.prefill(rb, xs, ids)
+        rs = self._request_sampling(batch.reqs)
+        first_fn = None
+        if not self._plain(batch.reqs, rs):
+            st = self._sampler_state()
+            for i in rpi:
+                st.reset_slot(i)
+
+            def first_fn(rows, which):
+                sub = [batch.reqs[b] for b in which]
+                masks = current_masks([getattr(r, "grammar", None) for r in sub], eng.cfg.vocab)
+                smp = st.batch([rs[b] for b in which], rb.rpi[torch.tensor(which, device=self.device)].contiguous(),
+                               None if masks is None else pack_allowed(masks).to(self.device))
+                return first_tokens(eng, rows, len(which), smp, status=rb.status,
+                                    custom=self._custom_hook(sub, 1, None))
+        first = eng.prefill(rb, xs, ids, first_fn=first_fn)
         batch.seq_lens.copy_(rb.seq_lens)
         batch.seq_lens_cpu = rb.seq_lens.cpu()
         for req, t in zip(batch.reqs, first):
             req.output_ids.append(t)
             req.check_finished()
+            if getattr(req, "grammar", None) is not None and not req.finished():
+                grammar_accept_or_abort(req, t)   # AR decode feeds every output token to the grammar
             req._spec_seed_ready = True
         return GenerationBatchResult(next_token_ids=torch.tensor(first, dtype=torch.int64, device=self.device),
                                      next_token_ids_cpu=[[t] for t in first], finish_checked=True)
@@ -168,10 +241,6 @@ class SelfSpecDiffusionWorker:
         [a0, d1..d_{K-1}] stays on the device as the verify input, so nothing is returned)."""
         if not all(getattr(r, "_spec_seed_ready", False) for r in batch.reqs):
             raise AssertionError("no carried seed (prefill/extend must seed the pool)")
-        for r in batch.reqs:
-            sp = r.sampling_params
-            if getattr(sp, "temperature", 0.0) not in (0.0, None) and not getattr(sp, "greedy", True):
-                raise ValueError("non-greedy sampling is not on the CUDA path")
         bs = len(batch.reqs)
         rb = self._buffers(bs)
         rb.rpi.copy_(batch.req_pool_indices)
@@ -187,6 +256,9 @@ class SelfSpecDiffusionWorker:
         graph (draft, verify, accept-and-commit) replayed per batch-size bucket."""
         rb = self._cur
         eng = self.engine
+        rs = self._request_sampling(batch.reqs)
+        if not self._plain(batch.reqs, rs):
+            return self._sampled_round(batch, rb, rs)
         if self._graphs:
             if rb.graph is None:
                 snap = (rb.seq_lens.clone(), rb.seeds.clone(), rb.n_committed.clone(), rb.rounds.clone())
@@ -199,6 +271,30 @@ class SelfSpecDiffusionWorker:
         else:
             eng.round_launch(rb)
         return self._fast_commit_round(batch, None, None)
+
+    def _sampled_round(self, batch, rb, rs: List[RequestSampling]) -> GenerationBatchResult:
+        """A non-plain batch: a0 drawn from AR's distribution of the draft's boundary rows (grammar mask of the current
+        state), then the verify rows' speculative sampling (grammar rows after a0, d1..dj), the commit and the
+        penalizer cumulation, all on the device; the host builds the grammar masks and runs custom processors."""
+        eng, reqs, K = self.engine, batch.reqs, self.draft_token_num
+        bs, V = len(reqs), eng.cfg.vocab
+        st = self._sampler_state()
+        sr = getattr(rb, "sampled", None)
+        if sr is None:
+            sr = rb.sampled = SampledRound(eng, rb)
+        grammars = [getattr(r, "grammar", None) for r in reqs]
+        m0 = current_masks(grammars, V)
+        smp = st.batch(rs, rb.rpi, None if m0 is None else pack_allowed(m0).to(self.device))
+        sr.draft(smp, custom=self._custom_hook(reqs, 1, None))
+        cand = None
+        need_host = any(g is not None for g in grammars) or \
+            any(getattr(r.sampling_params, "custom_logit_processor", None) for r in reqs)
+        if need_host:
+            cand = rb.am.view(bs, K).cpu()
+        m1 = verify_row_masks(grammars, cand, V) if cand is not None else None
+        smp = st.batch(rs, rb.rpi, None if m1 is None else pack_allowed(m1).to(self.device))
+        sr.verify(smp, st.rng, custom=self._custom_hook(reqs, K, None if cand is None else cand.tolist()))
+        return self._fast_commit_round(batch, None, None, plain=False)
 
     def _fast_commit_round(self, batch, verify_input, batch_result, plain: bool = True,
                            vocab_mask: Optional[torch.Tensor] = None) -> GenerationBatchResult:

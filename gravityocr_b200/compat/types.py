@@ -20,12 +20,25 @@ class ForwardMode(enum.Enum):
 
 @dataclass
 class SamplingParams:
+    """SGLang's per-request sampling fields the round reads (temperature 0 = greedy)."""
     max_new_tokens: int = 128
     ignore_eos: bool = False
     stop_token_ids: Optional[List[int]] = None
     stop_strs: Optional[List[str]] = None
     stop_regex_strs: Optional[List[str]] = None
     temperature: float = 0.0
+    top_p: float = 1.0
+    top_k: int = -1
+    min_p: float = 0.0
+    repetition_penalty: float = 1.0
+    frequency_penalty: float = 0.0
+    presence_penalty: float = 0.0
+    min_new_tokens: int = 0
+    logit_bias: Optional[dict] = None
+    # f(logits [n, vocab] fp32, params list) -> logits: SGLang's custom logit processor interface; each param dict
+    # carries "__req__" (a read-only request view whose output_ids hold the row's prefix)
+    custom_logit_processor: Optional[object] = None
+    custom_params: Optional[dict] = None
 
 
 @dataclass

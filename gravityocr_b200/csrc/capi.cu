@@ -219,6 +219,7 @@ const char* gr_status_string(int code) {
     case GR_ERR_BAD_PAGE: return "position beyond page-table capacity";
     case GR_ERR_UNSUPPORTED: return "unsupported configuration";
     case GR_ERR_SCRATCH_LIMIT: return "needs more scratch than the 8 MiB no-alloc array (use gr_bd_attention with a workspace)";
+    case GR_ERR_NO_TOKEN: return "a sampled row allowed no token";
     default: return "unknown status";
   }
 }
@@ -522,7 +523,121 @@ int gr_accept_commit(int bs, int K, const int32_t* am, const int32_t* v, int64_t
   p.n_committed = n_committed;
   p.rounds = rounds;
   p.accept_len = accept_len;
+  p.accept = nullptr;
+  p.sample = nullptr;
+  p.predict = nullptr;
+  p.rng = nullptr;
   return launch_accept_commit(p, static_cast<cudaStream_t>(stream), g_pdl) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
+}
+
+int gr_commit_sampled(int bs, int K, const int32_t* am, const int32_t* accept, const int32_t* sample, int64_t* seeds,
+                      const int64_t* req_pool_idx, int64_t* seq_lens, int32_t* predict, int32_t* packed,
+                      int64_t* released, int32_t* n_released, int64_t* out_next, int32_t* n_committed,
+                      int32_t* rounds, int32_t* accept_len, uint64_t* rng, void* stream) {
+  if (bs <= 0 || K < 2 || !am || !accept || !sample || !seeds || !req_pool_idx || !seq_lens || !predict || !packed ||
+      !released || !out_next)
+    return GR_ERR_ARG;
+  CommitParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.bs = bs;
+  p.K = K;
+  p.x0_committed = 0;
+  p.am = am;
+  p.v = predict;
+  p.seeds = seeds;
+  p.rpi = req_pool_idx;
+  p.seq_lens = seq_lens;
+  p.packed = packed;
+  p.released = released;
+  p.n_released = n_released;
+  p.out_next = out_next;
+  p.n_committed = n_committed;
+  p.rounds = rounds;
+  p.accept_len = accept_len;
+  p.accept = accept;
+  p.sample = sample;
+  p.predict = predict;
+  p.rng = rng;
+  return launch_accept_commit(p, static_cast<cudaStream_t>(stream), g_pdl) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
+}
+
+static int check_sampling(const gr_sampling* s) {
+  if (!s || s->vocab <= 0 || s->filter < GR_FILTER_JOINT || s->filter > GR_FILTER_TORCH || s->n_order < 0 ||
+      s->n_order > 4 || !s->req_pool_idx || !s->rng)
+    return GR_ERR_ARG;
+  for (int i = 0; i < s->n_order; ++i) {
+    const int op = s->order[i];
+    if (op < GR_PEN_REPETITION || op > GR_PEN_MIN_NEW_TOKENS) return GR_ERR_ARG;
+    if ((op == GR_PEN_REPETITION && (!s->repetition || !s->st_rep)) ||
+        (op == GR_PEN_FREQUENCY && (!s->frequency || !s->st_freq)) ||
+        (op == GR_PEN_PRESENCE && (!s->presence || !s->st_pres)) ||
+        (op == GR_PEN_MIN_NEW_TOKENS && (!s->min_new_tokens || !s->st_len || (s->n_stop > 0 && !s->stop_ids))))
+      return GR_ERR_ARG;
+  }
+  return GR_OK;
+}
+
+int gr_gather_rows(const void* src, int row_bytes, int n, int src_stride_rows, void* dst, void* stream) {
+  if (!src || !dst || n <= 0 || row_bytes <= 0 || row_bytes % 16 || src_stride_rows < 1) return GR_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) return GR_ERR_ARG;
+  return launch_gather_rows(src, row_bytes, n, src_stride_rows, dst, static_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? GR_OK
+             : GR_ERR_CUDA;
+}
+
+int gr_logits_process(float* logits, int bs, int K, const int32_t* cand, const gr_sampling* s, void* stream) {
+  int rc = check_sampling(s);
+  if (rc) return rc;
+  if (!logits || bs <= 0 || K <= 0 || (K > 1 && !cand) || K > 64) return GR_ERR_ARG;
+  SampleParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.s = *s;
+  p.logits = logits;
+  p.bs = bs;
+  p.K = K;
+  p.cand = cand;
+  return launch_logits_process(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
+}
+
+int gr_sample_rows(float* logits, int bs, int K, const int32_t* cand, const gr_sampling* s, int first_kind,
+                   int32_t* accept, int32_t* sample, float* p_next, int32_t* first_out, int first_stride,
+                   int32_t* status, void* stream) {
+  int rc = check_sampling(s);
+  if (rc) return rc;
+  if (!logits || bs <= 0 || K <= 0 || !sample || (K > 1 && (!cand || !accept)) || K > 64) return GR_ERR_ARG;
+  if (first_kind != GR_COIN_FIRST && first_kind != GR_COIN_PREFILL) return GR_ERR_ARG;
+  if (!s->temperature || !s->top_k || !s->top_p || !s->min_p) return GR_ERR_ARG;
+  SampleParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.s = *s;
+  p.logits = logits;
+  p.bs = bs;
+  p.K = K;
+  p.cand = cand;
+  p.first_kind = first_kind;
+  p.accept = accept;
+  p.sample = sample;
+  p.p_next = p_next;
+  p.first_out = first_out;
+  p.first_stride = first_stride;
+  p.status = status;
+  return launch_sample_rows(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
+}
+
+int gr_penalty_cumulate(int bs, const int32_t* tokens, int stride, const int32_t* counts, int add,
+                        const gr_sampling* s, void* stream) {
+  int rc = check_sampling(s);
+  if (rc) return rc;
+  if (bs <= 0 || !tokens || stride <= 0) return GR_ERR_ARG;
+  SampleParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.s = *s;
+  p.bs = bs;
+  p.tokens = tokens;
+  p.tok_stride = stride;
+  p.counts = counts;
+  p.add = add;
+  return launch_penalty_cumulate(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
 }
 
 int gr_draft_override(int bs, int K, int32_t* am, const int32_t* g, int g_stride, const int32_t* n_committed,

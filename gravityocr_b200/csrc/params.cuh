@@ -91,6 +91,28 @@ struct CommitParams {
   int32_t* n_committed;
   int32_t* rounds;
   int32_t* accept_len;
+  // sampled verify (accept != NULL): acc from the per-row accept bits, v[acc] = sample[acc], written to predict
+  const int32_t* accept;
+  const int32_t* sample;
+  int32_t* predict;
+  uint64_t* rng;
+};
+struct SampleParams {
+  gr_sampling s;
+  float* logits;
+  int bs, K;
+  const int32_t* cand;
+  int first_kind;
+  int32_t* accept;
+  int32_t* sample;
+  float* p_next;
+  int32_t* first_out;
+  int first_stride;
+  int32_t* status;
+  const int32_t* tokens;   // penalty cumulation
+  int tok_stride;
+  const int32_t* counts;
+  int add;
 };
 struct OverrideParams {
   int bs, K, g_stride, plan_stride, vocab, mask_id;
@@ -155,6 +177,10 @@ cudaError_t launch_embed_rows(const EmbedParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_residual_norm(const ResNormParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_accept_commit(const CommitParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_draft_override(const OverrideParams& p, cudaStream_t s, bool pdl);
+cudaError_t launch_gather_rows(const void* src, int row_bytes, int n, int src_stride_rows, void* dst, cudaStream_t s);
+cudaError_t launch_logits_process(const SampleParams& p, cudaStream_t s);
+cudaError_t launch_sample_rows(const SampleParams& p, cudaStream_t s);
+cudaError_t launch_penalty_cumulate(const SampleParams& p, cudaStream_t s);
 cudaError_t launch_pack_gate_up(const __nv_bfloat16* src, __nv_bfloat16* dst, int I, int H, cudaStream_t s);
 
 }  // namespace gr

@@ -138,9 +138,14 @@ __global__ void __launch_bounds__(kCommitThreads) accept_commit_kernel(const Com
     const bool act = b < p.bs;
     int acc = 0;
     if (act) {
-      const int32_t* d = p.am + (size_t)b * K;
-      const int32_t* v = p.v + (size_t)b * K;
-      while (acc + 1 < K && d[acc + 1] == v[acc]) ++acc;
+      if (p.accept) {  // sampled verify: row j's bit says whether d_{j+1} was accepted
+        const int32_t* a = p.accept + (size_t)b * K;
+        while (acc + 1 < K && a[acc] != 0) ++acc;
+      } else {  // greedy verify: d_{j+1} equals the argmax of row j
+        const int32_t* d = p.am + (size_t)b * K;
+        const int32_t* v = p.v + (size_t)b * K;
+        while (acc + 1 < K && d[acc + 1] == v[acc]) ++acc;
+      }
     }
     const int rej = act ? (K - 1 - acc) : 0;
     // block-wide exclusive scan of the rejected counts
@@ -157,12 +162,20 @@ __global__ void __launch_bounds__(kCommitThreads) accept_commit_kernel(const Com
     const int excl = before + x - rej;
     if (act) {
       const int32_t* d = p.am + (size_t)b * K;
-      const int32_t* v = p.v + (size_t)b * K;
+      // verified token j: the verify argmax, or for a sampled verify the accepted draft / the final draw
+      auto vtok = [&](int j) -> int32_t {
+        if (!p.accept) return p.v[(size_t)b * K + j];
+        return j < acc ? d[j + 1] : p.sample[(size_t)b * K + acc];
+      };
       int32_t* row = p.packed + (size_t)b * (K + 2);
       row[0] = d[0];
       row[1] = acc;
-      for (int j = 0; j < K; ++j) row[2 + j] = (j <= acc) ? v[j] : 0;
-      const int64_t seed = v[acc];
+      for (int j = 0; j < K; ++j) {
+        const int32_t t = (j <= acc) ? vtok(j) : 0;
+        row[2 + j] = t;
+        if (p.predict) p.predict[(size_t)b * K + j] = t;
+      }
+      const int64_t seed = vtok(acc);
       p.seeds[p.rpi[b]] = seed;
       p.out_next[b] = seed;
       const int64_t s = p.seq_lens[b];
@@ -179,6 +192,7 @@ __global__ void __launch_bounds__(kCommitThreads) accept_commit_kernel(const Com
     __syncthreads();
   }
   if (threadIdx.x == 0 && p.n_released) p.n_released[0] = carry;
+  if (threadIdx.x == 0 && p.rng) p.rng[1] += 1;  // the next round draws fresh coins
 }
 
 // ------------------------------------------------------------------ forced-accept replay

@@ -1,0 +1,451 @@
+// Non-greedy rounds on sm_100a: the logits processing AR decode applies to every row (penalizers, grammar mask, logit
+// bias), AR's target distribution (softmax at the request's temperature, then top-k / top-p / min-p), the speculative
+// accept test of each verify row and the draws, and the penalizer cumulation of committed tokens.  There is no
+// contraction here: every kernel streams fp32 logits rows (237 KB at the baseline vocabulary) from HBM / L2.
+//
+// Arithmetic that decides tokens is exact and order-independent: probability mass is summed in 2^-40 fixed point
+// (uint64; e = exp(x - max) <= 1, so a row's total stays below 2^56), the keep threshold of the filters is found by a
+// four-pass 8-bit radix select over the IEEE bits of e (non-negative floats order like their bits), and draws invert
+// the fixed-point CDF in vocabulary order.  Coins come from Philox-4x32-10 keyed by the round's seed.
+#include "params.cuh"
+
+namespace gr {
+
+constexpr int kProcChunk = 2048;   // logits_process: vocabulary entries per CTA
+constexpr int kProcThreads = 256;
+constexpr int kSampThreads = 1024; // sample_rows: one CTA per row
+constexpr int kSampWarps = kSampThreads / 32;
+
+// ---------------------------------------------------------------- Philox-4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11)
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
+#pragma unroll
+  for (int i = 0; i < 10; ++i) {
+    const uint32_t lo0 = 0xD2511F53u * c.x, hi0 = __umulhi(0xD2511F53u, c.x);
+    const uint32_t lo1 = 0xCD9E8D57u * c.z, hi1 = __umulhi(0xCD9E8D57u, c.z);
+    c = make_uint4(hi1 ^ c.y ^ k.x, lo1, hi0 ^ c.w ^ k.y, lo0);
+    k.x += 0x9E3779B9u;
+    k.y += 0xBB67AE85u;
+  }
+  return c;
+}
+// uniform in (0, 1]: ((x >> 8) + 1) * 2^-24, exact in fp32
+__device__ __forceinline__ float coin(const uint64_t* rng, int b, int j, int kind) {
+  const uint64_t seed = rng[0];
+  const uint4 x = philox4x32_10(make_uint4(static_cast<uint32_t>(rng[1]), static_cast<uint32_t>(b),
+                                           (static_cast<uint32_t>(j) & 0xFFFFFFu) | (static_cast<uint32_t>(kind) << 24), 0u),
+                                make_uint2(static_cast<uint32_t>(seed), static_cast<uint32_t>(seed >> 32)));
+  return static_cast<float>((x.x >> 8) + 1u) * 5.9604644775390625e-08f;
+}
+
+__device__ __forceinline__ uint64_t fixed40(float e) { return __float2ull_rn(e * 1099511627776.0f); }
+
+__device__ __forceinline__ void set_status(int32_t* st, int code) {
+  if (st) atomicCAS(st, 0, code);
+}
+
+// ---------------------------------------------------------------- logits processing
+// Grid (chunks, rows).  Row r = b * K + j sees the request's penalizer state plus the verify ids cand[b, 1..j]; the
+// ops run in the orchestrator's order with the same IEEE operations as SGLang's penalizers (repetition: l < 0 ? l * S
+// : l / S; presence / frequency: l - S; min_new_tokens: stop ids -> -inf), then the grammar mask and the bias.
+__global__ void __launch_bounds__(kProcThreads) logits_process_kernel(const SampleParams p) {
+  __shared__ uint32_t bits[kProcChunk / 32];
+  __shared__ int blk[64];
+  const gr_sampling& s = p.s;
+  const int V = s.vocab;
+  const int r = blockIdx.y;
+  const int b = r / p.K, j = r % p.K;
+  const int v0 = blockIdx.x * kProcChunk;
+  const int v1 = min(V, v0 + kProcChunk);
+  const int n_blk = p.cand ? j : 0;
+  for (int i = threadIdx.x; i < kProcChunk / 32; i += blockDim.x) bits[i] = 0u;
+  __syncthreads();
+  if (threadIdx.x < n_blk) {
+    const int t = p.cand[(size_t)b * p.K + 1 + threadIdx.x];
+    blk[threadIdx.x] = t;
+    if (t >= v0 && t < v1) atomicOr(&bits[(t - v0) >> 5], 1u << ((t - v0) & 31));
+  }
+  __syncthreads();
+  const int64_t slot = s.req_pool_idx[b];
+  const float rep = s.repetition ? s.repetition[b] : 1.f;
+  const float freq = s.frequency ? s.frequency[b] : 0.f;
+  const float pres = s.presence ? s.presence[b] : 0.f;
+  bool stop_on = false;
+  for (int o = 0; o < s.n_order; ++o)
+    if (s.order[o] == GR_PEN_MIN_NEW_TOKENS) stop_on = s.st_len[slot] + j < s.min_new_tokens[b];
+  const int words = (V + 31) >> 5;
+  float* row = p.logits + (size_t)r * V;
+  for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
+    float l = row[v];
+    int c = 0;
+    if ((bits[(v - v0) >> 5] >> ((v - v0) & 31)) & 1u)
+      for (int i = 0; i < n_blk; ++i) c += blk[i] == v;
+    const size_t sv = (size_t)slot * V + v;
+    for (int o = 0; o < s.n_order; ++o) {
+      const int op = s.order[o];
+      if (op == GR_PEN_REPETITION) {
+        if (rep != 1.f) {
+          const float S = c ? rep : s.st_rep[sv];
+          l = l < 0.f ? l * S : l / S;
+        }
+      } else if (op == GR_PEN_PRESENCE) {
+        if (pres != 0.f) l = l - (c ? pres : s.st_pres[sv]);
+      } else if (op == GR_PEN_FREQUENCY) {
+        if (freq != 0.f) {
+          float S = s.st_freq[sv];
+          for (int i = 0; i < c; ++i) S = S + freq;
+          l = l - S;
+        }
+      } else if (stop_on) {
+        for (int i = 0; i < s.n_stop; ++i)
+          if (s.stop_ids[(size_t)b * s.n_stop + i] == v) l = -INFINITY;
+      }
+    }
+    if (s.allowed && !((s.allowed[(size_t)r * words + (v >> 5)] >> (v & 31)) & 1u)) l = -INFINITY;
+    if (s.logit_bias) l = l + s.logit_bias[(size_t)b * V + v];
+    row[v] = l;
+  }
+}
+
+// ---------------------------------------------------------------- block reductions (1024 threads)
+__device__ __forceinline__ float block_max(float v, float* sh) {
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = l < kSampWarps ? sh[l] : -INFINITY;
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (l == 0) sh[0] = v;
+  }
+  __syncthreads();
+  v = sh[0];
+  __syncthreads();
+  return v;
+}
+__device__ __forceinline__ unsigned long long warp_sum64(unsigned long long v) {
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ unsigned long long block_sum64(unsigned long long v, unsigned long long* sh) {
+  v = warp_sum64(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = l < kSampWarps ? sh[l] : 0ull;
+    v = warp_sum64(v);
+    if (l == 0) sh[0] = v;
+  }
+  __syncthreads();
+  v = sh[0];
+  __syncthreads();
+  return v;
+}
+
+// ---------------------------------------------------------------- keep threshold (radix select)
+// Keep set of the filters: {x : #{y > x} < k and sum{y > x} < lim} (strict) or "<= lim" (non-strict), a prefix of the
+// descending order.  Returns the smallest bit pattern tau such that "bits(e) >= tau" is exactly that set.  Four passes
+// of 8 bits over the row (histograms of count and fixed-point mass per bucket, warp-aggregated shared atomics), each
+// followed by a warp scan of the 256 buckets from the top.
+struct SelectSmem {
+  uint32_t hc[256];
+  unsigned long long hs[256];
+  uint32_t prefix, tau, done;
+  unsigned long long c_above, s_above;
+};
+__device__ uint32_t select_threshold(const float* row, int V, long long k, double lim, bool strict, SelectSmem& sm) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    sm.prefix = 0;
+    sm.tau = 0;
+    sm.done = 0;
+    sm.c_above = 0;
+    sm.s_above = 0;
+  }
+  __syncthreads();
+  for (int level = 0; level < 4; ++level) {
+    const int shift = 24 - 8 * level;
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+      sm.hc[i] = 0;
+      sm.hs[i] = 0;
+    }
+    __syncthreads();
+    const uint32_t prefix = sm.prefix;
+    for (int v0 = 0; v0 < V; v0 += blockDim.x) {
+      const int v = v0 + threadIdx.x;
+      const float e = v < V ? row[v] : 0.f;
+      const uint32_t ub = __float_as_uint(e);
+      const bool match = v < V && e > 0.f && (level == 0 || (ub >> (shift + 8)) == prefix);
+      const uint32_t bin = (ub >> shift) & 255u;
+      // lanes of one bucket add up their count and mass (20-bit halves of the <= 2^40 fixed-point values, so the
+      // 32-lane sums fit 32 bits), and one of them updates the shared histogram
+      const unsigned mm = __match_any_sync(0xffffffffu, match ? bin : 256u + lane);
+      const uint64_t w = match ? fixed40(e) : 0ull;
+      const uint32_t lo = __reduce_add_sync(mm, static_cast<uint32_t>(w & 0xFFFFFu));
+      const uint32_t hi = __reduce_add_sync(mm, static_cast<uint32_t>(w >> 20));
+      if (match && lane == __ffs(mm) - 1) {
+        atomicAdd(&sm.hc[bin], static_cast<uint32_t>(__popc(mm)));
+        atomicAdd(&sm.hs[bin], (static_cast<unsigned long long>(hi) << 20) + lo);
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // lane t holds buckets 255 - 8t .. 248 - 8t (descending); inclusive scans from the top
+      uint32_t c[8];
+      unsigned long long sm8[8];
+      uint32_t ct = 0;
+      unsigned long long st = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int d = 255 - 8 * lane - i;
+        ct += sm.hc[d];
+        st += sm.hs[d];
+        c[i] = ct;
+        sm8[i] = st;
+      }
+      uint32_t cx = ct;
+      unsigned long long sx = st;
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t cy = __shfl_up_sync(0xffffffffu, cx, o);
+        const unsigned long long sy = __shfl_up_sync(0xffffffffu, sx, o);
+        if (lane >= o) {
+          cx += cy;
+          sx += sy;
+        }
+      }
+      const uint32_t c_before = cx - ct;            // buckets above this lane's eight
+      const unsigned long long s_before = sx - st;
+      const unsigned long long CA = sm.c_above, SA = sm.s_above;
+      // first bucket (from the top) whose inclusion breaks the criterion for the entries below it
+      int fail = -1;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const long long cc = static_cast<long long>(CA + c_before + c[i]);
+        const double ss = static_cast<double>(SA + s_before + sm8[i]);
+        const bool ok = cc < k && (strict ? ss < lim : ss <= lim);
+        if (!ok && fail < 0) fail = i;
+      }
+      const unsigned ball = __ballot_sync(0xffffffffu, fail >= 0);
+      if (ball == 0u) {
+        // every bucket of this level is kept entirely: the set reaches below the prefix range
+        if (lane == 0) {
+          sm.tau = level == 0 ? 0u : (prefix << (shift + 8));
+          sm.done = 1;
+        }
+      } else {
+        const int src = __ffs(ball) - 1;
+        if (lane == src) {
+          const int d = 255 - 8 * lane - fail;
+          const uint32_t c_ex = c_before + (fail ? c[fail - 1] : 0u);
+          const unsigned long long s_ex = s_before + (fail ? sm8[fail - 1] : 0ull);
+          const unsigned long long c_top = CA + c_ex, s_top = SA + s_ex;
+          const bool top_kept = static_cast<long long>(c_top) < k &&
+                                (strict ? static_cast<double>(s_top) < lim : static_cast<double>(s_top) <= lim);
+          const uint32_t here = (prefix << 8) | static_cast<uint32_t>(d);
+          if (!top_kept) {
+            // nothing of bucket d is kept: the set ends just above it
+            sm.tau = (here + 1u) << shift;
+            sm.done = 1;
+          } else if (level == 3) {
+            sm.tau = here;  // one value (tied entries): kept together
+            sm.done = 1;
+          } else {
+            sm.prefix = here;
+            sm.c_above = c_top;
+            sm.s_above = s_top;
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (sm.done) break;
+  }
+  const uint32_t t = sm.tau;
+  __syncthreads();
+  return t;
+}
+
+// ---------------------------------------------------------------- target distribution, accept test, draws
+__global__ void __launch_bounds__(kSampThreads, 1) sample_rows_kernel(const SampleParams p) {
+  __shared__ float shf[kSampWarps];
+  __shared__ unsigned long long shu[kSampWarps];
+  __shared__ SelectSmem sel;
+  __shared__ unsigned long long scan[kSampWarps];
+  __shared__ int found;
+  const gr_sampling& s = p.s;
+  const int V = s.vocab;
+  const int r = blockIdx.x;
+  const int b = r / p.K, j = r % p.K;
+  float* row = p.logits + (size_t)r * V;
+  const float T = s.temperature[b];
+  const long long k = s.top_k[b];
+  const float P = s.top_p[b];
+  const float mp = s.min_p[b];
+  // pass 1: x = l / T and the row maximum
+  float mx = -INFINITY;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) {
+    const float x = row[v] / T;
+    row[v] = x;
+    mx = fmaxf(mx, x);
+  }
+  const float m = block_max(mx, shf);
+  const int d = (p.K > 1 && j + 1 < p.K) ? p.cand[(size_t)b * p.K + j + 1] : -1;
+  if (!(m > -INFINITY)) {  // every token masked
+    if (threadIdx.x == 0) {
+      set_status(p.status, GR_ERR_NO_TOKEN);
+      p.sample[r] = 0;
+      if (p.accept) p.accept[r] = 0;
+      if (p.p_next) p.p_next[r] = 0.f;
+      if (p.first_out) p.first_out[(size_t)b * p.first_stride] = 0;
+    }
+    return;
+  }
+  // pass 2: e = exp(x - max) (the maximum maps to exactly 1) and the fixed-point total
+  uint64_t z = 0;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) {
+    const float e = expf(row[v] - m);
+    row[v] = e;
+    z += fixed40(e);
+  }
+  const uint64_t Z = block_sum64(z, shu);
+  // keep threshold of the filters
+  uint32_t tau = 0;
+  const bool want_k = k < V, want_p = P < 1.f;
+  if (k <= 1) {
+    tau = __float_as_uint(1.0f);  // the maximum's tie group
+  } else if (s.filter == GR_FILTER_JOINT) {
+    if (want_k || want_p)
+      tau = select_threshold(row, V, want_k ? k : (1ll << 62), want_p ? static_cast<double>(P) * Z : 1e300, true, sel);
+  } else if (s.filter == GR_FILTER_TORCH) {
+    if (want_k || want_p)
+      tau = select_threshold(row, V, want_k ? k : (1ll << 62), want_p ? static_cast<double>(P) * Z : 1e300, false, sel);
+    if (mp > 0.f) tau = max(tau, __float_as_uint(mp));
+  } else {  // sequential: top-k renorm, then top-p on the renormalised mass, then min-p
+    uint32_t t1 = 0;
+    if (want_k) t1 = select_threshold(row, V, k, 1e300, true, sel);
+    if (want_p) {
+      uint64_t zk = 0;
+      for (int v = threadIdx.x; v < V; v += blockDim.x) {
+        const float e = row[v];
+        if (__float_as_uint(e) >= t1 && e > 0.f) zk += fixed40(e);
+      }
+      const uint64_t Zk = block_sum64(zk, shu);
+      const uint32_t t2 = select_threshold(row, V, 1ll << 62, static_cast<double>(P) * Zk, true, sel);
+      t1 = max(t1, t2);
+    }
+    tau = t1;
+    if (mp > 0.f) tau = max(tau, __float_as_uint(mp));
+  }
+  // draw pass: each thread sums the kept mass of a contiguous slice (vocabulary order), then an exclusive block scan
+  const int per = (V + kSampThreads - 1) / kSampThreads;
+  const int lo = threadIdx.x * per, hi = min(V, lo + per);
+  uint64_t loc = 0, w_d = 0;
+  for (int v = lo; v < hi; ++v) {
+    const float e = row[v];
+    if (e > 0.f && __float_as_uint(e) >= tau) {
+      const uint64_t w = fixed40(e);
+      loc += w;
+      if (v == d) w_d = w;
+    }
+  }
+  const uint64_t W = block_sum64(loc, shu);
+  // w_d reached every thread through the owner's slice: broadcast it
+  if (d >= 0 && d >= lo && d < hi) shu[0] = w_d;
+  __syncthreads();
+  const uint64_t wd = d >= 0 ? static_cast<uint64_t>(shu[0]) : 0ull;
+  __syncthreads();
+  const bool exclude = d >= 0;
+  const uint64_t mine = loc - ((exclude && d >= lo && d < hi) ? wd : 0ull);
+  // exclusive scan of `mine` over the block (thread order = vocabulary order)
+  uint64_t x = mine;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint64_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) scan[warp] = x;
+  if (threadIdx.x == 0) found = -1;
+  __syncthreads();
+  uint64_t before = 0;
+  for (int i = 0; i < warp; ++i) before += scan[i];
+  before += x - mine;
+  const uint64_t Wx = W - (exclude ? wd : 0ull);
+  const float cf = p.K == 1 ? coin(s.rng, b, 0, p.first_kind) : coin(s.rng, b, 0, GR_COIN_FINAL);
+  uint64_t target = static_cast<uint64_t>(static_cast<double>(cf) * static_cast<double>(Wx));
+  if (Wx > 0 && target >= Wx) target = Wx - 1;
+  if (Wx > 0 && mine > 0 && target >= before && target < before + mine) {
+    uint64_t c = before;
+    for (int v = lo; v < hi; ++v) {
+      const float e = row[v];
+      if (e > 0.f && __float_as_uint(e) >= tau && v != (exclude ? d : -1)) {
+        c += fixed40(e);
+        if (c > target) {
+          found = v;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int smp = found;
+    if (smp < 0) smp = d >= 0 ? d : 0;  // no mass outside d (d held everything kept): never used, d is accepted
+    p.sample[r] = smp;
+    if (p.first_out) p.first_out[(size_t)b * p.first_stride] = smp;
+    if (p.K > 1) {
+      const float ca = coin(s.rng, b, j, GR_COIN_ACCEPT);
+      const bool acc = d >= 0 && W > 0 && static_cast<double>(ca) * static_cast<double>(W) <= static_cast<double>(wd);
+      p.accept[r] = acc ? 1 : 0;
+    }
+    if (p.p_next) p.p_next[r] = (d >= 0 && W > 0) ? static_cast<float>(static_cast<double>(wd) / static_cast<double>(W)) : 0.f;
+  }
+}
+
+// ---------------------------------------------------------------- penalizer cumulation
+__global__ void penalty_cumulate_kernel(const SampleParams p) {
+  const gr_sampling& s = p.s;
+  const int b = blockIdx.x;
+  const int n = (p.counts ? p.counts[b] : 0) + p.add;
+  const int64_t slot = s.req_pool_idx[b];
+  const int V = s.vocab;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int t = p.tokens[(size_t)b * p.tok_stride + i];
+    if (t < 0 || t >= V) continue;
+    const size_t sv = (size_t)slot * V + t;
+    for (int o = 0; o < s.n_order; ++o) {
+      const int op = s.order[o];
+      if (op == GR_PEN_REPETITION) s.st_rep[sv] = s.repetition[b];
+      else if (op == GR_PEN_PRESENCE) s.st_pres[sv] = s.presence[b];
+      else if (op == GR_PEN_FREQUENCY) atomicAdd(&s.st_freq[sv], s.frequency[b]);  // one addend value: order-free
+    }
+  }
+  if (threadIdx.x == 0 && s.st_len) s.st_len[slot] += n;
+}
+
+__global__ void gather_rows_kernel(const uint4* src, int words, int stride_rows, uint4* dst) {
+  const int i = blockIdx.x;
+  for (int w = threadIdx.x; w < words; w += blockDim.x)
+    dst[(size_t)i * words + w] = src[(size_t)i * stride_rows * words + w];
+}
+
+// ---------------------------------------------------------------- launchers
+cudaError_t launch_gather_rows(const void* src, int row_bytes, int n, int src_stride_rows, void* dst, cudaStream_t s) {
+  gather_rows_kernel<<<n, 128, 0, s>>>(static_cast<const uint4*>(src), row_bytes / 16, src_stride_rows,
+                                       static_cast<uint4*>(dst));
+  return cudaGetLastError();
+}
+cudaError_t launch_logits_process(const SampleParams& p, cudaStream_t s) {
+  const dim3 grid((p.s.vocab + kProcChunk - 1) / kProcChunk, p.bs * p.K);
+  logits_process_kernel<<<grid, kProcThreads, 0, s>>>(p);
+  return cudaGetLastError();
+}
+cudaError_t launch_sample_rows(const SampleParams& p, cudaStream_t s) {
+  sample_rows_kernel<<<p.bs * p.K, kSampThreads, 0, s>>>(p);
+  return cudaGetLastError();
+}
+cudaError_t launch_penalty_cumulate(const SampleParams& p, cudaStream_t s) {
+  penalty_cumulate_kernel<<<p.bs, 64, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace gr

@@ -325,11 +325,12 @@ class Engine:
             attn_chunk=chunk, attn_splits=splits)
 
     def prefill(self, rb: RoundBuffers, prefixes: List[torch.Tensor], prefix_ids: List[torch.Tensor],
-                chunk: int = 64, attn_chunk: Optional[int] = None) -> List[int]:
+                chunk: int = 64, attn_chunk: Optional[int] = None, first_fn=None) -> List[int]:
         """Causal prefill of each request's prefix through the same kernels (chunks of ``chunk`` rows, causal
         attention).  prefixes[b]: fp32 [P_b, H] layer-0 input rows (image embeddings + prompt embeddings);
         prefix_ids[b]: int64 [P_b] ids (< 0 where the row comes from ``prefixes``).  Sets seq_lens = P_b, the seed
-        pool (seeds[rpi[b]] = first generated token), n_committed = 1.  Returns the first tokens."""
+        pool (seeds[rpi[b]] = first generated token), n_committed = 1.  Returns the first tokens: the argmax of the
+        last prefix row, or first_fn(rows [n, H] bf16, request indices) for a batch that samples."""
         bs = rb.bs
         dev = self.device
         lens = [int(p.shape[0]) for p in prefixes]
@@ -365,11 +366,14 @@ class Engine:
                     if c * chunk <= lens[b] - 1 < (c + 1) * chunk]
             if ends:
                 rows = self.x[torch.tensor([r for _, r in ends], device=dev)].contiguous()
-                e = L.Epilogue()
-                e.mode = L.EPI_ARGMAX
-                e.out_idx = out_idx.data_ptr()
-                L.linear(self.w.lm_head, rows, len(ends), e, self.lin_ws, status=rb.status)
-                res = out_idx[: len(ends)].cpu()
+                if first_fn is not None:
+                    res = first_fn(rows, [b for b, _ in ends]).cpu()
+                else:
+                    e = L.Epilogue()
+                    e.mode = L.EPI_ARGMAX
+                    e.out_idx = out_idx.data_ptr()
+                    L.linear(self.w.lm_head, rows, len(ends), e, self.lin_ws, status=rb.status)
+                    res = out_idx[: len(ends)].cpu()
                 for k, (b, _) in enumerate(ends):
                     first[b] = int(res[k])
         rb.seq_lens.copy_(torch.tensor(lens, dtype=torch.int64))

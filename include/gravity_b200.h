@@ -27,7 +27,8 @@ enum gr_status_code {
   GR_ERR_BAD_ID = 5,      /* device: a token id outside [0, vocab) */
   GR_ERR_BAD_PAGE = 6,    /* device: a position beyond the request's page-table capacity */
   GR_ERR_UNSUPPORTED = 7, /* the build does not support this configuration */
-  GR_ERR_SCRATCH_LIMIT = 8 /* the call needs more scratch than gr_bd_attention_noalloc's fixed array holds */
+  GR_ERR_SCRATCH_LIMIT = 8, /* the call needs more scratch than gr_bd_attention_noalloc's fixed array holds */
+  GR_ERR_NO_TOKEN = 9       /* device: a sampled row allowed no token (every logit -inf after masks and penalties) */
 };
 
 /* Epilogues of gr_linear. */
@@ -177,6 +178,85 @@ int gr_draft_override(int bs, int K, int32_t* am, const int32_t* g, int g_stride
 /* Load-time helper: reorder gate_up rows [gate(I) | up(I)] so that row 2j is gate j and row 2j+1 is up j (the layout
  * GR_EPI_SWIGLU expects).  src/dst: bf16 [2*I, H] device buffers. */
 int gr_pack_gate_up(const void* src, void* dst, int intermediate, int hidden, void* stream);
+
+/* ------------------------------------------------------------------ non-greedy rounds (sampling, penalties, grammar)
+ * A batch with any sampled request, penalty, logit bias or grammar takes this path instead of the argmax epilogue:
+ * lm_head writes fp32 logits (gr_linear with GR_EPI_STORE_F32), gr_logits_process applies what AR decode applies to
+ * each row, gr_sample_rows draws / tests against AR's target distribution, and gr_commit_sampled commits.  The
+ * reference's counterparts: selfspec_sampling.py (penalize_rows, verify_target_probs, cumulate_block) and
+ * selfspec_fast_commit.py:150-230 (process_verify_logits, sampling_verify with sgl_kernel's
+ * tree_speculative_sampling_target_only), and the worker's a0 draw (selfspec_diffusion_worker.py:504-528). */
+enum gr_filter_mode {
+  GR_FILTER_JOINT = 0,      /* flashinfer backend without min-p: keep q iff #{p > p_q} < k and sum{p > p_q} < top_p */
+  GR_FILTER_SEQUENTIAL = 1, /* flashinfer backend with min-p: top-k renorm, then top-p renorm, then p >= min_p * max */
+  GR_FILTER_TORCH = 2       /* "pytorch" backend: #{p > p_q} < k, sum{p > p_q} <= top_p, p >= min_p * max */
+};
+enum gr_penalty_op { GR_PEN_REPETITION = 0, GR_PEN_FREQUENCY = 1, GR_PEN_PRESENCE = 2, GR_PEN_MIN_NEW_TOKENS = 3 };
+enum gr_coin_kind { GR_COIN_ACCEPT = 0, GR_COIN_FINAL = 1, GR_COIN_FIRST = 2, GR_COIN_PREFILL = 3 };
+
+/* Sampling parameters of a batch.  Per-request arrays are [bs] device arrays; NULL means the neutral value for every
+ * request.  The penalizer state is indexed by the request's pool slot, like the seed pool. */
+typedef struct gr_sampling {
+  int vocab;
+  int filter;                   /* gr_filter_mode */
+  const float* temperature;     /* > 0 (a greedy request has top_k = 1) */
+  const int32_t* top_k;         /* >= 1; >= vocab keeps every token */
+  const float* top_p;           /* (0, 1] */
+  const float* min_p;           /* [0, 1) */
+  int n_order;                  /* penalizers the batch uses, in the orchestrator's order (gr_penalty_op) */
+  int order[4];
+  const float* repetition;      /* 1 = off */
+  const float* frequency;       /* 0 = off */
+  const float* presence;        /* 0 = off */
+  const int32_t* min_new_tokens;
+  const int32_t* stop_ids;      /* [bs, n_stop] (-1 pads): masked while the output is shorter than min_new_tokens */
+  int n_stop;
+  float* st_rep;                /* [pool, vocab]: 1 where unseen, the repetition penalty where seen */
+  float* st_freq;               /* [pool, vocab]: the frequency penalty added once per occurrence */
+  float* st_pres;               /* [pool, vocab]: the presence penalty where seen */
+  int32_t* st_len;              /* [pool]: output tokens so far */
+  const int64_t* req_pool_idx;  /* [bs] */
+  const uint32_t* allowed;      /* grammar: [rows, ceil(vocab / 32)] allowed-token bits, or NULL */
+  const float* logit_bias;      /* [bs, vocab] or NULL */
+  uint64_t* rng;                /* [2] = seed, round; gr_commit_sampled advances the round */
+} gr_sampling;
+
+/* rows[i] = src[i * src_stride_rows] (row_bytes each, 16-byte multiples): the draft's boundary-token rows for their
+ * lm_head pass. */
+int gr_gather_rows(const void* src, int row_bytes, int n, int src_stride_rows, void* dst, void* stream);
+
+/* In place on logits [bs*K, vocab] fp32, row (b, j): the penalizers in s->order with the request's penalizer state
+ * plus the verify ids cand[b, 1..j] (cand [bs, K]; NULL with K = 1, the first-token rows), the min_new_tokens stop-id
+ * mask while st_len + j < min_new_tokens, the grammar mask (disallowed -> -inf), then logit_bias.
+ * Replaces selfspec_sampling.py penalize_rows (:120-170) and process_verify_logits (selfspec_fast_commit.py:170-195). */
+int gr_logits_process(float* logits, int bs, int K, const int32_t* cand, const gr_sampling* s, void* stream);
+
+/* AR's target distribution of each row (softmax(logits / T) filtered by s->filter; the row is overwritten with
+ * exp(x - max)), then: K = 1 (first-token rows): sample[b] = a draw with coin `first_kind` (GR_COIN_FIRST for a0,
+ * GR_COIN_PREFILL for the prefill's token), also written to first_out[b * first_stride] when given; K > 1 (verify
+ * rows, cand [bs, K] = [a0, d1..]): accept[r] = coin(ACCEPT, b, j) <= p_j(d_{j+1}) (0 on the last row),
+ * sample[r] = a draw from p_j without d_{j+1} with coin(FINAL, b), p_next[r] = p_j(d_{j+1}).  Coins are
+ * Philox-4x32-10 of (seed; round, b, j | kind << 24).
+ * Replaces verify_target_probs (selfspec_sampling.py:245-275), the sampler's a0 draw and the per-row half of
+ * tree_speculative_sampling_target_only (selfspec_fast_commit.py:197-230). */
+int gr_sample_rows(float* logits, int bs, int K, const int32_t* cand, const gr_sampling* s, int first_kind,
+                   int32_t* accept, int32_t* sample, float* p_next, int32_t* first_out, int first_stride,
+                   int32_t* status, void* stream);
+
+/* gr_accept_commit for a sampled verify: acc = the first row j < K-1 with accept == 0 (else K-1); the verified tokens
+ * are v[j] = am[j+1] for j < acc and v[acc] = sample[acc], written to predict [bs*K] (zeros past acc); then the same
+ * packed row, seed, seq_lens, released positions and counters as gr_accept_commit, and the round counter s->rng[1]
+ * advances.  The chain half of tree_speculative_sampling_target_only plus _ss_commit_kernel. */
+int gr_commit_sampled(int bs, int K, const int32_t* am, const int32_t* accept, const int32_t* sample, int64_t* seeds,
+                      const int64_t* req_pool_idx, int64_t* seq_lens, int32_t* predict, int32_t* packed,
+                      int64_t* released, int32_t* n_released, int64_t* out_next, int32_t* n_committed,
+                      int32_t* rounds, int32_t* accept_len, uint64_t* rng, void* stream);
+
+/* Penalizer cumulation of committed tokens: for request b the tokens[b * stride + i], i < (counts ? counts[b] + add
+ * : add); repetition / presence state set, frequency state increased by the penalty per occurrence, st_len advanced.
+ * Replaces selfspec_sampling.py cumulate_block (:60-100) and the worker's a0 cumulation (:523-527). */
+int gr_penalty_cumulate(int bs, const int32_t* tokens, int stride, const int32_t* counts, int add,
+                        const gr_sampling* s, void* stream);
 
 #ifdef __cplusplus
 }

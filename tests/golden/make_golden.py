@@ -14,6 +14,8 @@ Outputs (small JSON files next to this script):
   * ``commit_kernel.json``: the reference Triton ``_ss_commit_kernel`` (``selfspec_fast_commit.py:108-147``) executed
     by the Triton CPU interpreter on seeded inputs (its source is parsed out of the reference file at generation time).
   * ``commit_rules.json``: ``cut_index`` and ``host_commit`` of ``selfspec_commit_rules.py`` on seeded rows.
+  * ``sampling.json``: ``selfspec_sampling.py``'s penalties, penalizer cumulation and target distributions on seeded
+    small-vocabulary rows (the penalizers are stand-ins carrying SGLang's class names and state tensors).
 """
 from __future__ import annotations
 
@@ -246,11 +248,121 @@ def gen_commit_rules(ref: str):
                                 "cut_index": cut, "host_commit": hc})
 
 
+def gen_sampling(ref: str):
+    """The reference's selfspec_sampling.py (torch only) on seeded small-vocabulary inputs: penalize_rows with stand-in
+    penalizers carrying SGLang's class names and state tensors, cumulate_block, joint_top_k_top_p, torch_backend_filter,
+    min_p_filter and verify_target_probs."""
+    import torch
+    sys.path.insert(0, os.path.join(ref, "patches/sglang/python/sglang/srt/speculative"))
+    import selfspec_sampling as S
+    import base64
+    import numpy as np
+    g = torch.Generator().manual_seed(4242)
+    V, bs, K = 48, 3, 5
+
+    def b64(t):   # exact float32 values, compactly
+        return base64.b64encode(np.ascontiguousarray(t.detach().float().numpy(), dtype="<f4").tobytes()).decode()
+
+    def rnd(*shape):
+        return torch.randn(*shape, generator=g)
+
+    def mk(name, **attrs):
+        cls = type(name, (), {"is_prepared": lambda self: True})
+        o = cls()
+        for k, v in attrs.items():
+            setattr(o, k, v)
+        return o
+
+    def apply_scaling(logits, pen):   # SGLang's apply_scaling_penalties
+        logits[:] = torch.where(logits < 0, logits * pen, logits / pen)
+
+    out = {"V": V, "bs": bs, "K": K, "penalize": [], "filters": [], "target": []}
+    for case in range(4):
+        order = [["BatchedFrequencyPenalizer", "BatchedMinNewTokensPenalizer", "BatchedPresencePenalizer",
+                  "BatchedRepetitionPenalizer"], ["BatchedRepetitionPenalizer", "BatchedPresencePenalizer",
+                  "BatchedFrequencyPenalizer", "BatchedMinNewTokensPenalizer"]][case % 2]
+        rep_p = 1.0 + torch.rand(bs, 1, generator=g)
+        fre_p = torch.rand(bs, 1, generator=g)
+        pre_p = torch.rand(bs, 1, generator=g)
+        seen = torch.randint(0, V, (bs, 12), generator=g)
+        cum_rep = torch.ones(bs, V)
+        cum_rep.scatter_(1, seen, rep_p.expand(-1, 12))
+        cum_fre = torch.zeros(bs, V)
+        cum_fre.scatter_add_(1, seen, fre_p.expand(-1, 12).contiguous())
+        cum_pre = torch.zeros(bs, V)
+        cum_pre.scatter_(1, seen, pre_p.expand(-1, 12))
+        len_out = torch.randint(0, 6, (bs, 1), generator=g)
+        min_new = torch.randint(0, 8, (bs, 1), generator=g)
+        stop_ids = torch.randint(0, V, (bs, 2), generator=g)
+        stop_pen = torch.zeros(bs, V)
+        stop_pen.scatter_(1, stop_ids, float("-inf"))
+        pens = {
+            "BatchedRepetitionPenalizer": mk("BatchedRepetitionPenalizer", cumulated_repetition_penalties=cum_rep.clone(),
+                                             repetition_penalties=rep_p),
+            "BatchedFrequencyPenalizer": mk("BatchedFrequencyPenalizer", cumulated_frequency_penalties=cum_fre.clone(),
+                                            frequency_penalties=fre_p),
+            "BatchedPresencePenalizer": mk("BatchedPresencePenalizer", cumulated_presence_penalties=cum_pre.clone(),
+                                           presence_penalties=pre_p),
+            "BatchedMinNewTokensPenalizer": mk("BatchedMinNewTokensPenalizer", len_output_tokens=len_out.clone(),
+                                               min_new_tokens=min_new, stop_token_penalties=stop_pen),
+        }
+        orch = types.SimpleNamespace(is_required=True, penalizers={n: pens[n] for n in order})
+        cand = torch.randint(0, V, (bs, K), generator=g)
+        cand[:, 2] = cand[:, 1]                     # repeated in-block tokens
+        logits = rnd(bs * K, V) * 3
+        lg = logits.clone()
+        S.penalize_rows(orch, lg, cand, apply_scaling)
+        tok = torch.randint(0, V, (bs, 7), generator=g)
+        valid = torch.rand(bs, 7, generator=g) < 0.6
+        valid[0] = False
+        S.cumulate_block(orch, tok, valid)
+        out["penalize"].append({
+            "order": order, "rep": rep_p.view(-1).tolist(), "freq": fre_p.view(-1).tolist(),
+            "pres": pre_p.view(-1).tolist(), "seen": seen.tolist(), "len_out": len_out.view(-1).tolist(),
+            "min_new": min_new.view(-1).tolist(), "stop_ids": stop_ids.tolist(), "cand": cand.tolist(),
+            "logits": b64(logits), "out": b64(lg),
+            "cum_tok": tok.tolist(), "cum_valid": valid.tolist(),
+            "after": {"rep": b64(pens["BatchedRepetitionPenalizer"].cumulated_repetition_penalties),
+                      "freq": b64(pens["BatchedFrequencyPenalizer"].cumulated_frequency_penalties),
+                      "pres": b64(pens["BatchedPresencePenalizer"].cumulated_presence_penalties),
+                      "len_out": pens["BatchedMinNewTokensPenalizer"].len_output_tokens.view(-1).tolist()}})
+    for case in range(4):
+        rows = 6
+        # probabilities with tie groups (quantised logits)
+        lo = torch.round(rnd(rows, V) * 2) / 2
+        probs = torch.softmax(lo, dim=-1)
+        top_k = torch.tensor([1, 3, 8, V, 20, 1 << 30], dtype=torch.int64)[torch.randperm(6, generator=g)]
+        top_p = torch.tensor([0.3, 0.9, 1.0, 0.5, 0.99, 0.7])[torch.randperm(6, generator=g)]
+        min_p = torch.tensor([0.0, 0.05, 0.2, 0.0, 0.5, 0.1])[torch.randperm(6, generator=g)]
+        out["filters"].append({
+            "probs": b64(probs), "top_k": top_k.tolist(), "top_p": top_p.tolist(), "min_p": min_p.tolist(),
+            "joint": b64(S.joint_top_k_top_p(probs, top_k, top_p)),
+            "torch": b64(S.torch_backend_filter(probs, top_k, top_p, min_p, True)),
+            "torch_no_min_p": b64(S.torch_backend_filter(probs, top_k, top_p, min_p, False)),
+            "min_p_filtered": b64(S.min_p_filter(probs, min_p))})
+    for case in range(2):
+        lg = rnd(bs * K, V) * 2
+        si = types.SimpleNamespace(temperatures=(0.3 + torch.rand(bs, 1, generator=g)),
+                                   top_ks=torch.tensor([1, 5, 1 << 30], dtype=torch.int32),
+                                   top_ps=torch.tensor([1.0, 0.8, 0.6]), min_ps=torch.tensor([0.0, 0.1, 0.0]),
+                                   need_top_p_sampling=True, need_top_k_sampling=True, need_min_p_sampling=False)
+        fi = S.verify_target_probs(lg.clone(), si, K, "flashinfer")
+        si.need_min_p_sampling = True
+        pt = S.verify_target_probs(lg.clone(), si, K, "pytorch")
+        out["target"].append({"logits": b64(lg), "temperature": si.temperatures.view(-1).tolist(),
+                              "top_k": si.top_ks.tolist(), "top_p": si.top_ps.tolist(), "min_p": si.min_ps.tolist(),
+                              "flashinfer": b64(fi), "pytorch_min_p": b64(pt)})
+    _dump("sampling.json", {"source": "reference selfspec_sampling.py (penalize_rows, cumulate_block, "
+                                      "joint_top_k_top_p, torch_backend_filter, min_p_filter, verify_target_probs)",
+                            "encoding": "float tensors: base64 of little-endian float32, row-major", **out})
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("GRAVITYOCR_REF"),
                     help="path of the GravityOCR source tree (or set GRAVITYOCR_REF)")
-    ap.add_argument("--only", default="commit_kernel,commit_rules," + ",".join(f"natcache_{c}" for c in NATCACHE_CASES))
+    ap.add_argument("--only", default="commit_kernel,commit_rules,sampling," +
+                    ",".join(f"natcache_{c}" for c in NATCACHE_CASES))
     a = ap.parse_args()
     if not a.ref or not os.path.isdir(a.ref):
         ap.error("--ref (or GRAVITYOCR_REF) must name the GravityOCR source tree")
@@ -259,6 +371,8 @@ def main():
         gen_commit_rules(a.ref)
     if "commit_kernel" in only:
         gen_commit_kernel(a.ref)
+    if "sampling" in only:
+        gen_sampling(a.ref)
     for case in NATCACHE_CASES:
         if f"natcache_{case}" in only:
             gen_natcache(a.ref, case)
