@@ -421,7 +421,7 @@ def e2e_worker(eng, rb, cfg, K, steps, dev, warmup):
     pool.engine, pool.size, pool.pages_per_req = eng, bs, rb.page_table.shape[1]
     pool.table, pool.owned = rb.page_table.clone(), {}
     target = _t.SimpleNamespace(engine=eng, req_to_page=pool)
-    args = _t.SimpleNamespace(speculative_num_draft_tokens=K, page_size=16, model_path="")
+    args = _t.SimpleNamespace(speculative_num_draft_tokens=K, page_size=16, model_path="", ss_draft_ahead=True)
     os.environ["SELFSPEC_MASK_ID"] = str(cfg.mask_id)
     wk = SelfSpecDiffusionWorker(args, 0, 0, None, 0, 0, 0, 0, target)
     wk._seeds().copy_(rb.seeds)
@@ -452,7 +452,8 @@ def e2e_worker(eng, rb, cfg, K, steps, dev, warmup):
     final = (wrb.seq_lens.cpu().tolist(), wrb.seeds.cpu().tolist(), wrb.n_committed.cpu().tolist())
     return {"value": None, "unit": "tokens/s", "h2d_bytes_per_step": bs * 8,
             "d2h_bytes_per_step": int(rb.readback.numel() * 4), "steps": steps,
-            "api": "SelfSpecDiffusionWorker.forward_batch_generation", "tokens": toks, "ms": ms, "final": final}
+            "api": "SelfSpecDiffusionWorker.forward_batch_generation (draft-ahead on)",
+            "draft_ahead": dict(wk.ahead_stats), "tokens": toks, "ms": ms, "final": final}
 
 
 def bs1_crop(eng, cfg, w, K, dev, hbm_peak):

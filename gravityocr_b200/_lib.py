@@ -50,6 +50,8 @@ class Epilogue(ctypes.Structure):
         ("out_idx", ctypes.c_void_p),
         ("out_top1", ctypes.c_void_p),
         ("out_gap", ctypes.c_void_p),
+        ("row_pos3", ctypes.c_void_p),
+        ("mrope_section", ctypes.c_int * 3),
     ]
 
 
@@ -96,7 +98,7 @@ _SIGS = {
     "gr_linear_default_splits": (_I, [_I, _I, _I]),
     "gr_linear": (_I, [_P, _I, _I, _P, _I, ctypes.POINTER(Epilogue), _I, _P, _Z, _P, _Z, _P, _P]),
     "gr_embed_rows": (_I, [_I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _I, _I, _P, _F, _I, _P, _P, _P,
-                           _P, _P, _P, _P]),
+                           _P, _P, _P, _P, _P]),
     "gr_residual_norm": (_I, [_I, _I, _P, _P, _I, _P, _P, _F, _P, _P, _P]),
     "gr_bd_attention": (_I, [_P, _P, _P, _L, _P, _I, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _Z, _P, _P]),
     "gr_accept_commit": (_I, [_I, _I, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
@@ -199,12 +201,12 @@ def linear(w: torch.Tensor, x: torch.Tensor, m: int, epi: Epilogue, workspace: t
 
 def embed_rows(mode: int, bs: int, K: int, *, seeds=None, rpi=None, ids32=None, ids64=None, row_embeds=None,
                seq_lens, page_table, page_size: int, embed, vocab: int, mask_id: int, norm_w, eps: float,
-               h_out, x_out, row_pos, row_slot, row_ids=None, status=None, stream=None) -> None:
+               h_out, x_out, row_pos, row_slot, row_ids=None, rope_delta=None, status=None, stream=None) -> None:
     rc = load().gr_embed_rows(mode, bs, K, _ptr(seeds), _ptr(rpi), _ptr(ids32), _ptr(ids64), _ptr(row_embeds),
                               seq_lens.data_ptr(), page_table.data_ptr(), page_table.shape[1], page_size,
                               page_table.shape[1], embed.data_ptr(), vocab, mask_id, norm_w.data_ptr(), eps,
                               embed.shape[1], h_out.data_ptr(), x_out.data_ptr(), row_pos.data_ptr(),
-                              row_slot.data_ptr(), _ptr(row_ids), _ptr(status), _stream(stream))
+                              row_slot.data_ptr(), _ptr(row_ids), _ptr(rope_delta), _ptr(status), _stream(stream))
     _check(rc, "gr_embed_rows")
 
 

@@ -12,7 +12,9 @@ per round appended to ``trace`` with the reference's keys (``round``, ``k``, ``d
 ``SelfSpecModel`` around an ``Engine``.  For the reference model the decoder weights are copied once into an Engine on
 the model's GPU (``attach_engine``); the crop goes through the caller's own processor and vision tower
 (``get_image_features``, ``get_rope_index``, as ``:456-488`` does) and the image embeddings are injected at the
-image-token rows.  ``image`` may also be the image-embedding prefix itself (tensor [n_image, hidden]).
+image-token rows; 2-D multimodal positions of the image tokens go to the prefill's RoPE, and response token r sits at
+max position + 1 + r (``comb_pos``, :505-506).  ``image`` may also be the image-embedding prefix itself (tensor
+[n_image, hidden], or an object with ``.embeds`` and ``.positions``).
 
 The rounds are the reference's, on the CUDA path:
   * round 0 (no pending token): draft over B mask rows that all see each other (the draft mask of ``:508-510`` with
@@ -82,7 +84,8 @@ def _text_config(model) -> ModelConfig:
                        head_dim=head_dim, intermediate=int(tc.intermediate_size), vocab=int(tc.vocab_size),
                        rms_eps=float(tc.rms_norm_eps), rope_theta=float(rp.get("rope_theta", 10000.0)),
                        rotary_dim=int(head_dim * factor), mask_id=int(model.mask_id),
-                       image_token_id=int(model.image_token_id))
+                       image_token_id=int(model.image_token_id),
+                       mrope_section=tuple(int(x) for x in rp.get("mrope_section", (8, 12, 12))))
 
 
 def _text_weights(model) -> Dict[str, torch.Tensor]:
@@ -126,6 +129,8 @@ def _resolve(model) -> SelfSpecModel:
 
 # ---------------------------------------------------------------------- the prefix
 def _prefix_from_embeds(sm: SelfSpecModel, image, prompt):
+    """image: the image-embedding prefix [n_image, hidden], or an object with ``.embeds`` and optionally
+    ``.positions`` (int [3, n_image + n_prompt] multimodal positions of the whole prefix)."""
     eng = sm.engine
     img = getattr(image, "embeds", image)
     if img.dim() != 2 or img.shape[1] != eng.cfg.hidden:
@@ -138,7 +143,17 @@ def _prefix_from_embeds(sm: SelfSpecModel, image, prompt):
     emb = eng.w.embed[ids.to(eng.device)].float().cpu()
     x = torch.cat([img.float().cpu(), emb], dim=0)
     pid = torch.cat([torch.full((img.shape[0],), -1, dtype=torch.int64), ids])
-    return x, pid
+    pos = getattr(image, "positions", None)
+    return x, pid, (None if pos is None else _pos3_or_none(torch.as_tensor(pos), x.shape[0]))
+
+
+def _pos3_or_none(pos: torch.Tensor, P: int) -> Optional[torch.Tensor]:
+    """[3, P] multimodal positions, or None when they are the plain 0..P-1 on every axis."""
+    pos = pos.reshape(3, -1)[:, :P].to(torch.int64).cpu()
+    plain = torch.arange(P)
+    if all(torch.equal(pos[a], plain) for a in range(3)):
+        return None
+    return pos
 
 
 def _prefix_from_processor(model, sm: SelfSpecModel, image, prompt, max_long_side):
@@ -164,9 +179,7 @@ def _prefix_from_processor(model, sm: SelfSpecModel, image, prompt, max_long_sid
     pos, _ = model.mm_model.get_rope_index(input_ids, enc["mm_token_type_ids"], image_grid_thw=thw,
                                            video_grid_thw=None,
                                            attention_mask=torch.ones((1, P), dtype=torch.long, device=dev))
-    pos = pos.reshape(3, -1)[:, :P].to(torch.int64).cpu()
-    if not (torch.equal(pos[0], torch.arange(P)) and torch.equal(pos[1], pos[0]) and torch.equal(pos[2], pos[0])):
-        raise ValueError("2-D M-RoPE image positions are not on this path (1-D positions only)")
+    pos3 = _pos3_or_none(pos, P)
     img_rows = ids == sm.image_token_id
     x = eng.w.embed[ids.clamp(min=0).to(eng.device)].float().cpu()
     pid = ids.clone()
@@ -177,7 +190,7 @@ def _prefix_from_processor(model, sm: SelfSpecModel, image, prompt, max_long_sid
             raise ValueError(f"{emb.shape[0]} image embeddings for {int(img_rows.sum())} image tokens")
         x[img_rows] = emb
         pid[img_rows] = -1
-    return x, pid
+    return x, pid, pos3
 
 
 # ---------------------------------------------------------------------- the rounds
@@ -189,13 +202,14 @@ def _first_round(eng: Engine, rb, bd: int) -> None:
     cfg = eng.cfg
     rb.ids64[:bd].fill_(cfg.mask_id)
     eng.forward(L.ROWS_EXPLICIT, 1, bd, rb.seq_lens, rb.page_table, out_idx=rb.tmp_idx, ids64=rb.ids64[:bd],
-                attn_chunk=rb.attn_chunk, attn_splits=rb.attn_splits, status=rb.status, attn_draft=2)
+                attn_chunk=rb.attn_chunk, attn_splits=rb.attn_splits, status=rb.status, attn_draft=2,
+                rope_delta=rb.pos_delta)
     rb.am[0:1].copy_(rb.seeds[rb.rpi[0:1]])
     rb.am[1:K].copy_(rb.tmp_idx[:bd])
     rb.ids64.copy_(rb.am)
     eng.forward(L.ROWS_EXPLICIT, 1, K, rb.seq_lens, rb.page_table, out_idx=rb.v, out_top1=rb.top_v,
                 out_gap=rb.gap_v, ids64=rb.ids64, attn_chunk=rb.attn_chunk, attn_splits=rb.attn_splits,
-                status=rb.status, attn_draft=0)
+                status=rb.status, attn_draft=0, rope_delta=rb.pos_delta)
     L.accept_commit(1, K, rb.am, rb.v, rb.seeds, rb.rpi, rb.seq_lens, rb.packed, rb.released, rb.out_next,
                     x0_committed=True, n_released=rb.n_released, n_committed=rb.n_committed, rounds=rb.rounds,
                     accept_len=rb.accept_len)
@@ -226,14 +240,14 @@ def generate_speculative_natcache(model, image, prompt="Text Recognition:", max_
     bd = int(draft_bd) if draft_bd else int(getattr(model, "bd_size", sm.bd_size))
     K = bd + 1
     if torch.is_tensor(getattr(image, "embeds", image)):
-        x, pid = _prefix_from_embeds(sm, image, prompt)
+        x, pid, pos3 = _prefix_from_embeds(sm, image, prompt)
     else:
-        x, pid = _prefix_from_processor(model, sm, image, prompt, max_long_side)
+        x, pid, pos3 = _prefix_from_processor(model, sm, image, prompt, max_long_side)
     P = x.shape[0]
     max_len = P + max_new_tokens + 2 * K + 64
     pages = eng.pages_for(max_len)
     rb = sm.round_buffers(K, pages, max_len, P + max_new_tokens // 2)
-    eng.prefill(rb, [x], [pid])
+    eng.prefill(rb, [x], [pid], prefix_pos3=[pos3])
     tok = getattr(model, "tokenizer", None) or sm.tokenizer
     eos = getattr(tok, "eos_token_id", None) if tok is not None else None
     committed: List[int] = []

@@ -4,8 +4,16 @@ round (``SELFSPEC_FULLDRAFT=1``, ``SELFSPEC_FAST_COMMIT=1``, device positions) o
 
 Hooks kept 1:1 -- ``forward_batch_generation`` (:1127), ``_draft_block`` (:660), ``_fulldraft_verify`` (:822),
 ``_fast_commit_round`` (:963), ``clear_cache_pool`` / ``update_weights_from_tensor`` (:472-487) and the scheduler
-hooks ``ss_bind_scheduler`` / ``ss_release_stash`` (:1001, :1019; no draft is launched ahead, so there is never a
-stash to release).  The result carries the reference's contract (:954-961, :990-998): ``next_token_ids`` = the
+hooks ``ss_bind_scheduler`` / ``ss_release_stash`` (:1001, :1019).
+
+Draft-ahead (``SELFSPEC_DRAFT_AHEAD=1`` or ``draft_ahead=True``; :1000-1125 and ``selfspec_fast_commit.py:357-440``):
+after a plain round's readback, when the host pre-check ``cannot_finish`` says no request can end this round and the
+next scheduler iteration is expected to decode the same batch, the next round's draft graph is replayed at once (the
+commit kernel has already advanced the device lengths and seeds), and the host bookkeeping runs under it.  The next
+call with the same batch (same requests, pool slots and lengths) replays only the verify + commit graph.  Anything else
+discards the pre-launched draft: ``ss_release_stash`` before a prefill admission, a changed batch, a non-plain batch.
+Pages are owned per request here, so a discarded draft frees nothing: its K/V rows sit at positions the next draft
+rewrites before anything reads them.  The result carries the reference's contract (:954-961, :990-998): ``next_token_ids`` = the
 device next seeds [bs], ``next_token_ids_cpu`` = the committed tokens per request, ``accept_length_per_req_cpu``
 = j per request, ``num_accepted_tokens`` = sum(j), ``finish_checked=True``.
 
@@ -29,7 +37,7 @@ from typing import List, Optional
 import torch
 
 from .. import _lib as L
-from ..commit_rules import grammar_accept_or_abort, host_commit, stop_set
+from ..commit_rules import cannot_finish, grammar_accept_or_abort, host_commit, stop_set
 from ..engine import Engine
 from ..sampling import (RequestSampling, SampledRound, SamplerState, current_masks, first_tokens, pack_allowed,
                         verify_row_masks)
@@ -103,6 +111,11 @@ class SelfSpecDiffusionWorker:
         self._graphs = bool(int(os.environ.get("GR_GRAPHS", "1")))
         self.n_rounds = 0
         self._sampler: Optional[SamplerState] = None
+        self._draft_ahead = bool(int(os.environ.get("SELFSPEC_DRAFT_AHEAD", "0"))) or \
+            bool(getattr(server_args, "ss_draft_ahead", False))
+        self._sched = None
+        self._stash = None
+        self.ahead_stats = {"launched": 0, "used": 0, "released": 0, "skip_finish": 0, "skip_sched": 0}
         self._random_seed = int(getattr(server_args, "random_seed", 0) or 0)
         self._filter = L.FILTER_TORCH if getattr(server_args, "sampling_backend", "flashinfer") == "pytorch" \
             else L.FILTER_JOINT
@@ -117,10 +130,32 @@ class SelfSpecDiffusionWorker:
             self._seed_pool.zero_()
 
     def ss_bind_scheduler(self, scheduler) -> None:
-        self._scheduler = scheduler
+        """Read-only access to the scheduler's running batch and waiting queue, for the draft-ahead gate."""
+        self._sched = scheduler
 
     def ss_release_stash(self, reason: str = "") -> None:
-        return None
+        """Drop a pre-launched draft (the scheduler calls this before a prefill admission)."""
+        if self._stash is not None:
+            self._stash = None
+            self.ahead_stats["released"] += 1
+
+    def _ahead_allowed(self, batch) -> bool:
+        """The next iteration is expected to decode this same batch (no prefill admission pending)."""
+        s = self._sched
+        if s is None:
+            return True   # no scheduler bound: the caller either repeats the batch or releases the stash
+        if batch is not getattr(s, "running_batch", None):
+            return False
+        waiting = getattr(s, "waiting_queue", None) or []
+        full = getattr(getattr(s, "running_batch", None), "batch_is_full", False)
+        return getattr(s, "chunked_req", None) is None and (not waiting or full)
+
+    def _stash_matches(self, st, batch) -> bool:
+        if batch is not st["batch"] or batch.req_pool_indices is not st["rpi"] or len(batch.reqs) != len(st["reqs"]):
+            return False
+        if any(a is not b for a, b in zip(batch.reqs, st["reqs"])):
+            return False
+        return batch.seq_lens_cpu is not None and batch.seq_lens_cpu.tolist() == st["seq_lens"]
 
     def _sampler_state(self) -> SamplerState:
         if self._sampler is None:
@@ -169,6 +204,12 @@ class SelfSpecDiffusionWorker:
                     logits[rows] = fn(logits[rows], params)
         return hook
 
+    def _pos_delta(self) -> torch.Tensor:
+        """RoPE position - cache position of each pool slot (nonzero for a prefix with 2-D image positions)."""
+        if getattr(self, "_delta_pool", None) is None:
+            self._delta_pool = torch.zeros((self.req_to_page.size,), dtype=torch.int32, device=self.device)
+        return self._delta_pool
+
     def _seeds(self) -> torch.Tensor:
         if self._seed_pool is None:
             self._seed_pool = torch.zeros((self.req_to_page.size,), dtype=torch.int64, device=self.device)
@@ -193,7 +234,17 @@ class SelfSpecDiffusionWorker:
     # ------------------------------------------------------------------ hooks
     def forward_batch_generation(self, batch) -> GenerationBatchResult:
         if batch.forward_mode.is_extend():
+            self.ss_release_stash("prefill")
             return self._prefill(batch)
+        st, self._stash = self._stash, None
+        if st is not None:
+            if self._stash_matches(st, batch):
+                # this round's draft already ran right after the previous readback
+                self.ahead_stats["used"] += 1
+                self._cur = st["rb"]
+                st["rb"].gv.replay()
+                return self._fast_commit_round(batch, None, None)
+            self.ahead_stats["released"] += 1
         draft_tokens = self._draft_block(batch)
         return self._fulldraft_verify(batch, draft_tokens)
 
@@ -224,7 +275,9 @@ class SelfSpecDiffusionWorker:
                                None if masks is None else pack_allowed(masks).to(self.device))
                 return first_tokens(eng, rows, len(which), smp, status=rb.status,
                                     custom=self._custom_hook(sub, 1, None))
-        first = eng.prefill(rb, xs, ids, first_fn=first_fn)
+        pos3 = [getattr(r, "mrope_positions", None) for r in batch.reqs]
+        first = eng.prefill(rb, xs, ids, first_fn=first_fn, prefix_pos3=pos3)
+        self._pos_delta()[batch.req_pool_indices] = rb.pos_delta
         batch.seq_lens.copy_(rb.seq_lens)
         batch.seq_lens_cpu = rb.seq_lens.cpu()
         for req, t in zip(batch.reqs, first):
@@ -246,6 +299,7 @@ class SelfSpecDiffusionWorker:
         rb.rpi.copy_(batch.req_pool_indices)
         rb.page_table.copy_(self.req_to_page.table[batch.req_pool_indices])
         rb.seq_lens.copy_(batch.seq_lens)
+        rb.pos_delta.copy_(self._pos_delta()[batch.req_pool_indices])
         # longest-first attention launch order for this batch (the captured graph reads it in place)
         self.engine.refresh_order(rb)
         self._cur = rb
@@ -266,8 +320,10 @@ class SelfSpecDiffusionWorker:
                 torch.cuda.synchronize()
                 rb.seq_lens.copy_(snap[0]); rb.seeds.copy_(snap[1])
                 rb.n_committed.copy_(snap[2]); rb.rounds.copy_(snap[3])
-                rb.graph = eng.capture(rb)
-            rb.graph.replay()
+                rb.gd, rb.gv = eng.capture_split(rb)   # draft, and verify + commit (draft-ahead replays them apart)
+                rb.graph = True
+            rb.gd.replay()
+            rb.gv.replay()
         else:
             eng.round_launch(rb)
         return self._fast_commit_round(batch, None, None)
@@ -311,6 +367,18 @@ class SelfSpecDiffusionWorker:
         if st:
             raise RuntimeError(f"device status {st}: {L.load().gr_status_string(st).decode()}")
         rows = h[: bs * (K + 2)].view(bs, K + 2).tolist()
+        ahead = False
+        if plain and self._draft_ahead and self._graphs and getattr(rb, "gd", None) is not None:
+            if not all(cannot_finish(q, [r[0]] + r[2: 3 + r[1]]) for q, r in zip(batch.reqs, rows)):
+                self.ahead_stats["skip_finish"] += 1
+            elif not self._ahead_allowed(batch):
+                self.ahead_stats["skip_sched"] += 1
+            else:
+                # no request ends this round: the device lengths and seeds are the next round's already
+                self.engine.refresh_order(rb)
+                rb.gd.replay()
+                ahead = True
+                self.ahead_stats["launched"] += 1
         toks, js, accs = host_commit(batch.reqs, rows)
         # the kernel advanced seq_lens by acc + 2 (x0 + verify rows 0..acc); a request cut inside the round keeps j + 1
         fix = [accs[i] + 1 - js[i] for i in range(bs)]
@@ -321,5 +389,10 @@ class SelfSpecDiffusionWorker:
         for i in range(bs):
             sl[i] += js[i] + 1
         self.n_rounds += 1
+        if ahead:
+            if any(fix) or any(r.finished() for r in batch.reqs):
+                raise RuntimeError("draft-ahead: cannot_finish disagreed with the host finish rules")
+            self._stash = {"batch": batch, "rpi": batch.req_pool_indices, "reqs": list(batch.reqs), "rb": rb,
+                           "seq_lens": sl.tolist()}
         return GenerationBatchResult(next_token_ids=rb.out_next.clone(), num_accepted_tokens=sum(js),
                                      accept_length_per_req_cpu=js, next_token_ids_cpu=toks, finish_checked=True)

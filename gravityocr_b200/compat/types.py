@@ -67,6 +67,8 @@ class Req:
         self.spec_accepted_tokens = 0
         self.hist: List[int] = []
         self._spec_seed_ready = False
+        # multimodal (t, h, w) positions [3, prefix length] of the prefix (image tokens on a grid), or None for 1-D
+        self.mrope_positions = None
 
     def prefix_rows(self, engine):
         ids = torch.tensor(self.origin_input_ids, dtype=torch.int64)

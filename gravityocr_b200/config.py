@@ -35,6 +35,9 @@ class ModelConfig:
     # GLM-OCR's <|mask|> id (reference MODEL_CARD.md:98-100; worker _resolve_block_diffusion error text).
     mask_id: int = 59282
     image_token_id: int = 59280
+    # M-RoPE: rotary pairs [0, 8) rotate by the temporal position, [8, 20) by the row, [20, 32) by the column
+    # (transformers GlmOcrTextRotaryEmbedding mrope_section); text tokens have three equal positions.
+    mrope_section: Tuple[int, int, int] = (8, 12, 12)
 
     @property
     def q_dim(self) -> int:

@@ -276,6 +276,9 @@ static int build_linear(const void* w, int n_out, int k_in, const void* x, int m
         epi->rotary_dim % 32 || epi->rotary_dim > 128 || n_out != (epi->n_q_heads + 2 * epi->n_kv_heads) * 128 ||
         epi->page_size != 16)
       return GR_ERR_ARG;
+    if (epi->row_pos3 && (epi->mrope_section[0] < 0 || epi->mrope_section[1] < 0 || epi->mrope_section[2] < 0 ||
+                          epi->mrope_section[0] + epi->mrope_section[1] + epi->mrope_section[2] != epi->rotary_dim / 2))
+      return GR_ERR_ARG;
   } else if (epi->mode == GR_EPI_ARGMAX) {
     if (!epi->out_idx) return GR_ERR_ARG;
   } else if (!epi->out || epi->ld_out <= 0) {
@@ -315,6 +318,9 @@ static int build_linear(const void* w, int n_out, int k_in, const void* x, int m
   p.k_cache = static_cast<__nv_bfloat16*>(epi->k_cache);
   p.v_cache = static_cast<__nv_bfloat16*>(epi->v_cache);
   p.row_pos = epi->row_pos;
+  p.row_pos3 = epi->row_pos3;
+  p.mrope_s0 = epi->mrope_section[0];
+  p.mrope_s1 = epi->mrope_section[1];
   p.row_slot = epi->row_slot;
   p.inv_freq = epi->inv_freq;
   p.rotary_dim = epi->rotary_dim;
@@ -444,7 +450,7 @@ int gr_embed_rows(int mode, int bs, int K, const int64_t* seeds, const int64_t* 
                   const int64_t* ids64, const float* row_embeds, const int64_t* seq_lens, const int32_t* page_table,
                   int pt_stride, int page_size, int pages_per_req, const void* embed, int vocab, int mask_id,
                   const void* norm_w, float eps, int hidden, float* h_out, void* x_out, int32_t* row_pos,
-                  int64_t* row_slot, int32_t* row_ids, int32_t* status, void* stream) {
+                  int64_t* row_slot, int32_t* row_ids, const int32_t* rope_delta, int32_t* status, void* stream) {
   if (bs <= 0 || K <= 0 || !seq_lens || !page_table || !embed || !norm_w || !h_out || !x_out || !row_pos || !row_slot)
     return GR_ERR_ARG;
   if (hidden <= 0 || hidden % 8 || page_size <= 0 || pages_per_req <= 0) return GR_ERR_ARG;
@@ -470,6 +476,7 @@ int gr_embed_rows(int mode, int bs, int K, const int64_t* seeds, const int64_t* 
   p.row_embeds = row_embeds;
   p.seq_lens = seq_lens;
   p.page_table = page_table;
+  p.rope_delta = rope_delta;
   p.embed = static_cast<const __nv_bfloat16*>(embed);
   p.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
   p.eps = eps;

@@ -120,12 +120,24 @@ __device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, in
     if (rot) {
       // Lanes d and d ^ 1 rotate the same pair and need the same angles: the even lane computes cos / sin for
       // tokens 0-7 and the odd lane for tokens 8-15, and they swap the results.
-      const int pos_l = p.row_pos[tl];
       const float fr = p.inv_freq[d >> 1];
       const bool odd = d & 1;
+      // multimodal positions: every lane fetches its token's three axes and picks, after the shuffle, the axis of
+      // its own rotary pair (pairs of one warp can straddle a section boundary)
+      const bool mm = p.row_pos3 != nullptr;
+      const int pair = d >> 1;
+      const int axis = pair < p.mrope_s0 ? 0 : (pair < p.mrope_s0 + p.mrope_s1 ? 1 : 2);
+      const int pos_l = mm ? p.row_pos3[tl * 3] : p.row_pos[tl];
+      const int pos_h = mm ? p.row_pos3[tl * 3 + 1] : 0;
+      const int pos_w = mm ? p.row_pos3[tl * 3 + 2] : 0;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const int pos = __shfl_sync(0xffffffffu, pos_l, odd ? 8 + i : i);
+        int pos = __shfl_sync(0xffffffffu, pos_l, odd ? 8 + i : i);
+        if (mm) {
+          const int ph = __shfl_sync(0xffffffffu, pos_h, odd ? 8 + i : i);
+          const int pw = __shfl_sync(0xffffffffu, pos_w, odd ? 8 + i : i);
+          pos = axis == 0 ? pos : (axis == 1 ? ph : pw);
+        }
         float sn, cs;
         rope_sincos(__fmul_rn(static_cast<float>(pos), fr), &sn, &cs);  // the reference's fp32 pos * inv_freq
         const float cs_o = __shfl_xor_sync(0xffffffffu, cs, 1);

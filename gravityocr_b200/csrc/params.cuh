@@ -17,6 +17,8 @@ struct LinearParams {
   __nv_bfloat16* k_cache;
   __nv_bfloat16* v_cache;
   const int* row_pos;
+  const int* row_pos3;  // [M][3] (t, h, w) positions, or NULL: every pair uses row_pos
+  int mrope_s0, mrope_s1;  // pairs [0, s0) rotate by axis 0, [s0, s0 + s1) by axis 1, the rest by axis 2
   const int64_t* row_slot;
   const float* inv_freq;
   int rotary_dim, n_q_heads, n_kv_heads, page_size;
@@ -56,6 +58,7 @@ struct EmbedParams {
   const float* row_embeds;
   const int64_t* seq_lens;
   const int32_t* page_table;
+  const int32_t* rope_delta;
   const __nv_bfloat16* embed;
   const __nv_bfloat16* norm_w;
   float eps;

@@ -51,7 +51,7 @@ __global__ void __launch_bounds__(kRowThreads) embed_rows_kernel(const EmbedPara
       lp = p.pages_per_req - 1;
     }
     const int64_t phys = p.page_table[(size_t)b * p.pt_stride + lp];
-    p.row_pos[t] = static_cast<int32_t>(pos);
+    p.row_pos[t] = static_cast<int32_t>(pos + (p.rope_delta ? p.rope_delta[b] : 0));
     p.row_slot[t] = phys * p.page_size + (pos % p.page_size);
     if (p.row_ids) p.row_ids[t] = static_cast<int32_t>(id);
     s_id = id;

@@ -130,6 +130,7 @@ class RoundBuffers:
     attn_chunk: int
     attn_splits: int
     order: Optional[torch.Tensor] = None            # int32 [bs] attention launch order (longest first)
+    pos_delta: Optional[torch.Tensor] = None        # int32 [bs] RoPE position - cache position (M-RoPE delta)
     override_g: Optional[torch.Tensor] = None      # int32 [bs, g_len] forced-accept replay stream
     override_plan: Optional[torch.Tensor] = None   # int32 [bs, max_rounds]
 
@@ -216,10 +217,13 @@ class Engine:
                 out_idx: torch.Tensor, out_top1: Optional[torch.Tensor] = None, out_gap: Optional[torch.Tensor] = None,
                 seeds=None, rpi=None, ids32=None, ids64=None, row_embeds=None, attn_chunk: int = 64,
                 attn_splits: int = 1, status: Optional[torch.Tensor] = None, head: bool = True,
-                order: Optional[torch.Tensor] = None, attn_draft: Optional[int] = None) -> None:
+                order: Optional[torch.Tensor] = None, attn_draft: Optional[int] = None,
+                rope_delta: Optional[torch.Tensor] = None, rope_pos3: Optional[torch.Tensor] = None) -> None:
         """One pass of the decoder over M = bs*K rows; writes each row's argmax (and top-1 / gap) to out_idx.
         head=False stops before lm_head (the normed final hidden rows stay in ``self.x``).  attn_draft overrides the
-        attention mask the row mode implies (1 for draft rows, else causal); 2 = every row sees the whole window."""
+        attention mask the row mode implies (1 for draft rows, else causal); 2 = every row sees the whole window.
+        rope_delta (int32 [bs]): RoPE position = cache position + delta; rope_pos3 (int32 [M, 3]): explicit
+        multimodal (t, h, w) positions of the rows instead."""
         cfg, w, M = self.cfg, self.w, bs * K
         if M > self.max_rows:
             raise ValueError(f"{M} rows > max_rows {self.max_rows}")
@@ -233,14 +237,15 @@ class Engine:
         L.embed_rows(rows_mode, bs, K, seeds=seeds, rpi=rpi, ids32=ids32, ids64=ids64, row_embeds=row_embeds,
                      seq_lens=seq_lens, page_table=page_table, page_size=self.page_size, embed=w.embed, vocab=cfg.vocab,
                      mask_id=cfg.mask_id, norm_w=w.layers[0]["in"], eps=cfg.rms_eps, h_out=self.h[0], x_out=self.x,
-                     row_pos=self.row_pos, row_slot=self.row_slot, row_ids=self.row_ids, status=st)
+                     row_pos=self.row_pos, row_slot=self.row_slot, row_ids=self.row_ids, rope_delta=rope_delta,
+                     status=st)
         ws_attn = self._attn_workspace(bs, K, attn_splits) if attn_splits > 1 else None
         draft = int(rows_mode == L.ROWS_DRAFT) if attn_draft is None else int(attn_draft)
         self._forward_body(rows_mode, bs, K, seq_lens, page_table, out_idx, out_top1, out_gap, attn_chunk,
-                           attn_splits, st, head, order, ws_attn, draft)
+                           attn_splits, st, head, order, ws_attn, draft, rope_pos3)
 
     def _forward_body(self, rows_mode, bs, K, seq_lens, page_table, out_idx, out_top1, out_gap, attn_chunk,
-                      attn_splits, st, head, order, ws_attn, draft) -> None:
+                      attn_splits, st, head, order, ws_attn, draft, rope_pos3=None) -> None:
         """The layers and lm_head after the embedding rows."""
         ops = L
         cfg, w, M = self.cfg, self.w, bs * K
@@ -257,6 +262,10 @@ class Engine:
             e.row_slot = self.row_slot.data_ptr()
             e.inv_freq = w.inv_freq.data_ptr()
             e.rotary_dim = cfg.rotary_dim
+            if rope_pos3 is not None:
+                e.row_pos3 = rope_pos3.data_ptr()
+                for i in range(3):
+                    e.mrope_section[i] = cfg.mrope_section[i]
             e.n_q_heads = cfg.n_q_heads
             e.n_kv_heads = cfg.n_kv_heads
             e.page_size = self.page_size
@@ -322,15 +331,18 @@ class Engine:
             top_d=torch.zeros((bs * K,), **f32), top_v=torch.zeros((bs * K,), **f32),
             readback=torch.zeros((bs * (K + 2) + 4,), **i32), released=torch.zeros((bs * K,), **i64),
             out_next=torch.zeros((bs,), **i64), accept_len=torch.zeros((bs,), **i32),
-            attn_chunk=chunk, attn_splits=splits)
+            attn_chunk=chunk, attn_splits=splits, pos_delta=torch.zeros((bs,), **i32))
 
     def prefill(self, rb: RoundBuffers, prefixes: List[torch.Tensor], prefix_ids: List[torch.Tensor],
-                chunk: int = 64, attn_chunk: Optional[int] = None, first_fn=None) -> List[int]:
+                chunk: int = 64, attn_chunk: Optional[int] = None, first_fn=None,
+                prefix_pos3: Optional[List[Optional[torch.Tensor]]] = None) -> List[int]:
         """Causal prefill of each request's prefix through the same kernels (chunks of ``chunk`` rows, causal
         attention).  prefixes[b]: fp32 [P_b, H] layer-0 input rows (image embeddings + prompt embeddings);
         prefix_ids[b]: int64 [P_b] ids (< 0 where the row comes from ``prefixes``).  Sets seq_lens = P_b, the seed
         pool (seeds[rpi[b]] = first generated token), n_committed = 1.  Returns the first tokens: the argmax of the
-        last prefix row, or first_fn(rows [n, H] bf16, request indices) for a batch that samples."""
+        last prefix row, or first_fn(rows [n, H] bf16, request indices) for a batch that samples.
+        prefix_pos3[b] (int [3, P_b], optional): the request's multimodal (t, h, w) prefix positions (image tokens on a
+        grid); its decode rows then rotate by cache position + (max position + 1 - P_b), kept in rb.pos_delta."""
         bs = rb.bs
         dev = self.device
         lens = [int(p.shape[0]) for p in prefixes]
@@ -339,6 +351,7 @@ class Engine:
             if ((n + chunk - 1) // chunk) * chunk > cap:
                 raise ValueError(f"prefix of {n} rows needs {((n + chunk - 1) // chunk) * chunk} slots, capacity {cap}")
         n_chunks = max((n + chunk - 1) // chunk for n in lens)
+        mm = prefix_pos3 is not None and any(p is not None for p in prefix_pos3)
         H = self.cfg.hidden
         first = [0] * bs
         self.reserve(bs * chunk)
@@ -355,12 +368,21 @@ class Engine:
             seq = torch.full((nb,), c * chunk, dtype=torch.int64).to(dev)
             pt = rb.page_table[torch.tensor(active, device=dev)].contiguous()
             rows_e, ids = rows_e.to(dev), ids.to(dev)
+            pos3 = None
+            if mm:
+                pos3 = (torch.arange(c * chunk, (c + 1) * chunk, dtype=torch.int32)[None, :, None]
+                        .expand(nb, chunk, 3).contiguous())
+                for i, b in enumerate(active):
+                    if prefix_pos3[b] is not None:
+                        s0, s1 = c * chunk, min(lens[b], (c + 1) * chunk)
+                        pos3[i, : s1 - s0] = prefix_pos3[b][:, s0:s1].T.to(torch.int32)
+                pos3 = pos3.view(nb * chunk, 3).to(dev)
             ml = (c + 1) * chunk
             ach, asp = attention_split(nb, chunk, ml, ml, self.cfg.n_kv_heads, self.sms)
             if attn_chunk:
                 ach, asp = attn_chunk, int(math.ceil(ml / attn_chunk))
             self.forward(L.ROWS_EXPLICIT, nb, chunk, seq, pt, out_idx=out_idx, ids64=ids, row_embeds=rows_e,
-                         attn_chunk=ach, attn_splits=asp, status=rb.status, head=False)
+                         attn_chunk=ach, attn_splits=asp, status=rb.status, head=False, rope_pos3=pos3)
             # lm_head only on the rows that end a prefix (the first generated token of those requests)
             ends = [(b, i * chunk + (lens[b] - 1 - c * chunk)) for i, b in enumerate(active)
                     if c * chunk <= lens[b] - 1 < (c + 1) * chunk]
@@ -377,6 +399,11 @@ class Engine:
                 for k, (b, _) in enumerate(ends):
                     first[b] = int(res[k])
         rb.seq_lens.copy_(torch.tensor(lens, dtype=torch.int64))
+        delta = [0] * bs
+        for b in range(bs):
+            if prefix_pos3 is not None and prefix_pos3[b] is not None:
+                delta[b] = int(prefix_pos3[b].max()) + 1 - lens[b]
+        rb.pos_delta.copy_(torch.tensor(delta, dtype=torch.int32))
         self.refresh_order(rb)
         rb.seeds[rb.rpi] = torch.tensor(first, dtype=torch.int64, device=dev)
         rb.n_committed.fill_(1)
@@ -404,7 +431,7 @@ class Engine:
         bs, K = rb.bs, rb.K
         self.forward(L.ROWS_DRAFT, bs, K, rb.seq_lens, rb.page_table, out_idx=rb.am, out_top1=rb.top_d,
                      out_gap=rb.gap_d, seeds=rb.seeds, rpi=rb.rpi, attn_chunk=rb.attn_chunk,
-                     attn_splits=rb.attn_splits, status=rb.status, order=rb.order)
+                     attn_splits=rb.attn_splits, status=rb.status, order=rb.order, rope_delta=rb.pos_delta)
         if override:
             L.draft_override(bs, K, rb.am, rb.override_g, rb.n_committed, rb.override_plan, rb.rounds,
                              self.cfg.vocab, self.cfg.mask_id)
@@ -414,7 +441,7 @@ class Engine:
         bs, K = rb.bs, rb.K
         self.forward(L.ROWS_VERIFY, bs, K, rb.seq_lens, rb.page_table, out_idx=rb.v, out_top1=rb.top_v,
                      out_gap=rb.gap_v, ids32=rb.am, attn_chunk=rb.attn_chunk, attn_splits=rb.attn_splits,
-                     status=rb.status, order=rb.order)
+                     status=rb.status, order=rb.order, rope_delta=rb.pos_delta)
         L.accept_commit(bs, K, rb.am, rb.v, rb.seeds, rb.rpi, rb.seq_lens, rb.packed, rb.released, rb.out_next,
                         x0_committed=False, n_released=rb.n_released, n_committed=rb.n_committed, rounds=rb.rounds,
                         accept_len=rb.accept_len)

@@ -261,7 +261,7 @@ class SampledRound:
         bs, K = rb.bs, rb.K
         eng.forward(L.ROWS_VERIFY, bs, K, rb.seq_lens, rb.page_table, out_idx=rb.v, ids32=rb.am,
                     attn_chunk=rb.attn_chunk, attn_splits=rb.attn_splits, status=rb.status, order=rb.order,
-                    head=False)
+                    head=False, rope_delta=rb.pos_delta)
         self._lm_head_f32(eng.x, bs * K, self.logits)
         L.logits_process(self.logits, bs, K, rb.am, smp)
         if custom is not None:

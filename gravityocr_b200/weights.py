@@ -38,14 +38,19 @@ def weight_shapes(cfg: ModelConfig) -> List[Tuple[str, Tuple[int, ...]]]:
 
 
 def random_weights(cfg: ModelConfig, seed: int, dtype: torch.dtype = torch.bfloat16,
-                   embed_std: float = INIT_STD) -> Dict[str, torch.Tensor]:
+                   embed_std: float = INIT_STD, norm_center: float = 0.0,
+                   qk_std: float = INIT_STD) -> Dict[str, torch.Tensor]:
     """N(0, 0.02) for every tensor, drawn in ``weight_shapes`` order from one CPU generator.
 
     The values are drawn in fp32 and rounded once to ``dtype``; with dtype=float32 nothing is rounded.
     ``embed_std`` scales the token-embedding table only (same draw, multiplied by embed_std / 0.02).  At the baseline's
     0.02 every sublayer adds a vector of the same size as the token's own embedding, the context dominates and greedy
     streams settle on one repeated token within a few steps; at 0.25 the token identity carries through the 16 layers
-    and streams stay varied, which the parity fixtures use to exercise rejections and rollbacks."""
+    and streams stay varied, which the parity fixtures use to exercise rejections and rollbacks.
+    ``norm_center`` is added to every RMSNorm weight (1.0 gives norm weights near one, as a trained model has, so each
+    sublayer's output carries weight in the residual) and ``qk_std`` rescales the q/k projections (sharper attention);
+    together they make the committed stream depend on the RoPE positions, which the multimodal-position fixtures
+    need.  Defaults reproduce the baseline draw exactly."""
     g = torch.Generator().manual_seed(int(seed))
     w: Dict[str, torch.Tensor] = {}
     for name, shape in weight_shapes(cfg):
@@ -53,6 +58,10 @@ def random_weights(cfg: ModelConfig, seed: int, dtype: torch.dtype = torch.bfloa
         t.normal_(0.0, INIT_STD, generator=g)
         if name == "embed_tokens" and embed_std != INIT_STD:
             t.mul_(embed_std / INIT_STD)
+        if (name.endswith("_proj") and name.split(".")[-1] in ("q_proj", "k_proj")) and qk_std != INIT_STD:
+            t.mul_(qk_std / INIT_STD)
+        if (name.endswith("layernorm") or name == "norm") and norm_center:
+            t.add_(norm_center)
         w[name] = t if dtype == torch.float32 else t.to(dtype)
     return w
 
@@ -86,3 +95,15 @@ def prefix_embeddings(weights: Dict[str, torch.Tensor], cfg: ModelConfig, image_
     (reference ``src/fast_sampling.py:483-488`` masked_scatter)."""
     e = weights["embed_tokens"][prompt_ids.to(torch.int64)].float()
     return torch.cat([image_embeds.float(), e], dim=0)
+
+
+def grid_positions(n_image: int, n_prompt: int, grid_w: int) -> torch.Tensor:
+    """Multimodal (t, h, w) positions [3, n_image + n_prompt] of a prefix whose image tokens lie on a grid of width
+    grid_w (token k at row k // grid_w, column k % grid_w, temporal position 0), followed by the prompt tokens at
+    start, start + 1, ... on every axis, start = the largest image position + 1 -- the layout of an image in a
+    multimodal RoPE index (transformers GlmOcrModel.get_rope_index), as a synthetic stand-in for a real crop."""
+    k = torch.arange(n_image)
+    img = torch.stack([torch.zeros_like(k), k // grid_w, k % grid_w])
+    start = int(img.max()) + 1 if n_image else 0
+    txt = torch.arange(start, start + n_prompt).expand(3, -1)
+    return torch.cat([img, txt], dim=1).to(torch.int64)

@@ -65,6 +65,11 @@ typedef struct gr_epilogue {
   int32_t* out_idx;       /* [M] */
   float* out_top1;        /* [M] or NULL */
   float* out_gap;         /* [M] top-1 minus top-2 logit, or NULL */
+  /* QKV_ROPE with multimodal (3-axis) positions: row_pos3 [M][3] = (t, h, w) position of each row, or NULL for 1-D
+   * row_pos.  Rotary pair i uses axis 0 for i < mrope_section[0], axis 1 for the next mrope_section[1] pairs, axis 2
+   * after (transformers GlmOcrTextRotaryEmbedding.apply_mrope, sections [8, 12, 12]). */
+  const int32_t* row_pos3;
+  int mrope_section[3];
 } gr_epilogue;
 
 /* Library identity / diagnostics. */
@@ -100,7 +105,9 @@ int gr_linear(const void* w, int n_out, int k_in, const void* x, int m, const gr
               void* stream);
 
 /* Layer-0 input rows of a forward and the window plan: for each row its token id, RoPE position and cache slot;
- * h_out[t] = embedding row (fp32), x_out[t] = RMSNorm(h_out[t]) * norm_w (bf16).
+ * h_out[t] = embedding row (fp32), x_out[t] = RMSNorm(h_out[t]) * norm_w (bf16).  The RoPE position is the cache
+ * position plus rope_delta[b] (int32 [bs], or NULL for 0): the multimodal position offset of a request whose image
+ * tokens take fewer position values than cache slots (the M-RoPE delta, sglang_0.5.10_selfspec.patch:1371-1380).
  * Replaces the draft window build of selfspec_diffusion_worker.py:689-706 (_draft_block: [seed | mask x (K-1)],
  * positions seq_lens + j), the verify ids/positions of :849-884 (_fulldraft_verify: am[:, :K], seq_lens + 1 + j),
  * the embedding lookup with image-embedding injection of src/fast_sampling.py:483-488, and the first
@@ -109,7 +116,7 @@ int gr_embed_rows(int mode, int bs, int K, const int64_t* seeds, const int64_t* 
                   const int64_t* ids64, const float* row_embeds, const int64_t* seq_lens, const int32_t* page_table,
                   int pt_stride, int page_size, int pages_per_req, const void* embed, int vocab, int mask_id,
                   const void* norm_w, float eps, int hidden, float* h_out, void* x_out, int32_t* row_pos,
-                  int64_t* row_slot, int32_t* row_ids, int32_t* status, void* stream);
+                  int64_t* row_slot, int32_t* row_ids, const int32_t* rope_delta, int32_t* status, void* stream);
 
 /* Sandwich-norm step: h_out = h_in + w_a * RMSNorm(y); x_out = w_b * RMSNorm(h_out) (bf16).  y may arrive as
  * y_parts split-K partials (y[p * m * hidden + t * hidden + f], summed in order p = 0, 1, ...).  The decoder layer's

@@ -56,9 +56,17 @@ class OracleDecoder:
         return w * (x * torch.rsqrt(var + self.cfg.rms_eps))
 
     def rope(self, x: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
-        """x [T, heads, head_dim]; rotates pairs (2i, 2i+1) of the first rotary_dim lanes by pos * inv_freq[i]."""
+        """x [T, heads, head_dim]; rotates pairs (2i, 2i+1) of the first rotary_dim lanes by pos * inv_freq[i].
+        pos [T] (1-D) or [T, 3] multimodal (t, h, w): pair i then takes the axis of its M-RoPE section
+        (modeling_glm_ocr.py:730-735 apply_mrope: chunks of mrope_section along the frequencies, chunk c from axis c)."""
         rd = self.cfg.rotary_dim
-        f = pos.to(self.device).float()[:, None] * self.inv_freq[None, :]          # [T, rd/2]
+        pos = pos.to(self.device)
+        if pos.dim() == 2:
+            sec = getattr(self.cfg, "mrope_section", (8, 12, 12))
+            axis = torch.cat([torch.full((n,), a, dtype=torch.int64) for a, n in enumerate(sec)]).to(self.device)
+            f = pos.float()[:, axis] * self.inv_freq[None, :]                        # [T, rd/2]
+        else:
+            f = pos.float()[:, None] * self.inv_freq[None, :]                        # [T, rd/2]
         c, s = f.cos()[:, None, :], f.sin()[:, None, :]
         x0, x1 = x[..., 0:rd:2], x[..., 1:rd:2]
         out = x.clone()
@@ -118,13 +126,16 @@ class OracleDecoder:
         return self.rms(h, self.w["norm"]) @ self.w["lm_head"].T
 
     # ------------------------------------------------------------------ prefill / AR
-    def prefill(self, x: torch.Tensor, capacity: int) -> Tuple[OracleCache, torch.Tensor]:
-        """Causal pass over the prefix rows x [P, hidden]; returns (cache, last-row logits [V])."""
+    def prefill(self, x: torch.Tensor, capacity: int, pos3: Optional[torch.Tensor] = None
+                ) -> Tuple[OracleCache, torch.Tensor]:
+        """Causal pass over the prefix rows x [P, hidden] (RoPE positions 0..P-1, or pos3 [3, P] multimodal);
+        returns (cache, last-row logits [V])."""
         P = x.shape[0]
         cache = self.new_cache(capacity)
-        pos = torch.arange(P)
+        wpos = torch.arange(P)
+        rpos = wpos if pos3 is None else pos3.T.contiguous()
         vis = torch.ones((P, P), dtype=torch.bool).tril()
-        h = self.forward(x, pos, cache, pos, vis)
+        h = self.forward(x, rpos, cache, wpos, vis)
         return cache, self.logits(h[-1:])[0]
 
     def ar_greedy(self, x: torch.Tensor, n_new: int) -> List[int]:
@@ -139,19 +150,25 @@ class OracleDecoder:
             out.append(int(self.logits(h)[0].argmax()))
         return out
 
-    def teacher_force(self, x: torch.Tensor, gen: List[int], chunk: int = 512) -> Tuple[List[int], List[float], torch.Tensor]:
+    def teacher_force(self, x: torch.Tensor, gen: List[int], chunk: int = 512, pos3: Optional[torch.Tensor] = None
+                      ) -> Tuple[List[int], List[float], torch.Tensor]:
         """One causal pass over prefix + gen (``src/fast_sampling.py:631-690``): for every i, the argmax (and the top-2
-        logit gap) of the logits that predict gen[i] from gen[:i].  Returns (argmax list, gap list, logits [n, V])."""
+        logit gap) of the logits that predict gen[i] from gen[:i].  pos3 [3, P]: multimodal prefix positions, gen
+        token i then at max + 1 + i on every axis.  Returns (argmax list, gap list, logits [n, V])."""
         P, n = x.shape[0], len(gen)
         seq = torch.cat([x.float(), self.embed(torch.tensor(gen[:-1], dtype=torch.int64))], dim=0) if n > 1 else x.float()
         T = seq.shape[0]
         cache = self.new_cache(T)
+        rope = None
+        if pos3 is not None:
+            nxt = int(pos3.max()) + 1
+            rope = torch.cat([pos3.T, (torch.arange(T - P) + nxt)[:, None].expand(-1, 3)], dim=0)
         hs = []
         for s0 in range(0, T, chunk):
             s1 = min(T, s0 + chunk)
             pos = torch.arange(s0, s1)
             vis = torch.arange(s1)[None, :] <= pos[:, None]
-            hs.append(self.forward(seq[s0:s1], pos, cache, pos, vis))
+            hs.append(self.forward(seq[s0:s1], pos if rope is None else rope[s0:s1], cache, pos, vis))
         h = torch.cat(hs, dim=0)[P - 1: P - 1 + n]
         lg = self.logits(h)
         top = torch.topk(lg, 2, dim=-1).values
@@ -160,15 +177,17 @@ class OracleDecoder:
 
 # ---------------------------------------------------------------------- natcache form (pins the oracle to the reference)
 def natcache_generate(model: OracleDecoder, x: torch.Tensor, max_new_tokens: int, bd: int,
-                      trace: Optional[list] = None) -> List[int]:
+                      trace: Optional[list] = None, pos3: Optional[torch.Tensor] = None) -> List[int]:
     """Restatement of ``generate_speculative_natcache`` (``src/fast_sampling.py:425-612``) with temperature 0,
     draft_steps=1, full_draft=True, accept_conf=0 and no EOS.  Greedy picks are ``softmax(logits.float()).argmax``
-    (``src/models/glm_ocr_dllm.py:997-1002``)."""
+    (``src/models/glm_ocr_dllm.py:997-1002``).  pos3 [3, P]: the prefix's multimodal positions; response token r then
+    sits at position next_pos + r on every axis, next_pos = max(pos3) + 1 (``comb_pos``, :505-506)."""
     c = model.cfg
     mask_id = c.mask_id
     P = x.shape[0]
+    next_pos = P if pos3 is None else int(pos3.max()) + 1
     cap = P + max_new_tokens + 2 * bd + 8
-    cache, seed_logit = model.prefill(x, cap)
+    cache, seed_logit = model.prefill(x, cap, pos3)
     seed_logit = seed_logit[None]                                            # [1, V]
     clen = P
     committed: List[int] = []
@@ -179,7 +198,7 @@ def natcache_generate(model: OracleDecoder, x: torch.Tensor, max_new_tokens: int
         Q = pre + bd
         r0 = clen - P
         ids = ([pending] if pre else []) + [mask_id] * bd
-        pos = torch.arange(P + r0, P + r0 + Q)
+        pos = torch.arange(next_pos + r0, next_pos + r0 + Q)
         wpos = torch.arange(clen, clen + Q)
         qi = torch.arange(Q)[:, None]
         kv = torch.arange(clen + Q)[None, :]
@@ -191,7 +210,7 @@ def natcache_generate(model: OracleDecoder, x: torch.Tensor, max_new_tokens: int
         draft = torch.cat([block, x_extra]).tolist()                         # a0, d1..d_bd
         Qv = Q + 1
         vids = ([pending] if pre else []) + draft
-        pos_v = torch.arange(P + r0, P + r0 + Qv)
+        pos_v = torch.arange(next_pos + r0, next_pos + r0 + Qv)
         wpos_v = torch.arange(clen, clen + Qv)
         qi = torch.arange(Qv)[:, None]
         kv = torch.arange(clen + Qv)[None, :]
@@ -222,13 +241,16 @@ class SpecState:
     seed: int
     out: List[int]
     prefix_len: int
+    pos_delta: int = 0          # RoPE position - cache position (multimodal prefixes)
 
 
-def spec_start(model: OracleDecoder, x: torch.Tensor, capacity: int) -> SpecState:
+def spec_start(model: OracleDecoder, x: torch.Tensor, capacity: int, pos3: Optional[torch.Tensor] = None
+               ) -> SpecState:
     """Prefill; the first generated token (argmax of the last prefix logit) becomes the first seed."""
-    cache, lg = model.prefill(x, capacity)
+    cache, lg = model.prefill(x, capacity, pos3)
     s = int(lg.argmax())
-    return SpecState(cache, x.shape[0], s, [s], x.shape[0])
+    delta = 0 if pos3 is None else int(pos3.max()) + 1 - x.shape[0]
+    return SpecState(cache, x.shape[0], s, [s], x.shape[0], delta)
 
 
 def spec_draft(model: OracleDecoder, st: SpecState, K: int) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -240,7 +262,7 @@ def spec_draft(model: OracleDecoder, st: SpecState, K: int) -> Tuple[torch.Tenso
     kv = torch.arange(S + K)[None, :]
     lim = torch.full((K, 1), S + K)
     lim[0, 0] = S + 1
-    lg = model.logits(model.forward(model.embed(ids), pos, st.cache, pos, kv < lim))
+    lg = model.logits(model.forward(model.embed(ids), pos + st.pos_delta, st.cache, pos, kv < lim))
     return lg.argmax(-1), lg
 
 
@@ -251,7 +273,7 @@ def spec_verify(model: OracleDecoder, st: SpecState, vids: torch.Tensor) -> Tupl
     pos = torch.arange(S + 1, S + 1 + K)
     kv = torch.arange(S + 1 + K)[None, :]
     lim = torch.arange(S + 2, S + 2 + K)[:, None]
-    lg = model.logits(model.forward(model.embed(vids), pos, st.cache, pos, kv < lim))
+    lg = model.logits(model.forward(model.embed(vids), pos + st.pos_delta, st.cache, pos, kv < lim))
     return lg.argmax(-1), lg
 
 

@@ -33,15 +33,20 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 
 NATCACHE_CASES = {
-    # name: (n_layers, n_image, n_prompt, max_new_tokens, bd, weight_seed, input_seed, embed_std)
-    "small": (2, 64, 16, 48, 16, 0, 0, 0.02),
-    "config0": (16, 256, 32, 128, 16, 0, 0, 0.02),
+    # name: (n_layers, n_image, n_prompt, max_new_tokens, bd, weight_seed, input_seed, embed_std, grid_w)
+    "small": (2, 64, 16, 48, 16, 0, 0, 0.02, 0),
+    "config0": (16, 256, 32, 128, 16, 0, 0, 0.02, 0),
     # the config-0 model with its token-embedding table drawn at std 0.25: a varied stream (the baseline's 0.02 settles
     # on one repeated token), drafted at three block sizes -- the committed stream must not depend on B
-    "varied_bd16": (16, 256, 32, 128, 16, 0, 0, 0.25),
-    "varied_bd4": (16, 256, 32, 128, 4, 0, 0, 0.25),
-    "varied_bd32": (16, 256, 32, 128, 32, 0, 0, 0.25),
+    "varied_bd16": (16, 256, 32, 128, 16, 0, 0, 0.25, 0),
+    "varied_bd4": (16, 256, 32, 128, 4, 0, 0, 0.25, 0),
+    "varied_bd32": (16, 256, 32, 128, 32, 0, 0, 0.25, 0),
+    # image tokens on a 16 x 16 grid: 2-D multimodal RoPE positions (get_rope_index returns them), response tokens at
+    # max position + 1 + r; norm weights near one and q/k at std 0.05 (WEIGHT_VARIANTS) so the stream depends on them
+    "mrope": (16, 256, 32, 64, 16, 0, 0, 0.02, 16),
 }
+# extra random_weights arguments per case (the rest use the baseline draw)
+WEIGHT_VARIANTS = {"mrope": {"norm_center": 1.0, "qk_std": 0.05}}
 
 
 def _dump(name, obj):
@@ -59,9 +64,9 @@ def gen_natcache(ref: str, case: str):
     from models.glm_ocr_dllm import GlmOcrBlockDiffusion
     from transformers import GlmOcrConfig, GlmOcrForConditionalGeneration
     from gravityocr_b200.config import small_model
-    from gravityocr_b200.weights import random_weights, request_inputs, prefix_token_ids
+    from gravityocr_b200.weights import grid_positions, random_weights, request_inputs, prefix_token_ids
 
-    L, n_img, n_txt, new, bd, wseed, iseed, estd = NATCACHE_CASES[case]
+    L, n_img, n_txt, new, bd, wseed, iseed, estd, grid_w = NATCACHE_CASES[case]
     cfg = small_model(L)
     hf = GlmOcrConfig()
     tc = hf.text_config
@@ -78,7 +83,8 @@ def gen_natcache(ref: str, case: str):
     hf.vision_config.depth = 1
     torch.manual_seed(0)
     glm = GlmOcrForConditionalGeneration(hf).float().eval()
-    w = random_weights(cfg, wseed, torch.float32, embed_std=estd)
+    wv = WEIGHT_VARIANTS.get(case, {})
+    w = random_weights(cfg, wseed, torch.float32, embed_std=estd, **wv)
     sd = {}
     for k, t in w.items():
         if k == "lm_head":
@@ -119,8 +125,9 @@ def gen_natcache(ref: str, case: str):
     m.tokenizer = types.SimpleNamespace(eos_token_id=None, decode=lambda *a, **k: "")
     mm = glm.model
     mm.get_image_features = lambda pv, thw, return_dict=True: types.SimpleNamespace(pooler_output=[img])
+    pos3 = (grid_positions(n_img, n_txt, grid_w) if grid_w else torch.arange(n_img + n_txt).expand(3, -1))
     mm.get_rope_index = lambda ids_, mmtt, image_grid_thw=None, video_grid_thw=None, attention_mask=None: (
-        torch.arange(ids_.shape[1])[None, None, :].expand(3, 1, -1), None)
+        pos3[:, None, :].clone(), None)
     from PIL import Image
     im = Image.new("RGB", (8, 8))
     t0 = time.time()
@@ -134,7 +141,8 @@ def gen_natcache(ref: str, case: str):
     _dump(f"natcache_{case}.json", {
         "source": "reference src/fast_sampling.py generate_speculative_natcache + teacher_force_argmax (CPU, fp32)",
         "n_layers": L, "n_image": n_img, "n_prompt": n_txt, "max_new_tokens": new, "bd": bd,
-        "weight_seed": wseed, "input_seed": iseed, "embed_std": estd, "mask_id": cfg.mask_id,
+        "weight_seed": wseed, "input_seed": iseed, "embed_std": estd, "grid_w": grid_w, "weight_variant": wv,
+        "mask_id": cfg.mask_id,
         "prompt_ids": txt.tolist(),
         "stream": stream, "teacher_force_argmax": tf, "stats": st,
         "trace": [{"k": d["k"], "draft": d["draft"], "ar_pred": d["ar_pred"], "new_tokens": d["new_tokens"]} for d in tr],

@@ -27,7 +27,8 @@ from gravityocr_b200.compat.sglang_worker import ReqToPagePool, SelfSpecDiffusio
 from gravityocr_b200.compat.types import ForwardMode, Req, SamplingParams, ScheduleBatch
 from gravityocr_b200.config import ModelConfig, small_model
 from gravityocr_b200.engine import Engine
-from gravityocr_b200.weights import prefix_embeddings, prefix_token_ids, random_weights, request_inputs
+from gravityocr_b200.weights import (grid_positions, prefix_embeddings, prefix_token_ids, random_weights,
+                                     request_inputs)
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -40,7 +41,7 @@ class _RefShapedModel(torch.nn.Module):
     around a transformers GlmOcrForConditionalGeneration; the processor and vision tower are stand-ins that hand the
     seeded image embeddings and 1-D positions to the caller, as the golden generator's run of the reference did."""
 
-    def __init__(self, cfg, w32, n_img, txt, img, bd):
+    def __init__(self, cfg, w32, n_img, txt, img, bd, pos3=None):
         super().__init__()
         from transformers import GlmOcrConfig, GlmOcrForConditionalGeneration
         hf = GlmOcrConfig()
@@ -84,8 +85,9 @@ class _RefShapedModel(torch.nn.Module):
         self.tokenizer = types.SimpleNamespace(eos_token_id=None)
         mm = self.glm.model
         mm.get_image_features = lambda pv, thw, return_dict=True: types.SimpleNamespace(pooler_output=[img])
+        p3 = torch.arange(ids.shape[1]).expand(3, -1) if pos3 is None else pos3
         mm.get_rope_index = lambda i, t, image_grid_thw=None, video_grid_thw=None, attention_mask=None: (
-            torch.arange(i.shape[1])[None, None, :].expand(3, 1, -1), None)
+            p3[:, None, :].clone(), None)
 
     @property
     def mm_model(self):
@@ -100,14 +102,16 @@ def _natcache_vs_golden(golden_dir, name, via_reference_model):
     from oracle.decoder_ref import OracleDecoder
     g = json.load(open(os.path.join(golden_dir, name)))
     cfg = small_model(g["n_layers"]) if g["n_layers"] != 16 else ModelConfig()
-    w32 = random_weights(cfg, g["weight_seed"], torch.float32, embed_std=g.get("embed_std", 0.02))
+    w32 = random_weights(cfg, g["weight_seed"], torch.float32, embed_std=g.get("embed_std", 0.02),
+                         **g.get("weight_variant", {}))
     img, txt = request_inputs(cfg, g["input_seed"], g["n_image"], g["n_prompt"], 0, torch.float32)
     assert txt.tolist() == g["prompt_ids"]
     n, bd = g["max_new_tokens"], g["bd"]
+    pos3 = grid_positions(g["n_image"], g["n_prompt"], g["grid_w"]) if g.get("grid_w") else None
     tr = []
     if via_reference_model:
         from PIL import Image
-        model = _RefShapedModel(cfg, w32, g["n_image"], txt, img, bd)
+        model = _RefShapedModel(cfg, w32, g["n_image"], txt, img, bd, pos3)
         _, st = generate_speculative_natcache(model, Image.new("RGB", (8, 8)), max_new_tokens=n, return_stats=True,
                                               trace=tr)
         assert model.gr_engine.engine.cfg == cfg
@@ -124,7 +128,7 @@ def _natcache_vs_golden(golden_dir, name, via_reference_model):
     if first_div < m or len(ours) != len(ref):
         # only an fp32 argmax near-tie may separate the streams (teacher-forced gap of the reference model)
         x = prefix_embeddings(w32, cfg, img, txt)
-        _, gap, _ = OracleDecoder(cfg, w32).teacher_force(x, ours[: first_div + 1])
+        _, gap, _ = OracleDecoder(cfg, w32).teacher_force(x, ours[: first_div + 1], pos3=pos3)
         assert first_div < m and gap[first_div] < TIE, f"{name}: diverges at {first_div} with gap {gap[first_div]}"
         print(f"{name}: same stream for {first_div} tokens, then an fp32 near-tie (gap {gap[first_div]:.2e})")
         return

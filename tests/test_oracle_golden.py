@@ -98,7 +98,7 @@ def _natcache_varied(golden_dir, name):
     from gravityocr_b200.weights import prefix_embeddings, random_weights, request_inputs
     g = _load(golden_dir, name)
     cfg = ModelConfig()
-    w = random_weights(cfg, g["weight_seed"], torch.float32, embed_std=g["embed_std"])
+    w = random_weights(cfg, g["weight_seed"], torch.float32, embed_std=g["embed_std"], **g.get("weight_variant", {}))
     img, txt = request_inputs(cfg, g["input_seed"], g["n_image"], g["n_prompt"], 0, torch.float32)
     assert txt.tolist() == g["prompt_ids"]
     return g, OracleDecoder(cfg, w), prefix_embeddings(w, cfg, img, txt)
@@ -120,3 +120,19 @@ def test_natcache_restatement_reproduces_reference_varied(golden_dir):
     assert s == g["stream"]
     assert [d["k"] for d in tr] == [d["k"] for d in g["trace"]]
     assert [d["draft"] for d in tr] == [d["draft"] for d in g["trace"]]
+
+
+@pytest.mark.slow
+def test_natcache_restatement_reproduces_reference_mrope(golden_dir):
+    """Image tokens on a grid (2-D multimodal RoPE positions): the oracle's natcache reproduces the reference's run."""
+    from gravityocr_b200.weights import grid_positions
+    g, m, x = _natcache_varied(golden_dir, "natcache_mrope.json")
+    pos3 = grid_positions(g["n_image"], g["n_prompt"], g["grid_w"])
+    tr = []
+    s = natcache_generate(m, x, g["max_new_tokens"], g["bd"], tr, pos3=pos3)
+    assert s == g["stream"]
+    assert [d["k"] for d in tr] == [d["k"] for d in g["trace"]]
+    tf, _, _ = m.teacher_force(x, g["stream"][: g["max_new_tokens"]], pos3=pos3)
+    assert tf == g["teacher_force_argmax"]
+    # the positions matter: the 1-D layout gives another stream
+    assert natcache_generate(m, x, 16, g["bd"]) != s[:16]
