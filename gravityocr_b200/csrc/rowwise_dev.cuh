@@ -1,4 +1,4 @@
-// Row-wise device code shared by the per-launch kernels (rowwise.cu) and the persistent small-batch forward (small.cu).
+// Row-wise device code of the per-launch kernels (rowwise.cu).
 #pragma once
 
 #include "params.cuh"

@@ -7,7 +7,7 @@ the ``model.language_model.`` prefix dropped.
 """
 from __future__ import annotations
 
-from typing import Dict, List, Tuple
+from typing import Dict, List, Optional, Tuple
 
 import torch
 
@@ -107,3 +107,13 @@ def grid_positions(n_image: int, n_prompt: int, grid_w: int) -> torch.Tensor:
     start = int(img.max()) + 1 if n_image else 0
     txt = torch.arange(start, start + n_prompt).expand(3, -1)
     return torch.cat([img, txt], dim=1).to(torch.int64)
+
+
+def variant_weights(cfg: ModelConfig, seed: int, embed_std: float = INIT_STD, variant: Optional[dict] = None
+                    ) -> Dict[str, torch.Tensor]:
+    """fp32 weights of a fixture: ``random_weights`` with the variant's norm_center / qk_std, rounded through bf16 when
+    the variant says ``bf16_weights`` (the values the CUDA path holds)."""
+    v = dict(variant or {})
+    bf16 = v.pop("bf16_weights", False)
+    w = random_weights(cfg, seed, torch.bfloat16 if bf16 else torch.float32, embed_std=embed_std, **v)
+    return {k: t.float() for k, t in w.items()}

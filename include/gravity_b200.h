@@ -81,7 +81,7 @@ void gr_set_pdl(int enable);
  * grids of more than one CTA per SM and the mma.sync kernel below that; 2 the tcgen05 kernel for every grid (small
  * grids as thread-block clusters).  All compute the same rows; the switch exists to compare them. */
 void gr_set_attention_tc(int mode);
-/* Number of SMs the split heuristics assume (queried from device 0 on first use). */
+/* Number of SMs the split heuristics assume (queried for the current device on first use). */
 int gr_num_sms(void);
 
 /* Workspace (scratch) sizes in bytes for the calls below; the caller allocates them once, zero-filled, and passes

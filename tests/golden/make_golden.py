@@ -42,11 +42,13 @@ NATCACHE_CASES = {
     "varied_bd4": (16, 256, 32, 128, 4, 0, 0, 0.25, 0),
     "varied_bd32": (16, 256, 32, 128, 32, 0, 0, 0.25, 0),
     # image tokens on a 16 x 16 grid: 2-D multimodal RoPE positions (get_rope_index returns them), response tokens at
-    # max position + 1 + r; norm weights near one and q/k at std 0.05 (WEIGHT_VARIANTS) so the stream depends on them
-    "mrope": (16, 256, 32, 64, 16, 0, 0, 0.02, 16),
+    # max position + 1 + r; 4 layers with norm weights near one (WEIGHT_VARIANTS) so the stream depends on them
+    "mrope": (4, 256, 32, 64, 16, 0, 0, 0.02, 16),
 }
-# extra random_weights arguments per case (the rest use the baseline draw)
-WEIGHT_VARIANTS = {"mrope": {"norm_center": 1.0, "qk_std": 0.05}}
+# extra random_weights arguments per case (the rest use the baseline draw); "bf16_weights": the reference runs on the
+# bf16-rounded weights the CUDA path holds.  Sharper attention (q/k std 0.05) or 16 such layers make the bf16 and fp32
+# streams part at non-tied tokens within a few tokens even with 1-D positions, so the case stays at 4 layers.
+WEIGHT_VARIANTS = {"mrope": {"norm_center": 1.0, "bf16_weights": True}}
 
 
 def _dump(name, obj):
@@ -64,7 +66,7 @@ def gen_natcache(ref: str, case: str):
     from models.glm_ocr_dllm import GlmOcrBlockDiffusion
     from transformers import GlmOcrConfig, GlmOcrForConditionalGeneration
     from gravityocr_b200.config import small_model
-    from gravityocr_b200.weights import grid_positions, random_weights, request_inputs, prefix_token_ids
+    from gravityocr_b200.weights import grid_positions, request_inputs, prefix_token_ids, variant_weights
 
     L, n_img, n_txt, new, bd, wseed, iseed, estd, grid_w = NATCACHE_CASES[case]
     cfg = small_model(L)
@@ -84,7 +86,7 @@ def gen_natcache(ref: str, case: str):
     torch.manual_seed(0)
     glm = GlmOcrForConditionalGeneration(hf).float().eval()
     wv = WEIGHT_VARIANTS.get(case, {})
-    w = random_weights(cfg, wseed, torch.float32, embed_std=estd, **wv)
+    w = variant_weights(cfg, wseed, estd, wv)
     sd = {}
     for k, t in w.items():
         if k == "lm_head":

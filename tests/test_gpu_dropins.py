@@ -28,7 +28,7 @@ from gravityocr_b200.compat.types import ForwardMode, Req, SamplingParams, Sched
 from gravityocr_b200.config import ModelConfig, small_model
 from gravityocr_b200.engine import Engine
 from gravityocr_b200.weights import (grid_positions, prefix_embeddings, prefix_token_ids, random_weights,
-                                     request_inputs)
+                                     request_inputs, variant_weights)
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -102,8 +102,7 @@ def _natcache_vs_golden(golden_dir, name, via_reference_model):
     from oracle.decoder_ref import OracleDecoder
     g = json.load(open(os.path.join(golden_dir, name)))
     cfg = small_model(g["n_layers"]) if g["n_layers"] != 16 else ModelConfig()
-    w32 = random_weights(cfg, g["weight_seed"], torch.float32, embed_std=g.get("embed_std", 0.02),
-                         **g.get("weight_variant", {}))
+    w32 = variant_weights(cfg, g["weight_seed"], g.get("embed_std", 0.02), g.get("weight_variant"))
     img, txt = request_inputs(cfg, g["input_seed"], g["n_image"], g["n_prompt"], 0, torch.float32)
     assert txt.tolist() == g["prompt_ids"]
     n, bd = g["max_new_tokens"], g["bd"]

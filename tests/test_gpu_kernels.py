@@ -455,7 +455,8 @@ def test_attention_shared_workspace_across_batches():
         torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=1.5e-2)
 
 
-@pytest.mark.parametrize("n_out,k_in,m", [(1536, 2048, 17), (1536, 4608, 17), (1536, 4608, 1088), (1536, 2048, 300)])
+@pytest.mark.parametrize("n_out,k_in,m", [(1536, 2048, 17), (1536, 4608, 17), (1536, 4608, 1088), (1536, 2048, 300),
+                                          (1024, 2048, 33), (2048, 1024, 129)])
 def test_linear_partials_summed_by_residual_norm(n_out, k_in, m):
     """o_proj / down_proj write split-K partials; the residual norm sums them in split order."""
     g = torch.Generator().manual_seed(m + k_in)

@@ -88,7 +88,8 @@ def test_worker_with_grid_positions_commits_the_ar_stream():
     from gravityocr_b200.config import small_model
     from gravityocr_b200.engine import Engine
     cfg = small_model(2)
-    w = random_weights(cfg, 7, torch.bfloat16, embed_std=0.25)
+    # norm weights near one: the stream depends on the positions (checked below)
+    w = random_weights(cfg, 7, torch.bfloat16, norm_center=1.0)
     w32 = {k: v.float() for k, v in w.items()}
     eng = Engine(cfg, w, max_rows=4 * 64, n_pages=8 * 64 + 8)
     target = types.SimpleNamespace(engine=eng, req_to_page=ReqToPagePool(eng, size=8, max_context=1024))

@@ -95,10 +95,11 @@ def test_natcache_restatement_reproduces_reference_config0(golden_dir):
 
 def _natcache_varied(golden_dir, name):
     from gravityocr_b200.config import ModelConfig
-    from gravityocr_b200.weights import prefix_embeddings, random_weights, request_inputs
+    from gravityocr_b200.config import small_model
+    from gravityocr_b200.weights import prefix_embeddings, request_inputs, variant_weights
     g = _load(golden_dir, name)
-    cfg = ModelConfig()
-    w = random_weights(cfg, g["weight_seed"], torch.float32, embed_std=g["embed_std"], **g.get("weight_variant", {}))
+    cfg = small_model(g["n_layers"])
+    w = variant_weights(cfg, g["weight_seed"], g["embed_std"], g.get("weight_variant"))
     img, txt = request_inputs(cfg, g["input_seed"], g["n_image"], g["n_prompt"], 0, torch.float32)
     assert txt.tolist() == g["prompt_ids"]
     return g, OracleDecoder(cfg, w), prefix_embeddings(w, cfg, img, txt)
