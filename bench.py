@@ -392,6 +392,7 @@ def main():
         line["e2e"] = e2e
 
     if rank == 0 and world == 1 and not a.profile_small:
+        line["sampled"] = sampled_rounds(eng, rb, cfg, K, min(a.steps, 10), dev)
         if not a.no_bs1:
             line["bs1"] = bs1_crop(eng, cfg, w, K, dev, hbm_peak)
         if not a.no_cpu:
@@ -407,6 +408,53 @@ def main():
         print(json.dumps(line), flush=True)
     dp.finish()
     return 0
+
+
+def sampled_rounds(eng, rb, cfg, K, steps, dev):
+    """The same batch as a non-plain batch (temperature 0.8, top-p 0.95, top-k 50, repetition 1.1, frequency 0.1):
+    draft, a0 draw, verify, speculative sampling of the verify rows, commit, penalizer cumulation -- device time per
+    round against the greedy round's (eager launches, not graphs, on both sides of the comparison)."""
+    from gravityocr_b200.sampling import RequestSampling, SampledRound, SamplerState
+    bs = rb.bs
+    st = SamplerState(cfg.vocab, rb.seeds.shape[0], dev, seed=SEED)
+    rs = [RequestSampling(temperature=0.8, top_p=0.95, top_k=50, repetition_penalty=1.1, frequency_penalty=0.1)] * bs
+    smp = st.batch(rs, rb.rpi)
+    sr = SampledRound(eng, rb)
+    snap = (rb.seq_lens.clone(), rb.seeds.clone(), rb.n_committed.clone(), rb.rounds.clone())
+
+    def restore():
+        for t, t0 in zip((rb.seq_lens, rb.seeds, rb.n_committed, rb.rounds), snap):
+            t.copy_(t0)
+
+    out = {}
+    for name in ("greedy", "sampled"):
+        restore()
+        for _ in range(2):
+            if name == "greedy":
+                eng.round_launch(rb)
+            else:
+                sr.draft(smp)
+                sr.verify(smp, st.rng)
+        torch.cuda.synchronize()
+        c0 = rb.n_committed.clone()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            if name == "greedy":
+                eng.round_launch(rb)
+            else:
+                sr.draft(smp)
+                sr.verify(smp, st.rng)
+        e1.record()
+        torch.cuda.synchronize()
+        eng.check_status(rb)
+        ms = e0.elapsed_time(e1) / steps
+        toks = int((rb.n_committed - c0).sum())
+        out[name] = {"ms_per_round": round(ms, 4), "tokens_per_s": round(toks / (ms * steps / 1e3), 1),
+                     "tokens_per_forward": round(toks / (2 * steps * bs), 4)}
+    restore()
+    out["params"] = "temperature 0.8, top_p 0.95, top_k 50, repetition 1.1, frequency 0.1 (joint filter), eager launches"
+    return out
 
 
 def e2e_worker(eng, rb, cfg, K, steps, dev, warmup):

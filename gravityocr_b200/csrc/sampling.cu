@@ -145,15 +145,20 @@ __device__ __forceinline__ unsigned long long block_sum64(unsigned long long v, 
 // ---------------------------------------------------------------- keep threshold (radix select)
 // Keep set of the filters: {x : #{y > x} < k and sum{y > x} < lim} (strict) or "<= lim" (non-strict), a prefix of the
 // descending order.  Returns the smallest bit pattern tau such that "bits(e) >= tau" is exactly that set.  Four passes
-// of 8 bits over the row (histograms of count and fixed-point mass per bucket, warp-aggregated shared atomics), each
-// followed by a warp scan of the 256 buckets from the top.
+// of 8 bits over the row: each warp builds a private histogram of count and fixed-point mass per bucket with 32-bit
+// shared atomics (contention stays inside one warp even when a flat distribution puts every entry in one bucket), the
+// 32 histograms are summed per bucket, and warp 0 scans the 256 buckets from the top.
 struct SelectSmem {
+  uint32_t wc[kSampWarps][256];  // per-warp counts
+  uint32_t wl[kSampWarps][256];  // per-warp mass, low 20 bits of each entry's fixed-point value
+  uint32_t wh[kSampWarps][256];  // per-warp mass, the high bits (< 2^20 per entry: at most 2^31 per warp and bucket)
   uint32_t hc[256];
   unsigned long long hs[256];
   uint32_t prefix, tau, done;
   unsigned long long c_above, s_above;
 };
 __device__ uint32_t select_threshold(const float* row, int V, long long k, double lim, bool strict, SelectSmem& sm) {
+  const bool need_c = k < (1ll << 62), need_m = lim < 1e300;  // a criterion that is off needs no histogram
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     sm.prefix = 0;
@@ -165,28 +170,38 @@ __device__ uint32_t select_threshold(const float* row, int V, long long k, doubl
   __syncthreads();
   for (int level = 0; level < 4; ++level) {
     const int shift = 24 - 8 * level;
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
-      sm.hc[i] = 0;
-      sm.hs[i] = 0;
+    for (int i = lane; i < 256; i += 32) {
+      sm.wc[warp][i] = 0;
+      sm.wl[warp][i] = 0;
+      sm.wh[warp][i] = 0;
+    }
+    __syncwarp();
+    const uint32_t prefix = sm.prefix;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) {
+      const float e = row[v];
+      const uint32_t ub = __float_as_uint(e);
+      if (e > 0.f && (level == 0 || (ub >> (shift + 8)) == prefix)) {
+        const uint32_t bin = (ub >> shift) & 255u;
+        if (need_c) atomicAdd(&sm.wc[warp][bin], 1u);
+        if (need_m) {  // two 32-bit halves: 64-bit shared atomics measured slower
+          const uint64_t w = fixed40(e);
+          atomicAdd(&sm.wl[warp][bin], static_cast<uint32_t>(w & 0xFFFFFu));
+          atomicAdd(&sm.wh[warp][bin], static_cast<uint32_t>(w >> 20));
+        }
+      }
     }
     __syncthreads();
-    const uint32_t prefix = sm.prefix;
-    for (int v0 = 0; v0 < V; v0 += blockDim.x) {
-      const int v = v0 + threadIdx.x;
-      const float e = v < V ? row[v] : 0.f;
-      const uint32_t ub = __float_as_uint(e);
-      const bool match = v < V && e > 0.f && (level == 0 || (ub >> (shift + 8)) == prefix);
-      const uint32_t bin = (ub >> shift) & 255u;
-      // lanes of one bucket add up their count and mass (20-bit halves of the <= 2^40 fixed-point values, so the
-      // 32-lane sums fit 32 bits), and one of them updates the shared histogram
-      const unsigned mm = __match_any_sync(0xffffffffu, match ? bin : 256u + lane);
-      const uint64_t w = match ? fixed40(e) : 0ull;
-      const uint32_t lo = __reduce_add_sync(mm, static_cast<uint32_t>(w & 0xFFFFFu));
-      const uint32_t hi = __reduce_add_sync(mm, static_cast<uint32_t>(w >> 20));
-      if (match && lane == __ffs(mm) - 1) {
-        atomicAdd(&sm.hc[bin], static_cast<uint32_t>(__popc(mm)));
-        atomicAdd(&sm.hs[bin], (static_cast<unsigned long long>(hi) << 20) + lo);
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+      uint32_t c = 0;
+      unsigned long long lo = 0, hi = 0;
+#pragma unroll 8
+      for (int q = 0; q < kSampWarps; ++q) {
+        c += sm.wc[q][i];
+        lo += sm.wl[q][i];
+        hi += sm.wh[q][i];
       }
+      sm.hc[i] = c;
+      sm.hs[i] = (hi << 20) + lo;
     }
     __syncthreads();
     if (warp == 0) {
@@ -269,7 +284,8 @@ __device__ uint32_t select_threshold(const float* row, int V, long long k, doubl
 __global__ void __launch_bounds__(kSampThreads, 1) sample_rows_kernel(const SampleParams p) {
   __shared__ float shf[kSampWarps];
   __shared__ unsigned long long shu[kSampWarps];
-  __shared__ SelectSmem sel;
+  extern __shared__ __align__(16) uint8_t dyn_smem[];
+  SelectSmem& sel = *reinterpret_cast<SelectSmem*>(dyn_smem);
   __shared__ unsigned long long scan[kSampWarps];
   __shared__ int found;
   const gr_sampling& s = p.s;
@@ -336,54 +352,50 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_rows_kernel(const Samp
     tau = t1;
     if (mp > 0.f) tau = max(tau, __float_as_uint(mp));
   }
-  // draw pass: each thread sums the kept mass of a contiguous slice (vocabulary order), then an exclusive block scan
-  const int per = (V + kSampThreads - 1) / kSampThreads;
-  const int lo = threadIdx.x * per, hi = min(V, lo + per);
-  uint64_t loc = 0, w_d = 0;
-  for (int v = lo; v < hi; ++v) {
-    const float e = row[v];
-    if (e > 0.f && __float_as_uint(e) >= tau) {
-      const uint64_t w = fixed40(e);
-      loc += w;
-      if (v == d) w_d = w;
-    }
-  }
-  const uint64_t W = block_sum64(loc, shu);
-  // w_d reached every thread through the owner's slice: broadcast it
-  if (d >= 0 && d >= lo && d < hi) shu[0] = w_d;
-  __syncthreads();
-  const uint64_t wd = d >= 0 ? static_cast<uint64_t>(shu[0]) : 0ull;
-  __syncthreads();
-  const bool exclude = d >= 0;
-  const uint64_t mine = loc - ((exclude && d >= lo && d < hi) ? wd : 0ull);
-  // exclusive scan of `mine` over the block (thread order = vocabulary order)
-  uint64_t x = mine;
+  // draw pass: warp w owns the contiguous vocabulary segment [w * seg, (w + 1) * seg), read 32 entries at a time
+  // (coalesced); the block scans the warps' kept mass in vocabulary order, and the warp holding the target walks its
+  // segment again with a warp-wide inclusive scan per 32 entries
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint64_t y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) scan[warp] = x;
+  const int seg = ((V + kSampWarps - 1) / kSampWarps + 31) & ~31;
+  const int lo = warp * seg, hi = min(V, lo + seg);
+  auto kept_w = [&](int v) -> uint64_t {
+    const float e = row[v];
+    return (e > 0.f && __float_as_uint(e) >= tau) ? fixed40(e) : 0ull;
+  };
+  unsigned long long loc = 0;
+  for (int v = lo + lane; v < hi; v += 32) loc += kept_w(v);
+  loc = warp_sum64(loc);
+  const uint64_t wd = (d >= 0) ? kept_w(d) : 0ull;  // the same value every thread reads
+  if (lane == 0) scan[warp] = loc;
   if (threadIdx.x == 0) found = -1;
   __syncthreads();
-  uint64_t before = 0;
-  for (int i = 0; i < warp; ++i) before += scan[i];
-  before += x - mine;
+  uint64_t W = 0, before = 0;
+  for (int i = 0; i < kSampWarps; ++i) {
+    if (i == warp) before = W;
+    W += scan[i];
+  }
+  const bool exclude = d >= 0;
+  const uint64_t mine = loc - ((exclude && d >= lo && d < hi) ? wd : 0ull);
+  const uint64_t before_x = before - ((exclude && d < lo) ? wd : 0ull);
   const uint64_t Wx = W - (exclude ? wd : 0ull);
   const float cf = p.K == 1 ? coin(s.rng, b, 0, p.first_kind) : coin(s.rng, b, 0, GR_COIN_FINAL);
   uint64_t target = static_cast<uint64_t>(static_cast<double>(cf) * static_cast<double>(Wx));
   if (Wx > 0 && target >= Wx) target = Wx - 1;
-  if (Wx > 0 && mine > 0 && target >= before && target < before + mine) {
-    uint64_t c = before;
-    for (int v = lo; v < hi; ++v) {
-      const float e = row[v];
-      if (e > 0.f && __float_as_uint(e) >= tau && v != (exclude ? d : -1)) {
-        c += fixed40(e);
-        if (c > target) {
-          found = v;
-          break;
-        }
+  if (Wx > 0 && mine > 0 && target >= before_x && target < before_x + mine) {
+    uint64_t c = before_x;
+    for (int v0 = lo; v0 < hi; v0 += 32) {
+      const int v = v0 + lane;
+      uint64_t x = (v < hi && v != (exclude ? d : -1)) ? kept_w(v) : 0ull;
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint64_t y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
       }
+      const unsigned hit = __ballot_sync(0xffffffffu, c + x > target);
+      if (hit) {
+        if (lane == __ffs(hit) - 1) found = v;
+        break;
+      }
+      c += __shfl_sync(0xffffffffu, x, 31);
     }
   }
   __syncthreads();
@@ -440,7 +452,13 @@ cudaError_t launch_logits_process(const SampleParams& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 cudaError_t launch_sample_rows(const SampleParams& p, cudaStream_t s) {
-  sample_rows_kernel<<<p.bs * p.K, kSampThreads, 0, s>>>(p);
+  static PerDeviceOnce configured;
+  cudaError_t e = once_per_device(configured, [] {
+    return cudaFuncSetAttribute(sample_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(sizeof(SelectSmem)));
+  });
+  if (e != cudaSuccess) return e;
+  sample_rows_kernel<<<p.bs * p.K, kSampThreads, sizeof(SelectSmem), s>>>(p);
   return cudaGetLastError();
 }
 cudaError_t launch_penalty_cumulate(const SampleParams& p, cudaStream_t s) {
