@@ -392,6 +392,7 @@ def main():
         line["e2e"] = e2e
 
     if rank == 0 and world == 1 and not a.profile_small:
+        line["draining_batch_attention"] = draining_attention(eng, rb, cfg, K, hbm_peak)
         line["sampled"] = sampled_rounds(eng, rb, cfg, K, min(a.steps, 10), dev)
         if not a.no_bs1:
             line["bs1"] = bs1_crop(eng, cfg, w, K, dev, hbm_peak)
@@ -408,6 +409,44 @@ def main():
         print(json.dumps(line), flush=True)
     dp.finish()
     return 0
+
+
+def draining_attention(eng, rb, cfg, K, hbm_peak):
+    """The verify attention of a batch that drains as requests finish: the first bs requests of the workload (their
+    real K/V in the cache, config-3 prefixes) at bs 8, 16 and 32 with the engine's split plan; one layer per launch,
+    rotating layers so each launch reads K/V that is not in L2."""
+    from gravityocr_b200 import _lib as L
+    from gravityocr_b200.engine import attention_split
+    from gravityocr_b200.metrics import attention_bytes
+    out = {}
+    for bs in (8, 16, 32):
+        seq = rb.seq_lens[:bs].contiguous()
+        pt = rb.page_table[:bs].contiguous()
+        S = seq.cpu().tolist()
+        order = torch.argsort(seq, descending=True, stable=True).to(torch.int32)
+        chunk, splits = attention_split(bs, K, max(S), int(sum(S) / bs), cfg.n_kv_heads, eng.sms)
+        ws = torch.zeros((L.attention_workspace_bytes(bs, K, cfg.n_q_heads, cfg.n_kv_heads, splits),),
+                         dtype=torch.uint8, device=eng.device)
+        q = eng.q[: bs * K]
+        o = eng.attn[: bs * K]
+        def launch(l):
+            L.bd_attention(q, eng.pool.k[l], eng.pool.v[l], pt, seq, bs, K, False, 1, cfg.n_q_heads, cfg.n_kv_heads,
+                           16, chunk, splits, o, ws, status=rb.status, order=order)
+        for i in range(3):
+            launch(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(32):
+            launch(i % cfg.n_layers)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / 32 * 1000
+        b = attention_bytes(cfg, S, K, 1)
+        out[f"bs{bs}"] = {"us": round(us, 2), "chunk": chunk, "splits": splits, "gbs": round(b / us / 1e3, 1),
+                          "hbm_frac": round(b / us / 1e3 / hbm_peak, 4)}
+    eng.check_status(rb)
+    return out
 
 
 def sampled_rounds(eng, rb, cfg, K, steps, dev):

@@ -90,18 +90,25 @@ class PagePool:
         return 2 * cfg.n_layers * n_pages * cfg.n_kv_heads * page_size * cfg.head_dim * 2
 
 
+# Split chunk (cache tokens per CTA) by (request, kv head) pairs: measured on a B200 with the config-3 prefix mix
+# (U[256, 4096] + 32) at batch 4-32 and 2,738-token prefixes at batch 1-2, both kernels, chunks 256-4096.  A CTA has a
+# large fixed cost (TMEM allocation, query staging, pipeline fill, the split merge), so fewer, longer splits win until
+# the longest request's chain dominates: e.g. batch 32 takes 55.6 us at 2 splits against 70.6 at 4 and 102 at 12.
+_CHUNK_BY_PAIRS = ((16, 640), (64, 1024), (192, 1536))
+
+
 def attention_split(bs: int, K: int, max_len: int, avg_len: int, n_kv: int, sms: int) -> Tuple[int, int]:
     """Cache tokens per split and the split-grid extent.  With enough (request, head) pairs to fill the GPU twice the
-    requests run unsplit (no merge); otherwise each pair is cut into splits of >= 128 tokens so that about 2 x SMs
-    CTAs stream in parallel.  A small batch's splits merge inside one thread-block cluster, so there are at most 8
-    (a portable cluster); larger batches allow up to 16 (the global merge's limit)."""
+    requests run unsplit (no merge); below that the chunk grows with the number of pairs (_CHUNK_BY_PAIRS, then 2048
+    tokens), never so small that a request needs more splits than the merges take: 8 while the grid stays within one
+    CTA per SM (those splits merge inside one portable thread-block cluster), 16 otherwise.  avg_len is accepted for
+    callers that plan by the mean length; the measured plan depends on the pair count and the longest request."""
     L = max_len + K + 1
     units = max(1, bs * n_kv)
     if units >= 2 * sms:
         chunk = 4096
     else:
-        want = min(16, -(-2 * sms // units))
-        chunk = max(128, -(-max(1, avg_len) // want))
+        chunk = next((c for lim, c in _CHUNK_BY_PAIRS if units <= lim), 2048)
     chunk = max(chunk, -(-L // (8 if units < 2 * sms else 16)))
     chunk = min(4096, -(-chunk // 64) * 64)
     return chunk, max(1, -(-L // chunk))
