@@ -37,7 +37,7 @@ K_BD = 16
 SEED = 3
 # DRAM bytes / algorithmic bytes of one verify attention launch (attention_tc_kernel) on the config-3 mix:
 # dram__bytes_read.sum + dram__bytes_write.sum of an ncu capture of that launch over its algorithmic bytes
-ATTN_TRAFFIC_RATIO = (584.648704e6 + 6.316288e6) / 586.93632e6
+ATTN_TRAFFIC_RATIO = (584.61e6 + 6.20e6) / 586.94e6
 
 
 def _args():
@@ -648,7 +648,7 @@ def config4_sweep(a):
     rank, world, local = dp.dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    hbm_peak, _, peak_src = peaks()
+    hbm_peak, _, _, peak_src = peaks()
     cfg = ModelConfig()
     w = random_weights(cfg, 4, torch.bfloat16)
     P = 4096 + 64
@@ -701,5 +701,195 @@ def config4_sweep(a):
     return 0
 
 
+# ---------------------------------------------------------------------------------------------------------------------
+# Single-kernel cases for ncu captures: `python bench.py case attention|linear|sample ...`.  Each is a small,
+# self-contained workload (a few GB on the device at most, inputs larger than L2): one untimed warm-up launch, then
+# `--reps` launches; prints the mean CUDA-event time and the algorithmic bytes / FLOPs of one launch.  Example:
+#
+#     python bench.py case attention --bs 64 --mixed --reps 2
+#     ncu --set full --clock-control none -k regex:attention_tc -s 1 -c 1 -o prof \
+#         python bench.py case attention --bs 64 --mixed --reps 2
+# ---------------------------------------------------------------------------------------------------------------------
+
+def _case_time(fn, reps, graph):
+    fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if graph:
+        s = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(reps):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        e0.record()
+        g.replay()
+        e1.record()
+    else:
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def case_attention(a):
+    """One attention launch over a paged cache: --seq tokens per request, or the config-3 prefix mix (--mixed)."""
+    from gravityocr_b200 import _lib as L
+    from gravityocr_b200.config import ModelConfig
+    from gravityocr_b200.engine import attention_split
+    from gravityocr_b200.metrics import attention_bytes
+    cfg = ModelConfig()
+    bs, K = a.bs, a.bd + 1
+    g = torch.Generator().manual_seed(1)
+    nq, nkv, D, ps = cfg.n_q_heads, cfg.n_kv_heads, cfg.head_dim, 16
+    if a.mixed:
+        S = (torch.randint(256, 4097, (bs,), generator=torch.Generator().manual_seed(SEED)) + 32).tolist()
+    else:
+        S = [a.seq] * bs
+    seq_max = max(S)
+    ppr = (seq_max + K + 2 + ps - 1) // ps
+    n_pages = bs * ppr
+    kc = torch.randn((n_pages, nkv, ps, D), generator=g).to("cuda", torch.bfloat16)
+    vc = torch.randn((n_pages, nkv, ps, D), generator=g).to("cuda", torch.bfloat16)
+    pt = torch.randperm(n_pages, generator=g).to(torch.int32).view(bs, ppr).cuda()
+    seq = torch.tensor(S, dtype=torch.int64, device="cuda")
+    q = torch.randn((bs * K, nq, D), generator=g).to("cuda", torch.bfloat16)
+    out = torch.empty_like(q)
+    chunk, splits = attention_split(bs, K, seq_max, sum(S) // len(S), nkv, L.num_sms())
+    if a.chunk:
+        chunk, splits = a.chunk, int(math.ceil((seq_max + K + 1) / a.chunk))
+    ws = torch.zeros((L.attention_workspace_bytes(bs, K, nq, nkv, splits),), dtype=torch.uint8, device="cuda")
+    order = torch.argsort(seq, descending=True, stable=True).to(torch.int32) if a.mixed else None
+    base_add = 0 if a.draft else 1
+    fn = lambda: L.bd_attention(q, kc, vc, pt, seq, bs, K, a.draft, base_add, nq, nkv, ps, chunk, splits, out, ws,
+                                order=order)
+    L.set_attention_tc(0 if a.mma else (2 if a.tc_all else 1))
+    ms = _case_time(fn, a.reps, a.graph)
+    b = attention_bytes(cfg, S, K, base_add)
+    tc = not a.mma and nq // nkv * K <= 128 and (a.tc_all or bs * nkv * splits > L.num_sms())
+    return {"kernel": "attention_tc_kernel" if tc else "attention_kernel", "bs": bs,
+            "seq": "mixed" if a.mixed else a.seq, "K": K, "chunk": chunk, "splits": splits, "ms": ms, "bytes": b,
+            "GBps": b / ms / 1e6}
+
+
+def case_linear(a):
+    """One projection launch: an [n_out, k_in] bf16 weight against m token rows with the chosen epilogue."""
+    from gravityocr_b200 import _lib as L
+    from gravityocr_b200.config import ModelConfig
+    from gravityocr_b200.engine import rope_inv_freq
+    cfg = ModelConfig()
+    n_out, k_in, m = a.n_out, a.k_in, a.m
+    g = torch.Generator().manual_seed(2)
+    w = (torch.randn((n_out, k_in), generator=g) * 0.02).to("cuda", torch.bfloat16)
+    x = torch.randn((m, k_in), generator=g).to("cuda", torch.bfloat16)
+    mode = {"f32": L.EPI_STORE_F32, "partial": L.EPI_PARTIAL_F32, "swiglu": L.EPI_SWIGLU, "argmax": L.EPI_ARGMAX,
+            "qkv": L.EPI_QKV_ROPE}[a.epi]
+    sp = a.splits or L.linear_default_splits(n_out, k_in, m)
+    e = L.Epilogue()
+    e.mode = mode
+    keep = []
+    if mode in (L.EPI_STORE_F32, L.EPI_PARTIAL_F32):
+        out = torch.zeros(((sp if mode == L.EPI_PARTIAL_F32 else 1) * m, n_out), device="cuda")
+        e.out, e.ld_out = out.data_ptr(), n_out
+        keep.append(out)
+    elif mode == L.EPI_SWIGLU:
+        out = torch.zeros((m, n_out // 2), dtype=torch.bfloat16, device="cuda")
+        e.out, e.ld_out = out.data_ptr(), n_out // 2
+        keep.append(out)
+    elif mode == L.EPI_ARGMAX:
+        idx = torch.zeros((m,), dtype=torch.int32, device="cuda")
+        e.out_idx = idx.data_ptr()
+        keep.append(idx)
+    else:
+        q = torch.zeros((m, cfg.q_dim), dtype=torch.bfloat16, device="cuda")
+        kc = torch.zeros((m // 16 + 2, cfg.n_kv_heads, 16, 128), dtype=torch.bfloat16, device="cuda")
+        vc = torch.zeros_like(kc)
+        pos = torch.arange(m, dtype=torch.int32, device="cuda")
+        slot = torch.arange(m, dtype=torch.int64, device="cuda")
+        inv = rope_inv_freq(cfg).cuda()
+        e.q_out, e.k_cache, e.v_cache = q.data_ptr(), kc.data_ptr(), vc.data_ptr()
+        e.row_pos, e.row_slot, e.inv_freq = pos.data_ptr(), slot.data_ptr(), inv.data_ptr()
+        e.rotary_dim, e.n_q_heads, e.n_kv_heads, e.page_size = cfg.rotary_dim, cfg.n_q_heads, cfg.n_kv_heads, 16
+        keep += [q, kc, vc, pos, slot, inv]
+    ws_sp = 1 if mode == L.EPI_PARTIAL_F32 else sp
+    ws = torch.zeros((L.linear_workspace_bytes(n_out, m, ws_sp),), dtype=torch.uint8, device="cuda")
+    ms = _case_time(lambda: L.linear(w, x, m, e, ws, splits=sp), a.reps, a.graph)
+    fl = 2 * n_out * k_in * m
+    return {"kernel": "linear_kernel", "epi": a.epi, "n_out": n_out, "k_in": k_in, "m": m, "splits": sp, "ms": ms,
+            "weight_GBps": n_out * k_in * 2 / ms / 1e6, "TFLOPs": fl / ms / 1e9}
+
+
+def case_sample(a):
+    """One sample_rows launch over bs x K verify rows of fp32 logits (vocabulary 59,392): temperature 0.8, top-k 50,
+    top-p 0.95 under the joint filter (or --filter), accept bits against seeded draft tokens and the draws."""
+    from gravityocr_b200 import _lib as L
+    from gravityocr_b200.config import ModelConfig
+    from gravityocr_b200.sampling import RequestSampling, SamplerState
+    cfg = ModelConfig()
+    bs, K, V = a.bs, a.bd + 1, cfg.vocab
+    g = torch.Generator().manual_seed(5)
+    logits = (torch.randn((bs * K, V), generator=g) * a.scale).cuda()
+    cand = torch.randint(0, V, (bs * K,), generator=g).to("cuda", torch.int32)
+    rpi = torch.arange(bs, dtype=torch.int64, device="cuda")
+    flt = {"joint": L.FILTER_JOINT, "sequential": L.FILTER_SEQUENTIAL, "torch": L.FILTER_TORCH}[a.filter]
+    st = SamplerState(V, bs, "cuda", seed=SEED, filter=flt)
+    rs = [RequestSampling(temperature=0.8, top_k=a.top_k, top_p=a.top_p, min_p=a.min_p)] * bs
+    smp = st.batch(rs, rpi)
+    accept = torch.zeros((bs * K,), dtype=torch.int32, device="cuda")
+    sample = torch.zeros((bs * K,), dtype=torch.int32, device="cuda")
+    p_next = torch.zeros((bs * K,), dtype=torch.float32, device="cuda")
+    status = torch.zeros((1,), dtype=torch.int32, device="cuda")
+    work = logits.clone()
+
+    def fn():   # the kernel scales its rows in place, so each launch starts from a fresh copy
+        work.copy_(logits)
+        L.sample_rows(work, bs, K, cand, smp, L.COIN_FIRST, accept, sample, p_next, status=status)
+    ms = _case_time(fn, a.reps, a.graph)
+    assert int(status.item()) == 0
+    return {"kernel": "sample_rows_kernel", "rows": bs * K, "vocab": V, "filter": a.filter, "top_k": a.top_k,
+            "top_p": a.top_p, "ms_with_copy": ms, "logit_bytes": bs * K * V * 4}
+
+
+def case_main(argv):
+    ap = argparse.ArgumentParser(prog="bench.py case")
+    ap.add_argument("--graph", action="store_true", help="time launches captured in one CUDA graph")
+    sub = ap.add_subparsers(dest="case", required=True)
+    at = sub.add_parser("attention")
+    at.add_argument("--bs", type=int, default=16)
+    at.add_argument("--seq", type=int, default=2048)
+    at.add_argument("--bd", type=int, default=K_BD)
+    at.add_argument("--draft", action="store_true")
+    at.add_argument("--chunk", type=int, default=0)
+    at.add_argument("--mixed", action="store_true", help="config-3 prefix lengths instead of --seq")
+    at.add_argument("--mma", action="store_true", help="every grid on the mma.sync kernel")
+    at.add_argument("--tc-all", action="store_true", help="every grid on the tcgen05 kernel (small grids included)")
+    at.add_argument("--reps", type=int, default=3)
+    li = sub.add_parser("linear")
+    li.add_argument("--n-out", type=int, default=9216)
+    li.add_argument("--k-in", type=int, default=1536)
+    li.add_argument("--m", type=int, default=17)
+    li.add_argument("--epi", default="swiglu", choices=["f32", "partial", "swiglu", "argmax", "qkv"])
+    li.add_argument("--splits", type=int, default=0)
+    li.add_argument("--reps", type=int, default=3)
+    sa = sub.add_parser("sample")
+    sa.add_argument("--bs", type=int, default=64)
+    sa.add_argument("--bd", type=int, default=K_BD)
+    sa.add_argument("--filter", default="joint", choices=["joint", "sequential", "torch"])
+    sa.add_argument("--top-k", type=int, default=50)
+    sa.add_argument("--top-p", type=float, default=0.95)
+    sa.add_argument("--min-p", type=float, default=0.0)
+    sa.add_argument("--scale", type=float, default=3.0, help="std of the synthetic logits")
+    sa.add_argument("--reps", type=int, default=3)
+    a = ap.parse_args(argv)
+    fn = {"attention": case_attention, "linear": case_linear, "sample": case_sample}[a.case]
+    print(json.dumps(fn(a)), flush=True)
+    return 0
+
+
 if __name__ == "__main__":
+    if len(sys.argv) > 1 and sys.argv[1] == "case":
+        sys.exit(case_main(sys.argv[2:]))
     sys.exit(main())

@@ -101,12 +101,15 @@ def attention_split(bs: int, K: int, max_len: int, avg_len: int, n_kv: int, sms:
     """Cache tokens per split and the split-grid extent.  With enough (request, head) pairs to fill the GPU twice the
     requests run unsplit (no merge); below that the chunk grows with the number of pairs (_CHUNK_BY_PAIRS, then 2048
     tokens), never so small that a request needs more splits than the merges take: 8 while the grid stays within one
-    CTA per SM (those splits merge inside one portable thread-block cluster), 16 otherwise.  avg_len is accepted for
-    callers that plan by the mean length; the measured plan depends on the pair count and the longest request."""
+    CTA per SM (those splits merge inside one portable thread-block cluster), 16 otherwise.  A single request keeps a
+    finer cut (about 16 splits of its length, capped at 8 by the cluster), which measured fastest inside its
+    forward."""
     L = max_len + K + 1
     units = max(1, bs * n_kv)
     if units >= 2 * sms:
         chunk = 4096
+    elif bs == 1:
+        chunk = max(128, -(-max(1, avg_len) // 16))
     else:
         chunk = next((c for lim, c in _CHUNK_BY_PAIRS if units <= lim), 2048)
     chunk = max(chunk, -(-L // (8 if units < 2 * sms else 16)))

@@ -80,7 +80,9 @@ class RequestSampling:
 
 
 class SamplerState:
-    """Penalizer state by request pool slot, the coins' rng and the per-batch buffers of one engine."""
+    """Penalizer state by request pool slot, the coins' rng and the per-batch buffers of one engine.  `filter` names
+    the sampling backend: FILTER_JOINT for flashinfer (a batch with min-p then takes FILTER_SEQUENTIAL, as SGLang's
+    flashinfer path does), FILTER_TORCH for the "pytorch" backend."""
 
     def __init__(self, vocab: int, pool_size: int, device, seed: int = 0, filter: int = L.FILTER_JOINT,
                  order: Sequence[int] = DEFAULT_ORDER):
@@ -139,7 +141,10 @@ class SamplerState:
         order = [op for op in self.order if used[op]]
         s = L.Sampling()
         s.vocab = self.vocab
-        s.filter = self.filter
+        # the flashinfer backend switches to renorm-then-min-p as soon as one request of the batch uses min-p
+        # (verify_target_probs, selfspec_sampling.py:278-282)
+        s.filter = L.FILTER_SEQUENTIAL if self.filter == L.FILTER_JOINT and any(r.min_p > 0 for r in reqs) \
+            else self.filter
         for k, v in arrays.items():
             setattr(s, k, v.data_ptr())
         s.n_order = len(order)
