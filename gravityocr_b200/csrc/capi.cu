@@ -88,6 +88,7 @@ static int num_sms() {
 
 struct LinearShape {
   int nt, m_tiles, n_tiles, kc;
+  bool tail_last;  // a shorter last token tile's units run after all full tiles' (snake assignment)
 };
 static int round16(int x) { return ((x + 15) / 16) * 16; }
 
@@ -106,45 +107,145 @@ static void linear_launch_shape(int nt, int kc, int epi, int* stages, int* ctas_
   *ctas_per_sm = by_smem < by_tmem ? (by_smem < 1 ? 1 : by_smem) : by_tmem;
 }
 
-// Candidate token tilings of m rows: tile counts from the fewest whose tile fits one MMA (nt <= GR_MAX_NT) up to 4x
-// that; tiles narrower than 128 tokens only where the rows need no more (small batches stream weights: a second token
-// tile would read every weight tile twice).  Calls f(m_tiles, nt) for each; f returns false to stop.
+// Candidate token tilings of m rows, widest tile first within each kind:
+//  * balanced: mt tiles of round16(m / mt) rows, from the fewest tiles whose tile fits one MMA (nt <= GR_MAX_NT) up
+//    to 4x that; tiles narrower than 128 tokens only where the rows need no more (small batches stream weights: a
+//    second token tile would read every weight tile twice);
+//  * ragged: tiles of nt >= 128 rows and a shorter last tile, whose units run at MMA N = its rows.
+// At most kMaxTiles (feature tile, token tile) pairs.  Calls f(m_tiles, nt) for each.
+constexpr size_t kMaxTiles = 16384;  // feature tiles x token tiles of one call (lm_head at 8192 rows)
 template <class F>
-static void for_token_tilings(int m, F f) {
+static void for_token_tilings(int m, int n_tiles, F f) {
   const int min_tiles = (m + GR_MAX_NT - 1) / GR_MAX_NT;
+  int bal_nt[4 * 64 + 8];
+  int n_bal = 0;
   for (int mt = min_tiles; mt <= min_tiles * 4 && mt <= m; ++mt) {
     int nt = round16((m + mt - 1) / mt);
     if (mt > min_tiles && nt < 128) break;
     if (nt < 16) nt = 16;
-    if (!f(mt, nt)) break;
+    if (static_cast<size_t>(mt) * n_tiles > kMaxTiles) continue;
+    if (n_bal < static_cast<int>(sizeof(bal_nt) / sizeof(int))) bal_nt[n_bal++] = mt * 1024 + nt;
+    f(mt, nt);
+  }
+  for (int nt = GR_MAX_NT; nt >= 128; nt -= 16) {
+    const int mt = (m + nt - 1) / nt;
+    if (mt == 1 || mt > 4 * min_tiles || static_cast<size_t>(mt) * n_tiles > kMaxTiles) continue;
+    bool seen = false;
+    for (int i = 0; i < n_bal; ++i) seen |= bal_nt[i] == mt * 1024 + nt;
+    if (!seen) f(mt, nt);
   }
 }
 
-// Token tiling for a split-K count `sp`: the candidate minimising the persistent schedule's critical path,
-// (units per CTA, rounded up) x (K chunks per unit) x (per-chunk cost ~ 128 + nt: the 128-row weight tile and the
-// nt-row token tile both pass through shared memory).  The cost goes to *cost_out.
+// Whether a call may number a shorter last token tile's units after all full tiles': only where the weights stay in
+// L2 (otherwise that tile's pass would stream every weight tile from DRAM a second time).
+static bool tail_last_allowed(int n_out, int k_in) {
+  return static_cast<size_t>(n_out) * k_in * 2 <= (48u << 20);
+}
+
+// Output bytes per (row, feature) of an epilogue, for the cost model.
+static int epi_out_bytes(int epi) {
+  switch (epi) {
+    case GR_EPI_STORE_F32: case GR_EPI_PARTIAL_F32: return 4;
+    case GR_EPI_SWIGLU: return 1;
+    case GR_EPI_RESIDUAL_NORM: return 22;  // y staged, read back twice; h_in read; h written; x written
+    default: return 2;
+  }
+}
+
+// Critical path of the persistent schedule, in shared-memory cycles (~128 bytes each), as the kernel walks it: CTA c
+// takes unit k * grid + c in wave k (with tail_last: grid - 1 - c in odd waves, and the short tile's units last).
+// A unit costs a fixed kUnitCost (pipeline turn-around, accumulator hand-off) plus its main loop, (K chunks) x
+// (128 + N) -- the 128-row weight tile and the N-row token tile both pass through shared memory, N = nt or the
+// rounded rows of a shorter last tile; its epilogue the bytes it stores at ~64 bytes per cycle, plus, for a
+// split-K unit that finishes its tile, its own fp32 partial and the reads of all splits' partials.  An epilogue
+// overlaps the CTA's next main loop (double-buffered accumulators); the last one does not.  The maximum over CTAs.
+// kUnitCost and the epilogue rate were fitted to B200 timings of the decoder's projections at 17-4,224 rows.
+constexpr long long kUnitCost = 1024;
+static long long schedule_cost(int n_tiles, int mt, int nt, int m, int sp, int kc, long long cap, int epi,
+                               bool tail_last) {
+  const int full_m = (m % nt == 0) ? mt : mt - 1;
+  const long long full_units = static_cast<long long>(full_m) * sp * n_tiles;
+  const long long units = static_cast<long long>(mt) * sp * n_tiles;
+  const int last_rows = m - (mt - 1) * nt;
+  const bool split_epi = sp > 1 && epi != GR_EPI_PARTIAL_F32;
+  auto main_cost = [&](bool last) {
+    return kUnitCost + static_cast<long long>(kc) * (128 + (last ? round16(last_rows) : nt));
+  };
+  auto epi_cost = [&](bool last) {
+    const long long rows = last ? last_rows : nt;
+    long long c = rows * 128 * epi_out_bytes(epi) / 64;
+    if (split_epi) c += rows * 128 * 4 * (1 + sp) / 64;
+    return c;
+  };
+  const long long G = units < cap ? units : cap;
+  const long long waves = (units + G - 1) / G;
+  long long worst = 0;
+  for (long long c = 0; c < G; ++c) {
+    long long t = 0, prev_epi = 0;
+    for (long long w = 0; w < waves; ++w) {
+      const long long u = w * G + ((tail_last && (w & 1)) ? G - 1 - c : c);
+      if (u >= units) continue;
+      const bool last = tail_last ? u >= full_units : (full_m < mt && u % mt == mt - 1);
+      const long long mc = main_cost(last);
+      t += mc > prev_epi ? mc : prev_epi;
+      prev_epi = epi_cost(last);
+    }
+    t += prev_epi;
+    if (t > worst) worst = t;
+  }
+  return worst;
+}
+
+// Token tiling for a split-K count `sp`: the candidate with the shortest critical path (ties: the first candidate).
+// Memoised per shape: the schedule walk is O(units).  The cost goes to *cost_out.
 static LinearShape linear_shape(int n_out, int k_in, int m, int sp = 1, int epi = GR_EPI_STORE_F32,
                                 long long* cost_out = nullptr) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int, int, int>, std::pair<LinearShape, long long>> memo;
+  const auto key = std::make_tuple(n_out, k_in, m, sp, epi, num_sms());
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = memo.find(key);
+    if (it != memo.end()) {
+      if (cost_out) *cost_out = it->second.second;
+      return it->second.first;
+    }
+  }
   LinearShape s;
   s.n_tiles = n_out / 128;
   s.kc = k_in / 64;
+  s.m_tiles = 1;
+  s.nt = round16(m < GR_MAX_NT ? m : GR_MAX_NT);
+  s.tail_last = false;
   const int kc = s.kc / sp;
+  const bool tail_ok = tail_last_allowed(n_out, k_in);
   long long best = -1;
-  for_token_tilings(m, [&](int mt, int nt) {
+  for_token_tilings(m, s.n_tiles, [&](int mt, int nt) {
     // resident CTAs as for the full K depth (the deep ring): shallow split rings admit more CTAs per SM, which the
     // measurements do not reward
     int stages, per_sm;
     linear_launch_shape(nt, s.kc, epi, &stages, &per_sm);
     const long long cap = static_cast<long long>(num_sms()) * per_sm;
-    const long long units = static_cast<long long>(s.n_tiles) * mt * sp;
-    const long long cost = ((units + cap - 1) / cap) * kc * (128 + nt);
+    long long cost = schedule_cost(s.n_tiles, mt, nt, m, sp, kc, cap, epi, false);
+    bool tl = false;
+    if (tail_ok && m % nt) {  // the short tile last, only where that shortens the critical path
+      const long long c2 = schedule_cost(s.n_tiles, mt, nt, m, sp, kc, cap, epi, true);
+      if (c2 < cost) {
+        cost = c2;
+        tl = true;
+      }
+    }
     if (best < 0 || cost < best) {
       best = cost;
       s.m_tiles = mt;
       s.nt = nt;
+      s.tail_last = tl;
     }
-    return units < cap * 4;
   });
+  {
+    std::lock_guard<std::mutex> g(mu);
+    memo.emplace(key, std::make_pair(s, best));
+  }
   if (cost_out) *cost_out = best;
   return s;
 }
@@ -152,18 +253,32 @@ static LinearShape linear_shape(int n_out, int k_in, int m, int sp = 1, int epi 
 // Split-K count, chosen together with the token tiling: the cost above minimised over the split counts that divide
 // the K chunks (at most half of them) and whose fp32 partials stay a small, L2-resident fraction of the traffic;
 // ties go to fewer splits (less partial traffic).  The argmax epilogue runs unsplit.
+// Whether every CTA of the persistent grid owns at most one unit (all units resident at once), as the fused
+// residual norm's counter barriers require.
+static bool one_unit_per_cta(const LinearShape& s, int sp, int epi) {
+  int stages, per_sm;
+  linear_launch_shape(s.nt, s.kc / sp, epi, &stages, &per_sm);
+  return static_cast<long long>(s.n_tiles) * s.m_tiles * sp <= static_cast<long long>(num_sms()) * per_sm &&
+         s.m_tiles <= kMaxBarTiles;
+}
+
+// Split-K count, chosen together with the token tiling: the cost above minimised over the split counts that divide
+// the K chunks (at most half of them) and whose fp32 partials stay a small, L2-resident fraction of the traffic;
+// ties go to fewer splits (less partial traffic).  The argmax epilogue runs unsplit; the fused residual norm only
+// with one unit per CTA (0: no split count fits).
 static int default_splits(int n_out, int k_in, int m, int epi) {
   if (epi == GR_EPI_ARGMAX) return 1;
+  const bool one_unit = epi == GR_EPI_RESIDUAL_NORM;
   const int kc = k_in / 64;
-  long long best_cost = 0;
-  linear_shape(n_out, k_in, m, 1, epi, &best_cost);
-  int best = 1;
-  for (int sp = 2; sp <= kc / 2; ++sp) {
+  long long best_cost = -1;
+  int best = one_unit ? 0 : 1;
+  for (int sp = 1; sp <= (kc / 2 > 1 ? kc / 2 : 1); ++sp) {
     if (kc % sp) continue;
-    if (static_cast<double>(sp) * m * (n_out / 128) * 128 * 4 > 32.0 * (1 << 20)) break;
+    if (sp > 1 && static_cast<double>(sp) * m * (n_out / 128) * 128 * 4 > 32.0 * (1 << 20)) break;
     long long cost = 0;
-    linear_shape(n_out, k_in, m, sp, epi, &cost);
-    if (cost < best_cost) {
+    const LinearShape s = linear_shape(n_out, k_in, m, sp, epi, &cost);
+    if (one_unit && !one_unit_per_cta(s, sp, epi)) continue;
+    if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       best = sp;
     }
@@ -181,8 +296,8 @@ static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // Every call shares one scratch buffer, whatever its shape: the tickets live in a fixed region at its head (so a
 // later call of another shape never finds another call's partial sums where its tickets are), then the fp32
 // split-K partials, then the per-(token, feature tile) argmax records.
-constexpr size_t kMaxTiles = 16384;  // feature tiles x token tiles of one call (lm_head at 8192 rows)
-constexpr size_t kTicketBytes = kMaxTiles * sizeof(int);
+// tile tickets, then the fused residual norm's three arrival counters per token tile
+constexpr size_t kTicketBytes = (kMaxTiles + 3 * kMaxBarTiles) * sizeof(int);
 static LinearWs linear_ws_layout(void* base, const LinearShape& s, int m, int splits) {
   LinearWs w;
   uint8_t* p = static_cast<uint8_t*>(base);
@@ -233,12 +348,17 @@ int gr_linear_default_splits(int n_out, int k_in, int m) {
   return default_splits(n_out, k_in, m, GR_EPI_STORE_F32);
 }
 
+int gr_linear_residual_norm_splits(int n_out, int k_in, int m) {
+  if (n_out <= 0 || (n_out % 128) || k_in <= 0 || (k_in % 64) || m <= 0) return 0;
+  return default_splits(n_out, k_in, m, GR_EPI_RESIDUAL_NORM);
+}
+
 size_t gr_linear_workspace_bytes(int n_out, int m, int splits) {
   if (n_out <= 0 || m <= 0) return 0;
   if (splits < 1) splits = 1;
   // the largest layout over every token tiling a call of this shape may use (the tiling also depends on K)
   size_t bytes = 0;
-  for_token_tilings(m, [&](int mt, int nt) {
+  for_token_tilings(m, n_out / 128, [&](int mt, int nt) {
     LinearShape s;
     s.n_tiles = n_out / 128;
     s.kc = 1;
@@ -246,7 +366,6 @@ size_t gr_linear_workspace_bytes(int n_out, int m, int splits) {
     s.nt = nt;
     const size_t b = linear_ws_layout(nullptr, s, m, splits).bytes;
     if (b > bytes) bytes = b;
-    return true;
   });
   return bytes;
 }
@@ -262,8 +381,9 @@ static int build_linear(const void* w, int n_out, int k_in, const void* x, int m
                         void* workspace, size_t workspace_bytes, const void* prefetch, size_t prefetch_bytes,
                         int32_t* status, LinearLaunch* out) {
   if (!w || !x || !epi || m <= 0 || n_out <= 0 || (n_out % 128) || k_in <= 0 || (k_in % 64)) return GR_ERR_ARG;
-  if (epi->mode < GR_EPI_STORE_F32 || epi->mode > GR_EPI_PARTIAL_F32) return GR_ERR_ARG;
+  if (epi->mode < GR_EPI_STORE_F32 || epi->mode > GR_EPI_RESIDUAL_NORM) return GR_ERR_ARG;
   if (splits <= 0) splits = default_splits(n_out, k_in, m, epi->mode);
+  if (splits <= 0) return GR_ERR_UNSUPPORTED;  // no split count fits the fused residual norm
   if ((k_in / 64) % splits) return GR_ERR_ARG;
   LinearShape s = linear_shape(n_out, k_in, m, splits, epi->mode);
   const size_t ws_splits = epi->mode == GR_EPI_PARTIAL_F32 ? 1 : static_cast<size_t>(splits);
@@ -281,6 +401,11 @@ static int build_linear(const void* w, int n_out, int k_in, const void* x, int m
       return GR_ERR_ARG;
   } else if (epi->mode == GR_EPI_ARGMAX) {
     if (!epi->out_idx) return GR_ERR_ARG;
+  } else if (epi->mode == GR_EPI_RESIDUAL_NORM) {
+    if (!epi->h_in || !epi->h_out || !epi->x_out || !epi->norm_a || !epi->norm_b || epi->h_in == epi->h_out ||
+        !(epi->eps >= 0.f))
+      return GR_ERR_ARG;
+    if (!one_unit_per_cta(s, splits, epi->mode)) return GR_ERR_UNSUPPORTED;
   } else if (!epi->out || epi->ld_out <= 0) {
     return GR_ERR_ARG;
   }
@@ -308,6 +433,7 @@ static int build_linear(const void* w, int n_out, int k_in, const void* x, int m
   p.m = m;
   p.nt = s.nt;
   p.m_tiles = s.m_tiles;
+  p.tail_last = s.tail_last ? 1 : 0;
   p.n_tiles = s.n_tiles;
   p.splits = splits;
   p.kc_per_split = kc;
@@ -333,6 +459,16 @@ static int build_linear(const void* w, int n_out, int k_in, const void* x, int m
   p.ws_partial = ws.partial;
   p.ws_ticket = ws.ticket;
   p.ws_arg = ws.arg;
+  p.ws_ss = reinterpret_cast<float*>(ws.arg);  // RESIDUAL_NORM: [2][n_tiles][m] floats fit the records' region
+  p.ws_bar = ws.ticket + kMaxTiles;
+  if (epi->mode == GR_EPI_RESIDUAL_NORM) {
+    p.h_in = epi->h_in;
+    p.h_out = epi->h_out;
+    p.x_out = static_cast<__nv_bfloat16*>(epi->x_out);
+    p.norm_a = static_cast<const __nv_bfloat16*>(epi->norm_a);
+    p.norm_b = static_cast<const __nv_bfloat16*>(epi->norm_b);
+    p.eps = epi->eps;
+  }
   p.prefetch = static_cast<const uint8_t*>(prefetch);
   p.prefetch_bytes = prefetch ? prefetch_bytes : 0;
   p.status = status;

@@ -37,9 +37,12 @@ template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
                   const LinearParams p) {
-  // Persistent: CTA c processes units c, c + gridDim.x, ...  The producer and the MMA issuer walk the same global
-  // sequence of (unit, K chunk) through one S-stage ring, so the next unit's weights stream while the current unit's
-  // epilogue runs; the accumulator is double-buffered in TMEM (acc_full / acc_empty per buffer).
+  // Persistent: CTA c processes one unit per wave k, unit k * grid + c.  With tail_last (chosen by the host's
+  // schedule model) the units of full token tiles are numbered before those of a shorter last tile and odd waves run
+  // in reverse (unit k * grid + grid - 1 - c), so the short units land on the CTAs whose earlier units were short.
+  // The producer and the MMA issuer walk the same sequence of (unit, K chunk) through one S-stage ring, so the next
+  // unit's weights stream while the current unit's epilogue runs; the accumulator is double-buffered in TMEM
+  // (acc_full / acc_empty per buffer).
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = p.stages;
@@ -57,7 +60,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kc = p.kc_per_split;
   const int n_units = p.n_tiles * p.m_tiles * p.splits;
-  const int n_my = blockIdx.x < n_units ? (n_units - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  const int G = gridDim.x, waves = n_units / G, rem = n_units % G;
+  const int n_my = waves + ((rem > 0 && ((p.tail_last && (waves & 1)) ? (int)blockIdx.x >= G - rem
+                                                                        : (int)blockIdx.x < rem)) ? 1 : 0);
+  auto unit_of = [&](int k) { return k * G + ((p.tail_last && (k & 1)) ? G - 1 - (int)blockIdx.x : (int)blockIdx.x); };
+  // token tiles 0 .. full_m - 1 hold nt rows; a shorter last tile runs its MMAs at N = its rows (rounded to 16)
+  const int full_m = (p.m % p.nt == 0 || !p.tail_last) ? p.m_tiles : p.m_tiles - 1;
+  const int full_units = full_m * p.splits * p.n_tiles;
   const uint32_t acc_cols = p.nt <= 32 ? 32u : (p.nt <= 64 ? 64u : (p.nt <= 128 ? 128u : 256u));
   const uint32_t tmem_cols = 2 * acc_cols;
 
@@ -90,10 +99,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   pdl_trigger();
 
-  // unit u -> (m_tile fastest, then split, then n_tile): the token tiles of one weight slab run side by side (L2 reuse)
+  // unit u -> (m_tile fastest, then split, then n_tile): the token tiles of one weight slab run side by side (L2
+  // reuse); with tail_last the units of a shorter last token tile come after all full ones
   auto decode = [&](int u, int& m_tile, int& split, int& n_tile) {
-    m_tile = u % p.m_tiles;
-    u /= p.m_tiles;
+    if (u < full_units) {
+      m_tile = u % full_m;
+      u /= full_m;
+    } else {
+      u -= full_units;
+      m_tile = p.m_tiles - 1;
+    }
     split = u % p.splits;
     n_tile = u / p.splits;
   };
@@ -106,7 +121,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ring's round trip
       int k = 0, c = 0, m_tile = 0, split = 0, n_tile = 0, xk = 0;
       auto start_unit = [&]() {
-        decode(blockIdx.x + k * gridDim.x, m_tile, split, n_tile);
+        decode(unit_of(k), m_tile, split, n_tile);
         xk = split * kc * 64;
       };
       auto advance = [&]() {
@@ -159,7 +174,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(128, p.nt);
+      const uint32_t idesc_full = idesc_bf16_f32(128, p.nt);
+      const int n_last = min(p.nt, ((p.m - (p.m_tiles - 1) * p.nt) + 15) & ~15);
+      const uint32_t idesc_last = idesc_bf16_f32(128, n_last);
       // descriptors of stage 0; a stage / K step moves the 16-byte start-address field (shared memory < 256 KB)
       const uint64_t a0 = smem_desc_sw128(smem_u32(w_smem)), b0 = smem_desc_sw128(smem_u32(x_smem));
       int st = 0;
@@ -173,6 +190,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t acc = tmem + b * acc_cols;
+        int m_tile, split, n_tile;
+        decode(unit_of(k), m_tile, split, n_tile);
+        const uint32_t idesc = m_tile == p.m_tiles - 1 ? idesc_last : idesc_full;
         for (int c = 0; c < kc; ++c) {
           if (!mbar_wait(full + st, par, p.status, GR_ERR_TIMEOUT)) {
             flags[0] = 1;
@@ -201,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int k = 0; k < n_my; ++k) {
       const int b = k & 1;
       int m_tile, split, n_tile;
-      decode(blockIdx.x + k * gridDim.x, m_tile, split, n_tile);
+      decode(unit_of(k), m_tile, split, n_tile);
       const bool ok = mbar_wait(acc_full + b, (k >> 1) & 1, p.status, GR_ERR_TIMEOUT);
       tc_fence_after();
       const uint32_t t_lane = tmem + b * acc_cols + (static_cast<uint32_t>(quad * 32) << 16);
@@ -270,6 +290,7 @@ cudaError_t launch_linear(int epi, const CUtensorMap& tmw, const CUtensorMap& tm
     case GR_EPI_QKV_ROPE: return launch_linear_t<GR_EPI_QKV_ROPE>(tmw, tmx, p, grid, smem, stream, pdl);
     case GR_EPI_ARGMAX: return launch_linear_t<GR_EPI_ARGMAX>(tmw, tmx, p, grid, smem, stream, pdl);
     case GR_EPI_PARTIAL_F32: return launch_linear_t<GR_EPI_PARTIAL_F32>(tmw, tmx, p, grid, smem, stream, pdl);
+    case GR_EPI_RESIDUAL_NORM: return launch_linear_t<GR_EPI_RESIDUAL_NORM>(tmw, tmx, p, grid, smem, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
