@@ -787,7 +787,7 @@ def case_linear(a):
     x = torch.randn((m, k_in), generator=g).to("cuda", torch.bfloat16)
     mode = {"f32": L.EPI_STORE_F32, "partial": L.EPI_PARTIAL_F32, "swiglu": L.EPI_SWIGLU, "argmax": L.EPI_ARGMAX,
             "qkv": L.EPI_QKV_ROPE}[a.epi]
-    sp = a.splits or L.linear_default_splits(n_out, k_in, m)
+    sp = a.splits or L.linear_default_splits(n_out, k_in, m, mode)
     e = L.Epilogue()
     e.mode = mode
     keep = []

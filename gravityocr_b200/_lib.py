@@ -17,12 +17,12 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("GRAVITY_B200_LIB", os.path.join(_HERE, "libgravity_b200.so"))
 
 GR_OK = 0
-EPI_STORE_F32, EPI_STORE_BF16, EPI_SWIGLU, EPI_QKV_ROPE, EPI_ARGMAX, EPI_PARTIAL_F32, EPI_RESIDUAL_NORM = range(7)
+EPI_STORE_F32, EPI_STORE_BF16, EPI_SWIGLU, EPI_QKV_ROPE, EPI_ARGMAX, EPI_PARTIAL_F32 = range(6)
 ROWS_DRAFT, ROWS_VERIFY, ROWS_EXPLICIT = range(3)
 
 # every symbol include/gravity_b200.h declares
 EXPORTS = ("gr_version", "gr_status_string", "gr_set_pdl", "gr_set_attention_tc", "gr_num_sms", "gr_linear_workspace_bytes",
-           "gr_attention_workspace_bytes", "gr_linear_default_splits", "gr_linear_residual_norm_splits", "gr_linear", "gr_embed_rows",
+           "gr_attention_workspace_bytes", "gr_linear_default_splits", "gr_linear", "gr_embed_rows",
            "gr_residual_norm", "gr_bd_attention", "gr_accept_commit", "gr_draft_override", "gr_pack_gate_up",
            "gr_bd_attention_noalloc", "gr_bd_attention_ordered", "gr_gather_rows", "gr_logits_process",
            "gr_sample_rows", "gr_commit_sampled", "gr_penalty_cumulate")
@@ -52,12 +52,6 @@ class Epilogue(ctypes.Structure):
         ("out_gap", ctypes.c_void_p),
         ("row_pos3", ctypes.c_void_p),
         ("mrope_section", ctypes.c_int * 3),
-        ("h_in", ctypes.c_void_p),
-        ("h_out", ctypes.c_void_p),
-        ("x_out", ctypes.c_void_p),
-        ("norm_a", ctypes.c_void_p),
-        ("norm_b", ctypes.c_void_p),
-        ("eps", ctypes.c_float),
     ]
 
 
@@ -101,8 +95,7 @@ _SIGS = {
     "gr_num_sms": (_I, []),
     "gr_linear_workspace_bytes": (_Z, [_I, _I, _I]),
     "gr_attention_workspace_bytes": (_Z, [_I, _I, _I, _I, _I]),
-    "gr_linear_default_splits": (_I, [_I, _I, _I]),
-    "gr_linear_residual_norm_splits": (_I, [_I, _I, _I]),
+    "gr_linear_default_splits": (_I, [_I, _I, _I, _I]),
     "gr_linear": (_I, [_P, _I, _I, _P, _I, ctypes.POINTER(Epilogue), _I, _P, _Z, _P, _Z, _P, _P]),
     "gr_embed_rows": (_I, [_I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _I, _I, _P, _F, _I, _P, _P, _P,
                            _P, _P, _P, _P, _P]),
@@ -184,22 +177,9 @@ def linear_workspace_bytes(n_out: int, m: int, splits: int) -> int:
     return int(load().gr_linear_workspace_bytes(n_out, m, splits))
 
 
-def linear_default_splits(n_out: int, k_in: int, m: int) -> int:
-    return int(load().gr_linear_default_splits(n_out, k_in, m))
-
-
-def linear_residual_norm_splits(n_out: int, k_in: int, m: int) -> int:
-    """Split-K count of the fused residual-norm projection at this shape, 0 where it cannot run."""
-    return int(load().gr_linear_residual_norm_splits(n_out, k_in, m))
-
-
-def residual_norm_epilogue(h_in, h_out, x_out, norm_a, norm_b, eps: float) -> "Epilogue":
-    e = Epilogue()
-    e.mode = EPI_RESIDUAL_NORM
-    e.h_in, e.h_out, e.x_out = h_in.data_ptr(), h_out.data_ptr(), x_out.data_ptr()
-    e.norm_a, e.norm_b = norm_a.data_ptr(), norm_b.data_ptr()
-    e.eps = float(eps)
-    return e
+def linear_default_splits(n_out: int, k_in: int, m: int, mode: int = EPI_STORE_F32) -> int:
+    """Split-K count gr_linear plans for this shape and epilogue mode."""
+    return int(load().gr_linear_default_splits(n_out, k_in, m, mode))
 
 
 def attention_workspace_bytes(bs: int, K: int, n_q_heads: int, n_kv_heads: int, max_splits: int) -> int:

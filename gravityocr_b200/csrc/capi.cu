@@ -147,7 +147,6 @@ static int epi_out_bytes(int epi) {
   switch (epi) {
     case GR_EPI_STORE_F32: case GR_EPI_PARTIAL_F32: return 4;
     case GR_EPI_SWIGLU: return 1;
-    case GR_EPI_RESIDUAL_NORM: return 22;  // y staged, read back twice; h_in read; h written; x written
     default: return 2;
   }
 }
@@ -253,31 +252,19 @@ static LinearShape linear_shape(int n_out, int k_in, int m, int sp = 1, int epi 
 // Split-K count, chosen together with the token tiling: the cost above minimised over the split counts that divide
 // the K chunks (at most half of them) and whose fp32 partials stay a small, L2-resident fraction of the traffic;
 // ties go to fewer splits (less partial traffic).  The argmax epilogue runs unsplit.
-// Whether every CTA of the persistent grid owns at most one unit (all units resident at once), as the fused
-// residual norm's counter barriers require.
-static bool one_unit_per_cta(const LinearShape& s, int sp, int epi) {
-  int stages, per_sm;
-  linear_launch_shape(s.nt, s.kc / sp, epi, &stages, &per_sm);
-  return static_cast<long long>(s.n_tiles) * s.m_tiles * sp <= static_cast<long long>(num_sms()) * per_sm &&
-         s.m_tiles <= kMaxBarTiles;
-}
-
 // Split-K count, chosen together with the token tiling: the cost above minimised over the split counts that divide
 // the K chunks (at most half of them) and whose fp32 partials stay a small, L2-resident fraction of the traffic;
-// ties go to fewer splits (less partial traffic).  The argmax epilogue runs unsplit; the fused residual norm only
-// with one unit per CTA (0: no split count fits).
+// ties go to fewer splits (less partial traffic).  The argmax epilogue runs unsplit.
 static int default_splits(int n_out, int k_in, int m, int epi) {
   if (epi == GR_EPI_ARGMAX) return 1;
-  const bool one_unit = epi == GR_EPI_RESIDUAL_NORM;
   const int kc = k_in / 64;
   long long best_cost = -1;
-  int best = one_unit ? 0 : 1;
+  int best = 1;
   for (int sp = 1; sp <= (kc / 2 > 1 ? kc / 2 : 1); ++sp) {
     if (kc % sp) continue;
     if (sp > 1 && static_cast<double>(sp) * m * (n_out / 128) * 128 * 4 > 32.0 * (1 << 20)) break;
     long long cost = 0;
-    const LinearShape s = linear_shape(n_out, k_in, m, sp, epi, &cost);
-    if (one_unit && !one_unit_per_cta(s, sp, epi)) continue;
+    linear_shape(n_out, k_in, m, sp, epi, &cost);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       best = sp;
@@ -296,8 +283,7 @@ static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // Every call shares one scratch buffer, whatever its shape: the tickets live in a fixed region at its head (so a
 // later call of another shape never finds another call's partial sums where its tickets are), then the fp32
 // split-K partials, then the per-(token, feature tile) argmax records.
-// tile tickets, then the fused residual norm's three arrival counters per token tile
-constexpr size_t kTicketBytes = (kMaxTiles + 3 * kMaxBarTiles) * sizeof(int);
+constexpr size_t kTicketBytes = kMaxTiles * sizeof(int);
 static LinearWs linear_ws_layout(void* base, const LinearShape& s, int m, int splits) {
   LinearWs w;
   uint8_t* p = static_cast<uint8_t*>(base);
@@ -343,14 +329,10 @@ void gr_set_pdl(int enable) { g_pdl = enable != 0; }
 void gr_set_attention_tc(int mode) { g_attention_tc = mode < 0 ? 0 : (mode > 2 ? 2 : mode); }
 int gr_num_sms(void) { return num_sms(); }
 
-int gr_linear_default_splits(int n_out, int k_in, int m) {
-  if (n_out <= 0 || k_in <= 0 || m <= 0 || (k_in % 64)) return 1;
-  return default_splits(n_out, k_in, m, GR_EPI_STORE_F32);
-}
-
-int gr_linear_residual_norm_splits(int n_out, int k_in, int m) {
-  if (n_out <= 0 || (n_out % 128) || k_in <= 0 || (k_in % 64) || m <= 0) return 0;
-  return default_splits(n_out, k_in, m, GR_EPI_RESIDUAL_NORM);
+int gr_linear_default_splits(int n_out, int k_in, int m, int mode) {
+  if (mode < GR_EPI_STORE_F32 || mode > GR_EPI_PARTIAL_F32) return 0;
+  if (n_out <= 0 || (n_out % 128) || k_in <= 0 || (k_in % 64) || m <= 0) return 1;
+  return default_splits(n_out, k_in, m, mode);
 }
 
 size_t gr_linear_workspace_bytes(int n_out, int m, int splits) {
@@ -381,9 +363,8 @@ static int build_linear(const void* w, int n_out, int k_in, const void* x, int m
                         void* workspace, size_t workspace_bytes, const void* prefetch, size_t prefetch_bytes,
                         int32_t* status, LinearLaunch* out) {
   if (!w || !x || !epi || m <= 0 || n_out <= 0 || (n_out % 128) || k_in <= 0 || (k_in % 64)) return GR_ERR_ARG;
-  if (epi->mode < GR_EPI_STORE_F32 || epi->mode > GR_EPI_RESIDUAL_NORM) return GR_ERR_ARG;
+  if (epi->mode < GR_EPI_STORE_F32 || epi->mode > GR_EPI_PARTIAL_F32) return GR_ERR_ARG;
   if (splits <= 0) splits = default_splits(n_out, k_in, m, epi->mode);
-  if (splits <= 0) return GR_ERR_UNSUPPORTED;  // no split count fits the fused residual norm
   if ((k_in / 64) % splits) return GR_ERR_ARG;
   LinearShape s = linear_shape(n_out, k_in, m, splits, epi->mode);
   const size_t ws_splits = epi->mode == GR_EPI_PARTIAL_F32 ? 1 : static_cast<size_t>(splits);
@@ -401,11 +382,6 @@ static int build_linear(const void* w, int n_out, int k_in, const void* x, int m
       return GR_ERR_ARG;
   } else if (epi->mode == GR_EPI_ARGMAX) {
     if (!epi->out_idx) return GR_ERR_ARG;
-  } else if (epi->mode == GR_EPI_RESIDUAL_NORM) {
-    if (!epi->h_in || !epi->h_out || !epi->x_out || !epi->norm_a || !epi->norm_b || epi->h_in == epi->h_out ||
-        !(epi->eps >= 0.f))
-      return GR_ERR_ARG;
-    if (!one_unit_per_cta(s, splits, epi->mode)) return GR_ERR_UNSUPPORTED;
   } else if (!epi->out || epi->ld_out <= 0) {
     return GR_ERR_ARG;
   }
@@ -459,16 +435,6 @@ static int build_linear(const void* w, int n_out, int k_in, const void* x, int m
   p.ws_partial = ws.partial;
   p.ws_ticket = ws.ticket;
   p.ws_arg = ws.arg;
-  p.ws_ss = reinterpret_cast<float*>(ws.arg);  // RESIDUAL_NORM: [2][n_tiles][m] floats fit the records' region
-  p.ws_bar = ws.ticket + kMaxTiles;
-  if (epi->mode == GR_EPI_RESIDUAL_NORM) {
-    p.h_in = epi->h_in;
-    p.h_out = epi->h_out;
-    p.x_out = static_cast<__nv_bfloat16*>(epi->x_out);
-    p.norm_a = static_cast<const __nv_bfloat16*>(epi->norm_a);
-    p.norm_b = static_cast<const __nv_bfloat16*>(epi->norm_b);
-    p.eps = epi->eps;
-  }
   p.prefetch = static_cast<const uint8_t*>(prefetch);
   p.prefetch_bytes = prefetch ? prefetch_bytes : 0;
   p.status = status;

@@ -96,23 +96,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
   }
 }
 
-// Bounded wait until the int at `ctr` (written by other CTAs with atomics) reaches `target`; acquire ordering, so
-// what the arriving CTAs published before their increment is visible afterwards.  Returns false (and records `code`)
-// on timeout.
-__device__ __forceinline__ bool count_reaches(const int* ctr, int target, int* status, int code) {
-  const uint64_t t0 = globaltimer();
-  while (true) {
-    int v;
-    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
-    if (v >= target) return true;
-    if (globaltimer() - t0 > GR_WAIT_NS) {
-      report(status, code);
-      return false;
-    }
-    __nanosleep(32);
-  }
-}
-
 // ------------------------------------------------------------------ TMA / bulk copies
 __device__ __forceinline__ void tma_prefetch_desc(const void* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -290,7 +290,6 @@ cudaError_t launch_linear(int epi, const CUtensorMap& tmw, const CUtensorMap& tm
     case GR_EPI_QKV_ROPE: return launch_linear_t<GR_EPI_QKV_ROPE>(tmw, tmx, p, grid, smem, stream, pdl);
     case GR_EPI_ARGMAX: return launch_linear_t<GR_EPI_ARGMAX>(tmw, tmx, p, grid, smem, stream, pdl);
     case GR_EPI_PARTIAL_F32: return launch_linear_t<GR_EPI_PARTIAL_F32>(tmw, tmx, p, grid, smem, stream, pdl);
-    case GR_EPI_RESIDUAL_NORM: return launch_linear_t<GR_EPI_RESIDUAL_NORM>(tmw, tmx, p, grid, smem, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -11,8 +11,7 @@ constexpr uint32_t kWStageBytes = 128 * 128;  // 128 rows x 64 bf16
 // each warp's 16 tokens x 32 rows (1 KB per warp) so that global stores go out as 16-byte vectors per lane.
 __host__ __device__ constexpr uint32_t epi_scratch_bytes(int epi) {
   return epi == GR_EPI_ARGMAX ? 16384u
-                              : ((epi == GR_EPI_SWIGLU || epi == GR_EPI_QKV_ROPE || epi == GR_EPI_STORE_BF16 ||
-                                  epi == GR_EPI_RESIDUAL_NORM) ? 8192u : 0u);
+                              : ((epi == GR_EPI_SWIGLU || epi == GR_EPI_QKV_ROPE || epi == GR_EPI_STORE_BF16) ? 8192u : 0u);
 }
 
 // all 8 epilogue warps
@@ -206,196 +205,6 @@ __device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, in
 }
 
 
-// Sum over the warp's 32 lanes of each of a lane's 16 values, by halving exchanges (16 shuffles): lane l ends with
-// the sum of a[l >> 1].
-__device__ __forceinline__ float warp_sum16(const float (&a)[16], int lane) {
-  float b8[8], b4[4], b2[2];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const bool up = lane & 16;
-    b8[j] = (up ? a[8 + j] : a[j]) + __shfl_xor_sync(0xffffffffu, up ? a[j] : a[8 + j], 16);
-  }
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const bool up = lane & 8;
-    b4[j] = (up ? b8[4 + j] : b8[j]) + __shfl_xor_sync(0xffffffffu, up ? b8[j] : b8[4 + j], 8);
-  }
-#pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const bool up = lane & 4;
-    b2[j] = (up ? b4[2 + j] : b4[j]) + __shfl_xor_sync(0xffffffffu, up ? b4[j] : b4[2 + j], 4);
-  }
-  const bool up = lane & 2;
-  const float b1 = (up ? b2[1] : b2[0]) + __shfl_xor_sync(0xffffffffu, up ? b2[0] : b2[1], 2);
-  return b1 + __shfl_xor_sync(0xffffffffu, b1, 1);
-}
-
-// RESIDUAL_NORM epilogue of o_proj / down_proj: y = the projection's rows (split-K partials summed in split order by
-// the tile's last split), then the decoder's sandwich-norm step h_out = h_in + w_a * RMSNorm(y) and
-// x_out = w_b * RMSNorm(h_out) (bf16), each RMSNorm over the whole row, i.e. across the n_tiles feature tiles of a
-// token tile.  The finisher of each (feature tile, token tile) -- the unit itself without split-K, else the last
-// split to arrive -- stages y in h_out, publishes its 128 features' per-row sums of squares, and meets the token
-// tile's other finishers at an arrival counter; then the same for h.  The host runs this mode only where every CTA
-// owns at most one unit, so the finishers of a token tile are distinct resident CTAs; every wait is bounded.
-// Scratch: ss4 [4 lane quadrants][256 rows], rs [256 rows] floats.
-__device__ __forceinline__ void unit_epilogue_resnorm(const LinearParams& p, uint32_t t_lane, int n_tile, int m_tile,
-                                                      int split, bool run, float* scratch, int* flag_last,
-                                                      uint64_t* acc_empty) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int half = (warp - 2) >> 2, quad = warp & 3;
-  const int f_local = quad * 32 + lane;
-  const int wt = threadIdx.x - 64;  // 0..255
-  const bool leader = wt == 0;
-  const int t_beg = m_tile * p.nt;
-  const int rows = min(p.nt, p.m - t_beg);
-  const int H = p.n_out;
-  const int f = n_tile * 128 + f_local;
-  float* ss4 = scratch;          // [4][256]
-  float* rs = scratch + 4 * 256;  // [256]
-  const int tile = n_tile * p.m_tiles + m_tile;
-  float* part = p.ws_partial + ((size_t)tile * p.splits + split) * p.nt * 128;
-
-  // ---- y of this unit: from TMEM, or (split-K) this split's partial, then the finisher's sum in split order
-  if (p.splits == 1) {
-    for (int c0 = half * 16; c0 < rows; c0 += 32) {
-      float v[16];
-      if (run) {
-        tmem_ld16(t_lane + c0, v);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = 0.f;
-      }
-#pragma unroll
-      for (int i = 0; i < 16; ++i)
-        if (c0 + i < rows) p.h_out[(size_t)(t_beg + c0 + i) * H + f] = v[i];
-    }
-    tc_fence_before();
-    if (lane == 0) mbar_arrive(acc_empty);
-  } else {
-    if (run) {
-      for (int c0 = half * 16; c0 < rows; c0 += 32) {
-        float v[16];
-        tmem_ld16(t_lane + c0, v);
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          if (c0 + i < rows) part[(c0 + i) * 128 + f_local] = v[i];
-      }
-    }
-    tc_fence_before();
-    if (lane == 0) mbar_arrive(acc_empty);
-    __threadfence();
-    epi_bar();
-    if (leader) {
-      const int prev = atomicAdd(&p.ws_ticket[tile], 1);
-      *flag_last = (prev == p.splits - 1);
-    }
-    epi_bar();
-    if (!*flag_last) return;
-    __threadfence();
-    const float* base = p.ws_partial + (size_t)tile * p.splits * p.nt * 128;
-    for (int c0 = half * 16; c0 < rows; c0 += 32) {
-      float v[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = 0.f;
-      for (int s = 0; s < p.splits; ++s) {
-        const float* src = base + ((size_t)s * p.nt + c0) * 128 + f_local;
-        float x[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) x[i] = (c0 + i < rows) ? __ldcg(src + i * 128) : 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] += x[i];
-      }
-#pragma unroll
-      for (int i = 0; i < 16; ++i)
-        if (c0 + i < rows) p.h_out[(size_t)(t_beg + c0 + i) * H + f] = v[i];
-    }
-    if (leader) p.ws_ticket[tile] = 0;
-  }
-  // From here every thread reads back only the h_out elements it wrote itself (same thread, same address).
-  int* bar1 = p.ws_bar + m_tile;
-  int* bar2 = bar1 + kMaxBarTiles;
-  int* bar3 = bar2 + kMaxBarTiles;
-  float* ss_y = p.ws_ss + (size_t)n_tile * p.m;
-  float* ss_h = p.ws_ss + ((size_t)p.n_tiles + n_tile) * p.m;
-  const float wa = __bfloat162float(p.norm_a[f]);
-  const float wb = __bfloat162float(p.norm_b[f]);
-
-  // per row of the tile: this feature tile's sum of squares of `src` rows (read back from h_out), published to `dst`
-  auto publish_sumsq = [&](float* dst) {
-    for (int c0 = half * 16; c0 < rows; c0 += 32) {
-      float sq[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float y = (c0 + i < rows) ? p.h_out[(size_t)(t_beg + c0 + i) * H + f] : 0.f;
-        sq[i] = y * y;
-      }
-      const float s = warp_sum16(sq, lane);
-      if (!(lane & 1) && c0 + (lane >> 1) < rows) ss4[quad * 256 + c0 + (lane >> 1)] = s;
-    }
-    epi_bar();
-    if (wt < rows) dst[t_beg + wt] = ((ss4[wt] + ss4[256 + wt]) + ss4[512 + wt]) + ss4[768 + wt];
-    __threadfence();
-    epi_bar();
-  };
-  // arrival of this finisher at a counter and the bounded wait for the token tile's n_tiles finishers
-  auto meet = [&](int* ctr) {
-    if (leader) {
-      atomicAdd(ctr, 1);
-      flag_last[1] = count_reaches(ctr, p.n_tiles, p.status, GR_ERR_TIMEOUT) ? 1 : 0;
-      __threadfence();
-    }
-    epi_bar();
-    return flag_last[1] != 0;
-  };
-  // 1 / rms of each row from the n_tiles feature tiles' sums (in feature-tile order) into rs
-  auto row_scale = [&](const float* src0) {
-    if (wt < rows) {
-      float tot = 0.f;
-      for (int q = 0; q < p.n_tiles; ++q) tot += __ldcg(src0 + (size_t)q * p.m + t_beg + wt);
-      rs[wt] = rsqrtf(tot / H + p.eps);
-    }
-    epi_bar();
-  };
-
-  publish_sumsq(ss_y);
-  bool ok = meet(bar1);
-  if (ok) {
-    row_scale(p.ws_ss);
-    // h = h_in + w_a * (y * rms_y); staged over y in h_out
-    for (int c0 = half * 16; c0 < rows; c0 += 32) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        if (c0 + i >= rows) break;
-        const size_t o = (size_t)(t_beg + c0 + i) * H + f;
-        p.h_out[o] = p.h_in[o] + wa * (p.h_out[o] * rs[c0 + i]);
-      }
-    }
-    epi_bar();  // rs is rewritten below
-    publish_sumsq(ss_h);
-  }
-  ok = meet(bar2) && ok;
-  if (ok) {
-    row_scale(p.ws_ss + (size_t)p.n_tiles * p.m);
-    for (int c0 = half * 16; c0 < rows; c0 += 32) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        if (c0 + i >= rows) break;
-        const size_t o = (size_t)(t_beg + c0 + i) * H + f;
-        p.x_out[o] = __float2bfloat16_rn(wb * (p.h_out[o] * rs[c0 + i]));
-      }
-    }
-  }
-  // re-arm: the last finisher past both barriers resets the token tile's counters for the next launch
-  if (leader) {
-    const int prev = atomicAdd(bar3, 1);
-    if (prev == p.n_tiles - 1) {
-      *bar1 = 0;
-      *bar2 = 0;
-      *bar3 = 0;
-    }
-  }
-}
-
 // One unit's epilogue, run by the 8 epilogue warps (warps 2-9, 256 threads) of the CTA that owns the unit: the TMEM
 // accumulator (this warp's lane quadrant at t_lane) -> epilogue16, or, for a split-K unit, a partial tile -> ticket ->
 // the last split sums the partials in split order and runs the epilogue.  Arrives once per warp on `acc_empty` as
@@ -403,10 +212,6 @@ __device__ __forceinline__ void unit_epilogue_resnorm(const LinearParams& p, uin
 template <int EPI>
 __device__ __forceinline__ void unit_epilogue(const LinearParams& p, uint32_t t_lane, int n_tile, int m_tile, int split,
                                               bool run, float* scratch, int* flag_last, uint64_t* acc_empty) {
-  if constexpr (EPI == GR_EPI_RESIDUAL_NORM) {
-    unit_epilogue_resnorm(p, t_lane, n_tile, m_tile, split, run, scratch, flag_last, acc_empty);
-    return;
-  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int half = (warp - 2) >> 2;
   const int f_local = (warp & 3) * 32 + lane;

@@ -29,20 +29,10 @@ struct LinearParams {
   float* ws_partial;
   int* ws_ticket;
   float4* ws_arg;  // lm_head: per (token, feature tile) top-2 record {v1, i1 bits, v2, 0}, token-major
-  // RESIDUAL_NORM: the decoder's sandwich-norm step fused into o_proj / down_proj (row length n_out)
-  const float* h_in;
-  float* h_out;             // also stages y between the two norms
-  __nv_bfloat16* x_out;
-  const __nv_bfloat16* norm_a;
-  const __nv_bfloat16* norm_b;
-  float eps;
-  float* ws_ss;  // [2][n_tiles][m] per feature tile and row: sums of squares of y, then of h
-  int* ws_bar;   // [3][kMaxBarTiles] arrival counters per token tile (re-armed by the last finisher)
   const uint8_t* prefetch;
   unsigned long long prefetch_bytes;
   int* status;
 };
-constexpr int kMaxBarTiles = 1024;  // token tiles of one RESIDUAL_NORM call
 struct AttnParams {
   const __nv_bfloat16* q;
   __nv_bfloat16* out;

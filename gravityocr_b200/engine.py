@@ -161,12 +161,8 @@ class Engine:
     """One model replica on one GPU: the forward, the round and graph capture."""
 
     def __init__(self, cfg: ModelConfig, weights: Dict[str, torch.Tensor], *, max_rows: int, n_pages: int,
-                 page_size: int = 16, device: Optional[torch.device] = None, pdl: bool = True,
-                 fuse_norm: bool = True):
+                 page_size: int = 16, device: Optional[torch.device] = None, pdl: bool = True):
         L.load()
-        # o_proj / down_proj with the sandwich norm in their epilogue where the shape allows (one launch instead of
-        # two); False keeps the projection and gr_residual_norm apart
-        self.fuse_norm = fuse_norm
         if page_size != 16:
             raise ValueError("the attention kernel's TMA box is one 16-token page")
         self.cfg = cfg
@@ -194,29 +190,21 @@ class Engine:
         self.graphs: Dict[Tuple[int, int], torch.cuda.CUDAGraph] = {}
 
     # ------------------------------------------------------------------ workspace
-    def gemm_shapes(self) -> List[Tuple[int, int]]:
+    def gemm_shapes(self) -> List[Tuple[int, int, int]]:
+        """(n_out, k_in, epilogue mode) of every projection a forward or a sampled round runs."""
         c = self.cfg
-        return [(c.qkv_dim, c.hidden), (c.hidden, c.q_dim), (2 * c.intermediate, c.hidden), (c.hidden, c.intermediate),
-                (c.vocab, c.hidden)]
+        return [(c.qkv_dim, c.hidden, L.EPI_QKV_ROPE), (c.hidden, c.q_dim, L.EPI_PARTIAL_F32),
+                (2 * c.intermediate, c.hidden, L.EPI_SWIGLU), (c.hidden, c.intermediate, L.EPI_PARTIAL_F32),
+                (c.vocab, c.hidden, L.EPI_ARGMAX), (c.vocab, c.hidden, L.EPI_STORE_F32)]
 
     def linear_ws_bytes(self, m: int) -> int:
-        """Scratch of every projection at M = m rows with its default split-K (tickets, partials, argmax tiles), and
-        of the fused residual-norm projections."""
-        c = self.cfg
-        need = [L.linear_workspace_bytes(n, m, L.linear_default_splits(n, k, m)) for n, k in self.gemm_shapes()]
-        for k in (c.q_dim, c.intermediate):
-            sp = self.fused_norm_splits(k, m)
-            if sp:
-                need.append(L.linear_workspace_bytes(c.hidden, m, sp))
-        return max(need)
+        """Scratch of every projection at M = m rows with its default split-K (tickets, partials, argmax tiles)."""
+        return max(L.linear_workspace_bytes(n, m, L.linear_default_splits(n, k, m, mode))
+                   for n, k, mode in self.gemm_shapes())
 
     def splits(self, n_out: int, k_in: int, m: int) -> int:
-        return L.linear_default_splits(n_out, k_in, m)
-
-    def fused_norm_splits(self, k_in: int, m: int) -> int:
-        """Split-K count of o_proj (k_in = q_dim) / down_proj (k_in = intermediate) with the residual norm fused into
-        its epilogue, 0 where the projection and the norm run apart."""
-        return L.linear_residual_norm_splits(self.cfg.hidden, k_in, m) if self.fuse_norm else 0
+        """Split-K count of o_proj / down_proj writing partials for gr_residual_norm."""
+        return L.linear_default_splits(n_out, k_in, m, L.EPI_PARTIAL_F32)
 
     def _grow_y(self, m: int) -> None:
         c = self.cfg
@@ -299,40 +287,29 @@ class Engine:
             ops.bd_attention(self.q, self.pool.k[l], self.pool.v[l], page_table, seq_lens, bs, K, draft, base_add,
                            cfg.n_q_heads, cfg.n_kv_heads, self.page_size, attn_chunk, attn_splits, self.attn, ws_attn,
                            status=st, order=order)
-            sp_o = self.fused_norm_splits(cfg.q_dim, M)
-            if sp_o:
-                e = L.residual_norm_epilogue(self.h[cur], self.h[1 - cur], self.x, d["psa"], d["pa"], cfg.rms_eps)
-                ops.linear(d["o"], self.attn, M, e, self.lin_ws, splits=sp_o, prefetch=d["gate_up"], status=st)
-            else:
-                e = L.Epilogue()
-                e.mode = L.EPI_PARTIAL_F32
-                e.out = self.y.data_ptr()
-                e.ld_out = cfg.hidden
-                sp_o = self.splits(cfg.hidden, cfg.q_dim, M)
-                ops.linear(d["o"], self.attn, M, e, self.lin_ws, splits=sp_o, prefetch=d["gate_up"], status=st)
-                ops.residual_norm(M, self.h[cur], self.y, d["psa"], d["pa"], cfg.rms_eps, self.h[1 - cur], self.x,
-                                  y_parts=sp_o)
+            e = L.Epilogue()
+            e.mode = L.EPI_PARTIAL_F32
+            e.out = self.y.data_ptr()
+            e.ld_out = cfg.hidden
+            sp_o = self.splits(cfg.hidden, cfg.q_dim, M)
+            ops.linear(d["o"], self.attn, M, e, self.lin_ws, splits=sp_o, prefetch=d["gate_up"], status=st)
+            ops.residual_norm(M, self.h[cur], self.y, d["psa"], d["pa"], cfg.rms_eps, self.h[1 - cur], self.x,
+                              y_parts=sp_o)
             cur ^= 1
             e = L.Epilogue()
             e.mode = L.EPI_SWIGLU
             e.out = self.act.data_ptr()
             e.ld_out = cfg.intermediate
             ops.linear(d["gate_up"], self.x, M, e, self.lin_ws, prefetch=d["down"], status=st)
+            e = L.Epilogue()
+            e.mode = L.EPI_PARTIAL_F32
+            e.out = self.y.data_ptr()
+            e.ld_out = cfg.hidden
+            sp_d = self.splits(cfg.hidden, cfg.intermediate, M)
             pf = nxt["qkv"] if nxt is not None else w.lm_head[: min(w.lm_head.shape[0], 16384)]
-            norm_b = nxt["in"] if nxt is not None else w.norm
-            sp_d = self.fused_norm_splits(cfg.intermediate, M)
-            if sp_d:
-                e = L.residual_norm_epilogue(self.h[cur], self.h[1 - cur], self.x, d["pm"], norm_b, cfg.rms_eps)
-                ops.linear(d["down"], self.act, M, e, self.lin_ws, splits=sp_d, prefetch=pf, status=st)
-            else:
-                e = L.Epilogue()
-                e.mode = L.EPI_PARTIAL_F32
-                e.out = self.y.data_ptr()
-                e.ld_out = cfg.hidden
-                sp_d = self.splits(cfg.hidden, cfg.intermediate, M)
-                ops.linear(d["down"], self.act, M, e, self.lin_ws, splits=sp_d, prefetch=pf, status=st)
-                ops.residual_norm(M, self.h[cur], self.y, d["pm"], norm_b, cfg.rms_eps, self.h[1 - cur], self.x,
-                                  y_parts=sp_d)
+            ops.linear(d["down"], self.act, M, e, self.lin_ws, splits=sp_d, prefetch=pf, status=st)
+            ops.residual_norm(M, self.h[cur], self.y, d["pm"], nxt["in"] if nxt is not None else w.norm, cfg.rms_eps,
+                              self.h[1 - cur], self.x, y_parts=sp_d)
             cur ^= 1
         if not head:
             return

@@ -38,11 +38,8 @@ enum gr_epilogue_mode {
   GR_EPI_SWIGLU = 2,     /* out[t, j] = up * silu(gate), bf16; weight rows 2j / 2j+1 = gate j / up j (gr_pack_gate_up) */
   GR_EPI_QKV_ROPE = 3,   /* q -> q_out, k/v -> paged cache with partial interleaved RoPE */
   GR_EPI_ARGMAX = 4,     /* vocab-wide argmax per row: out_idx, out_top1, out_gap; no logits written */
-  GR_EPI_PARTIAL_F32 = 5, /* split-K partials, out[split][t][f] fp32 (split stride m * ld_out); the consumer sums
+  GR_EPI_PARTIAL_F32 = 5 /* split-K partials, out[split][t][f] fp32 (split stride m * ld_out); the consumer sums
                             them (gr_residual_norm with y_parts = splits) */
-  GR_EPI_RESIDUAL_NORM = 6 /* y = the projection (split-K summed in split order), then gr_residual_norm's step on
-                            whole rows of n_out features: h_out = h_in + norm_a * RMSNorm(y), x_out = norm_b *
-                            RMSNorm(h_out); see gr_linear_residual_norm_splits for when it can run */
 };
 
 /* Row sources of gr_embed_rows. */
@@ -73,14 +70,6 @@ typedef struct gr_epilogue {
    * after (transformers GlmOcrTextRotaryEmbedding.apply_mrope, sections [8, 12, 12]). */
   const int32_t* row_pos3;
   int mrope_section[3];
-  /* RESIDUAL_NORM: rows of n_out features; h_in / h_out fp32 [M, n_out] (distinct buffers), x_out bf16 [M, n_out],
-   * norm_a / norm_b bf16 [n_out] */
-  const float* h_in;
-  float* h_out;
-  void* x_out;
-  const void* norm_a;
-  const void* norm_b;
-  float eps;
 } gr_epilogue;
 
 /* Library identity / diagnostics. */
@@ -100,14 +89,11 @@ int gr_num_sms(void);
 size_t gr_linear_workspace_bytes(int n_out, int m, int splits);
 size_t gr_attention_workspace_bytes(int bs, int K, int n_q_heads, int n_kv_heads, int max_splits);
 
-/* Split-K count gr_linear would use by default for this shape (0 in `splits` below). */
-int gr_linear_default_splits(int n_out, int k_in, int m);
-/* The split-K count gr_linear uses for GR_EPI_RESIDUAL_NORM at this shape, or 0 where that mode cannot run: it needs
- * every CTA of the persistent grid to own at most one (feature tile, token tile, split) unit, because the feature
- * tiles of a token tile meet at counter barriers to take the row norms.  Replaces the decoder layer's o_proj /
- * down_proj followed by the sandwich norms (modeling_glm_ocr.py:281-302) in one launch; callers fall back to
- * GR_EPI_PARTIAL_F32 + gr_residual_norm where it returns 0. */
-int gr_linear_residual_norm_splits(int n_out, int k_in, int m);
+/* Split-K count gr_linear uses by default (0 in `splits` below) for this shape and epilogue mode (gr_epilogue_mode):
+ * the token tiling and the split count are planned together, and the plan depends on what the epilogue stores (a
+ * split-K tile's last split reads every split's partial before it runs the epilogue; GR_EPI_PARTIAL_F32 leaves the
+ * sum to its consumer). */
+int gr_linear_default_splits(int n_out, int k_in, int m, int mode);
 
 /* Weight-streaming projection with a fused epilogue:  y[t, f] = sum_k x[t, k] * w[f, k].
  * w: bf16 [n_out, k_in] row-major (nn.Linear); x: bf16 [m, k_in] row-major; n_out % 128 == 0, k_in % 64 == 0,

@@ -17,8 +17,10 @@ DEV = "cuda"
 
 
 def _ws(n_out, k_in, m, splits=0):
-    sp = splits or L.linear_default_splits(n_out, k_in, m)
-    return torch.zeros((L.linear_workspace_bytes(n_out, m, sp),), dtype=torch.uint8, device=DEV)
+    # room for whichever epilogue mode the call plans (the split count depends on it)
+    modes = (L.EPI_STORE_F32, L.EPI_STORE_BF16, L.EPI_SWIGLU, L.EPI_QKV_ROPE, L.EPI_ARGMAX, L.EPI_PARTIAL_F32)
+    sps = [splits] if splits else [L.linear_default_splits(n_out, k_in, m, md) for md in modes]
+    return torch.zeros((max(L.linear_workspace_bytes(n_out, m, sp) for sp in sps),), dtype=torch.uint8, device=DEV)
 
 
 def _rand(shape, g, scale=1.0, dtype=torch.bfloat16):
@@ -412,7 +414,8 @@ def test_shared_workspace_across_shapes():
     g = torch.Generator().manual_seed(41)
     shapes = [(4096, 1536, 17), (59392, 1536, 64), (1536, 2048, 17), (9216, 1536, 64), (1536, 4608, 17),
               (59392, 1536, 17), (4096, 1536, 64), (59392, 1536, 64)]
-    need = max(L.linear_workspace_bytes(n, m, L.linear_default_splits(n, k, m)) for n, k, m in shapes)
+    need = max(L.linear_workspace_bytes(n, m, L.linear_default_splits(n, k, m, md)) for n, k, m in shapes
+               for md in (L.EPI_STORE_F32, L.EPI_PARTIAL_F32))
     ws = torch.zeros((need,), dtype=torch.uint8, device=DEV)
     for n_out, k_in, m in shapes:
         w, x = _rand((n_out, k_in), g, 0.02), _rand((m, k_in), g)
@@ -463,7 +466,7 @@ def test_linear_partials_summed_by_residual_norm(n_out, k_in, m):
     """o_proj / down_proj write split-K partials; the residual norm sums them in split order."""
     g = torch.Generator().manual_seed(m + k_in)
     w, x = _rand((n_out, k_in), g, 0.02), _rand((m, k_in), g)
-    sp = L.linear_default_splits(n_out, k_in, m)
+    sp = L.linear_default_splits(n_out, k_in, m, L.EPI_PARTIAL_F32)
     y = torch.full((sp, m, n_out), float("nan"), device=DEV)
     e = L.Epilogue()
     e.mode, e.out, e.ld_out = L.EPI_PARTIAL_F32, y.data_ptr(), n_out
@@ -480,66 +483,6 @@ def test_linear_partials_summed_by_residual_norm(n_out, k_in, m):
     hr = h + rms(ref_y, wa)
     torch.testing.assert_close(h2, hr, rtol=1e-3, atol=1e-5)
     torch.testing.assert_close(xo.float(), rms(hr, wb), rtol=1e-2, atol=1e-4)
-
-
-@pytest.mark.parametrize("n_out,k_in,m", [(1536, 2048, 17), (1536, 4608, 17), (1536, 2048, 34), (1536, 4608, 136),
-                                          (1536, 2048, 300), (1536, 2048, 1088), (1536, 4608, 1088),
-                                          (1536, 4608, 2176), (1024, 2048, 33), (2048, 1024, 129)])
-def test_linear_residual_norm_fused(n_out, k_in, m):
-    """GR_EPI_RESIDUAL_NORM (o_proj / down_proj with the sandwich norm in the epilogue, the row norms taken across the
-    feature tiles' CTAs) against the fp32 reference and against the projection + gr_residual_norm pair: the same
-    tolerances as the pair; three launches in a row on one scratch (the arrival counters re-arm) give bit-identical
-    results."""
-    sp = L.linear_residual_norm_splits(n_out, k_in, m)
-    assert sp > 0
-    g = torch.Generator().manual_seed(m + k_in + 1)
-    w, x = _rand((n_out, k_in), g, 0.02), _rand((m, k_in), g)
-    h = torch.randn((m, n_out), generator=g).to(DEV) * 0.1
-    wa, wb = _rand((n_out,), g, 0.02), _rand((n_out,), g, 0.02)
-    ws = torch.zeros((L.linear_workspace_bytes(n_out, m, sp),), dtype=torch.uint8, device=DEV)
-    st = torch.zeros((1,), dtype=torch.int32, device=DEV)
-    outs = []
-    for _ in range(3):
-        h2 = torch.full_like(h, float("nan"))
-        xo = torch.zeros((m, n_out), dtype=torch.bfloat16, device=DEV)
-        L.linear(w, x, m, L.residual_norm_epilogue(h, h2, xo, wa, wb, 1e-5), ws, splits=sp, status=st)
-        outs.append((h2, xo))
-    torch.cuda.synchronize()
-    assert int(st.item()) == 0
-    for h2, xo in outs[1:]:
-        assert torch.equal(h2, outs[0][0]) and torch.equal(xo, outs[0][1])
-    h2, xo = outs[0]
-    ref_y = x.float() @ w.float().T
-    rms = lambda t, ww: ww.float() * (t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + 1e-5))
-    hr = h + rms(ref_y, wa)
-    torch.testing.assert_close(h2, hr, rtol=1e-3, atol=1e-5)
-    torch.testing.assert_close(xo.float(), rms(hr, wb), rtol=1e-2, atol=1e-4)
-    # against the two-launch pair on the same inputs
-    sp2 = L.linear_default_splits(n_out, k_in, m)
-    y = torch.zeros((sp2, m, n_out), device=DEV)
-    e = L.Epilogue()
-    e.mode, e.out, e.ld_out = L.EPI_PARTIAL_F32, y.data_ptr(), n_out
-    L.linear(w, x, m, e, _ws(n_out, k_in, m, 1), splits=sp2)
-    h3 = torch.zeros_like(h)
-    x3 = torch.zeros_like(xo)
-    L.residual_norm(m, h, y, wa, wb, 1e-5, h3, x3, y_parts=sp2)
-    torch.cuda.synchronize()
-    torch.testing.assert_close(h2, h3, rtol=1e-4, atol=1e-6)
-    torch.testing.assert_close(xo.float(), x3.float(), rtol=1e-2, atol=1e-4)
-
-
-def test_linear_residual_norm_refused_where_units_exceed_the_grid():
-    """Row counts whose units cannot all be resident at once run the projection and the norm apart."""
-    assert L.linear_residual_norm_splits(1536, 4608, 16384) == 0
-    m = 16384
-    w = torch.zeros((1536, 4608), dtype=torch.bfloat16, device=DEV)
-    x = torch.zeros((m, 4608), dtype=torch.bfloat16, device=DEV)
-    h = torch.zeros((m, 1536), device=DEV)
-    h2, xo = torch.zeros_like(h), torch.zeros((m, 1536), dtype=torch.bfloat16, device=DEV)
-    wa = torch.zeros((1536,), dtype=torch.bfloat16, device=DEV)
-    ws = torch.zeros((L.linear_workspace_bytes(1536, m, 1),), dtype=torch.uint8, device=DEV)
-    with pytest.raises(RuntimeError, match="unsupported"):
-        L.linear(w, x, m, L.residual_norm_epilogue(h, h2, xo, wa, wa, 1e-5), ws, splits=1)
 
 
 @pytest.mark.parametrize("bs,K,draft,chunk,q_scale", [(64, 17, False, 4096, 1.0), (64, 17, True, 4096, 1.0),

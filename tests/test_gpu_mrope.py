@@ -60,7 +60,7 @@ def test_qkv_epilogue_with_multimodal_positions(m):
     for i in range(3):
         e.mrope_section[i] = cfg.mrope_section[i]
     e.rotary_dim, e.n_q_heads, e.n_kv_heads, e.page_size = cfg.rotary_dim, nq, nkv, ps
-    ws = torch.zeros((L.linear_workspace_bytes(cfg.qkv_dim, m, L.linear_default_splits(cfg.qkv_dim, H, m)),),
+    ws = torch.zeros((L.linear_workspace_bytes(cfg.qkv_dim, m, L.linear_default_splits(cfg.qkv_dim, H, m, L.EPI_QKV_ROPE)),),
                      dtype=torch.uint8, device=DEV)
     L.linear(w, x, m, e, ws)
     torch.cuda.synchronize()
