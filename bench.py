@@ -785,8 +785,8 @@ def case_linear(a):
     g = torch.Generator().manual_seed(2)
     w = (torch.randn((n_out, k_in), generator=g) * 0.02).to("cuda", torch.bfloat16)
     x = torch.randn((m, k_in), generator=g).to("cuda", torch.bfloat16)
-    mode = {"f32": L.EPI_STORE_F32, "partial": L.EPI_PARTIAL_F32, "swiglu": L.EPI_SWIGLU, "argmax": L.EPI_ARGMAX,
-            "qkv": L.EPI_QKV_ROPE}[a.epi]
+    mode = {"f32": L.EPI_STORE_F32, "bf16": L.EPI_STORE_BF16, "partial": L.EPI_PARTIAL_F32, "swiglu": L.EPI_SWIGLU,
+            "argmax": L.EPI_ARGMAX, "qkv": L.EPI_QKV_ROPE}[a.epi]
     sp = a.splits or L.linear_default_splits(n_out, k_in, m, mode)
     e = L.Epilogue()
     e.mode = mode
@@ -798,6 +798,10 @@ def case_linear(a):
     elif mode == L.EPI_SWIGLU:
         out = torch.zeros((m, n_out // 2), dtype=torch.bfloat16, device="cuda")
         e.out, e.ld_out = out.data_ptr(), n_out // 2
+        keep.append(out)
+    elif mode == L.EPI_STORE_BF16:
+        out = torch.zeros((m, n_out), dtype=torch.bfloat16, device="cuda")
+        e.out, e.ld_out = out.data_ptr(), n_out
         keep.append(out)
     elif mode == L.EPI_ARGMAX:
         idx = torch.zeros((m,), dtype=torch.int32, device="cuda")
@@ -871,7 +875,7 @@ def case_main(argv):
     li.add_argument("--n-out", type=int, default=9216)
     li.add_argument("--k-in", type=int, default=1536)
     li.add_argument("--m", type=int, default=17)
-    li.add_argument("--epi", default="swiglu", choices=["f32", "partial", "swiglu", "argmax", "qkv"])
+    li.add_argument("--epi", default="swiglu", choices=["f32", "bf16", "partial", "swiglu", "argmax", "qkv"])
     li.add_argument("--splits", type=int, default=0)
     li.add_argument("--reps", type=int, default=3)
     sa = sub.add_parser("sample")

@@ -53,9 +53,31 @@ __device__ __forceinline__ Top2 top2_warp(Top2 x) {
 // Apply the epilogue to 16 consecutive tokens [t0, t0+16) of feature row f_local of this tile.  Called by the 128
 // epilogue threads of one column half together (it may use warp shuffles, the half's barrier and the CTA's
 // epilogue shared memory `scratch`).
+// Per-row inputs of the QKV epilogue for one 16-token chunk as lane l holds them (token t0 + (l & 15), clamped to the
+// tile's rows): RoPE position(s) and cache slot.  Loaded one chunk ahead, so their L2 round trip overlaps the
+// previous chunk's work instead of opening every chunk.
+struct RowIn {
+  int pos_l, pos_h, pos_w;
+  long long slot;
+};
+__device__ __forceinline__ RowIn qkv_row_inputs(const LinearParams& p, int t0, int t_end) {
+  const int tl = min(t0 + (static_cast<int>(threadIdx.x) & 15), t_end - 1);
+  RowIn r;
+  if (p.row_pos3) {
+    r.pos_l = p.row_pos3[tl * 3];
+    r.pos_h = p.row_pos3[tl * 3 + 1];
+    r.pos_w = p.row_pos3[tl * 3 + 2];
+  } else {
+    r.pos_l = p.row_pos[tl];
+    r.pos_h = r.pos_w = 0;
+  }
+  r.slot = p.row_slot[tl];
+  return r;
+}
+
 template <int EPI>
 __device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, int m_tile, int f_local, int t0,
-                                           const float* v, float* scratch, int split) {
+                                           const float* v, float* scratch, int split, const RowIn& ri) {
   const int lane = threadIdx.x & 31;
   const int t_end = min(p.m, (m_tile + 1) * p.nt);
   // bf16 staging area of this warp: [16 tokens][32 rows]
@@ -111,11 +133,10 @@ __device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, in
     const bool is_q = head < p.n_q_heads;
     const bool is_v = head >= p.n_q_heads + p.n_kv_heads;
     const bool rot = !is_v && (d & ~31) < p.rotary_dim;  // warp-uniform: rotary_dim is a multiple of 32
-    // The chunk's 16 positions / cache slots take one coalesced load per warp (lanes l and l + 16 fetch token l) and
-    // reach every lane by shuffles; cos / sin are computed in registers.  Per-token loads here would share the SM's
-    // L1 / shared-memory bandwidth with the tensor core's operand reads of the next unit.
-    const int tl = min(t0 + (lane & 15), t_end - 1);
-    const long long slot_l = is_q ? 0ll : p.row_slot[tl];
+    // The chunk's 16 positions / cache slots came with one coalesced load per warp (lanes l and l + 16 hold token l,
+    // qkv_row_inputs) and reach every lane by shuffles; cos / sin are computed in registers.  Per-token loads here
+    // would share the SM's L1 / shared-memory bandwidth with the tensor core's operand reads of the next unit.
+    const long long slot_l = is_q ? 0ll : ri.slot;
     float o[16];
     if (rot) {
       // Lanes d and d ^ 1 rotate the same pair and need the same angles: the even lane computes cos / sin for
@@ -127,9 +148,7 @@ __device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, in
       const bool mm = p.row_pos3 != nullptr;
       const int pair = d >> 1;
       const int axis = pair < p.mrope_s0 ? 0 : (pair < p.mrope_s0 + p.mrope_s1 ? 1 : 2);
-      const int pos_l = mm ? p.row_pos3[tl * 3] : p.row_pos[tl];
-      const int pos_h = mm ? p.row_pos3[tl * 3 + 1] : 0;
-      const int pos_w = mm ? p.row_pos3[tl * 3 + 2] : 0;
+      const int pos_l = ri.pos_l, pos_h = ri.pos_h, pos_w = ri.pos_w;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         int pos = __shfl_sync(0xffffffffu, pos_l, odd ? 8 + i : i);
@@ -222,24 +241,36 @@ __device__ __forceinline__ void unit_epilogue(const LinearParams& p, uint32_t t_
     if (run) {
       // the next chunk's TMEM load is in flight while this chunk's epilogue runs
       // (chunks past the tile's rows hold no tokens: a short last tile is computed at N = its rows)
+      // (and, for QKV, the next chunk's row inputs)
+      const int t_end = t_beg + rows;
       uint32_t ra[16], rb[16];
+      RowIn ia{}, ib{};
       int c0 = half * 16;
-      if (c0 < rows) tmem_ld16_issue(t_lane + c0, ra);
+      if (c0 < rows) {
+        tmem_ld16_issue(t_lane + c0, ra);
+        if constexpr (EPI == GR_EPI_QKV_ROPE) ia = qkv_row_inputs(p, t_beg + c0, t_end);
+      }
       while (c0 < rows) {
         float v[16];
         tmem_ld16_wait(ra);
         const int c1 = c0 + 32;
-        if (c1 < rows) tmem_ld16_issue(t_lane + c1, rb);
+        if (c1 < rows) {
+          tmem_ld16_issue(t_lane + c1, rb);
+          if constexpr (EPI == GR_EPI_QKV_ROPE) ib = qkv_row_inputs(p, t_beg + c1, t_end);
+        }
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(ra[i]);
-        epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, scratch, split);
+        epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, scratch, split, ia);
         if (c1 >= rows) break;
         tmem_ld16_wait(rb);
         c0 = c1 + 32;
-        if (c0 < rows) tmem_ld16_issue(t_lane + c0, ra);
+        if (c0 < rows) {
+          tmem_ld16_issue(t_lane + c0, ra);
+          if constexpr (EPI == GR_EPI_QKV_ROPE) ia = qkv_row_inputs(p, t_beg + c0, t_end);
+        }
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(rb[i]);
-        epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c1, v, scratch, split);
+        epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c1, v, scratch, split, ib);
       }
     }
     tc_fence_before();
@@ -269,11 +300,28 @@ __device__ __forceinline__ void unit_epilogue(const LinearParams& p, uint32_t t_
       __threadfence();
       const float* base = p.ws_partial + (size_t)tile * p.splits * p.nt * 128;
       for (int c0 = half * 16; c0 < rows; c0 += 32) {
-        // split order is fixed (deterministic sums); the 16 rows' loads of one split are independent
+        RowIn ri{};  // issued with the partials' loads: one round trip
+        if constexpr (EPI == GR_EPI_QKV_ROPE) ri = qkv_row_inputs(p, t_beg + c0, t_beg + rows);
+        // split order is fixed (deterministic sums); four splits' 16 rows each in flight at a time (one L2 round
+        // trip per four splits)
         float v[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = 0.f;
-        for (int s = 0; s < p.splits; ++s) {
+        int s = 0;
+        for (; s + 4 <= p.splits; s += 4) {
+          float x[4][16];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float* src = base + ((size_t)(s + u) * p.nt + c0) * 128 + f_local;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) x[u][i] = (c0 + i < rows) ? __ldcg(src + i * 128) : 0.f;
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] += x[u][i];
+        }
+        for (; s < p.splits; ++s) {
           const float* src = base + ((size_t)s * p.nt + c0) * 128 + f_local;
           float x[16];
 #pragma unroll
@@ -281,7 +329,7 @@ __device__ __forceinline__ void unit_epilogue(const LinearParams& p, uint32_t t_
 #pragma unroll
           for (int i = 0; i < 16; ++i) v[i] += x[i];
         }
-        epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, scratch, split);
+        epilogue16<EPI>(p, n_tile, m_tile, f_local, t_beg + c0, v, scratch, split, ri);
       }
       if (leader) p.ws_ticket[tile] = 0;
     }
