@@ -99,15 +99,17 @@ _CHUNK_BY_PAIRS = ((16, 640), (64, 1024), (192, 1536))
 
 def attention_split(bs: int, K: int, max_len: int, avg_len: int, n_kv: int, sms: int) -> Tuple[int, int]:
     """Cache tokens per split and the split-grid extent.  With enough (request, head) pairs to fill the GPU twice the
-    requests run unsplit (no merge); below that the chunk grows with the number of pairs (_CHUNK_BY_PAIRS, then 2048
-    tokens), never so small that a request needs more splits than the merges take: 8 while the grid stays within one
+    requests run in 4096-token splits (2560 just above twice); below that the chunk grows with the number of pairs
+    (_CHUNK_BY_PAIRS, then 2048 tokens), never so small that a request needs more splits than the merges take: 8 while the grid stays within one
     CTA per SM (those splits merge inside one portable thread-block cluster), 16 otherwise.  A single request keeps a
     finer cut (about 16 splits of its length, capped at 8 by the cluster), which measured fastest inside its
     forward."""
     L = max_len + K + 1
     units = max(1, bs * n_kv)
     if units >= 2 * sms:
-        chunk = 4096
+        # just above two CTAs per SM a 4096-token chunk leaves a thin second wave (measured: 40 requests 71.5 us at
+        # 2560 against 86.4 at 4096); from ~2.4 CTAs per SM on, the widest chunk wins
+        chunk = 2560 if units < (12 * sms) // 5 else 4096
     elif bs == 1:
         chunk = max(128, -(-max(1, avg_len) // 16))
     else:
