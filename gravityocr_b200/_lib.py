@@ -22,7 +22,7 @@ ROWS_DRAFT, ROWS_VERIFY, ROWS_EXPLICIT = range(3)
 
 # every symbol include/gravity_b200.h declares
 EXPORTS = ("gr_version", "gr_status_string", "gr_set_pdl", "gr_set_attention_tc", "gr_num_sms", "gr_linear_workspace_bytes",
-           "gr_attention_workspace_bytes", "gr_linear_default_splits", "gr_linear", "gr_embed_rows",
+           "gr_attention_workspace_bytes", "gr_linear_default_splits", "gr_linear_plan", "gr_linear", "gr_embed_rows",
            "gr_residual_norm", "gr_bd_attention", "gr_accept_commit", "gr_draft_override", "gr_pack_gate_up",
            "gr_bd_attention_noalloc", "gr_bd_attention_ordered", "gr_gather_rows", "gr_logits_process",
            "gr_sample_rows", "gr_commit_sampled", "gr_penalty_cumulate")
@@ -96,6 +96,7 @@ _SIGS = {
     "gr_linear_workspace_bytes": (_Z, [_I, _I, _I]),
     "gr_attention_workspace_bytes": (_Z, [_I, _I, _I, _I, _I]),
     "gr_linear_default_splits": (_I, [_I, _I, _I, _I]),
+    "gr_linear_plan": (_I, [_I, _I, _I, _I, _I, _P]),
     "gr_linear": (_I, [_P, _I, _I, _P, _I, ctypes.POINTER(Epilogue), _I, _P, _Z, _P, _Z, _P, _P]),
     "gr_embed_rows": (_I, [_I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _I, _I, _P, _F, _I, _P, _P, _P,
                            _P, _P, _P, _P, _P]),
@@ -180,6 +181,13 @@ def linear_workspace_bytes(n_out: int, m: int, splits: int) -> int:
 def linear_default_splits(n_out: int, k_in: int, m: int, mode: int = EPI_STORE_F32) -> int:
     """Split-K count gr_linear plans for this shape and epilogue mode."""
     return int(load().gr_linear_default_splits(n_out, k_in, m, mode))
+
+
+def linear_plan(n_out: int, k_in: int, m: int, mode: int = EPI_STORE_F32, splits: int = 0) -> dict:
+    """The plan gr_linear runs for this call: split count, token-tile height and count, unit order, grid."""
+    out = (ctypes.c_int32 * 5)()
+    _check(load().gr_linear_plan(n_out, k_in, m, mode, splits, out), "gr_linear_plan")
+    return {"splits": out[0], "nt": out[1], "m_tiles": out[2], "tail_last": bool(out[3]), "grid": out[4]}
 
 
 def attention_workspace_bytes(bs: int, K: int, n_q_heads: int, n_kv_heads: int, max_splits: int) -> int:

@@ -335,6 +335,25 @@ int gr_linear_default_splits(int n_out, int k_in, int m, int mode) {
   return default_splits(n_out, k_in, m, mode);
 }
 
+int gr_linear_plan(int n_out, int k_in, int m, int mode, int splits, int32_t* out) {
+  if (!out || mode < GR_EPI_STORE_F32 || mode > GR_EPI_PARTIAL_F32 || n_out <= 0 || (n_out % 128) || k_in <= 0 ||
+      (k_in % 64) || m <= 0)
+    return GR_ERR_ARG;
+  if (splits <= 0) splits = default_splits(n_out, k_in, m, mode);
+  if ((k_in / 64) % splits) return GR_ERR_ARG;
+  const LinearShape s = linear_shape(n_out, k_in, m, splits, mode);
+  int stages, per_sm;
+  linear_launch_shape(s.nt, s.kc / splits, mode, &stages, &per_sm);
+  const long long units = static_cast<long long>(s.n_tiles) * s.m_tiles * splits;
+  const long long cap = static_cast<long long>(num_sms()) * per_sm;
+  out[0] = splits;
+  out[1] = s.nt;
+  out[2] = s.m_tiles;
+  out[3] = s.tail_last ? 1 : 0;
+  out[4] = static_cast<int32_t>(units < cap ? units : cap);
+  return GR_OK;
+}
+
 size_t gr_linear_workspace_bytes(int n_out, int m, int splits) {
   if (n_out <= 0 || m <= 0) return 0;
   if (splits < 1) splits = 1;

@@ -149,24 +149,33 @@ __device__ __forceinline__ void epilogue16(const LinearParams& p, int n_tile, in
       const int pair = d >> 1;
       const int axis = pair < p.mrope_s0 ? 0 : (pair < p.mrope_s0 + p.mrope_s1 ? 1 : 2);
       const int pos_l = ri.pos_l, pos_h = ri.pos_h, pos_w = ri.pos_w;
+      // In phases, each an independent unrolled loop: with one or two epilogue warps per scheduler there is nothing
+      // else to hide latency behind, and the eight tokens' shuffle -> angle -> exchange chains interleave only when
+      // no shuffle sits between one token's steps and the next token's.
+      int pos[8];
+      float pa[16], sn[8], cs[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        int pos = __shfl_sync(0xffffffffu, pos_l, odd ? 8 + i : i);
+        pos[i] = __shfl_sync(0xffffffffu, pos_l, odd ? 8 + i : i);
         if (mm) {
           const int ph = __shfl_sync(0xffffffffu, pos_h, odd ? 8 + i : i);
           const int pw = __shfl_sync(0xffffffffu, pos_w, odd ? 8 + i : i);
-          pos = axis == 0 ? pos : (axis == 1 ? ph : pw);
+          pos[i] = axis == 0 ? pos[i] : (axis == 1 ? ph : pw);
         }
-        float sn, cs;
-        rope_sincos(__fmul_rn(static_cast<float>(pos), fr), &sn, &cs);  // the reference's fp32 pos * inv_freq
-        const float cs_o = __shfl_xor_sync(0xffffffffu, cs, 1);
-        const float sn_o = __shfl_xor_sync(0xffffffffu, sn, 1);
-        const float ca = odd ? cs_o : cs, sa = odd ? sn_o : sn;  // token i
-        const float cb = odd ? cs : cs_o, sb = odd ? sn : sn_o;  // token 8 + i
-        const float pa = __shfl_xor_sync(0xffffffffu, v[i], 1);
-        const float pb = __shfl_xor_sync(0xffffffffu, v[8 + i], 1);
-        o[i] = odd ? (v[i] * ca + pa * sa) : (v[i] * ca - pa * sa);
-        o[8 + i] = odd ? (v[8 + i] * cb + pb * sb) : (v[8 + i] * cb - pb * sb);
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) pa[i] = __shfl_xor_sync(0xffffffffu, v[i], 1);  // the pair partner's values
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        rope_sincos(__fmul_rn(static_cast<float>(pos[i]), fr), &sn[i], &cs[i]);  // the reference's fp32 pos * inv_freq
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float cs_o = __shfl_xor_sync(0xffffffffu, cs[i], 1);
+        const float sn_o = __shfl_xor_sync(0xffffffffu, sn[i], 1);
+        const float ca = odd ? cs_o : cs[i], sa = odd ? sn_o : sn[i];  // token i
+        const float cb = odd ? cs[i] : cs_o, sb = odd ? sn[i] : sn_o;  // token 8 + i
+        o[i] = odd ? (v[i] * ca + pa[i] * sa) : (v[i] * ca - pa[i] * sa);
+        o[8 + i] = odd ? (v[8 + i] * cb + pa[8 + i] * sb) : (v[8 + i] * cb - pa[8 + i] * sb);
       }
     } else {
 #pragma unroll

@@ -94,6 +94,10 @@ size_t gr_attention_workspace_bytes(int bs, int K, int n_q_heads, int n_kv_heads
  * split-K tile's last split reads every split's partial before it runs the epilogue; GR_EPI_PARTIAL_F32 leaves the
  * sum to its consumer). */
 int gr_linear_default_splits(int n_out, int k_in, int m, int mode);
+/* The plan gr_linear runs for this call shape (splits = 0: the default): out[0] split-K count, out[1] token-tile
+ * height nt, out[2] token tiles, out[3] 1 when a shorter last tile's units run after the full tiles' (odd waves in
+ * reverse), out[4] persistent grid.  Diagnostics: no reference counterpart. */
+int gr_linear_plan(int n_out, int k_in, int m, int mode, int splits, int32_t* out);
 
 /* Weight-streaming projection with a fused epilogue:  y[t, f] = sum_k x[t, k] * w[f, k].
  * w: bf16 [n_out, k_in] row-major (nn.Linear); x: bf16 [m, k_in] row-major; n_out % 128 == 0, k_in % 64 == 0,
