@@ -491,7 +491,7 @@ def test_linear_partials_summed_by_residual_norm(n_out, k_in, m):
                                                      (12, 33, True, 1024, 1.0), (20, 64, False, 4096, 2.0),
                                                      (1, 17, False, 256, 1.0), (2, 17, True, 512, 4.0),
                                                      (1, 17, True, 192, 1.0), (4, 33, False, 4096, 1.0),
-                                                     (3, 17, False, 1024, 8.0)])
+                                                     (3, 17, False, 1024, 8.0), (40, 17, False, 2560, 1.0)])
 def test_attention_tc_matches_mma_kernel(bs, K, draft, chunk, q_scale):
     """The tcgen05 / TMEM kernel against the fp32 reference and the mma.sync kernel on the same inputs: large grids
     (more units than SMs; global split merge) and small grids (one CTA per SM; the splits of a (request, kv head) as
