@@ -702,7 +702,7 @@ def config4_sweep(a):
 
 
 # ---------------------------------------------------------------------------------------------------------------------
-# Single-kernel cases for ncu captures: `python bench.py case attention|linear|sample ...`.  Each is a small,
+# Single-kernel cases for ncu captures: `python bench.py case attention|linear|norm|sample ...`.  Each is a small,
 # self-contained workload (a few GB on the device at most, inputs larger than L2): one untimed warm-up launch, then
 # `--reps` launches; prints the mean CUDA-event time and the algorithmic bytes / FLOPs of one launch.  Example:
 #
@@ -826,6 +826,22 @@ def case_linear(a):
             "weight_GBps": n_out * k_in * 2 / ms / 1e6, "TFLOPs": fl / ms / 1e9}
 
 
+def case_norm(a):
+    """One residual + sandwich norm launch over --m rows of hidden 1,536 summing --parts split-K partials."""
+    from gravityocr_b200 import _lib as L
+    m, H, sp = a.m, 1536, a.parts
+    g = torch.Generator().manual_seed(3)
+    y = (torch.randn((sp, m, H), generator=g) * 0.3).cuda()
+    h = (torch.randn((m, H), generator=g) * 0.1).cuda()
+    wa = (torch.randn((H,), generator=g) * 0.02).to("cuda", torch.bfloat16)
+    wb = (torch.randn((H,), generator=g) * 0.02).to("cuda", torch.bfloat16)
+    h2 = torch.empty_like(h)
+    xo = torch.empty((m, H), dtype=torch.bfloat16, device="cuda")
+    ms = _case_time(lambda: L.residual_norm(m, h, y, wa, wb, 1e-5, h2, xo, y_parts=sp), a.reps, a.graph)
+    b = m * H * (4 * sp + 4 + 4 + 2)
+    return {"kernel": "residual_norm", "m": m, "parts": sp, "ms": ms, "bytes": b, "GBps": b / ms / 1e6}
+
+
 def case_sample(a):
     """One sample_rows launch over bs x K verify rows of fp32 logits (vocabulary 59,392): temperature 0.8, top-k 50,
     top-p 0.95 under the joint filter (or --filter), accept bits against seeded draft tokens and the draws."""
@@ -878,6 +894,10 @@ def case_main(argv):
     li.add_argument("--epi", default="swiglu", choices=["f32", "bf16", "partial", "swiglu", "argmax", "qkv"])
     li.add_argument("--splits", type=int, default=0)
     li.add_argument("--reps", type=int, default=3)
+    nm = sub.add_parser("norm")
+    nm.add_argument("--m", type=int, default=1088)
+    nm.add_argument("--parts", type=int, default=2)
+    nm.add_argument("--reps", type=int, default=3)
     sa = sub.add_parser("sample")
     sa.add_argument("--bs", type=int, default=64)
     sa.add_argument("--bd", type=int, default=K_BD)
@@ -888,7 +908,7 @@ def case_main(argv):
     sa.add_argument("--scale", type=float, default=3.0, help="std of the synthetic logits")
     sa.add_argument("--reps", type=int, default=3)
     a = ap.parse_args(argv)
-    fn = {"attention": case_attention, "linear": case_linear, "sample": case_sample}[a.case]
+    fn = {"attention": case_attention, "linear": case_linear, "norm": case_norm, "sample": case_sample}[a.case]
     print(json.dumps(fn(a)), flush=True)
     return 0
 

@@ -625,6 +625,7 @@ int gr_residual_norm(int m, int hidden, const float* h_in, const float* y, int y
   p.eps = eps;
   p.h_out = h_out;
   p.x_out = static_cast<__nv_bfloat16*>(x_out);
+  p.sms = num_sms();
   return launch_residual_norm(p, static_cast<cudaStream_t>(stream), g_pdl) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
 }
 

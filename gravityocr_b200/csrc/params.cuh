@@ -72,6 +72,7 @@ struct EmbedParams {
 };
 struct ResNormParams {
   int m, hidden, y_parts;
+  int sms;  // SMs of the device: the many-rows kernel runs a fixed number of CTAs per SM
   const float* h_in;
   const float* y;
   const __nv_bfloat16* w_a;

@@ -485,6 +485,32 @@ def test_linear_partials_summed_by_residual_norm(n_out, k_in, m):
     torch.testing.assert_close(xo.float(), rms(hr, wb), rtol=1e-2, atol=1e-4)
 
 
+@pytest.mark.parametrize("parts", [1, 2, 3, 4, 5])
+def test_residual_norm_many_rows_kernel(parts):
+    """Above 512 rows the norm runs a fixed grid of CTAs that walk the rows with the next row's loads in flight (up to
+    four partials; five fall back to one CTA per row).  Against the fp32 reference, and bit for bit against the
+    few-rows kernel on the rows both calls compute (same arithmetic in the same order)."""
+    m, H = 1088, 1536
+    g = torch.Generator().manual_seed(parts)
+    y = torch.randn((parts, m, H), generator=g).to(DEV) * 0.3
+    h = torch.randn((m, H), generator=g).to(DEV) * 0.1
+    wa, wb = _rand((H,), g, 0.02), _rand((H,), g, 0.02)
+    h2 = torch.full_like(h, float("nan"))
+    xo = torch.zeros((m, H), dtype=torch.bfloat16, device=DEV)
+    L.residual_norm(m, h, y, wa, wb, 1e-5, h2, xo, y_parts=parts)
+    few = 500
+    yf = y[:, :few].contiguous()
+    h2f = torch.full((few, H), float("nan"), device=DEV)
+    xof = torch.zeros((few, H), dtype=torch.bfloat16, device=DEV)
+    L.residual_norm(few, h[:few].contiguous(), yf, wa, wb, 1e-5, h2f, xof, y_parts=parts)
+    torch.cuda.synchronize()
+    rms = lambda t, ww: ww.float() * (t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + 1e-5))
+    hr = h + rms(y.sum(0), wa)
+    torch.testing.assert_close(h2, hr, rtol=1e-4, atol=1e-6)
+    torch.testing.assert_close(xo.float(), rms(hr, wb), rtol=1e-2, atol=1e-4)
+    assert torch.equal(h2[:few], h2f) and torch.equal(xo[:few], xof)
+
+
 @pytest.mark.parametrize("bs,K,draft,chunk,q_scale", [(64, 17, False, 4096, 1.0), (64, 17, True, 4096, 1.0),
                                                      (24, 17, False, 512, 1.0), (24, 17, True, 256, 4.0),
                                                      (40, 9, False, 1024, 8.0), (20, 32, True, 4096, 1.0),
