@@ -43,6 +43,7 @@ struct AttnParams {
   int n_q_heads, n_kv_heads, page_size;
   int chunk, max_splits, groups;
   int cluster;           // 1: the max_splits CTAs of a (request, kv head) form one cluster and merge through DSMEM
+  int split_outer;       // 1: grid (kv head, request, split) instead of (split, kv head, request); tcgen05 kernel only
   const int32_t* order;  // optional: grid z -> request (longest first), NULL = identity
   float scale_log2;
   float* ws_o;
