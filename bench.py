@@ -702,7 +702,7 @@ def config4_sweep(a):
 
 
 # ---------------------------------------------------------------------------------------------------------------------
-# Single-kernel cases for ncu captures: `python bench.py case attention|linear|norm|sample ...`.  Each is a small,
+# Single-kernel cases for ncu captures: `python bench.py case attention|linear|norm|sample|timeline ...`.  Each is a small,
 # self-contained workload (a few GB on the device at most, inputs larger than L2): one untimed warm-up launch, then
 # `--reps` launches; prints the mean CUDA-event time and the algorithmic bytes / FLOPs of one launch.  Example:
 #
@@ -842,6 +842,129 @@ def case_norm(a):
     return {"kernel": "residual_norm", "m": m, "parts": sp, "ms": ms, "bytes": b, "GBps": b / ms / 1e6}
 
 
+_TL_KINDS = {1: "attention_kernel", 2: "attention_tc_kernel", 3: "argmax_reduce_kernel", 4: "residual_norm",
+             6: "embed_rows_kernel", 7: "accept_commit_kernel", 10: "linear f32", 11: "linear bf16",
+             12: "linear gate_up+SwiGLU", 13: "linear QKV+RoPE", 14: "linear lm_head+argmax", 15: "linear o/down partials"}
+
+
+def _timeline_records(lib):
+    """(kind, block, entry, dependency release or 0, exit) per CTA, from every unit's record array: the release record
+    of a CTA is the latest one of its block inside its [entry, exit] (an earlier kernel's CTA with the same block index
+    may release inside that window too, but before it)."""
+    import ctypes
+
+    class Rec(ctypes.Structure):
+        _fields_ = [("kind", ctypes.c_uint32), ("block", ctypes.c_uint32), ("t0", ctypes.c_uint64),
+                    ("t1", ctypes.c_uint64)]
+    out = []
+    for unit in ("linear", "attention", "attention_tc", "rowwise"):
+        buf = (Rec * (1 << 19))()
+        n = ctypes.c_uint32(0)
+        assert getattr(lib, "gr_timeline_read_" + unit)(buf, ctypes.byref(n)) == 0
+        rs = [(r.kind, r.block, r.t0, r.t1) for r in buf[:min(n.value, 1 << 19)]]
+        deps = {}
+        for r in rs:
+            if r[0] == 0:
+                deps.setdefault(r[1], []).append(r[2])
+        for r in rs:
+            if r[0]:
+                d = [t for t in deps.get(r[1], ()) if r[2] <= t <= r[3]]
+                out.append((r[0], r[1], r[2], max(d) if d else 0, r[3]))
+    return out
+
+
+def _timeline_launches(recs):
+    """Group CTA records into launches: in entry order, a launch is a run of one kind with distinct blocks (the next
+    kernel's CTAs start only after every CTA of this one has started)."""
+    out = []
+    for r in sorted(recs, key=lambda r: r[2]):
+        if not (out and out[-1]["kind"] == r[0] and r[1] not in out[-1]["blocks"]):
+            out.append({"kind": r[0], "blocks": set(), "t0": r[2], "dep": None, "t1": 0})
+        L = out[-1]
+        L["blocks"].add(r[1])
+        L["t1"] = max(L["t1"], r[4])
+        if r[3]:
+            L["dep"] = r[3] if L["dep"] is None else min(L["dep"], r[3])
+    return out
+
+
+def case_timeline(a):
+    """Live per-kernel timeline of one self-spec round (draft + verify + commit graphs) from the timeline build
+    (python -m gravityocr_b200.build --timeline): per kernel kind, its share of the round (the time from the previous
+    launch's last CTA exit to this launch's last exit), its critical path after its dependency was released, and the
+    release latency.  Batch 1: the config-2 crop (prefix 288); larger batches: the first --batch config-3 requests."""
+    os.environ["GRAVITY_B200_LIB"] = os.path.join(ROOT, "gravityocr_b200", "libgravity_b200_timeline.so")
+    import ctypes
+    from gravityocr_b200 import _lib as L
+    from gravityocr_b200.config import ModelConfig
+    from gravityocr_b200.engine import Engine
+    from gravityocr_b200.weights import random_weights
+    lib = ctypes.CDLL(L.LIB_PATH)
+    cfg = ModelConfig()
+    dev = torch.device("cuda", 0)
+    K, bs = a.bd + 1, a.batch
+    w = random_weights(cfg, SEED, torch.bfloat16)
+    if bs == 1:
+        P = 288
+        cap = P + 2 * 1024 + 4 * K + 64
+        ppr = (cap + 15) // 16
+        eng = Engine(cfg, w, max_rows=64, n_pages=ppr + 16, device=dev)
+        eng.reserve(K)
+        rb = eng.new_round_buffers(1, K, ppr, max_len=cap, avg_len=P + 512)
+        rb.page_table[0] = torch.tensor(eng.pool.alloc(ppr), dtype=torch.int32, device=dev)
+        x, ids = request_rows(cfg, w, 2, 0, 256)
+        eng.prefill(rb, [x], [ids])
+    else:
+        n_img, _ = workload(cfg, bs, SEED)
+        prefix = [n_img[i] + 32 for i in range(bs)]
+        cap = max(prefix) + 40 * (K + 1) + 2 * K + 64
+        ppr = (cap + 15) // 16
+        eng = Engine(cfg, w, max_rows=max(bs * K, bs * 64), n_pages=bs * ppr + 8, device=dev)
+        eng.reserve(bs * K)
+        rb = eng.new_round_buffers(bs, K, ppr, max_len=cap, avg_len=int(sum(prefix) / bs))
+        for b in range(bs):
+            rb.page_table[b] = torch.tensor(eng.pool.alloc(ppr), dtype=torch.int32, device=dev)
+        xs, ids = zip(*[request_rows(cfg, w, SEED, i, n_img[i]) for i in range(bs)])
+        eng.prefill(rb, list(xs), list(ids), chunk=64)
+    eng.round_launch(rb)
+    torch.cuda.synchronize()
+    gd, gv = eng.capture_split(rb)
+    for _ in range(4):
+        gd.replay()
+        gv.replay()
+    torch.cuda.synchronize()
+    for unit in ("linear", "attention", "attention_tc", "rowwise"):
+        assert getattr(lib, "gr_timeline_clear_" + unit)() == 0
+    gd.replay()
+    gv.replay()
+    torch.cuda.synchronize()
+    eng.check_status(rb)
+    ls = _timeline_launches(_timeline_records(lib))
+    agg = {}
+    prev = ls[0]["t0"]
+    for L_ in ls:
+        name = _TL_KINDS.get(L_["kind"], str(L_["kind"]))
+        dep = L_["dep"] or L_["t0"]
+        g = agg.setdefault(name, {"launches": 0, "round_us": 0.0, "busy_us": 0.0, "release_us": 0.0})
+        g["launches"] += 1
+        g["round_us"] += (L_["t1"] - prev) / 1e3
+        g["busy_us"] += (L_["t1"] - dep) / 1e3
+        g["release_us"] += (dep - prev) / 1e3
+        prev = L_["t1"]
+    total = (ls[-1]["t1"] - ls[0]["t0"]) / 1e3
+    kinds = {}
+    for name, g in sorted(agg.items(), key=lambda kv: -kv[1]["round_us"]):
+        n = g["launches"]
+        kinds[name] = {"launches": n, "round_us": round(g["round_us"], 1), "share": round(g["round_us"] / total, 4),
+                       "avg_us": round(g["round_us"] / n, 2), "avg_busy_us": round(g["busy_us"] / n, 2),
+                       "avg_release_us": round(g["release_us"] / n, 2)}
+    return {"case": "timeline", "batch": bs, "K": K, "launches": len(ls), "round_us": round(total, 1),
+            "forward_us": round(total / 2, 1), "kinds": kinds,
+            "note": "avg_us: launch share of the round (previous launch's last exit to this one's); avg_busy_us: "
+                    "dependency release to last CTA exit (PDL lets a launch's CTAs start before that); "
+                    "avg_release_us: previous launch's last exit to this launch's first griddepcontrol.wait return"}
+
+
 def case_sample(a):
     """One sample_rows launch over bs x K verify rows of fp32 logits (vocabulary 59,392): temperature 0.8, top-k 50,
     top-p 0.95 under the joint filter (or --filter), accept bits against seeded draft tokens and the draws."""
@@ -898,6 +1021,9 @@ def case_main(argv):
     nm.add_argument("--m", type=int, default=1088)
     nm.add_argument("--parts", type=int, default=2)
     nm.add_argument("--reps", type=int, default=3)
+    tl = sub.add_parser("timeline")
+    tl.add_argument("--batch", type=int, default=1)
+    tl.add_argument("--bd", type=int, default=K_BD)
     sa = sub.add_parser("sample")
     sa.add_argument("--bs", type=int, default=64)
     sa.add_argument("--bd", type=int, default=K_BD)
@@ -908,7 +1034,8 @@ def case_main(argv):
     sa.add_argument("--scale", type=float, default=3.0, help="std of the synthetic logits")
     sa.add_argument("--reps", type=int, default=3)
     a = ap.parse_args(argv)
-    fn = {"attention": case_attention, "linear": case_linear, "norm": case_norm, "sample": case_sample}[a.case]
+    fn = {"attention": case_attention, "linear": case_linear, "norm": case_norm, "sample": case_sample,
+          "timeline": case_timeline}[a.case]
     print(json.dumps(fn(a)), flush=True)
     return 0
 

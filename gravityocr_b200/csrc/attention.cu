@@ -32,6 +32,7 @@ template <int MAXT, int MINB, int ST>
 __global__ void __launch_bounds__(MAXT, MINB) attention_kernel(const __grid_constant__ CUtensorMap tmk,
                                                                const __grid_constant__ CUtensorMap tmv,
                                                                const AttnParams p) {
+  GR_TL_BEGIN
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int G = p.n_q_heads / p.n_kv_heads;
@@ -55,6 +56,7 @@ __global__ void __launch_bounds__(MAXT, MINB) attention_kernel(const __grid_cons
   if ((threadIdx.x >> 5) == p.groups * n_mt) attn_preload_pages(p, b, blockIdx.x, threadIdx.x & 31, c.pages);
   pdl_wait();
   attention_unit<ST, true>(&tmk, &tmv, p, blockIdx.x, blockIdx.y, b, threadIdx.x, blockDim.x, 1, 2, c);
+  GR_TL_END(kTlAttentionMma)
 }
 
 size_t attention_smem_bytes(int K, int G, int stages) { return 1024 + attn_region_bytes(attn_rows_pad(G, K), stages); }
@@ -139,3 +141,5 @@ cudaError_t launch_attention(const CUtensorMap& tmk, const CUtensorMap& tmv, con
 }
 
 }  // namespace gr
+
+GR_TIMELINE_EXPORTS(attention)

@@ -58,6 +58,7 @@ template <int ST, int H>
 __global__ void __launch_bounds__(320) attention_tc_kernel(const __grid_constant__ CUtensorMap tmk,
                                                            const __grid_constant__ CUtensorMap tmv,
                                                            const AttnParams p) {
+  GR_TL_BEGIN
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int G = p.n_q_heads / p.n_kv_heads;
@@ -384,6 +385,7 @@ __global__ void __launch_bounds__(320) attention_tc_kernel(const __grid_constant
   } else if (active && n_active > 1) {  // the ring is idle: the merge's weights go there
     attention_merge_global(p, b, kvh, n_active, threadIdx.x, blockDim.x, 1, flag, reinterpret_cast<float*>(ring));
   }
+  GR_TL_END(kTlAttentionTc)
 }
 
 template <int ST, int H>
@@ -470,3 +472,5 @@ cudaError_t launch_attention_tc(const CUtensorMap& tmk, const CUtensorMap& tmv, 
 }
 
 }  // namespace gr
+
+GR_TIMELINE_EXPORTS(attention_tc)

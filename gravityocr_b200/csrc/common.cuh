@@ -42,8 +42,71 @@ __device__ __forceinline__ void report(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
 
+// ------------------------------------------------------------------ launch timeline (timeline build only)
+// Built with -DGR_TIMELINE (python -m gravityocr_b200.build --timeline): thread 0 of every CTA of every round kernel
+// appends (kind, block, entry, exit) globaltimer stamps to its translation unit's record array, and a (0, block, t, t)
+// record when griddepcontrol.wait returns; the host reads them with gr_timeline_read_<unit>.  This shows each
+// launch's dependency release and its CTAs' critical path as the graphs replay, which a serialising profiler does
+// not.  The product build compiles all of it out.
+#ifdef GR_TIMELINE
+struct TimelineRec {
+  uint32_t kind, block;
+  uint64_t t0, t1;
+};
+constexpr uint32_t kTimelineCap = 1u << 19;
+static __device__ TimelineRec g_timeline[kTimelineCap];
+static __device__ uint32_t g_timeline_n;
+__device__ __forceinline__ void timeline_put(uint32_t kind, uint64_t t0, uint64_t t1) {
+  const uint32_t i = atomicAdd(&g_timeline_n, 1u);
+  if (i < kTimelineCap) {
+    TimelineRec r;
+    r.kind = kind;
+    r.block = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    r.t0 = t0;
+    r.t1 = t1;
+    g_timeline[i] = r;
+  }
+}
+#define GR_TL_BEGIN const uint64_t gr_tl_t0 = globaltimer();
+#define GR_TL_END(kind) \
+  if (threadIdx.x == 0) timeline_put((kind), gr_tl_t0, globaltimer());
+#define GR_TL_DEP                        \
+  if (threadIdx.x == 0) {                \
+    const uint64_t gr_tl_t = globaltimer(); \
+    timeline_put(0, gr_tl_t, gr_tl_t);   \
+  }
+#define GR_TIMELINE_EXPORTS(unit)                                                                              \
+  extern "C" int gr_timeline_read_##unit(void* host, uint32_t* n) {                                           \
+    if (cudaMemcpyFromSymbol(n, gr::g_timeline_n, sizeof(uint32_t)) != cudaSuccess) return 1;                \
+    const uint32_t m = *n < gr::kTimelineCap ? *n : gr::kTimelineCap;                                          \
+    return cudaMemcpyFromSymbol(host, gr::g_timeline, m * sizeof(gr::TimelineRec)) == cudaSuccess ? 0 : 1;    \
+  }                                                                                                            \
+  extern "C" int gr_timeline_clear_##unit(void) {                                                              \
+    const uint32_t z = 0;                                                                                      \
+    return cudaMemcpyToSymbol(gr::g_timeline_n, &z, sizeof(uint32_t)) == cudaSuccess ? 0 : 1;                  \
+  }
+#else
+#define GR_TL_BEGIN
+#define GR_TL_END(kind)
+#define GR_TL_DEP
+#define GR_TIMELINE_EXPORTS(unit)
+#endif
+// kinds of the timeline records (linear kernels: kTlLinear + epilogue mode)
+enum : uint32_t {
+  kTlAttentionMma = 1,
+  kTlAttentionTc = 2,
+  kTlArgmaxReduce = 3,
+  kTlResidualNorm = 4,
+  kTlEmbed = 6,
+  kTlCommit = 7,
+  kTlLinear = 10
+};
+
 // ------------------------------------------------------------------ programmatic dependent launch
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  GR_TL_DEP
+}
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ------------------------------------------------------------------ mbarrier

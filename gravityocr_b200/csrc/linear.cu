@@ -27,16 +27,19 @@ constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue (tw
 // lm_head, second step: one warp per token (argmax_reduce_token).
 constexpr int kReduceWarps = 8;
 __global__ void __launch_bounds__(kReduceWarps * 32) argmax_reduce_kernel(const LinearParams p) {
+  GR_TL_BEGIN
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x * kReduceWarps + (threadIdx.x >> 5);
   if (t < p.m) argmax_reduce_token(p, t);
+  GR_TL_END(kTlArgmaxReduce)
 }
 
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_kernel(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
                   const LinearParams p) {
+  GR_TL_BEGIN
   // Persistent: CTA c processes one unit per wave k, unit k * grid + c.  With tail_last (chosen by the host's
   // schedule model) the units of full token tiles are numbered before those of a shorter last tile and odd waves run
   // in reverse (unit k * grid + grid - 1 - c), so the short units land on the CTAs whose earlier units were short.
@@ -236,6 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, tmem_cols);
   }
+  GR_TL_END(kTlLinear + EPI)
 }
 
 // ------------------------------------------------------------------ host side
@@ -295,3 +299,5 @@ cudaError_t launch_linear(int epi, const CUtensorMap& tmw, const CUtensorMap& tm
 }
 
 }  // namespace gr
+
+GR_TIMELINE_EXPORTS(linear)

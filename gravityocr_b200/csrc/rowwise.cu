@@ -21,6 +21,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 // ------------------------------------------------------------------ embedding rows + window plan + input norm
 __global__ void __launch_bounds__(kRowThreads) embed_rows_kernel(const EmbedParams p) {
+  GR_TL_BEGIN
   __shared__ float red[32];
   __shared__ int64_t s_id;
   if (threadIdx.x == 0) pdl_trigger();
@@ -94,6 +95,7 @@ __global__ void __launch_bounds__(kRowThreads) embed_rows_kernel(const EmbedPara
       o[i] = pack_bf16(__bfloat162float(w[2 * i]) * (hv[2 * i] * r), __bfloat162float(w[2 * i + 1]) * (hv[2 * i + 1] * r));
     *reinterpret_cast<uint4*>(xrow + c) = out;
   }
+  GR_TL_END(kTlEmbed)
 }
 
 // ------------------------------------------------------------------ residual + sandwich norm
@@ -106,17 +108,21 @@ __global__ void __launch_bounds__(kRowThreads) embed_rows_kernel(const EmbedPara
 constexpr int kNormFewRows = 512;
 template <int MC>
 __global__ void __launch_bounds__(kRowThreads) residual_norm_kernel(const ResNormParams p) {
+  GR_TL_BEGIN
   __shared__ float red[32];
   if (threadIdx.x == 0) pdl_trigger();
   pdl_wait();
   resnorm_row<MC>(p, blockIdx.x, threadIdx.x, blockDim.x, 1, red);
+  GR_TL_END(kTlResidualNorm)
 }
 template <int MC>
 __global__ void __launch_bounds__(kRowThreads, 1) residual_norm_few_rows_kernel(const ResNormParams p) {
+  GR_TL_BEGIN
   __shared__ float red[32];
   if (threadIdx.x == 0) pdl_trigger();
   pdl_wait();
   resnorm_row<MC>(p, blockIdx.x, threadIdx.x, blockDim.x, 1, red);
+  GR_TL_END(kTlResidualNorm)
 }
 
 // Many rows (> kNormFewRows, hidden == 8 * kRowThreads, NP split-K partials): kNormCtasPerSm CTAs per SM walk the rows
@@ -129,6 +135,7 @@ __global__ void __launch_bounds__(kRowThreads, 1) residual_norm_few_rows_kernel(
 __host__ __device__ constexpr int norm_ctas_per_sm(int np) { return np <= 2 ? 4 : 3; }
 template <int NP>
 __global__ void __launch_bounds__(kRowThreads, norm_ctas_per_sm(NP)) residual_norm_rows_kernel(const ResNormParams p) {
+  GR_TL_BEGIN
   __shared__ float red[32];
   if (threadIdx.x == 0) pdl_trigger();
   const int H = p.hidden;
@@ -188,12 +195,14 @@ __global__ void __launch_bounds__(kRowThreads, norm_ctas_per_sm(NP)) residual_no
       o[i] = pack_bf16(__bfloat162float(wbv[2 * i]) * (yv[2 * i] * rb), __bfloat162float(wbv[2 * i + 1]) * (yv[2 * i + 1] * rb));
     *reinterpret_cast<uint4*>(p.x_out + (size_t)t * H + c) = out;
   }
+  GR_TL_END(kTlResidualNorm)
 }
 
 // ------------------------------------------------------------------ accept and commit
 constexpr int kCommitThreads = 256;
 
 __global__ void __launch_bounds__(kCommitThreads) accept_commit_kernel(const CommitParams p) {
+  GR_TL_BEGIN
   __shared__ int warp_tot[kCommitThreads / 32];
   __shared__ int carry;
   if (threadIdx.x == 0) {
@@ -264,6 +273,7 @@ __global__ void __launch_bounds__(kCommitThreads) accept_commit_kernel(const Com
   }
   if (threadIdx.x == 0 && p.n_released) p.n_released[0] = carry;
   if (threadIdx.x == 0 && p.rng) p.rng[1] += 1;  // the next round draws fresh coins
+  GR_TL_END(kTlCommit)
 }
 
 // ------------------------------------------------------------------ forced-accept replay
@@ -342,3 +352,5 @@ cudaError_t launch_pack_gate_up(const __nv_bfloat16* src, __nv_bfloat16* dst, in
 }
 
 }  // namespace gr
+
+GR_TIMELINE_EXPORTS(rowwise)

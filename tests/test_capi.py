@@ -33,6 +33,17 @@ def test_library_loads_and_exports_every_symbol():
     assert lib.gr_status_string(4).decode() == "device wait timed out"
 
 
+def test_product_library_is_not_the_timeline_build():
+    """The per-CTA timeline stamps exist only in the separately built libgravity_b200_timeline.so (-DGR_TIMELINE);
+    the library the product loads has none of their code or symbols."""
+    if not os.path.exists(L.LIB_PATH):
+        from gravityocr_b200.build import build
+        build()
+    lib = ctypes.CDLL(L.LIB_PATH)
+    for unit in ("linear", "attention", "attention_tc", "rowwise"):
+        assert not hasattr(lib, "gr_timeline_read_" + unit)
+
+
 def test_workspace_queries_without_gpu():
     lib = L.load()
     # fixed ticket region + partials; argmax scratch grows with rows
