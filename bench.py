@@ -893,7 +893,7 @@ def case_timeline(a):
     (python -m gravityocr_b200.build --timeline): per kernel kind, its share of the round (the time from the previous
     launch's last CTA exit to this launch's last exit), its critical path after its dependency was released, and the
     release latency.  Batch 1: the config-2 crop (prefix 288); larger batches: the first --batch config-3 requests."""
-    os.environ["GRAVITY_B200_LIB"] = os.path.join(ROOT, "gravityocr_b200", "libgravity_b200_timeline.so")
+    os.environ.setdefault("GRAVITY_B200_LIB", os.path.join(ROOT, "gravityocr_b200", "libgravity_b200_timeline.so"))
     import ctypes
     from gravityocr_b200 import _lib as L
     from gravityocr_b200.config import ModelConfig
