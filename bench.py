@@ -37,7 +37,7 @@ K_BD = 16
 SEED = 3
 # DRAM bytes / algorithmic bytes of one verify attention launch (attention_tc_kernel) on the config-3 mix:
 # dram__bytes_read.sum + dram__bytes_write.sum of an ncu capture of that launch over its algorithmic bytes
-ATTN_TRAFFIC_RATIO = (584.61e6 + 6.20e6) / 586.94e6
+ATTN_TRAFFIC_RATIO = (584.55e6 + 5.84e6) / 586.94e6
 
 
 def _args():
