@@ -843,7 +843,8 @@ def case_norm(a):
 
 
 _TL_KINDS = {1: "attention_kernel", 2: "attention_tc_kernel", 3: "argmax_reduce_kernel", 4: "residual_norm",
-             6: "embed_rows_kernel", 7: "accept_commit_kernel", 10: "linear f32", 11: "linear bf16",
+             5: "penalty_cumulate_kernel", 6: "embed_rows_kernel", 7: "accept_commit_kernel",
+             8: "logits_process_kernel", 9: "sample_rows_kernel", 10: "linear f32 (lm_head logits)", 11: "linear bf16",
              12: "linear gate_up+SwiGLU", 13: "linear QKV+RoPE", 14: "linear lm_head+argmax", 15: "linear o/down partials"}
 
 
@@ -857,7 +858,7 @@ def _timeline_records(lib):
         _fields_ = [("kind", ctypes.c_uint32), ("block", ctypes.c_uint32), ("t0", ctypes.c_uint64),
                     ("t1", ctypes.c_uint64)]
     out = []
-    for unit in ("linear", "attention", "attention_tc", "rowwise"):
+    for unit in ("linear", "attention", "attention_tc", "rowwise", "sampling"):
         buf = (Rec * (1 << 19))()
         n = ctypes.c_uint32(0)
         assert getattr(lib, "gr_timeline_read_" + unit)(buf, ctypes.byref(n)) == 0
@@ -892,7 +893,8 @@ def case_timeline(a):
     """Live per-kernel timeline of one self-spec round (draft + verify + commit graphs) from the timeline build
     (python -m gravityocr_b200.build --timeline): per kernel kind, its share of the round (the time from the previous
     launch's last CTA exit to this launch's last exit), its critical path after its dependency was released, and the
-    release latency.  Batch 1: the config-2 crop (prefix 288); larger batches: the first --batch config-3 requests."""
+    release latency.  Batch 1: the config-2 crop (prefix 288); larger batches: the first --batch config-3 requests.
+    --sampled: a sampled round instead (eager launches, as the worker runs non-plain batches)."""
     os.environ.setdefault("GRAVITY_B200_LIB", os.path.join(ROOT, "gravityocr_b200", "libgravity_b200_timeline.so"))
     import ctypes
     from gravityocr_b200 import _lib as L
@@ -933,10 +935,25 @@ def case_timeline(a):
         gd.replay()
         gv.replay()
     torch.cuda.synchronize()
-    for unit in ("linear", "attention", "attention_tc", "rowwise"):
+    if a.sampled:
+        from gravityocr_b200.sampling import RequestSampling, SampledRound, SamplerState
+        st = SamplerState(cfg.vocab, rb.seeds.shape[0], dev, seed=SEED)
+        rs = [RequestSampling(temperature=0.8, top_p=0.95, top_k=50, repetition_penalty=1.1,
+                              frequency_penalty=0.1)] * bs
+        smp = st.batch(rs, rb.rpi)
+        sr = SampledRound(eng, rb)
+        for _ in range(2):
+            sr.draft(smp)
+            sr.verify(smp, st.rng)
+        torch.cuda.synchronize()
+    for unit in ("linear", "attention", "attention_tc", "rowwise", "sampling"):
         assert getattr(lib, "gr_timeline_clear_" + unit)() == 0
-    gd.replay()
-    gv.replay()
+    if a.sampled:  # eager launches, as the worker runs a non-plain batch
+        sr.draft(smp)
+        sr.verify(smp, st.rng)
+    else:
+        gd.replay()
+        gv.replay()
     torch.cuda.synchronize()
     eng.check_status(rb)
     ls = _timeline_launches(_timeline_records(lib))
@@ -958,7 +975,8 @@ def case_timeline(a):
         kinds[name] = {"launches": n, "round_us": round(g["round_us"], 1), "share": round(g["round_us"] / total, 4),
                        "avg_us": round(g["round_us"] / n, 2), "avg_busy_us": round(g["busy_us"] / n, 2),
                        "avg_release_us": round(g["release_us"] / n, 2)}
-    return {"case": "timeline", "batch": bs, "K": K, "launches": len(ls), "round_us": round(total, 1),
+    return {"case": "timeline", "batch": bs, "K": K, "sampled": bool(a.sampled), "launches": len(ls),
+            "round_us": round(total, 1),
             "forward_us": round(total / 2, 1), "kinds": kinds,
             "note": "avg_us: launch share of the round (previous launch's last exit to this one's); avg_busy_us: "
                     "dependency release to last CTA exit (PDL lets a launch's CTAs start before that); "
@@ -1024,6 +1042,8 @@ def case_main(argv):
     tl = sub.add_parser("timeline")
     tl.add_argument("--batch", type=int, default=1)
     tl.add_argument("--bd", type=int, default=K_BD)
+    tl.add_argument("--sampled", action="store_true",
+                    help="a sampled round (temperature 0.8, top-k 50, top-p 0.95, penalties), eager launches")
     sa = sub.add_parser("sample")
     sa.add_argument("--bs", type=int, default=64)
     sa.add_argument("--bd", type=int, default=K_BD)

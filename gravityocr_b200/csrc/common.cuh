@@ -99,6 +99,9 @@ enum : uint32_t {
   kTlResidualNorm = 4,
   kTlEmbed = 6,
   kTlCommit = 7,
+  kTlLogitsProcess = 8,
+  kTlSampleRows = 9,
+  kTlPenaltyCumulate = 5,
   kTlLinear = 10
 };
 

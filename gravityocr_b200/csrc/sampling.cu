@@ -15,6 +15,10 @@ constexpr int kProcChunk = 2048;   // logits_process: vocabulary entries per CTA
 constexpr int kProcThreads = 256;
 constexpr int kSampThreads = 1024; // sample_rows: one CTA per row
 constexpr int kSampWarps = kSampThreads / 32;
+// Row loops load kRowBatch entries per thread before using any: a row pass is bound by L2 latency, and one load in
+// flight per thread (a dependent load per iteration) left 0.9 ms per 1,088-row launch in long-scoreboard stalls.
+// The entries a thread visits, and their order, are unchanged.
+constexpr int kRowBatch = 8;
 
 // ---------------------------------------------------------------- Philox-4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11)
 __device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint2 k) {
@@ -48,6 +52,7 @@ __device__ __forceinline__ void set_status(int32_t* st, int code) {
 // ops run in the orchestrator's order with the same IEEE operations as SGLang's penalizers (repetition: l < 0 ? l * S
 // : l / S; presence / frequency: l - S; min_new_tokens: stop ids -> -inf), then the grammar mask and the bias.
 __global__ void __launch_bounds__(kProcThreads) logits_process_kernel(const SampleParams p) {
+  GR_TL_BEGIN
   __shared__ uint32_t bits[kProcChunk / 32];
   __shared__ int blk[64];
   const gr_sampling& s = p.s;
@@ -104,6 +109,7 @@ __global__ void __launch_bounds__(kProcThreads) logits_process_kernel(const Samp
     if (s.logit_bias) l = l + s.logit_bias[(size_t)b * V + v];
     row[v] = l;
   }
+  GR_TL_END(kTlLogitsProcess)
 }
 
 // ---------------------------------------------------------------- block reductions (1024 threads)
@@ -177,16 +183,25 @@ __device__ uint32_t select_threshold(const float* row, int V, long long k, doubl
     }
     __syncwarp();
     const uint32_t prefix = sm.prefix;
-    for (int v = threadIdx.x; v < V; v += blockDim.x) {
-      const float e = row[v];
-      const uint32_t ub = __float_as_uint(e);
-      if (e > 0.f && (level == 0 || (ub >> (shift + 8)) == prefix)) {
-        const uint32_t bin = (ub >> shift) & 255u;
-        if (need_c) atomicAdd(&sm.wc[warp][bin], 1u);
-        if (need_m) {  // two 32-bit halves: 64-bit shared atomics measured slower
-          const uint64_t w = fixed40(e);
-          atomicAdd(&sm.wl[warp][bin], static_cast<uint32_t>(w & 0xFFFFFu));
-          atomicAdd(&sm.wh[warp][bin], static_cast<uint32_t>(w >> 20));
+    for (int v0 = threadIdx.x; v0 < V; v0 += kRowBatch * blockDim.x) {
+      float ev[kRowBatch];
+#pragma unroll
+      for (int u = 0; u < kRowBatch; ++u) {
+        const int v = v0 + u * blockDim.x;
+        ev[u] = v < V ? row[v] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kRowBatch; ++u) {
+        const float e = ev[u];
+        const uint32_t ub = __float_as_uint(e);
+        if (e > 0.f && (level == 0 || (ub >> (shift + 8)) == prefix)) {
+          const uint32_t bin = (ub >> shift) & 255u;
+          if (need_c) atomicAdd(&sm.wc[warp][bin], 1u);
+          if (need_m) {  // two 32-bit halves: 64-bit shared atomics measured slower
+            const uint64_t w = fixed40(e);
+            atomicAdd(&sm.wl[warp][bin], static_cast<uint32_t>(w & 0xFFFFFu));
+            atomicAdd(&sm.wh[warp][bin], static_cast<uint32_t>(w >> 20));
+          }
         }
       }
     }
@@ -282,6 +297,7 @@ __device__ uint32_t select_threshold(const float* row, int V, long long k, doubl
 
 // ---------------------------------------------------------------- target distribution, accept test, draws
 __global__ void __launch_bounds__(kSampThreads, 1) sample_rows_kernel(const SampleParams p) {
+  GR_TL_BEGIN
   __shared__ float shf[kSampWarps];
   __shared__ unsigned long long shu[kSampWarps];
   extern __shared__ __align__(16) uint8_t dyn_smem[];
@@ -299,10 +315,22 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_rows_kernel(const Samp
   const float mp = s.min_p[b];
   // pass 1: x = l / T and the row maximum
   float mx = -INFINITY;
-  for (int v = threadIdx.x; v < V; v += blockDim.x) {
-    const float x = row[v] / T;
-    row[v] = x;
-    mx = fmaxf(mx, x);
+  for (int v0 = threadIdx.x; v0 < V; v0 += kRowBatch * blockDim.x) {
+    float lv[kRowBatch];
+#pragma unroll
+    for (int u = 0; u < kRowBatch; ++u) {
+      const int v = v0 + u * blockDim.x;
+      lv[u] = v < V ? row[v] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kRowBatch; ++u) {
+      const int v = v0 + u * blockDim.x;
+      if (v < V) {
+        const float x = lv[u] / T;
+        row[v] = x;
+        mx = fmaxf(mx, x);
+      }
+    }
   }
   const float m = block_max(mx, shf);
   const int d = (p.K > 1 && j + 1 < p.K) ? p.cand[(size_t)b * p.K + j + 1] : -1;
@@ -318,10 +346,22 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_rows_kernel(const Samp
   }
   // pass 2: e = exp(x - max) (the maximum maps to exactly 1) and the fixed-point total
   uint64_t z = 0;
-  for (int v = threadIdx.x; v < V; v += blockDim.x) {
-    const float e = expf(row[v] - m);
-    row[v] = e;
-    z += fixed40(e);
+  for (int v0 = threadIdx.x; v0 < V; v0 += kRowBatch * blockDim.x) {
+    float xv[kRowBatch];
+#pragma unroll
+    for (int u = 0; u < kRowBatch; ++u) {
+      const int v = v0 + u * blockDim.x;
+      xv[u] = v < V ? row[v] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kRowBatch; ++u) {
+      const int v = v0 + u * blockDim.x;
+      if (v < V) {
+        const float e = expf(xv[u] - m);
+        row[v] = e;
+        z += fixed40(e);
+      }
+    }
   }
   const uint64_t Z = block_sum64(z, shu);
   // keep threshold of the filters
@@ -341,9 +381,16 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_rows_kernel(const Samp
     if (want_k) t1 = select_threshold(row, V, k, 1e300, true, sel);
     if (want_p) {
       uint64_t zk = 0;
-      for (int v = threadIdx.x; v < V; v += blockDim.x) {
-        const float e = row[v];
-        if (__float_as_uint(e) >= t1 && e > 0.f) zk += fixed40(e);
+      for (int v0 = threadIdx.x; v0 < V; v0 += kRowBatch * blockDim.x) {
+        float ev[kRowBatch];
+#pragma unroll
+        for (int u = 0; u < kRowBatch; ++u) {
+          const int v = v0 + u * blockDim.x;
+          ev[u] = v < V ? row[v] : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kRowBatch; ++u)
+          if (__float_as_uint(ev[u]) >= t1 && ev[u] > 0.f) zk += fixed40(ev[u]);
       }
       const uint64_t Zk = block_sum64(zk, shu);
       const uint32_t t2 = select_threshold(row, V, 1ll << 62, static_cast<double>(P) * Zk, true, sel);
@@ -362,8 +409,18 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_rows_kernel(const Samp
     const float e = row[v];
     return (e > 0.f && __float_as_uint(e) >= tau) ? fixed40(e) : 0ull;
   };
+  auto kept_e = [&](float e) -> uint64_t { return (e > 0.f && __float_as_uint(e) >= tau) ? fixed40(e) : 0ull; };
   unsigned long long loc = 0;
-  for (int v = lo + lane; v < hi; v += 32) loc += kept_w(v);
+  for (int v0 = lo + lane; v0 < hi; v0 += 32 * kRowBatch) {
+    float ev[kRowBatch];
+#pragma unroll
+    for (int u = 0; u < kRowBatch; ++u) {
+      const int v = v0 + 32 * u;
+      ev[u] = v < hi ? row[v] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kRowBatch; ++u) loc += kept_e(ev[u]);
+  }
   loc = warp_sum64(loc);
   const uint64_t wd = (d >= 0) ? kept_w(d) : 0ull;  // the same value every thread reads
   if (lane == 0) scan[warp] = loc;
@@ -383,19 +440,31 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_rows_kernel(const Samp
   if (Wx > 0 && target >= Wx) target = Wx - 1;
   if (Wx > 0 && mine > 0 && target >= before_x && target < before_x + mine) {
     uint64_t c = before_x;
-    for (int v0 = lo; v0 < hi; v0 += 32) {
-      const int v = v0 + lane;
-      uint64_t x = (v < hi && v != (exclude ? d : -1)) ? kept_w(v) : 0ull;
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint64_t y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
+    bool hit_any = false;
+    for (int g0 = lo; g0 < hi && !hit_any; g0 += 32 * kRowBatch) {
+      float ev[kRowBatch];  // kRowBatch groups of 32 entries loaded together, then scanned in order
+#pragma unroll
+      for (int u = 0; u < kRowBatch; ++u) {
+        const int v = g0 + 32 * u + lane;
+        ev[u] = v < hi ? row[v] : 0.f;
       }
-      const unsigned hit = __ballot_sync(0xffffffffu, c + x > target);
-      if (hit) {
-        if (lane == __ffs(hit) - 1) found = v;
-        break;
+#pragma unroll
+      for (int u = 0; u < kRowBatch; ++u) {
+        const int v = g0 + 32 * u + lane;
+        if (g0 + 32 * u >= hi) break;
+        uint64_t x = (v < hi && v != (exclude ? d : -1)) ? kept_e(ev[u]) : 0ull;
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint64_t y = __shfl_up_sync(0xffffffffu, x, o);
+          if (lane >= o) x += y;
+        }
+        const unsigned hit = __ballot_sync(0xffffffffu, c + x > target);
+        if (hit) {
+          if (lane == __ffs(hit) - 1) found = v;
+          hit_any = true;
+          break;
+        }
+        c += __shfl_sync(0xffffffffu, x, 31);
       }
-      c += __shfl_sync(0xffffffffu, x, 31);
     }
   }
   __syncthreads();
@@ -411,10 +480,12 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_rows_kernel(const Samp
     }
     if (p.p_next) p.p_next[r] = (d >= 0 && W > 0) ? static_cast<float>(static_cast<double>(wd) / static_cast<double>(W)) : 0.f;
   }
+  GR_TL_END(kTlSampleRows)
 }
 
 // ---------------------------------------------------------------- penalizer cumulation
 __global__ void penalty_cumulate_kernel(const SampleParams p) {
+  GR_TL_BEGIN
   const gr_sampling& s = p.s;
   const int b = blockIdx.x;
   const int n = (p.counts ? p.counts[b] : 0) + p.add;
@@ -432,6 +503,7 @@ __global__ void penalty_cumulate_kernel(const SampleParams p) {
     }
   }
   if (threadIdx.x == 0 && s.st_len) s.st_len[slot] += n;
+  GR_TL_END(kTlPenaltyCumulate)
 }
 
 __global__ void gather_rows_kernel(const uint4* src, int words, int stride_rows, uint4* dst) {
@@ -467,3 +539,5 @@ cudaError_t launch_penalty_cumulate(const SampleParams& p, cudaStream_t s) {
 }
 
 }  // namespace gr
+
+GR_TIMELINE_EXPORTS(sampling)

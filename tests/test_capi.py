@@ -40,7 +40,7 @@ def test_product_library_is_not_the_timeline_build():
         from gravityocr_b200.build import build
         build()
     lib = ctypes.CDLL(L.LIB_PATH)
-    for unit in ("linear", "attention", "attention_tc", "rowwise"):
+    for unit in ("linear", "attention", "attention_tc", "rowwise", "sampling"):
         assert not hasattr(lib, "gr_timeline_read_" + unit)
 
 
