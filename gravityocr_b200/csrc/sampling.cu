@@ -48,66 +48,77 @@ __device__ __forceinline__ void set_status(int32_t* st, int code) {
 }
 
 // ---------------------------------------------------------------- logits processing
-// Grid (chunks, rows).  Row r = b * K + j sees the request's penalizer state plus the verify ids cand[b, 1..j]; the
-// ops run in the orchestrator's order with the same IEEE operations as SGLang's penalizers (repetition: l < 0 ? l * S
-// : l / S; presence / frequency: l - S; min_new_tokens: stop ids -> -inf), then the grammar mask and the bias.
+// Grid (chunks, requests).  Row r = b * K + j sees the request's penalizer state plus the verify ids cand[b, 1..j];
+// the ops run in the orchestrator's order with the same IEEE operations as SGLang's penalizers (repetition: l < 0 ?
+// l * S : l / S; presence / frequency: l - S; min_new_tokens: stop ids -> -inf), then the grammar mask and the bias.
+// A CTA takes one vocabulary chunk of all K rows of a request: the request's penalizer state is read once for its K
+// rows (one CTA per row read it K times), and a thread's K logits of an entry are loaded together.
+constexpr int kProcMaxK = 128;
 __global__ void __launch_bounds__(kProcThreads) logits_process_kernel(const SampleParams p) {
   GR_TL_BEGIN
-  __shared__ uint32_t bits[kProcChunk / 32];
-  __shared__ int blk[64];
+  __shared__ int cand_s[kProcMaxK];
   const gr_sampling& s = p.s;
   const int V = s.vocab;
-  const int r = blockIdx.y;
-  const int b = r / p.K, j = r % p.K;
+  const int K = p.K;
+  const int b = blockIdx.y;
   const int v0 = blockIdx.x * kProcChunk;
   const int v1 = min(V, v0 + kProcChunk);
-  const int n_blk = p.cand ? j : 0;
-  for (int i = threadIdx.x; i < kProcChunk / 32; i += blockDim.x) bits[i] = 0u;
-  __syncthreads();
-  if (threadIdx.x < n_blk) {
-    const int t = p.cand[(size_t)b * p.K + 1 + threadIdx.x];
-    blk[threadIdx.x] = t;
-    if (t >= v0 && t < v1) atomicOr(&bits[(t - v0) >> 5], 1u << ((t - v0) & 31));
-  }
+  for (int i = threadIdx.x; i < K; i += blockDim.x) cand_s[i] = p.cand ? p.cand[(size_t)b * K + i] : -1;
   __syncthreads();
   const int64_t slot = s.req_pool_idx[b];
   const float rep = s.repetition ? s.repetition[b] : 1.f;
   const float freq = s.frequency ? s.frequency[b] : 0.f;
   const float pres = s.presence ? s.presence[b] : 0.f;
-  bool stop_on = false;
-  for (int o = 0; o < s.n_order; ++o)
-    if (s.order[o] == GR_PEN_MIN_NEW_TOKENS) stop_on = s.st_len[slot] + j < s.min_new_tokens[b];
+  bool has_stop = false;
+  for (int o = 0; o < s.n_order; ++o) has_stop |= s.order[o] == GR_PEN_MIN_NEW_TOKENS;
+  const long long stop_len = has_stop ? static_cast<long long>(s.st_len[slot]) : 0;
+  const int min_new = has_stop ? s.min_new_tokens[b] : 0;
   const int words = (V + 31) >> 5;
-  float* row = p.logits + (size_t)r * V;
   for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
-    float l = row[v];
-    int c = 0;
-    if ((bits[(v - v0) >> 5] >> ((v - v0) & 31)) & 1u)
-      for (int i = 0; i < n_blk; ++i) c += blk[i] == v;
     const size_t sv = (size_t)slot * V + v;
-    for (int o = 0; o < s.n_order; ++o) {
-      const int op = s.order[o];
-      if (op == GR_PEN_REPETITION) {
-        if (rep != 1.f) {
-          const float S = c ? rep : s.st_rep[sv];
-          l = l < 0.f ? l * S : l / S;
+    const float srep = (rep != 1.f) ? s.st_rep[sv] : 1.f;
+    const float spres = (pres != 0.f) ? s.st_pres[sv] : 0.f;
+    const float sfreq = (freq != 0.f) ? s.st_freq[sv] : 0.f;
+    const float bias = s.logit_bias ? s.logit_bias[(size_t)b * V + v] : 0.f;
+    int c = 0;  // occurrences of v among cand[b, 1..j] for the current row j
+    for (int j0 = 0; j0 < K; j0 += 8) {
+      float lv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        lv[u] = (j0 + u < K) ? p.logits[(size_t)(b * K + j0 + u) * V + v] : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = j0 + u;
+        if (j >= K) break;
+        if (j >= 1 && cand_s[j] == v) ++c;
+        float l = lv[u];
+        const bool stop_on = has_stop && stop_len + j < min_new;
+        for (int o = 0; o < s.n_order; ++o) {
+          const int op = s.order[o];
+          if (op == GR_PEN_REPETITION) {
+            if (rep != 1.f) {
+              const float S = c ? rep : srep;
+              l = l < 0.f ? l * S : l / S;
+            }
+          } else if (op == GR_PEN_PRESENCE) {
+            if (pres != 0.f) l = l - (c ? pres : spres);
+          } else if (op == GR_PEN_FREQUENCY) {
+            if (freq != 0.f) {
+              float S = sfreq;
+              for (int i = 0; i < c; ++i) S = S + freq;
+              l = l - S;
+            }
+          } else if (stop_on) {
+            for (int i = 0; i < s.n_stop; ++i)
+              if (s.stop_ids[(size_t)b * s.n_stop + i] == v) l = -INFINITY;
+          }
         }
-      } else if (op == GR_PEN_PRESENCE) {
-        if (pres != 0.f) l = l - (c ? pres : s.st_pres[sv]);
-      } else if (op == GR_PEN_FREQUENCY) {
-        if (freq != 0.f) {
-          float S = s.st_freq[sv];
-          for (int i = 0; i < c; ++i) S = S + freq;
-          l = l - S;
-        }
-      } else if (stop_on) {
-        for (int i = 0; i < s.n_stop; ++i)
-          if (s.stop_ids[(size_t)b * s.n_stop + i] == v) l = -INFINITY;
+        const size_t r = (size_t)b * K + j;
+        if (s.allowed && !((s.allowed[r * words + (v >> 5)] >> (v & 31)) & 1u)) l = -INFINITY;
+        if (s.logit_bias) l = l + bias;
+        p.logits[r * V + v] = l;
       }
     }
-    if (s.allowed && !((s.allowed[(size_t)r * words + (v >> 5)] >> (v & 31)) & 1u)) l = -INFINITY;
-    if (s.logit_bias) l = l + s.logit_bias[(size_t)b * V + v];
-    row[v] = l;
   }
   GR_TL_END(kTlLogitsProcess)
 }
@@ -519,7 +530,8 @@ cudaError_t launch_gather_rows(const void* src, int row_bytes, int n, int src_st
   return cudaGetLastError();
 }
 cudaError_t launch_logits_process(const SampleParams& p, cudaStream_t s) {
-  const dim3 grid((p.s.vocab + kProcChunk - 1) / kProcChunk, p.bs * p.K);
+  if (p.K > kProcMaxK) return cudaErrorInvalidValue;
+  const dim3 grid((p.s.vocab + kProcChunk - 1) / kProcChunk, p.bs);
   logits_process_kernel<<<grid, kProcThreads, 0, s>>>(p);
   return cudaGetLastError();
 }
