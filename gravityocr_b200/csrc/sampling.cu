@@ -174,7 +174,68 @@ struct SelectSmem {
   uint32_t prefix, tau, done;
   unsigned long long c_above, s_above;
 };
-__device__ uint32_t select_threshold(const float* row, int V, long long k, double lim, bool strict, SelectSmem& sm) {
+// One pass of the select: every positive entry whose higher bits equal `prefix` adds its count and fixed-point mass to
+// bucket (bits >> shift) & 255 of this warp's histogram.  AGG keeps two buckets' sums in registers and adds them to the
+// histogram only when a third bucket shows up or the pass ends.  On a flat row the first pass puts most entries in one
+// or two buckets of the exponent, and every lane's atomic on the same word serialised; on a peaked row the entries
+// spread over many buckets and the register cache only adds divergent branches.  The sums are integers, so both
+// forms build the same histogram.
+template <bool AGG>
+__device__ __forceinline__ void histogram_pass(const float* row, int V, int level, uint32_t prefix, bool need_c,
+                                               bool need_m, uint32_t* wc, uint32_t* wl, uint32_t* wh) {
+  const int shift = 24 - 8 * level;
+  uint32_t bin_a = 0xFFFFFFFFu, bin_b = 0xFFFFFFFFu, cnt_a = 0, cnt_b = 0;
+  uint64_t mass_a = 0, mass_b = 0;
+  auto add = [&](uint32_t bin, uint32_t cnt, uint64_t mass) {
+    if (cnt == 0) return;
+    if (need_c) atomicAdd(&wc[bin], cnt);
+    if (need_m) {  // two 32-bit halves: 64-bit shared atomics measured slower
+      atomicAdd(&wl[bin], static_cast<uint32_t>(mass & 0xFFFFFu));
+      atomicAdd(&wh[bin], static_cast<uint32_t>(mass >> 20));
+    }
+  };
+  for (int v0 = threadIdx.x; v0 < V; v0 += kRowBatch * blockDim.x) {
+    float ev[kRowBatch];
+#pragma unroll
+    for (int u = 0; u < kRowBatch; ++u) {
+      const int v = v0 + u * blockDim.x;
+      ev[u] = v < V ? row[v] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kRowBatch; ++u) {
+      const float e = ev[u];
+      const uint32_t ub = __float_as_uint(e);
+      if (e > 0.f && (level == 0 || (ub >> (shift + 8)) == prefix)) {
+        const uint32_t bin = (ub >> shift) & 255u;
+        const uint64_t w = need_m ? fixed40(e) : 0ull;
+        if (!AGG) {
+          add(bin, 1u, w);
+        } else if (bin == bin_a) {
+          ++cnt_a;
+          mass_a += w;
+        } else if (bin == bin_b) {
+          ++cnt_b;
+          mass_b += w;
+        } else {
+          add(bin_b, cnt_b, mass_b);
+          bin_b = bin_a;
+          cnt_b = cnt_a;
+          mass_b = mass_a;
+          bin_a = bin;
+          cnt_a = 1;
+          mass_a = w;
+        }
+      }
+    }
+  }
+  if (AGG) {
+    add(bin_a, cnt_a, mass_a);
+    add(bin_b, cnt_b, mass_b);
+  }
+}
+
+__device__ uint32_t select_threshold(const float* row, int V, long long k, double lim, bool strict, bool flat,
+                                     SelectSmem& sm) {
   const bool need_c = k < (1ll << 62), need_m = lim < 1e300;  // a criterion that is off needs no histogram
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
@@ -194,28 +255,10 @@ __device__ uint32_t select_threshold(const float* row, int V, long long k, doubl
     }
     __syncwarp();
     const uint32_t prefix = sm.prefix;
-    for (int v0 = threadIdx.x; v0 < V; v0 += kRowBatch * blockDim.x) {
-      float ev[kRowBatch];
-#pragma unroll
-      for (int u = 0; u < kRowBatch; ++u) {
-        const int v = v0 + u * blockDim.x;
-        ev[u] = v < V ? row[v] : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < kRowBatch; ++u) {
-        const float e = ev[u];
-        const uint32_t ub = __float_as_uint(e);
-        if (e > 0.f && (level == 0 || (ub >> (shift + 8)) == prefix)) {
-          const uint32_t bin = (ub >> shift) & 255u;
-          if (need_c) atomicAdd(&sm.wc[warp][bin], 1u);
-          if (need_m) {  // two 32-bit halves: 64-bit shared atomics measured slower
-            const uint64_t w = fixed40(e);
-            atomicAdd(&sm.wl[warp][bin], static_cast<uint32_t>(w & 0xFFFFFu));
-            atomicAdd(&sm.wh[warp][bin], static_cast<uint32_t>(w >> 20));
-          }
-        }
-      }
-    }
+    if (flat && level == 0)
+      histogram_pass<true>(row, V, 0, prefix, need_c, need_m, sm.wc[warp], sm.wl[warp], sm.wh[warp]);
+    else
+      histogram_pass<false>(row, V, level, prefix, need_c, need_m, sm.wc[warp], sm.wl[warp], sm.wh[warp]);
     __syncthreads();
     for (int i = threadIdx.x; i < 256; i += blockDim.x) {
       uint32_t c = 0;
@@ -375,6 +418,8 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_rows_kernel(const Samp
     }
   }
   const uint64_t Z = block_sum64(z, shu);
+  // a mean weight of at least 1/32 (the maximum is 1) marks a flat row, whose first select pass aggregates in registers
+  const bool flat = Z >= (static_cast<uint64_t>(V) << 35);
   // keep threshold of the filters
   uint32_t tau = 0;
   const bool want_k = k < V, want_p = P < 1.f;
@@ -382,14 +427,16 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_rows_kernel(const Samp
     tau = __float_as_uint(1.0f);  // the maximum's tie group
   } else if (s.filter == GR_FILTER_JOINT) {
     if (want_k || want_p)
-      tau = select_threshold(row, V, want_k ? k : (1ll << 62), want_p ? static_cast<double>(P) * Z : 1e300, true, sel);
+      tau = select_threshold(row, V, want_k ? k : (1ll << 62), want_p ? static_cast<double>(P) * Z : 1e300, true, flat,
+                             sel);
   } else if (s.filter == GR_FILTER_TORCH) {
     if (want_k || want_p)
-      tau = select_threshold(row, V, want_k ? k : (1ll << 62), want_p ? static_cast<double>(P) * Z : 1e300, false, sel);
+      tau = select_threshold(row, V, want_k ? k : (1ll << 62), want_p ? static_cast<double>(P) * Z : 1e300, false, flat,
+                             sel);
     if (mp > 0.f) tau = max(tau, __float_as_uint(mp));
   } else {  // sequential: top-k renorm, then top-p on the renormalised mass, then min-p
     uint32_t t1 = 0;
-    if (want_k) t1 = select_threshold(row, V, k, 1e300, true, sel);
+    if (want_k) t1 = select_threshold(row, V, k, 1e300, true, flat, sel);
     if (want_p) {
       uint64_t zk = 0;
       for (int v0 = threadIdx.x; v0 < V; v0 += kRowBatch * blockDim.x) {
@@ -404,7 +451,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) sample_rows_kernel(const Samp
           if (__float_as_uint(ev[u]) >= t1 && ev[u] > 0.f) zk += fixed40(ev[u]);
       }
       const uint64_t Zk = block_sum64(zk, shu);
-      const uint32_t t2 = select_threshold(row, V, 1ll << 62, static_cast<double>(P) * Zk, true, sel);
+      const uint32_t t2 = select_threshold(row, V, 1ll << 62, static_cast<double>(P) * Zk, true, flat, sel);
       t1 = max(t1, t2);
     }
     tau = t1;

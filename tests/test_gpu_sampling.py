@@ -138,18 +138,21 @@ def _draw_margin(p, u, exclude):
     return float((c - t).abs().min() / c[-1])
 
 
+@pytest.mark.parametrize("shape", ["peaked", "flat"])
 @pytest.mark.parametrize("mode", [L.FILTER_JOINT, L.FILTER_SEQUENTIAL, L.FILTER_TORCH])
-def test_sample_rows_match_oracle(mode):
-    g = torch.Generator().manual_seed(10 + mode)
+def test_sample_rows_match_oracle(mode, shape):
+    g = torch.Generator().manual_seed(10 + mode + (100 if shape == "flat" else 0))
     bs, K, seed = 6, 5, 1234567
     st = SamplerState(V, bs, DEV, seed=seed, filter=mode)
     reqs = [RequestSampling(temperature=[0.6, 1.0, 1.3, 0.9, 0.0, 1.0][b], top_k=[-1, 40, 1000, 5, -1, -1][b],
                             top_p=[0.9, 1.0, 0.8, 0.95, 1.0, 0.5][b],
                             min_p=0.0 if mode == L.FILTER_JOINT else [0.0, 0.1, 0.02, 0.0, 0.0, 0.3][b])
             for b in range(bs)]   # a flashinfer batch with min-p takes the sequential filter (tested on its own)
-    # peaked rows (a few dominant tokens) and flat ones
-    logits = torch.randn((bs * K, V), generator=g) * 2
-    logits[:, :20] += torch.randn((bs * K, 20), generator=g) * 3 + 6
+    if shape == "peaked":   # a few dominant tokens over a spread-out bulk
+        logits = torch.randn((bs * K, V), generator=g) * 2
+        logits[:, :20] += torch.randn((bs * K, 20), generator=g) * 3 + 6
+    else:   # mean weight above 1/32 of the maximum: the kernel's first select pass aggregates in registers
+        logits = torch.randn((bs * K, V), generator=g) * 0.3
     cand = torch.randint(0, 20, (bs, K), generator=g, dtype=torch.int32)
     rpi = torch.arange(bs, dtype=torch.int64)
     smp = st.batch(reqs, rpi.to(DEV))
