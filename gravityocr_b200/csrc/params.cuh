@@ -186,6 +186,8 @@ cudaError_t launch_draft_override(const OverrideParams& p, cudaStream_t s, bool 
 cudaError_t launch_gather_rows(const void* src, int row_bytes, int n, int src_stride_rows, void* dst, cudaStream_t s);
 cudaError_t launch_logits_process(const SampleParams& p, cudaStream_t s);
 cudaError_t launch_sample_rows(const SampleParams& p, cudaStream_t s);
+// Largest vocabulary sample_rows takes: a warp adds at most 4,095 entries per pass to its 32-bit bucket words.
+constexpr int kSampleMaxVocab = 65024;
 cudaError_t launch_penalty_cumulate(const SampleParams& p, cudaStream_t s);
 cudaError_t launch_pack_gate_up(const __nv_bfloat16* src, __nv_bfloat16* dst, int I, int H, cudaStream_t s);
 

@@ -13,8 +13,10 @@ namespace gr {
 
 constexpr int kProcChunk = 2048;   // logits_process: vocabulary entries per CTA
 constexpr int kProcThreads = 256;
-constexpr int kSampThreads = 1024; // sample_rows: one CTA per row
+constexpr int kSampThreads = 512;  // sample_rows: one CTA per row, two per SM
 constexpr int kSampWarps = kSampThreads / 32;
+// A warp's bucket words are 32-bit and take under 2^20 + 1 per entry (count 1, mass halves of a weight <= 2^40).
+static_assert(32 * ((kSampleMaxVocab + kSampThreads - 1) / kSampThreads) <= 4095, "bucket words could wrap");
 // Row loops load kRowBatch entries per thread before using any: a row pass is bound by L2 latency, and one load in
 // flight per thread (a dependent load per iteration) left 0.9 ms per 1,088-row launch in long-scoreboard stalls.
 // The entries a thread visits, and their order, are unchanged.
@@ -123,7 +125,7 @@ __global__ void __launch_bounds__(kProcThreads) logits_process_kernel(const Samp
   GR_TL_END(kTlLogitsProcess)
 }
 
-// ---------------------------------------------------------------- block reductions (1024 threads)
+// ---------------------------------------------------------------- block reductions (kSampThreads threads)
 __device__ __forceinline__ float block_max(float v, float* sh) {
   for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -164,11 +166,11 @@ __device__ __forceinline__ unsigned long long block_sum64(unsigned long long v, 
 // descending order.  Returns the smallest bit pattern tau such that "bits(e) >= tau" is exactly that set.  Four passes
 // of 8 bits over the row: each warp builds a private histogram of count and fixed-point mass per bucket with 32-bit
 // shared atomics (contention stays inside one warp even when a flat distribution puts every entry in one bucket), the
-// 32 histograms are summed per bucket, and warp 0 scans the 256 buckets from the top.
+// warps' histograms are summed per bucket, and warp 0 scans the 256 buckets from the top.
 struct SelectSmem {
   uint32_t wc[kSampWarps][256];  // per-warp counts
   uint32_t wl[kSampWarps][256];  // per-warp mass, low 20 bits of each entry's fixed-point value
-  uint32_t wh[kSampWarps][256];  // per-warp mass, the high bits (< 2^20 per entry: at most 2^31 per warp and bucket)
+  uint32_t wh[kSampWarps][256];  // per-warp mass, the high bits (<= 2^20 per entry, at most 4,095 entries a warp)
   uint32_t hc[256];
   unsigned long long hs[256];
   uint32_t prefix, tau, done;
@@ -350,7 +352,7 @@ __device__ uint32_t select_threshold(const float* row, int V, long long k, doubl
 }
 
 // ---------------------------------------------------------------- target distribution, accept test, draws
-__global__ void __launch_bounds__(kSampThreads, 1) sample_rows_kernel(const SampleParams p) {
+__global__ void __launch_bounds__(kSampThreads, 2) sample_rows_kernel(const SampleParams p) {
   GR_TL_BEGIN
   __shared__ float shf[kSampWarps];
   __shared__ unsigned long long shu[kSampWarps];

@@ -211,7 +211,7 @@ enum gr_coin_kind { GR_COIN_ACCEPT = 0, GR_COIN_FINAL = 1, GR_COIN_FIRST = 2, GR
 /* Sampling parameters of a batch.  Per-request arrays are [bs] device arrays; NULL means the neutral value for every
  * request.  The penalizer state is indexed by the request's pool slot, like the seed pool. */
 typedef struct gr_sampling {
-  int vocab;
+  int vocab;                    /* 1 .. 65,024; larger is GR_ERR_ARG */
   int filter;                   /* gr_filter_mode */
   const float* temperature;     /* > 0 (a greedy request has top_k = 1) */
   const int32_t* top_k;         /* >= 1; >= vocab keeps every token */

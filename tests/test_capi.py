@@ -64,6 +64,18 @@ def test_argument_errors_are_returned_not_raised():
     assert rc == 1
 
 
+def test_sampling_rejects_a_vocabulary_above_its_bound():
+    """sample_rows' per-warp 32-bit bucket words hold at most 4,095 entries a warp: a larger vocabulary is refused
+    before any CUDA call (the pointers below are never dereferenced)."""
+    lib = L.load()
+    s = L.Sampling()
+    s.vocab, s.filter = 65025, L.FILTER_JOINT
+    s.temperature = s.top_k = s.top_p = s.min_p = s.req_pool_idx = s.rng = 16
+    assert lib.gr_sample_rows(16, 1, 1, None, ctypes.byref(s), L.COIN_FIRST, None, 16, None, None, 0, None,
+                              None) == 1
+    assert lib.gr_logits_process(16, 1, 1, None, ctypes.byref(s), None) == 1
+
+
 def test_missing_library_fails_loudly(tmp_path, monkeypatch):
     monkeypatch.setattr(L, "_lib", None)
     with pytest.raises(RuntimeError, match="not found"):
