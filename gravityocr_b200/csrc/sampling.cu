@@ -369,26 +369,20 @@ __global__ void __launch_bounds__(kSampThreads, 2) sample_rows_kernel(const Samp
   const long long k = s.top_k[b];
   const float P = s.top_p[b];
   const float mp = s.min_p[b];
-  // pass 1: x = l / T and the row maximum
+  // pass 1: the maximum of x = l / T.  Rounding a division by T > 0 is monotone, so max(l / T) = max(l) / T exactly:
+  // the pass takes the logits' maximum and divides once.
   float mx = -INFINITY;
   for (int v0 = threadIdx.x; v0 < V; v0 += kRowBatch * blockDim.x) {
     float lv[kRowBatch];
 #pragma unroll
     for (int u = 0; u < kRowBatch; ++u) {
       const int v = v0 + u * blockDim.x;
-      lv[u] = v < V ? row[v] : 0.f;
+      lv[u] = v < V ? row[v] : -INFINITY;
     }
 #pragma unroll
-    for (int u = 0; u < kRowBatch; ++u) {
-      const int v = v0 + u * blockDim.x;
-      if (v < V) {
-        const float x = lv[u] / T;
-        row[v] = x;
-        mx = fmaxf(mx, x);
-      }
-    }
+    for (int u = 0; u < kRowBatch; ++u) mx = fmaxf(mx, lv[u]);
   }
-  const float m = block_max(mx, shf);
+  const float m = block_max(mx, shf) / T;
   const int d = (p.K > 1 && j + 1 < p.K) ? p.cand[(size_t)b * p.K + j + 1] : -1;
   if (!(m > -INFINITY)) {  // every token masked
     if (threadIdx.x == 0) {
@@ -400,20 +394,20 @@ __global__ void __launch_bounds__(kSampThreads, 2) sample_rows_kernel(const Samp
     }
     return;
   }
-  // pass 2: e = exp(x - max) (the maximum maps to exactly 1) and the fixed-point total
+  // pass 2: x = l / T, e = exp(x - max) (the maximum maps to exactly 1) and the fixed-point total
   uint64_t z = 0;
   for (int v0 = threadIdx.x; v0 < V; v0 += kRowBatch * blockDim.x) {
-    float xv[kRowBatch];
+    float lv[kRowBatch];
 #pragma unroll
     for (int u = 0; u < kRowBatch; ++u) {
       const int v = v0 + u * blockDim.x;
-      xv[u] = v < V ? row[v] : 0.f;
+      lv[u] = v < V ? row[v] : 0.f;
     }
 #pragma unroll
     for (int u = 0; u < kRowBatch; ++u) {
       const int v = v0 + u * blockDim.x;
       if (v < V) {
-        const float e = expf(xv[u] - m);
+        const float e = expf(lv[u] / T - m);
         row[v] = e;
         z += fixed40(e);
       }

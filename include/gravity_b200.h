@@ -246,7 +246,8 @@ int gr_gather_rows(const void* src, int row_bytes, int n, int src_stride_rows, v
 int gr_logits_process(float* logits, int bs, int K, const int32_t* cand, const gr_sampling* s, void* stream);
 
 /* AR's target distribution of each row (softmax(logits / T) filtered by s->filter; the row is overwritten with
- * exp(x - max)), then: K = 1 (first-token rows): sample[b] = a draw with coin `first_kind` (GR_COIN_FIRST for a0,
+ * exp(x - max), except a row whose every token is masked: it keeps its logits and sets GR_ERR_NO_TOKEN), then:
+ * K = 1 (first-token rows): sample[b] = a draw with coin `first_kind` (GR_COIN_FIRST for a0,
  * GR_COIN_PREFILL for the prefill's token), also written to first_out[b * first_stride] when given; K > 1 (verify
  * rows, cand [bs, K] = [a0, d1..]): accept[r] = coin(ACCEPT, b, j) <= p_j(d_{j+1}) (0 on the last row),
  * sample[r] = a draw from p_j without d_{j+1} with coin(FINAL, b), p_next[r] = p_j(d_{j+1}).  Coins are
