@@ -691,8 +691,8 @@ int gr_commit_sampled(int bs, int K, const int32_t* am, const int32_t* accept, c
 }
 
 static int check_sampling(const gr_sampling* s) {
-  if (!s || s->vocab <= 0 || s->vocab > kSampleMaxVocab || s->filter < GR_FILTER_JOINT || s->filter > GR_FILTER_TORCH || s->n_order < 0 ||
-      s->n_order > 4 || !s->req_pool_idx || !s->rng)
+  if (!s || s->vocab <= 0 || s->vocab > kSampleMaxVocab || s->filter < GR_FILTER_JOINT ||
+      s->filter > GR_FILTER_TORCH || s->n_order < 0 || s->n_order > 4 || !s->req_pool_idx || !s->rng)
     return GR_ERR_ARG;
   for (int i = 0; i < s->n_order; ++i) {
     const int op = s->order[i];

@@ -228,8 +228,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool ok = mbar_wait(acc_full + b, (k >> 1) & 1, p.status, GR_ERR_TIMEOUT);
       tc_fence_after();
       const uint32_t t_lane = tmem + b * acc_cols + (static_cast<uint32_t>(quad * 32) << 16);
-      epi_bar();
-      unit_epilogue<EPI>(p, t_lane, n_tile, m_tile, split, ok && !flags[0], scratch, &flags[1], acc_empty + b);
+      const bool run = epi_bar_and(ok && !flags[0]);
+      unit_epilogue<EPI>(p, t_lane, n_tile, m_tile, split, run, scratch, &flags[1], acc_empty + b);
       epi_bar();  // flags / scratch are reused by the next unit
     }
   }

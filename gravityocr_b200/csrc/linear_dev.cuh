@@ -1,5 +1,4 @@
-// Device code of the projection kernels shared by the per-launch kernel (linear.cu) and the persistent small-batch
-// forward (small.cu): shared-memory sizes, the epilogues and the argmax reduction.
+// Device code of the projection kernel (linear.cu): shared-memory sizes, the epilogues and the argmax reduction.
 #pragma once
 
 #include "params.cuh"
@@ -16,6 +15,18 @@ __host__ __device__ constexpr uint32_t epi_scratch_bytes(int epi) {
 
 // all 8 epilogue warps
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// the same barrier, returning the AND of v over the 8 warps: a decision every epilogue thread takes alike (the argmax
+// epilogue meets at the column halves' named barriers inside a unit, so no warp may run a unit that another skips)
+__device__ __forceinline__ bool epi_bar_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pv, pr;\n\tsetp.ne.u32 pv, %1, 0;\n\tbar.red.and.pred pr, 1, 256, pv;\n\t"
+      "selp.u32 %0, 1, 0, pr;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v))
+      : "memory");
+  return r != 0;
+}
 // the 4 epilogue warps of one column half (one warp per TMEM lane quadrant)
 __device__ __forceinline__ void half_bar(int half) { asm volatile("bar.sync %0, 128;" ::"r"(2 + half) : "memory"); }
 
