@@ -1014,6 +1014,35 @@ def case_sample(a):
             "top_p": a.top_p, "ms_with_copy": ms, "logit_bytes": bs * K * V * 4}
 
 
+def case_process(a):
+    """One logits_process launch over bs x K verify rows of fp32 logits (vocabulary 59,392): repetition 1.1 and
+    frequency 0.1 from seeded penalizer state, the in-block draft ids counted per row."""
+    from gravityocr_b200 import _lib as L
+    from gravityocr_b200.config import ModelConfig
+    from gravityocr_b200.sampling import RequestSampling, SamplerState
+    cfg = ModelConfig()
+    bs, K, V = a.bs, a.bd + 1, cfg.vocab
+    g = torch.Generator().manual_seed(6)
+    logits = (torch.randn((bs * K, V), generator=g) * 3.0).cuda()
+    cand = torch.randint(0, V, (bs * K,), generator=g).to("cuda", torch.int32)
+    rpi = torch.arange(bs, dtype=torch.int64, device="cuda")
+    st = SamplerState(V, bs, "cuda", seed=SEED)
+    seen = torch.rand((bs, V), generator=g) < 0.01   # about 1% of the vocabulary already generated per request
+    st.st_rep.copy_(torch.where(seen, 1.1, 1.0).cuda())
+    st.st_freq.copy_(torch.where(seen, 0.1, 0.0).cuda())
+    rs = [RequestSampling(temperature=0.8, top_k=50, top_p=0.95, repetition_penalty=a.repetition,
+                          frequency_penalty=a.frequency)] * bs
+    smp = st.batch(rs, rpi)
+    work = logits.clone()
+
+    def fn():   # the kernel rewrites its rows in place, so each launch starts from a fresh copy
+        work.copy_(logits)
+        L.logits_process(work, bs, K, cand, smp)
+    ms = _case_time(fn, a.reps, a.graph)
+    return {"kernel": "logits_process_kernel", "rows": bs * K, "vocab": V, "repetition": a.repetition,
+            "frequency": a.frequency, "ms_with_copy": ms, "logit_bytes": bs * K * V * 4}
+
+
 def case_main(argv):
     ap = argparse.ArgumentParser(prog="bench.py case")
     ap.add_argument("--graph", action="store_true", help="time launches captured in one CUDA graph")
@@ -1053,9 +1082,15 @@ def case_main(argv):
     sa.add_argument("--min-p", type=float, default=0.0)
     sa.add_argument("--scale", type=float, default=3.0, help="std of the synthetic logits")
     sa.add_argument("--reps", type=int, default=3)
+    pr = sub.add_parser("process")
+    pr.add_argument("--bs", type=int, default=64)
+    pr.add_argument("--bd", type=int, default=K_BD)
+    pr.add_argument("--repetition", type=float, default=1.1)
+    pr.add_argument("--frequency", type=float, default=0.1)
+    pr.add_argument("--reps", type=int, default=3)
     a = ap.parse_args(argv)
     fn = {"attention": case_attention, "linear": case_linear, "norm": case_norm, "sample": case_sample,
-          "timeline": case_timeline}[a.case]
+          "process": case_process, "timeline": case_timeline}[a.case]
     print(json.dumps(fn(a)), flush=True)
     return 0
 

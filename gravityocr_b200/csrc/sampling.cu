@@ -59,13 +59,20 @@ constexpr int kProcMaxK = 128;
 __global__ void __launch_bounds__(kProcThreads) logits_process_kernel(const SampleParams p) {
   GR_TL_BEGIN
   __shared__ int cand_s[kProcMaxK];
+  __shared__ uint32_t cand_map[kProcChunk / 32];  // bit v - v0: v is one of cand[b, 1..K-1]
   const gr_sampling& s = p.s;
   const int V = s.vocab;
   const int K = p.K;
   const int b = blockIdx.y;
   const int v0 = blockIdx.x * kProcChunk;
   const int v1 = min(V, v0 + kProcChunk);
+  for (int i = threadIdx.x; i < kProcChunk / 32; i += blockDim.x) cand_map[i] = 0u;
   for (int i = threadIdx.x; i < K; i += blockDim.x) cand_s[i] = p.cand ? p.cand[(size_t)b * K + i] : -1;
+  __syncthreads();
+  for (int i = 1 + threadIdx.x; i < K; i += blockDim.x) {
+    const int c = cand_s[i];
+    if (c >= v0 && c < v1) atomicOr(&cand_map[(c - v0) >> 5], 1u << ((c - v0) & 31));
+  }
   __syncthreads();
   const int64_t slot = s.req_pool_idx[b];
   const float rep = s.repetition ? s.repetition[b] : 1.f;
@@ -76,49 +83,83 @@ __global__ void __launch_bounds__(kProcThreads) logits_process_kernel(const Samp
   const long long stop_len = has_stop ? static_cast<long long>(s.st_len[slot]) : 0;
   const int min_new = has_stop ? s.min_new_tokens[b] : 0;
   const int words = (V + 31) >> 5;
+  // the op order, decoded once: each op then runs over 8 rows' values at a time
+  int ops[4];
+#pragma unroll
+  for (int o = 0; o < 4; ++o) ops[o] = o < s.n_order ? s.order[o] : -1;
+  const int n_stop = s.n_stop;
+  const int* stop_ids = s.stop_ids + (size_t)b * n_stop;
   for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
     const size_t sv = (size_t)slot * V + v;
     const float srep = (rep != 1.f) ? s.st_rep[sv] : 1.f;
     const float spres = (pres != 0.f) ? s.st_pres[sv] : 0.f;
     const float sfreq = (freq != 0.f) ? s.st_freq[sv] : 0.f;
     const float bias = s.logit_bias ? s.logit_bias[(size_t)b * V + v] : 0.f;
+    bool stop_v = false;  // v is one of the request's stop ids
+    if (has_stop)
+      for (int i = 0; i < n_stop; ++i) stop_v |= stop_ids[i] == v;
+    // An entry that no op changes in any row is neither read nor written: never generated (repetition state 1,
+    // presence and frequency state 0), not a draft id of the block, no stop mask, and no grammar mask or bias.  The
+    // ops are then x * 1, x / 1 and x - 0, which return x exactly.
+    const bool is_cand = (cand_map[(v - v0) >> 5] >> ((v - v0) & 31)) & 1u;
+    if (!s.allowed && !s.logit_bias && !is_cand && srep == 1.f && spres == 0.f && sfreq == 0.f &&
+        !(stop_v && stop_len < min_new))
+      continue;
+    float* col = p.logits + (size_t)b * K * V + v;  // row j of entry v at col[j * V]
     int c = 0;  // occurrences of v among cand[b, 1..j] for the current row j
     for (int j0 = 0; j0 < K; j0 += 8) {
       float lv[8];
+      int cn[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
-        lv[u] = (j0 + u < K) ? p.logits[(size_t)(b * K + j0 + u) * V + v] : 0.f;
+      for (int u = 0; u < 8; ++u) lv[u] = (j0 + u < K) ? col[(size_t)(j0 + u) * V] : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = j0 + u;
+        if (j >= 1 && j < K && cand_s[j] == v) ++c;
+        cn[u] = c;
+      }
+#pragma unroll
+      for (int o = 0; o < 4; ++o) {
+        const int op = ops[o];
+        if (op == GR_PEN_REPETITION) {
+          if (rep != 1.f) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const float S = cn[u] ? rep : srep;
+              if (S != 1.f) lv[u] = lv[u] < 0.f ? lv[u] * S : lv[u] / S;  // x * 1 = x / 1 = x exactly
+            }
+          }
+        } else if (op == GR_PEN_PRESENCE) {
+          if (pres != 0.f) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) lv[u] = lv[u] - (cn[u] ? pres : spres);
+          }
+        } else if (op == GR_PEN_FREQUENCY) {
+          if (freq != 0.f) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              float S = sfreq;
+              for (int i = 0; i < cn[u]; ++i) S = S + freq;
+              lv[u] = lv[u] - S;
+            }
+          }
+        } else if (op == GR_PEN_MIN_NEW_TOKENS) {
+          if (stop_v) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              if (stop_len + j0 + u < min_new) lv[u] = -INFINITY;
+          }
+        }
+      }
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const int j = j0 + u;
         if (j >= K) break;
-        if (j >= 1 && cand_s[j] == v) ++c;
-        float l = lv[u];
-        const bool stop_on = has_stop && stop_len + j < min_new;
-        for (int o = 0; o < s.n_order; ++o) {
-          const int op = s.order[o];
-          if (op == GR_PEN_REPETITION) {
-            if (rep != 1.f) {
-              const float S = c ? rep : srep;
-              l = l < 0.f ? l * S : l / S;
-            }
-          } else if (op == GR_PEN_PRESENCE) {
-            if (pres != 0.f) l = l - (c ? pres : spres);
-          } else if (op == GR_PEN_FREQUENCY) {
-            if (freq != 0.f) {
-              float S = sfreq;
-              for (int i = 0; i < c; ++i) S = S + freq;
-              l = l - S;
-            }
-          } else if (stop_on) {
-            for (int i = 0; i < s.n_stop; ++i)
-              if (s.stop_ids[(size_t)b * s.n_stop + i] == v) l = -INFINITY;
-          }
-        }
         const size_t r = (size_t)b * K + j;
+        float l = lv[u];
         if (s.allowed && !((s.allowed[r * words + (v >> 5)] >> (v & 31)) & 1u)) l = -INFINITY;
         if (s.logit_bias) l = l + bias;
-        p.logits[r * V + v] = l;
+        col[(size_t)j * V] = l;
       }
     }
   }

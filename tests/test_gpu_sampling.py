@@ -88,6 +88,45 @@ def test_logits_process_bit_exact(order):
             assert torch.equal(got[b * K + j], ref), (b, j)
 
 
+def test_logits_process_without_grammar_or_bias_bit_exact():
+    """No grammar mask and no logit bias: the kernel leaves every entry that no op changes unread and unwritten, and
+    rewrites the rest (generated tokens, the block's draft ids, stop ids under min_new_tokens).  Every row equals the
+    oracle's, and the untouched entries keep their exact bits (-0.0 and infinities included)."""
+    import dataclasses
+    g = torch.Generator().manual_seed(8)
+    bs, K, pool = 3, 17, 11
+    order = list(S.NAMES.values())
+    st, reqs, rpi, ost = _state_and_params(bs, pool, 2, order, g)
+    reqs = [dataclasses.replace(r, logit_bias=None) for r in reqs]
+    cand = torch.randint(0, V, (bs, K), generator=g, dtype=torch.int32)
+    cand[:, 4] = cand[:, 2]
+    cand[1, 6] = 7   # a stop id drafted inside the block
+    logits = torch.randn((bs * K, V), generator=g) * 4
+    logits[:, 100:110] = -0.0
+    logits[:, 200] = float("inf")
+    logits[:, 201] = -float("inf")
+    smp = st.batch(reqs, rpi.to(DEV))
+    dev = logits.to(DEV)
+    L.logits_process(dev, bs, K, cand.to(DEV), smp)
+    torch.cuda.synchronize()
+    got = dev.cpu()
+    used = [op for op in order if {S.REP: any(r.repetition_penalty != 1 for r in reqs),
+                                   S.FREQ: any(r.frequency_penalty != 0 for r in reqs),
+                                   S.PRES: any(r.presence_penalty != 0 for r in reqs),
+                                   S.MIN_NEW: any(r.min_new_tokens > 0 for r in reqs)}[op]]
+    changed = 0
+    for b in range(bs):
+        r = reqs[b]
+        for j in range(K):
+            ref = S.process_row(logits[b * K + j], ost[b], cand[b, 1: j + 1].tolist(), j, used, r.repetition_penalty,
+                                r.frequency_penalty, r.presence_penalty, r.min_new_tokens, list(r.stop_ids), None,
+                                None)
+            row = got[b * K + j]
+            assert torch.equal(row.view(torch.int32), ref.view(torch.int32)), (b, j)
+            changed += int((row.view(torch.int32) != logits[b * K + j].view(torch.int32)).sum())
+    assert 0 < changed < bs * K * V // 100   # a few entries rewritten, the rest left as they were
+
+
 def test_penalty_cumulate_bit_exact():
     g = torch.Generator().manual_seed(4)
     bs, K, pool = 3, 6, 8
