@@ -7,11 +7,13 @@ Hooks kept 1:1 -- ``forward_batch_generation`` (:1127), ``_draft_block`` (:660),
 hooks ``ss_bind_scheduler`` / ``ss_release_stash`` (:1001, :1019).
 
 Draft-ahead (``SELFSPEC_DRAFT_AHEAD=1`` or ``draft_ahead=True``; :1000-1125 and ``selfspec_fast_commit.py:357-440``):
-after a plain round's readback, when the host pre-check ``cannot_finish`` says no request can end this round and the
-next scheduler iteration is expected to decode the same batch, the next round's draft graph is replayed at once (the
-commit kernel has already advanced the device lengths and seeds), and the host bookkeeping runs under it.  The next
-call with the same batch (same requests, pool slots and lengths) replays only the verify + commit graph.  Anything else
-discards the pre-launched draft: ``ss_release_stash`` before a prefill admission, a changed batch, a non-plain batch.
+when the next scheduler iteration is expected to decode the same batch, a plain round's readback copy is followed at
+once by the next round's draft graph (the commit kernel has already advanced the device lengths and seeds), so the GPU
+runs it while the host waits for and reads the rows.  The reference replays it only after its host pre-check
+``cannot_finish``; here the check runs on the rows afterwards and decides whether the draft is kept, which leaves the
+GPU no gap between the verify and the next draft.  The next call with the same batch (same requests, pool slots and
+lengths) replays only the verify + commit graph.  Anything else discards the pre-launched draft: a request that can
+end this round, ``ss_release_stash`` before a prefill admission, a changed batch, a non-plain batch.
 Pages are owned per request here, so a discarded draft frees nothing: its K/V rows sit at positions the next draft
 rewrites before anything reads them.  The result carries the reference's contract (:954-961, :990-998): ``next_token_ids`` = the
 device next seeds [bs], ``next_token_ids_cpu`` = the committed tokens per request, ``accept_length_per_req_cpu``
@@ -361,6 +363,23 @@ class SelfSpecDiffusionWorker:
         bs = len(batch.reqs)
         rb.host.copy_(rb.readback, non_blocking=True)
         rb.event.record()
+        # Draft-ahead goes out before the readback is waited on, so the GPU runs it while the host reads the rows.  It
+        # is kept only if no request can end this round; otherwise it is dropped, which is harmless: the draft writes
+        # K/V beyond the committed lengths (rewritten before anything reads them) and its own outputs, and the
+        # readback was copied before it in stream order.
+        launched = False
+        if plain and self._draft_ahead and self._graphs and getattr(rb, "gd", None) is not None:
+            if self._ahead_allowed(batch):
+                # the longest-first attention order only schedules (results do not depend on it), and lengths move by
+                # at most K + 1 a round: on an unchanged batch it is refreshed every 8th round, not between every
+                # verify and the next draft
+                if self.n_rounds % 8 == 0:
+                    self.engine.refresh_order(rb)
+                rb.gd.replay()
+                launched = True
+                self.ahead_stats["launched"] += 1
+            else:
+                self.ahead_stats["skip_sched"] += 1
         rb.event.synchronize()
         h = rb.host
         st = int(h[bs * (K + 2) + 1])
@@ -368,17 +387,11 @@ class SelfSpecDiffusionWorker:
             raise RuntimeError(f"device status {st}: {L.load().gr_status_string(st).decode()}")
         rows = h[: bs * (K + 2)].view(bs, K + 2).tolist()
         ahead = False
-        if plain and self._draft_ahead and self._graphs and getattr(rb, "gd", None) is not None:
-            if not all(cannot_finish(q, [r[0]] + r[2: 3 + r[1]]) for q, r in zip(batch.reqs, rows)):
-                self.ahead_stats["skip_finish"] += 1
-            elif not self._ahead_allowed(batch):
-                self.ahead_stats["skip_sched"] += 1
+        if launched:
+            if all(cannot_finish(q, [r[0]] + r[2: 3 + r[1]]) for q, r in zip(batch.reqs, rows)):
+                ahead = True  # no request ends this round: the device lengths and seeds were the next round's
             else:
-                # no request ends this round: the device lengths and seeds are the next round's already
-                self.engine.refresh_order(rb)
-                rb.gd.replay()
-                ahead = True
-                self.ahead_stats["launched"] += 1
+                self.ahead_stats["skip_finish"] += 1
         toks, js, accs = host_commit(batch.reqs, rows)
         # the kernel advanced seq_lens by acc + 2 (x0 + verify rows 0..acc); a request cut inside the round keeps j + 1
         fix = [accs[i] + 1 - js[i] for i in range(bs)]
