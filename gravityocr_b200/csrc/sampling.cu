@@ -208,13 +208,19 @@ __device__ __forceinline__ unsigned long long block_sum64(unsigned long long v, 
 // of 8 bits over the row: each warp builds a private histogram of count and fixed-point mass per bucket with 32-bit
 // shared atomics (contention stays inside one warp even when a flat distribution puts every entry in one bucket), the
 // warps' histograms are summed per bucket, and warp 0 scans the 256 buckets from the top.
+// Once the bucket a level picked holds at most kCompactCap entries, the next level's pass over the row also copies
+// those entries' bits into shared memory, and the levels after it read only that copy.
+constexpr int kCompactCap = 4096;
 struct SelectSmem {
   uint32_t wc[kSampWarps][256];  // per-warp counts
   uint32_t wl[kSampWarps][256];  // per-warp mass, low 20 bits of each entry's fixed-point value
   uint32_t wh[kSampWarps][256];  // per-warp mass, the high bits (<= 2^20 per entry, at most 4,095 entries a warp)
   uint32_t hc[256];
   unsigned long long hs[256];
+  uint32_t comp[kCompactCap];    // bits of the entries in the picked bucket (any order)
   uint32_t prefix, tau, done;
+  uint32_t n_comp;               // entries copied to comp
+  uint32_t c_bucket;             // entries in the bucket the last level picked
   unsigned long long c_above, s_above;
 };
 // One pass of the select: every positive entry whose higher bits equal `prefix` adds its count and fixed-point mass to
@@ -223,9 +229,14 @@ struct SelectSmem {
 // or two buckets of the exponent, and every lane's atomic on the same word serialised; on a peaked row the entries
 // spread over many buckets and the register cache only adds divergent branches.  The sums are integers, so both
 // forms build the same histogram.
+// comp (when given): every counted entry's bits are also appended there, n_comp counting them; the caller guarantees
+// room (the count of the bucket this pass filters on is known from the previous level).  A warp's lanes run the same
+// iterations, so the appends take one ballot and one shared atomic per warp.
 template <bool AGG>
 __device__ __forceinline__ void histogram_pass(const float* row, int V, int level, uint32_t prefix, bool need_c,
-                                               bool need_m, uint32_t* wc, uint32_t* wl, uint32_t* wh) {
+                                               bool need_m, uint32_t* wc, uint32_t* wl, uint32_t* wh,
+                                               uint32_t* comp = nullptr, uint32_t* n_comp = nullptr) {
+  const int lane = threadIdx.x & 31;
   const int shift = 24 - 8 * level;
   uint32_t bin_a = 0xFFFFFFFFu, bin_b = 0xFFFFFFFFu, cnt_a = 0, cnt_b = 0;
   uint64_t mass_a = 0, mass_b = 0;
@@ -237,7 +248,8 @@ __device__ __forceinline__ void histogram_pass(const float* row, int V, int leve
       atomicAdd(&wh[bin], static_cast<uint32_t>(mass >> 20));
     }
   };
-  for (int v0 = threadIdx.x; v0 < V; v0 += kRowBatch * blockDim.x) {
+  for (int w0 = threadIdx.x - lane; w0 < V; w0 += kRowBatch * blockDim.x) {  // uniform across the warp
+    const int v0 = w0 + lane;
     float ev[kRowBatch];
 #pragma unroll
     for (int u = 0; u < kRowBatch; ++u) {
@@ -248,7 +260,18 @@ __device__ __forceinline__ void histogram_pass(const float* row, int V, int leve
     for (int u = 0; u < kRowBatch; ++u) {
       const float e = ev[u];
       const uint32_t ub = __float_as_uint(e);
-      if (e > 0.f && (level == 0 || (ub >> (shift + 8)) == prefix)) {
+      const bool counted = e > 0.f && (level == 0 || (ub >> (shift + 8)) == prefix);
+      if (comp) {
+        const unsigned bal = __ballot_sync(0xffffffffu, counted);
+        if (bal) {
+          uint32_t base = 0;
+          if (lane == 0) base = atomicAdd(n_comp, static_cast<uint32_t>(__popc(bal)));
+          base = __shfl_sync(0xffffffffu, base, 0);
+          const uint32_t at = base + static_cast<uint32_t>(__popc(bal & ((1u << lane) - 1u)));
+          if (counted && at < kCompactCap) comp[at] = ub;
+        }
+      }
+      if (counted) {
         const uint32_t bin = (ub >> shift) & 255u;
         const uint64_t w = need_m ? fixed40(e) : 0ull;
         if (!AGG) {
@@ -279,7 +302,9 @@ __device__ __forceinline__ void histogram_pass(const float* row, int V, int leve
 
 __device__ uint32_t select_threshold(const float* row, int V, long long k, double lim, bool strict, bool flat,
                                      SelectSmem& sm) {
-  const bool need_c = k < (1ll << 62), need_m = lim < 1e300;  // a criterion that is off needs no histogram
+  // Counts are always taken (an off count criterion has k = 2^62): the picked bucket's count decides the copy.
+  // The mass histogram is skipped when top-p is off.
+  const bool need_m = lim < 1e300;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     sm.prefix = 0;
@@ -287,8 +312,13 @@ __device__ uint32_t select_threshold(const float* row, int V, long long k, doubl
     sm.done = 0;
     sm.c_above = 0;
     sm.s_above = 0;
+    sm.n_comp = 0;
+    sm.c_bucket = 0xFFFFFFFFu;
   }
   __syncthreads();
+  const float* src = row;  // the row, or the shared copy of the picked bucket's entries once made
+  int n_src = V;
+  bool from_copy = false;
   for (int level = 0; level < 4; ++level) {
     const int shift = 24 - 8 * level;
     for (int i = lane; i < 256; i += 32) {
@@ -298,11 +328,19 @@ __device__ uint32_t select_threshold(const float* row, int V, long long k, doubl
     }
     __syncwarp();
     const uint32_t prefix = sm.prefix;
+    const bool copy =
+        !from_copy && (level == 1 || level == 2) && sm.c_bucket <= static_cast<uint32_t>(kCompactCap);
     if (flat && level == 0)
-      histogram_pass<true>(row, V, 0, prefix, need_c, need_m, sm.wc[warp], sm.wl[warp], sm.wh[warp]);
+      histogram_pass<true>(row, V, 0, prefix, true, need_m, sm.wc[warp], sm.wl[warp], sm.wh[warp]);
     else
-      histogram_pass<false>(row, V, level, prefix, need_c, need_m, sm.wc[warp], sm.wl[warp], sm.wh[warp]);
+      histogram_pass<false>(src, n_src, level, prefix, true, need_m, sm.wc[warp], sm.wl[warp], sm.wh[warp],
+                            copy ? sm.comp : nullptr, &sm.n_comp);
     __syncthreads();
+    if (copy) {
+      src = reinterpret_cast<const float*>(sm.comp);
+      n_src = static_cast<int>(min(sm.n_comp, static_cast<uint32_t>(kCompactCap)));
+      from_copy = true;
+    }
     for (int i = threadIdx.x; i < 256; i += blockDim.x) {
       uint32_t c = 0;
       unsigned long long lo = 0, hi = 0;
@@ -380,6 +418,8 @@ __device__ uint32_t select_threshold(const float* row, int V, long long k, doubl
             sm.prefix = here;
             sm.c_above = c_top;
             sm.s_above = s_top;
+            sm.c_bucket = sm.hc[d];
+            sm.n_comp = 0;
           }
         }
       }
