@@ -750,6 +750,7 @@ int gr_sample_rows(float* logits, int bs, int K, const int32_t* cand, const gr_s
   p.first_out = first_out;
   p.first_stride = first_stride;
   p.status = status;
+  p.sms = num_sms();
   return launch_sample_rows(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? GR_OK : GR_ERR_CUDA;
 }
 

@@ -119,6 +119,7 @@ struct SampleParams {
   int tok_stride;
   const int32_t* counts;
   int add;
+  int sms;                 // SMs of the device (sample_rows picks its CTA size by the rows per SM)
 };
 struct OverrideParams {
   int bs, K, g_stride, plan_stride, vocab, mask_id;

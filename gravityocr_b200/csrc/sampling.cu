@@ -13,10 +13,13 @@ namespace gr {
 
 constexpr int kProcChunk = 2048;   // logits_process: vocabulary entries per CTA
 constexpr int kProcThreads = 256;
-constexpr int kSampThreads = 512;  // sample_rows: one CTA per row, two per SM
-constexpr int kSampWarps = kSampThreads / 32;
+// sample_rows: one CTA per row.  512 threads, two CTAs per SM, when the launch has at least as many rows as SMs (one
+// row's barrier waits overlap the other's loads); 1,024 threads, one CTA per SM, below that, where a row's latency
+// is the launch's (the a0 and prefill draws of one row per request).
+constexpr int kSampThreadsMany = 512;
+constexpr int kSampThreadsFew = 1024;
 // A warp's bucket words are 32-bit and take under 2^20 + 1 per entry (count 1, mass halves of a weight <= 2^40).
-static_assert(32 * ((kSampleMaxVocab + kSampThreads - 1) / kSampThreads) <= 4095, "bucket words could wrap");
+static_assert(32 * ((kSampleMaxVocab + kSampThreadsMany - 1) / kSampThreadsMany) <= 4095, "bucket words could wrap");
 // Row loops load kRowBatch entries per thread before using any: a row pass is bound by L2 latency, and one load in
 // flight per thread (a dependent load per iteration) left 0.9 ms per 1,088-row launch in long-scoreboard stalls.
 // The entries a thread visits, and their order, are unchanged.
@@ -166,14 +169,15 @@ __global__ void __launch_bounds__(kProcThreads) logits_process_kernel(const Samp
   GR_TL_END(kTlLogitsProcess)
 }
 
-// ---------------------------------------------------------------- block reductions (kSampThreads threads)
+// ---------------------------------------------------------------- block reductions (W warps)
+template <int W>
 __device__ __forceinline__ float block_max(float v, float* sh) {
   for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   if (l == 0) sh[w] = v;
   __syncthreads();
   if (w == 0) {
-    v = l < kSampWarps ? sh[l] : -INFINITY;
+    v = l < W ? sh[l] : -INFINITY;
     for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     if (l == 0) sh[0] = v;
   }
@@ -186,13 +190,14 @@ __device__ __forceinline__ unsigned long long warp_sum64(unsigned long long v) {
   for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
+template <int W>
 __device__ __forceinline__ unsigned long long block_sum64(unsigned long long v, unsigned long long* sh) {
   v = warp_sum64(v);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   if (l == 0) sh[w] = v;
   __syncthreads();
   if (w == 0) {
-    v = l < kSampWarps ? sh[l] : 0ull;
+    v = l < W ? sh[l] : 0ull;
     v = warp_sum64(v);
     if (l == 0) sh[0] = v;
   }
@@ -211,10 +216,11 @@ __device__ __forceinline__ unsigned long long block_sum64(unsigned long long v, 
 // Once the bucket a level picked holds at most kCompactCap entries, the next level's pass over the row also copies
 // those entries' bits into shared memory, and the levels after it read only that copy.
 constexpr int kCompactCap = 4096;
+template <int W>
 struct SelectSmem {
-  uint32_t wc[kSampWarps][256];  // per-warp counts
-  uint32_t wl[kSampWarps][256];  // per-warp mass, low 20 bits of each entry's fixed-point value
-  uint32_t wh[kSampWarps][256];  // per-warp mass, the high bits (<= 2^20 per entry, at most 4,095 entries a warp)
+  uint32_t wc[W][256];  // per-warp counts
+  uint32_t wl[W][256];  // per-warp mass, low 20 bits of each entry's fixed-point value
+  uint32_t wh[W][256];  // per-warp mass, the high bits (<= 2^20 per entry, at most 4,095 entries a warp)
   uint32_t hc[256];
   unsigned long long hs[256];
   uint32_t comp[kCompactCap];    // bits of the entries in the picked bucket (any order)
@@ -300,8 +306,9 @@ __device__ __forceinline__ void histogram_pass(const float* row, int V, int leve
   }
 }
 
+template <int W>
 __device__ uint32_t select_threshold(const float* row, int V, long long k, double lim, bool strict, bool flat,
-                                     SelectSmem& sm) {
+                                     SelectSmem<W>& sm) {
   // Counts are always taken (an off count criterion has k = 2^62): the picked bucket's count decides the copy.
   // The mass histogram is skipped when top-p is off.
   const bool need_m = lim < 1e300;
@@ -345,7 +352,7 @@ __device__ uint32_t select_threshold(const float* row, int V, long long k, doubl
       uint32_t c = 0;
       unsigned long long lo = 0, hi = 0;
 #pragma unroll 8
-      for (int q = 0; q < kSampWarps; ++q) {
+      for (int q = 0; q < W; ++q) {
         c += sm.wc[q][i];
         lo += sm.wl[q][i];
         hi += sm.wh[q][i];
@@ -433,13 +440,15 @@ __device__ uint32_t select_threshold(const float* row, int V, long long k, doubl
 }
 
 // ---------------------------------------------------------------- target distribution, accept test, draws
-__global__ void __launch_bounds__(kSampThreads, 2) sample_rows_kernel(const SampleParams p) {
+template <int NT>
+__global__ void __launch_bounds__(NT, NT == kSampThreadsMany ? 2 : 1) sample_rows_kernel(const SampleParams p) {
+  constexpr int NW = NT / 32;  // warps
   GR_TL_BEGIN
-  __shared__ float shf[kSampWarps];
-  __shared__ unsigned long long shu[kSampWarps];
+  __shared__ float shf[NW];
+  __shared__ unsigned long long shu[NW];
   extern __shared__ __align__(16) uint8_t dyn_smem[];
-  SelectSmem& sel = *reinterpret_cast<SelectSmem*>(dyn_smem);
-  __shared__ unsigned long long scan[kSampWarps];
+  SelectSmem<NW>& sel = *reinterpret_cast<SelectSmem<NW>*>(dyn_smem);
+  __shared__ unsigned long long scan[NW];
   __shared__ int found;
   const gr_sampling& s = p.s;
   const int V = s.vocab;
@@ -463,7 +472,7 @@ __global__ void __launch_bounds__(kSampThreads, 2) sample_rows_kernel(const Samp
 #pragma unroll
     for (int u = 0; u < kRowBatch; ++u) mx = fmaxf(mx, lv[u]);
   }
-  const float m = block_max(mx, shf) / T;
+  const float m = block_max<NW>(mx, shf) / T;
   const int d = (p.K > 1 && j + 1 < p.K) ? p.cand[(size_t)b * p.K + j + 1] : -1;
   if (!(m > -INFINITY)) {  // every token masked
     if (threadIdx.x == 0) {
@@ -494,7 +503,7 @@ __global__ void __launch_bounds__(kSampThreads, 2) sample_rows_kernel(const Samp
       }
     }
   }
-  const uint64_t Z = block_sum64(z, shu);
+  const uint64_t Z = block_sum64<NW>(z, shu);
   // a mean weight of at least 1/32 (the maximum is 1) marks a flat row, whose first select pass aggregates in registers
   const bool flat = Z >= (static_cast<uint64_t>(V) << 35);
   // keep threshold of the filters
@@ -527,7 +536,7 @@ __global__ void __launch_bounds__(kSampThreads, 2) sample_rows_kernel(const Samp
         for (int u = 0; u < kRowBatch; ++u)
           if (__float_as_uint(ev[u]) >= t1 && ev[u] > 0.f) zk += fixed40(ev[u]);
       }
-      const uint64_t Zk = block_sum64(zk, shu);
+      const uint64_t Zk = block_sum64<NW>(zk, shu);
       const uint32_t t2 = select_threshold(row, V, 1ll << 62, static_cast<double>(P) * Zk, true, flat, sel);
       t1 = max(t1, t2);
     }
@@ -538,7 +547,7 @@ __global__ void __launch_bounds__(kSampThreads, 2) sample_rows_kernel(const Samp
   // (coalesced); the block scans the warps' kept mass in vocabulary order, and the warp holding the target walks its
   // segment again with a warp-wide inclusive scan per 32 entries
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int seg = ((V + kSampWarps - 1) / kSampWarps + 31) & ~31;
+  const int seg = ((V + NW - 1) / NW + 31) & ~31;
   const int lo = warp * seg, hi = min(V, lo + seg);
   auto kept_w = [&](int v) -> uint64_t {
     const float e = row[v];
@@ -562,7 +571,7 @@ __global__ void __launch_bounds__(kSampThreads, 2) sample_rows_kernel(const Samp
   if (threadIdx.x == 0) found = -1;
   __syncthreads();
   uint64_t W = 0, before = 0;
-  for (int i = 0; i < kSampWarps; ++i) {
+  for (int i = 0; i < NW; ++i) {
     if (i == warp) before = W;
     W += scan[i];
   }
@@ -659,15 +668,21 @@ cudaError_t launch_logits_process(const SampleParams& p, cudaStream_t s) {
   logits_process_kernel<<<grid, kProcThreads, 0, s>>>(p);
   return cudaGetLastError();
 }
-cudaError_t launch_sample_rows(const SampleParams& p, cudaStream_t s) {
+template <int NT>
+static cudaError_t launch_sample_rows_t(const SampleParams& p, cudaStream_t s) {
+  using Smem = SelectSmem<NT / 32>;
   static PerDeviceOnce configured;
   cudaError_t e = once_per_device(configured, [] {
-    return cudaFuncSetAttribute(sample_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(sizeof(SelectSmem)));
+    return cudaFuncSetAttribute(sample_rows_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(sizeof(Smem)));
   });
   if (e != cudaSuccess) return e;
-  sample_rows_kernel<<<p.bs * p.K, kSampThreads, sizeof(SelectSmem), s>>>(p);
+  sample_rows_kernel<NT><<<p.bs * p.K, NT, sizeof(Smem), s>>>(p);
   return cudaGetLastError();
+}
+cudaError_t launch_sample_rows(const SampleParams& p, cudaStream_t s) {
+  return p.bs * p.K < p.sms ? launch_sample_rows_t<kSampThreadsFew>(p, s)
+                             : launch_sample_rows_t<kSampThreadsMany>(p, s);
 }
 cudaError_t launch_penalty_cumulate(const SampleParams& p, cudaStream_t s) {
   penalty_cumulate_kernel<<<p.bs, 64, 0, s>>>(p);
