@@ -177,15 +177,18 @@ def _draw_margin(p, u, exclude):
     return float((c - t).abs().min() / c[-1])
 
 
+# (6, 5, 3): 30 rows, fewer than the SMs (the launch runs 1,024-thread CTAs); (10, 17, 1): 170 rows (two
+# 512-thread CTAs per SM), one round
+@pytest.mark.parametrize("bs,K,rounds", [(6, 5, 3), (10, 17, 1)])
 @pytest.mark.parametrize("shape", ["peaked", "flat"])
 @pytest.mark.parametrize("mode", [L.FILTER_JOINT, L.FILTER_SEQUENTIAL, L.FILTER_TORCH])
-def test_sample_rows_match_oracle(mode, shape):
-    g = torch.Generator().manual_seed(10 + mode + (100 if shape == "flat" else 0))
-    bs, K, seed = 6, 5, 1234567
+def test_sample_rows_match_oracle(mode, shape, bs, K, rounds):
+    g = torch.Generator().manual_seed(10 + mode + (100 if shape == "flat" else 0) + bs)
+    seed = 1234567
     st = SamplerState(V, bs, DEV, seed=seed, filter=mode)
-    reqs = [RequestSampling(temperature=[0.6, 1.0, 1.3, 0.9, 0.0, 1.0][b], top_k=[-1, 40, 1000, 5, -1, -1][b],
-                            top_p=[0.9, 1.0, 0.8, 0.95, 1.0, 0.5][b],
-                            min_p=0.0 if mode == L.FILTER_JOINT else [0.0, 0.1, 0.02, 0.0, 0.0, 0.3][b])
+    reqs = [RequestSampling(temperature=[0.6, 1.0, 1.3, 0.9, 0.0, 1.0][b % 6],
+                            top_k=[-1, 40, 1000, 5, -1, -1][b % 6], top_p=[0.9, 1.0, 0.8, 0.95, 1.0, 0.5][b % 6],
+                            min_p=0.0 if mode == L.FILTER_JOINT else [0.0, 0.1, 0.02, 0.0, 0.0, 0.3][b % 6])
             for b in range(bs)]   # a flashinfer batch with min-p takes the sequential filter (tested on its own)
     if shape == "peaked":   # a few dominant tokens over a spread-out bulk
         logits = torch.randn((bs * K, V), generator=g) * 2
@@ -197,7 +200,7 @@ def test_sample_rows_match_oracle(mode, shape):
     smp = st.batch(reqs, rpi.to(DEV))
     assert smp.filter == mode
     ties, mism = [], []
-    for rnd in range(3):
+    for rnd in range(rounds):
         dev = logits.to(DEV)
         accept = torch.zeros(bs * K, dtype=torch.int32, device=DEV)
         sample = torch.zeros(bs * K, dtype=torch.int32, device=DEV)
