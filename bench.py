@@ -67,6 +67,18 @@ def peaks():
     return 6650.0, 1590.0, 1400.0, "fallback"
 
 
+def prefill_line(cfg, prefix, seconds, tc_sustained, peak_src, chunk):
+    """The prefill before the timed rounds (wall clock, host input staging included), against the dense causal
+    prefill's algorithmic FLOPs at the sustained bf16 peak."""
+    from gravityocr_b200.metrics import prefill_flops
+    fl = prefill_flops(cfg, prefix)
+    return {"tokens": int(sum(prefix)), "s": round(seconds, 3), "tokens_per_s": round(sum(prefix) / seconds, 1),
+            "tflops": round(fl / seconds / 1e12, 1), "tensor_frac": round(fl / seconds / 1e12 / tc_sustained, 4),
+            "peak": f"{peak_src} bf16 GEMM sustained", "flops": fl,
+            "how": f"chunks of {chunk} rows per request through the decode kernels (the attention kernel holds a "
+                   f"request's {chunk} query rows in one tile); not in the timed region"}
+
+
 def forward_bound(cfg, seqs, K, verify, ms, hbm_peak, tc_sustained):
     """A forward's time against its roofline.  hbm_frac / tensor_frac: all bytes / HBM peak and all FLOPs / sustained
     tensor peak over the forward's time.  serial_bound_frac: the forward runs its phases one after another, so its
@@ -370,6 +382,7 @@ def main():
                      "algorithmic_bytes": attn_b, "avg_launch_ms": round(attn_ms, 5), "peak_source": peak_src},
         "gpu_launches": launches,
         "prefill_s": round(t_pf, 2),
+        "prefill": prefill_line(cfg, prefix, t_pf, tc_sus, peak_src, chunk),
     }
     if rank == 0:
         line["clocks"] = clk.summary()

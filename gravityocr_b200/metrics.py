@@ -31,3 +31,13 @@ def attention_bytes(cfg: ModelConfig, seq_lens: Sequence[int], K: int, base_add:
     kv = sum(int(s) + base_add + K for s in seq_lens) * cfg.n_kv_heads * cfg.head_dim * 2 * 2
     qo = 2 * len(seq_lens) * K * cfg.q_dim * 2
     return kv + qo
+
+
+def prefill_flops(cfg: ModelConfig, prefix_lens: Sequence[int]) -> int:
+    """Dense causal prefill of each prefix (the algorithmic work, whatever the chunking): every decoder weight once per
+    prefix token, causal attention (token t sees t + 1 positions), and lm_head for each request's last token."""
+    decoder = cfg.streamed_params() - cfg.vocab * cfg.hidden - cfg.hidden
+    n = sum(int(x) for x in prefix_lens)
+    causal = sum(int(x) * (int(x) + 1) // 2 for x in prefix_lens)
+    attn = 4 * cfg.n_q_heads * cfg.head_dim * causal * cfg.n_layers
+    return 2 * decoder * n + attn + 2 * cfg.vocab * cfg.hidden * len(prefix_lens)
