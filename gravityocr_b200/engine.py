@@ -369,21 +369,35 @@ class Engine:
         n_chunks = max((n + chunk - 1) // chunk for n in lens)
         mm = prefix_pos3 is not None and any(p is not None for p in prefix_pos3)
         H = self.cfg.hidden
-        first = [0] * bs
         self.reserve(bs * chunk)
         out_idx = torch.zeros((bs * chunk,), dtype=torch.int32, device=dev)
+        # Every prefix row and id goes to the device once; a chunk gathers its rows there (row `pad` is zeros, for the
+        # rows past a prefix that ends inside the chunk).  The first tokens stay on the device until the end, so the
+        # host never waits for a chunk and stays ahead of the GPU.
+        offs = [0]
+        for n in lens:
+            offs.append(offs[-1] + n)
+        pad = offs[-1]
+        all_rows = torch.empty((pad + 1, H), dtype=torch.float32, device=dev)
+        all_ids = torch.empty((pad + 1,), dtype=torch.int64, device=dev)
+        for b in range(bs):
+            all_rows[offs[b]: offs[b + 1]].copy_(prefixes[b])
+            all_ids[offs[b]: offs[b + 1]].copy_(prefix_ids[b])
+        all_rows[pad].zero_()
+        all_ids[pad] = 0
+        first_dev = torch.zeros((bs,), dtype=torch.int64, device=dev)
         for c in range(n_chunks):
             active = [b for b in range(bs) if lens[b] > c * chunk]
             nb = len(active)
-            rows_e = torch.zeros((nb * chunk, H), dtype=torch.float32)
-            ids = torch.zeros((nb * chunk,), dtype=torch.int64)
+            gather = torch.full((nb * chunk,), pad, dtype=torch.int64)
             for i, b in enumerate(active):
                 s0, s1 = c * chunk, min(lens[b], (c + 1) * chunk)
-                rows_e[i * chunk: i * chunk + s1 - s0] = prefixes[b][s0:s1].float()
-                ids[i * chunk: i * chunk + s1 - s0] = prefix_ids[b][s0:s1]
+                gather[i * chunk: i * chunk + s1 - s0] = torch.arange(offs[b] + s0, offs[b] + s1)
+            gather = gather.to(dev)
+            rows_e = all_rows.index_select(0, gather)
+            ids = all_ids.index_select(0, gather)
             seq = torch.full((nb,), c * chunk, dtype=torch.int64).to(dev)
             pt = rb.page_table[torch.tensor(active, device=dev)].contiguous()
-            rows_e, ids = rows_e.to(dev), ids.to(dev)
             pos3 = None
             if mm:
                 pos3 = (torch.arange(c * chunk, (c + 1) * chunk, dtype=torch.int32)[None, :, None]
@@ -405,15 +419,14 @@ class Engine:
             if ends:
                 rows = self.x[torch.tensor([r for _, r in ends], device=dev)].contiguous()
                 if first_fn is not None:
-                    res = first_fn(rows, [b for b, _ in ends]).cpu()
+                    res = first_fn(rows, [b for b, _ in ends])
                 else:
                     e = L.Epilogue()
                     e.mode = L.EPI_ARGMAX
                     e.out_idx = out_idx.data_ptr()
                     L.linear(self.w.lm_head, rows, len(ends), e, self.lin_ws, status=rb.status)
-                    res = out_idx[: len(ends)].cpu()
-                for k, (b, _) in enumerate(ends):
-                    first[b] = int(res[k])
+                    res = out_idx[: len(ends)]
+                first_dev[torch.tensor([b for b, _ in ends], device=dev)] = res.to(device=dev, dtype=torch.int64)
         rb.seq_lens.copy_(torch.tensor(lens, dtype=torch.int64))
         delta = [0] * bs
         for b in range(bs):
@@ -421,11 +434,11 @@ class Engine:
                 delta[b] = int(prefix_pos3[b].max()) + 1 - lens[b]
         rb.pos_delta.copy_(torch.tensor(delta, dtype=torch.int32))
         self.refresh_order(rb)
-        rb.seeds[rb.rpi] = torch.tensor(first, dtype=torch.int64, device=dev)
+        rb.seeds[rb.rpi] = first_dev
         rb.n_committed.fill_(1)
         rb.rounds.zero_()
         self.check_status(rb)
-        return first
+        return first_dev.cpu().tolist()
 
     def refresh_order(self, rb: RoundBuffers) -> None:
         """Longest-first attention launch order from the current lengths (scheduling only; results do not depend on
